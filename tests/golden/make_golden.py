@@ -1,0 +1,267 @@
+"""Writes the golden fixtures under tests/golden/ by running the REFERENCE's
+own code (imported from the reference checkout named by --reference, default
+/root/reference) on seeded inputs. Run once, in a machine that has the
+reference; the fixtures are committed and the tests read only them:
+
+    python tests/golden/make_golden.py --reference /root/reference
+
+What each fixture pins (paths relative to the reference repository):
+  exact_small.npz       pytorch_kernels.exact_attention (+ top-k choice, LSE
+                        read from the autograd node's saved tensors),
+                        packages/wpt-model/src/wpt_model/pytorch_kernels.py:98-146
+  exact_generation.npz  the same on a generation pass: ragged rows, a query past
+                        the table, k/v halves of one entries table
+                        (tests/test_triton_kernels.py:51-77's case)
+  sparse_small.npz      pytorch_kernels.sparse_attention, :171-217
+  window_small.npz      attention.window_attention with WINDOW patched to 8,
+                        attention.py:85-107
+  config1.npz           BASELINE config 1 (B=2, T=512, H=8, c=64, window 128,
+                        fp32): window_attention (sink 0 and sink ~ N(0, .5)),
+                        causal exact_attention, sparse_attention with no chosen
+                        rows; a strided subset of row 0's queries is stored
+  tree.npz              attention.dense_attention with an ancestor mask
+                        (attention.py:74-82), and exact_attention for a chain
+  accept_*.npz          wpt_inference.Writer._speculate (__init__.py:196-233)
+                        with a fake model and drafter, torch.rand and
+                        torch.multinomial replaced by explicit draws
+"""
+
+import argparse
+import os
+import sys
+
+import numpy as np
+import torch
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+
+
+def _import_reference(root):
+    for package in ("wpt-model", "wpt-utils", "wpt-inference"):
+        sys.path.insert(0, os.path.join(root, "packages", package, "src"))
+    from wpt_model import attention, pytorch_kernels  # noqa: E402
+    import wpt_inference  # noqa: E402
+    return attention, pytorch_kernels, wpt_inference
+
+
+def _np(x):
+    return x.detach().cpu().numpy()
+
+
+def _lse_of(out):
+    """The LSE the reference's _Exact/_Sparse saved for its backward pass."""
+    return _np(out.grad_fn.saved_tensors[-1])
+
+
+def _inputs(B, T, H, c, N, seed):
+    g = torch.Generator().manual_seed(seed)
+
+    def rand(*shape):
+        return torch.randn(*shape, generator=g).requires_grad_()
+    positions = (N - T + torch.arange(T)).expand(B, T).contiguous()
+    return rand(B, T, H, c), rand(B, N, c), rand(B, N, c), rand(H), positions
+
+
+def exact_small(pk):
+    q, k, v, _, positions = _inputs(2, 30, 3, 16, 50, 0)
+    out, chosen = pk.exact_attention(q, k, v, positions, 0.3, 5, 8)
+    np.savez(os.path.join(HERE, "exact_small.npz"), q=_np(q), k=_np(k), v=_np(v), positions=_np(positions),
+             scale=0.3, top_k=5, window=8, out=_np(out), lse=_lse_of(out), chosen=_np(chosen))
+
+
+def exact_generation(pk):
+    g = torch.Generator().manual_seed(0)
+    B, T, H, c, N, top_k, window = 3, 4, 4, 32, 60, 8, 4
+    q = torch.randn(B, T, H, c, generator=g).requires_grad_()
+    entries = torch.randn(B, N, 2 * c, generator=g)
+    k, v = entries[..., :c], entries[..., c:]
+    positions = torch.tensor([[56, 57, 58, 59], [20, 21, 22, 23], [58, 59, 60, 61]])
+    out, chosen = pk.exact_attention(q, k, v, positions, c ** -0.5, top_k, window)
+    np.savez(os.path.join(HERE, "exact_generation.npz"), q=_np(q), entries=_np(entries), positions=_np(positions),
+             scale=c ** -0.5, top_k=top_k, window=window, out=_np(out), lse=_lse_of(out), chosen=_np(chosen))
+
+
+def sparse_small(pk):
+    q, k, v, sink, positions = _inputs(2, 30, 3, 16, 50, 1)
+    g = torch.Generator().manual_seed(2)
+    idx = torch.stack([torch.stack([torch.randperm(int(p) - 4, generator=g)[:6] if int(p) >= 10
+                                    else torch.full((6,), -1) for p in row]) for row in positions])
+    idx[:, ::3, -2:] = -1
+    out = pk.sparse_attention(q, k, v, sink, idx, positions, 0.3, 5)
+    np.savez(os.path.join(HERE, "sparse_small.npz"), q=_np(q), k=_np(k), v=_np(v), sink=_np(sink), idx=_np(idx),
+             positions=_np(positions), scale=0.3, window=5, out=_np(out), lse=_lse_of(out))
+
+
+def window_small(at):
+    g = torch.Generator().manual_seed(3)
+    W, B, T, H, c = 8, 2, 20, 3, 16
+    q = torch.randn(B, T, H, c, generator=g)
+    k = torch.randn(B, W - 1 + T, c, generator=g)
+    v = torch.randn(B, W - 1 + T, c, generator=g)
+    sink = torch.randn(H, generator=g) * 0.5
+    positions = torch.stack([3 + torch.arange(T), 40 + torch.arange(T)])  # row 0 starts near the text's start
+    saved = at.WINDOW
+    at.WINDOW = W
+    try:
+        out = at.window_attention(q, k, v, sink, positions, 0.25)
+    finally:
+        at.WINDOW = saved
+    np.savez(os.path.join(HERE, "window_small.npz"), q=_np(q), k=_np(k), v=_np(v), sink=_np(sink),
+             positions=_np(positions), scale=0.25, window=W, out=_np(out))
+
+
+def config1(at, pk):
+    """BASELINE config 1; a strided subset of row 0's queries is stored."""
+    g = torch.Generator().manual_seed(0)
+    B, T, H, c, W = 2, 512, 8, 64, 128
+    q = torch.randn(B, T, H, c, generator=g)
+    k = torch.randn(B, T, c, generator=g)
+    v = torch.randn(B, T, c, generator=g)
+    sink = torch.randn(H, generator=g) * 0.5
+    positions = torch.arange(T).expand(B, T).contiguous()
+    scale = c ** -0.5
+    tail = torch.zeros(B, W - 1, c)
+    kt, vt = torch.cat([tail, k], 1), torch.cat([tail, v], 1)
+    keep = slice(None, None, 8)
+    results = {}
+    with torch.no_grad():
+        results["window_sink0"] = at.window_attention(q, kt, vt, torch.zeros(H), positions, scale)
+        results["window_sink"] = at.window_attention(q, kt, vt, sink, positions, scale)
+        results["exact"], _ = pk.exact_attention(q, k, v, positions, scale, 0, W)
+        empty = torch.zeros(B, T, 0, dtype=torch.long)
+        results["sparse_window"] = pk.sparse_attention(q, k, v, sink, empty, positions, scale, W)
+    np.savez(os.path.join(HERE, "config1.npz"), seed=0, sink=_np(sink), keep_step=8,
+             **{name: _np(x[0, keep]) for name, x in results.items()})
+
+
+def tree(at, pk):
+    g = torch.Generator().manual_seed(4)
+    B, L, n, H, c = 2, 40, 7, 4, 32
+    q = torch.randn(B, n, H, c, generator=g)
+    k = torch.randn(B, L + n + 3, c, generator=g)  # 3 stale rows past the tree
+    v = torch.randn(B, L + n + 3, c, generator=g)
+    sink = torch.randn(H, generator=g) * 0.5
+    parents = torch.tensor([-1, 0, 0, 1, 1, 2, 4])
+    seen = torch.zeros(n, n, dtype=torch.bool)
+    for i in range(n):
+        j = i
+        while j >= 0:
+            seen[i, j] = True
+            j = int(parents[j])
+    visible = torch.cat([torch.ones(n, L, dtype=torch.bool), seen], 1)
+    scale = c ** -0.5
+    out_tree = at.dense_attention(q, k[:, :L + n], v[:, :L + n], sink, visible.expand(B, n, L + n), scale)
+    positions = (L + torch.arange(n)).expand(B, n).contiguous()
+    out_chain, _ = pk.exact_attention(q, k, v, positions, scale, 0, 1)
+    np.savez(os.path.join(HERE, "tree.npz"), q=_np(q), k=_np(k), v=_np(v), sink=_np(sink), parents=_np(parents),
+             cache_len=L, scale=scale, out_tree=_np(out_tree), out_chain=_np(out_chain))
+
+
+class _FakeModel(torch.nn.Module):
+    """Hands the Writer fixed target scores for one speculative step."""
+
+    def __init__(self, scores):
+        super().__init__()
+        self.weight = torch.nn.Parameter(torch.zeros(1))
+        self.scores = scores
+        self.kept = None
+
+    def new_cache(self, rows, routes=False):
+        return _FakeCache(rows)
+
+    def extend(self, ids, cache, counts, undoable=False, features=()):
+        return (self.scores[:, :ids.shape[1]],)
+
+    def undo(self, cache, kept):
+        self.kept = list(kept)
+
+
+class _FakeCache:
+    def __init__(self, rows):
+        self.lengths = torch.zeros(rows, dtype=torch.long)
+
+    def select(self, index):
+        return _FakeCache(len(index))
+
+
+class _FakeDrafter:
+    features, window = (), 0
+
+    def __init__(self, tokens, q):
+        self.tokens, self.q = tokens, q
+
+    def draft(self, model, histories, context, count, probabilities, generator):
+        return self.tokens[:, :count], self.q[:, :count], None
+
+
+def accept_case(wi, name, R, n, V, temperature, top_k, seed):
+    g = torch.Generator().manual_seed(seed)
+    scores = torch.randn(R, n + 1, V, generator=g) * 2.0
+    q_logits = torch.randn(R, n, V, generator=g) * 2.0
+    # half of the rows draft near the target (many accepted), half far (early rejections)
+    q_logits[: R // 2] = scores[: R // 2, :n] + 0.3 * q_logits[: R // 2]
+    writer_probs = wi.Writer.__dict__["_probabilities"]
+
+    class _P:
+        pass
+    holder = _P()
+    holder.temperature, holder.top_k = temperature, top_k
+    q = writer_probs(holder, q_logits)
+    drafted = torch.multinomial(q.reshape(-1, V), 1, generator=g).view(R, n)
+    uniforms = torch.rand(R, n, generator=g)
+    resample = torch.rand(R, generator=g)
+
+    state = {"row": 0, "j": 0}
+    real_rand, real_multinomial = torch.rand, torch.multinomial
+
+    def rand(*args, **kwargs):
+        u = uniforms[state["row"], state["j"]].clone()
+        state["j"] += 1
+        return u
+
+    def multinomial(weights, num, generator=None):
+        cs = torch.cumsum(weights.double(), -1)
+        target = float(resample[state["row"]]) * float(cs[-1])
+        token = min(int(torch.searchsorted(cs, torch.tensor([target], dtype=torch.float64), right=True)), V - 1)
+        state["row"] += 1
+        state["j"] = 0
+        return torch.tensor([token])
+
+    model = _FakeModel(scores)
+    writer = wi.Writer(model, [1], R, temperature=temperature, top_k=top_k, generator=torch.Generator(),
+                       drafter=_FakeDrafter(drafted, q), draft=n)
+    torch.rand, torch.multinomial = rand, multinomial
+    try:
+        written = writer.write({}, {row: n + 10 for row in range(R)})
+    finally:
+        torch.rand, torch.multinomial = real_rand, real_multinomial
+    tokens = np.full((R, n + 1), -1, np.int64)
+    for row, toks in written.items():
+        tokens[row, :len(toks)] = toks
+    accepted = np.array([len(written[row]) - 1 for row in range(R)], np.int64)
+    np.savez(os.path.join(HERE, f"accept_{name}.npz"), scores=_np(scores), q=_np(q), drafted=_np(drafted),
+             uniforms=_np(uniforms), resample=_np(resample), temperature=temperature,
+             top_k=-1 if top_k is None else top_k, tokens=tokens, accepted=accepted,
+             kept=np.array(model.kept, np.int64))
+
+
+def main():
+    parser = argparse.ArgumentParser()
+    parser.add_argument("--reference", default="/root/reference")
+    args = parser.parse_args()
+    torch.set_num_threads(max(1, os.cpu_count() or 1))
+    at, pk, wi = _import_reference(args.reference)
+    exact_small(pk)
+    exact_generation(pk)
+    sparse_small(pk)
+    window_small(at)
+    config1(at, pk)
+    tree(at, pk)
+    accept_case(wi, "stochastic", R=8, n=6, V=1000, temperature=1.0, top_k=None, seed=5)
+    accept_case(wi, "topk", R=8, n=6, V=1000, temperature=0.8, top_k=40, seed=6)
+    accept_case(wi, "greedy", R=8, n=6, V=1000, temperature=1.0, top_k=1, seed=7)
+    print("wrote", sorted(f for f in os.listdir(HERE) if f.endswith(".npz")))
+
+
+if __name__ == "__main__":
+    main()

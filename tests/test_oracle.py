@@ -1,0 +1,134 @@
+"""The CPU oracle against the golden vectors the reference itself produced
+(tests/golden/make_golden.py). This pins the oracle before any GPU result is
+compared with it."""
+
+import numpy as np
+import torch
+
+from oracle import accept as oa
+from oracle import attention as oat
+
+
+def _chosen_sets(chosen):
+    return [[set(r[r >= 0].tolist()) for r in row] for row in chosen]
+
+
+def test_exact_small_matches_reference(gold):
+    d = gold("exact_small.npz")
+    out, lse, chosen = oat.exact_attention(d["q"], d["k"], d["v"], d["positions"], float(d["scale"]),
+                                           int(d["top_k"]), int(d["window"]))
+    assert np.abs(out - d["out"]).max() < 1e-5
+    assert np.abs(lse - d["lse"]).max() < 1e-5
+    assert chosen.shape == d["chosen"].shape
+    assert _chosen_sets(chosen) == _chosen_sets(d["chosen"])
+
+
+def test_exact_generation_pass_matches_reference(gold):
+    # ragged rows, one query past the table's last row, k/v halves of one table
+    d = gold("exact_generation.npz")
+    c = d["q"].shape[-1]
+    e = d["entries"]
+    out, lse, chosen = oat.exact_attention(d["q"], e[..., :c], e[..., c:], d["positions"], float(d["scale"]),
+                                           int(d["top_k"]), int(d["window"]))
+    assert np.abs(out - d["out"]).max() < 1e-5
+    assert np.abs(lse - d["lse"]).max() < 1e-5
+    assert _chosen_sets(chosen) == _chosen_sets(d["chosen"])
+
+
+def test_sparse_small_matches_reference(gold):
+    d = gold("sparse_small.npz")
+    out, lse = oat.sparse_attention(d["q"], d["k"], d["v"], d["sink"], d["idx"], d["positions"], float(d["scale"]),
+                                    int(d["window"]))
+    assert np.abs(out - d["out"]).max() < 1e-5
+    assert np.abs(lse - d["lse"]).max() < 1e-5
+
+
+def test_window_attention_matches_reference(gold):
+    d = gold("window_small.npz")
+    out, _ = oat.window_attention(d["q"], d["k"], d["v"], d["sink"], d["positions"], float(d["scale"]),
+                                  int(d["window"]))
+    assert np.abs(out - d["out"]).max() < 1e-5
+
+
+def _config1_inputs():
+    g = torch.Generator().manual_seed(0)
+    B, T, H, c = 2, 512, 8, 64
+    q = torch.randn(B, T, H, c, generator=g).numpy()
+    k = torch.randn(B, T, c, generator=g).numpy()
+    v = torch.randn(B, T, c, generator=g).numpy()
+    sink = (torch.randn(H, generator=g) * 0.5).numpy()
+    return q, k, v, sink
+
+
+def test_config1_window_exact_sparse_match_reference(gold):
+    # B=2, T=512, 8 heads, c=64, window 128, fp32
+    d = gold("config1.npz")
+    q, k, v, sink = _config1_inputs()
+    assert np.array_equal(sink, d["sink"])
+    B, T, H, c = q.shape
+    W, scale, keep = 128, c ** -0.5, slice(None, None, int(d["keep_step"]))
+    positions = np.broadcast_to(np.arange(T), (B, T))
+    tail = np.zeros((B, W - 1, c), np.float32)
+    kt, vt = np.concatenate([tail, k], 1), np.concatenate([tail, v], 1)
+    out, _ = oat.window_attention(q[:1], kt[:1], vt[:1], np.zeros(H), positions[:1], scale, W)
+    assert np.abs(out[0, keep] - d["window_sink0"]).max() < 1e-5
+    out, _ = oat.window_attention(q[:1], kt[:1], vt[:1], sink, positions[:1], scale, W)
+    assert np.abs(out[0, keep] - d["window_sink"]).max() < 1e-5
+    out, _, _ = oat.exact_attention(q[:1], k[:1], v[:1], positions[:1], scale, 0, W)
+    assert np.abs(out[0, keep] - d["exact"]).max() < 1e-5
+    out, _ = oat.sparse_attention(q[:1], k[:1], v[:1], sink, np.zeros((1, T, 0), np.int64), positions[:1], scale, W)
+    assert np.abs(out[0, keep] - d["sparse_window"]).max() < 1e-5
+    # the window pass equals the sparse pass over the same rows (tail rows are before the text)
+    assert np.abs(d["window_sink"] - d["sparse_window"]).max() < 1e-5
+
+
+def test_tree_attention_matches_reference_dense_and_chain(gold):
+    d = gold("tree.npz")
+    B, n = d["q"].shape[:2]
+    L = int(d["cache_len"])
+    out, _ = oat.tree_attention(d["q"], d["k"], d["v"], np.full(B, L), d["parents"], float(d["scale"]), d["sink"])
+    assert np.abs(out - d["out_tree"]).max() < 1e-5
+    chain = np.arange(n) - 1
+    out, _ = oat.tree_attention(d["q"], d["k"], d["v"], np.full(B, L), chain, float(d["scale"]))
+    assert np.abs(out - d["out_chain"]).max() < 1e-5
+
+
+def test_merge_partials_equals_whole():
+    rng = np.random.default_rng(0)
+    B, T, H, c, N = 1, 3, 2, 8, 40
+    q, k, v = rng.normal(size=(B, T, H, c)), rng.normal(size=(B, N, c)), rng.normal(size=(B, N, c))
+    sink = rng.normal(size=H)
+    positions = np.full((B, T), N - 1)
+    whole, lse = oat.sparse_over_rows(q, k, v, sink, np.broadcast_to(np.arange(N), (B, T, N)), 0.3)
+    parts = [np.arange(0, 13), np.arange(13, 29), np.arange(29, 40)]
+    os_, ls_ = [], []
+    for rows in parts:
+        o, l = oat.sparse_over_rows(q, k, v, np.full(H, -np.inf), np.broadcast_to(rows, (B, T, len(rows))), 0.3)
+        os_.append(o)
+        ls_.append(l)
+    merged, mlse = oat.merge_partials(np.stack(os_), np.stack(ls_), np.ones_like(np.stack(ls_)), sink)
+    assert np.abs(merged - whole).max() < 1e-10 and np.abs(mlse - lse).max() < 1e-10
+    del positions
+
+
+def test_accept_matches_reference_writer(gold):
+    # the reference's own Writer._speculate, with explicit draws, gave these
+    for name in ("stochastic", "topk", "greedy"):
+        d = gold(f"accept_{name}.npz")
+        top_k = None if int(d["top_k"]) < 0 else int(d["top_k"])
+        tokens, accepted = oa.accept(d["scores"], d["drafted"], d["q"], d["uniforms"], d["resample"],
+                                     float(d["temperature"]), top_k)
+        assert np.array_equal(accepted, d["accepted"]), name
+        assert np.array_equal(tokens, d["tokens"]), name
+
+
+def test_greedy_accept_is_argmax_agreement():
+    rng = np.random.default_rng(1)
+    R, n, V = 4, 5, 64
+    scores = rng.normal(size=(R, n + 1, V)).astype(np.float32)
+    q = oa.probabilities(rng.normal(size=(R, n, V)), 1.0, 1)
+    drafted = scores[:, :n].argmax(-1)
+    drafted[1, 2] = (drafted[1, 2] + 1) % V
+    tokens, accepted = oa.accept(scores, drafted, q, rng.random((R, n)), rng.random(R), 1.0, 1)
+    assert accepted.tolist() == [n, 2, n, n]
+    assert tokens[1, 2] == scores[1, 2].argmax()
