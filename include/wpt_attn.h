@@ -1,0 +1,94 @@
+/*
+ * wpt_attn.h: the C ABI of the B200 (sm_100a) attention library
+ * libwpt_b200.so. Plain pointers, sizes and a CUDA stream handle; no torch
+ * types. Every entry point only enqueues work on `stream` (no host
+ * synchronisation, no allocation: buffers, including scratch, come from
+ * the caller) and returns WPT_OK or an error code whose text
+ * wpt_last_error() gives.
+ *
+ * These replace the kernel-form contract of the reference (paths relative
+ * to the reference repository, packages/wpt-model/src/wpt_model/):
+ *   pytorch_kernels.py:18-26   the contract: q (B, T, H, c), k and v (B, N, c)
+ *                              in one dtype, positions (B, T) int64, sink (H,)
+ *                              fp32, indices (B, T, K) int64 with -1 for none
+ *   kernels.py:161-184         exact_attention / sparse_attention dispatch
+ *   attention.py:85-107        window_attention
+ *   packages/wpt-inference/src/wpt_inference/__init__.py:173-179,210-222
+ *                              the speculative-decoding acceptance step
+ *
+ * Conventions shared by the attention entry points:
+ *   q, out     bf16, contiguous (B, T, H, C); C is 64 or 128, H <= 128.
+ *   k, v       bf16 tables (B, N, C) with the last dim contiguous and any
+ *              row / batch strides (in elements, multiples of 8), e.g. the
+ *              two halves of one (B, N, 2C) entries table.
+ *   positions  int64 (B, T): each query's own row. A query reads rows up to
+ *              min(position, N - 1) (pytorch_kernels.py:18-26: a padding query
+ *              past the table reads up to its last row).
+ *   lse        fp32 (B, T, H): natural-log softmax denominators, the sink's
+ *              term included when a sink is given.
+ *   scale      the softmax scale (c ** -0.5 in WPT).
+ *   stream     a cudaStream_t (e.g. torch.cuda.current_stream().cuda_stream).
+ */
+#ifndef WPT_ATTN_H_
+#define WPT_ATTN_H_
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum {
+  WPT_OK = 0,
+  WPT_ERR_INVALID = 1,      /* an argument breaks the contract */
+  WPT_ERR_UNSUPPORTED = 2,  /* a shape this library does not compute (e.g. C not 64 or 128) */
+  WPT_ERR_CUDA = 3          /* a CUDA call failed */
+};
+
+/* Text of the last error on this host thread. */
+const char* wpt_last_error(void);
+
+/* The device-side status word of the current device (bit 0: an mbarrier
+ * wait ran out of time, bit 1: a kernel met a shape it does not handle);
+ * synchronises the device. reset != 0 clears it after reading. */
+int wpt_status(unsigned* status, int reset);
+
+/*
+ * Attention of many queries per batch row over a contiguous range of rows,
+ * on the tensor cores (tcgen05, TMEM accumulators, TMA-fed tiles).
+ * Replaces exact_attention's forward (pytorch_kernels.py:98-121; the
+ * Triton form's _exact_forward_kernel, triton_kernels.py:300-326) and the
+ * window/sink attention (pytorch_kernels.py:171-187 over the window rows
+ * :149-153; attention.py:85-107), and computes tree-masked verification.
+ *   window      > 0: a query at position p reads rows p - window + 1 .. p
+ *   floor_rows  int64 (B, T) or NULL: the lowest row each query may read
+ *   tree_bits   uint64 (B, T) or NULL: rows tree_base[b] + i, i < 64, are
+ *               visible to query t only when bit i of tree_bits[b, t] is set
+ *   tree_base   int64 (B,) or NULL (required with tree_bits)
+ *   sink        fp32 (H,) or NULL: one logit per head added to the denominator
+ *   splits      > 1 splits each CTA's rows; part_o (splits, B*T*H, C) fp32
+ *               and part_lse (splits, B*T*H) fp32 are then caller scratch
+ */
+int wpt_attn_prefill(const void* q, const void* k, const void* v, int64_t k_stride_b, int64_t k_stride_n,
+                     int64_t v_stride_b, int64_t v_stride_n, const int64_t* positions, const int64_t* floor_rows,
+                     const uint64_t* tree_bits, const int64_t* tree_base, const float* sink, void* out, float* lse,
+                     float* part_o, float* part_lse, int splits, int B, int T, int H, int C, int N, int window,
+                     float scale, void* stream);
+
+/*
+ * Merge of split-KV partial results (o normalised per split, fp32; lse per
+ * split, natural log, -inf for none) into out (bf16) and lse, adding the
+ * sink. part_o (splits, rows, C) at split stride split_stride rows;
+ * part_lse (splits, rows). rows = B*T*H, head = row % H. Used by the
+ * split-KV paths and by the multi-GPU long-sequence decode (merges the
+ * GPUs' partials after an NCCL all-gather). No reference counterpart
+ * beyond the log-sum-exp algebra of pytorch_kernels.py:183-184.
+ */
+int wpt_attn_merge(const float* part_o, const float* part_lse, int splits, int64_t rows, int64_t split_stride,
+                   int H, int C, const float* sink, void* out, float* lse, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* WPT_ATTN_H_ */

@@ -1,0 +1,121 @@
+"""wpt_b200: WPT's attention hot path on B200 (sm_100a).
+
+A kernel-form module with the reference's contract (packages/wpt-model/src/
+wpt_model/pytorch_kernels.py:18-26; chosen by kernels.py:86-112), so that
+
+    from wpt_model import kernels
+    import wpt_b200
+    kernels._kernels, kernels._form = wpt_b200, "b200"
+
+makes WPT's exact and sparse layers run on these kernels. It exposes
+
+    NAME
+    exact_attention(q, k, v, positions, scale, top_k, window) -> (out, chosen)
+    sparse_attention(q, k, v, sink, idx, positions, scale, window) -> out
+    window_attention(q, k, v, sink, positions, scale)   (attention.py:85-107)
+    tree_attention(q, k, v, cache_len, parents, scale, sink=None) -> (out, lse)
+    accept(scores, drafted, q, uniforms, resample, temperature, top_k)
+
+with the reference's argument meanings, dtypes, -1 conventions and errors.
+Forward passes run hand-written CUDA kernels (libwpt_b200.so, C ABI in
+include/wpt_attn.h); there is no CPU path and no other backend: a missing
+library or a CPU tensor raises. The backward passes evaluate the reference's
+own gradient formulas (pytorch_kernels.py:123-139,189-210) with torch on
+the GPU from the saved log-sum-exp.
+"""
+
+import torch
+
+from . import ops
+from ._lib import LibraryMissing, device_status  # noqa: F401
+
+NAME = "B200"
+WINDOW = 128  # attention.py:53, what window_attention reads when not given a window
+
+
+def chosen_columns(top_k, window, N):
+    """pytorch_kernels.py:73-77."""
+    return max(0, min(top_k, N - window))
+
+
+def _compute(x):
+    return x if x.dtype == torch.bfloat16 else x.to(torch.bfloat16)
+
+
+def _positions(positions, B):
+    return positions.to(torch.int64).expand(B, -1).contiguous()
+
+
+# ------------------------------------------------------------ exact attention
+
+class _Exact(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, q, k, v, positions, scale, top_k, window):
+        B, T, H, c = q.shape
+        N = k.shape[1]
+        positions = _positions(positions, B)
+        out, lse = ops.prefill_forward(q, k, v, positions, scale)
+        K = chosen_columns(top_k, window, N)
+        if K:
+            raise NotImplementedError("top-k selection kernel not built yet")
+        chosen = torch.empty(B, T, 0, dtype=torch.long, device=q.device)
+        ctx.save_for_backward(q, k, v, positions, out, lse)
+        ctx.scale = scale
+        ctx.mark_non_differentiable(chosen)
+        return out.to(q.dtype), chosen
+
+    @staticmethod
+    def backward(ctx, d_out, _d_chosen):
+        from .backward import exact_backward
+        q, k, v, positions, out, lse = ctx.saved_tensors
+        dq, dk, dv = exact_backward(q, k, v, positions, out, lse, d_out, ctx.scale)
+        return dq, dk, dv, None, None, None, None
+
+
+def exact_attention(q, k, v, positions, scale, top_k, window):
+    """pytorch_kernels.exact_attention's result: (output (B, T, H, c) in q's
+    dtype, chosen rows (B, T, K) int64, -1 padded)."""
+    return _Exact.apply(q, k, v, positions, scale, top_k, window)
+
+
+def forward_with_lse(q, k, v, positions, scale, window=0, sink=None):
+    """Forward only, with the log-sum-exp: (out bf16, lse fp32)."""
+    return ops.prefill_forward(q, k, v, _positions(positions, q.shape[0]), scale, window=window, sink=sink)
+
+
+# ----------------------------------------------------------- window attention
+
+def window_attention(q, k, v, sink, positions, scale, window=None):
+    """attention.py:85-107: q (B, T, H, c) at positions (T,) or (B, T); k, v
+    (B, window - 1 + T, c), the window - 1 rows before the pass then its own;
+    query t reads table rows t .. t + window - 1 that are not before the
+    text, with the sink in each head's denominator. window defaults to
+    WINDOW (128, attention.py:53)."""
+    W = WINDOW if window is None else int(window)
+    B, T, H, c = q.shape
+    positions = _positions(positions, B)
+    t = torch.arange(T, device=q.device, dtype=torch.int64)
+    rows = (t + W - 1).expand(B, T).contiguous()  # each query's own row in the table
+    floor = rows - positions  # the row of position 0: rows before it are before the text
+    out, _ = ops.prefill_forward(q, k, v, rows, scale, window=W, floor=floor, sink=sink)
+    return out.to(q.dtype)
+
+
+# ----------------------------------------------------------- tree attention
+
+def tree_attention(q, k, v, cache_len, parents, scale, sink=None):
+    """Verification attention of a draft tree: q (B, n, H, c) for n nodes
+    whose keys and values sit at table rows cache_len[b] + i; node i reads
+    the rows before cache_len[b] and those of its ancestors and itself
+    (parents (n,) or (B, n), -1 for a root). A chain (parents[i] = i - 1) is
+    exact_attention at positions cache_len + i. Returns (out bf16, lse)."""
+    B, n, H, c = q.shape
+    cache_len = torch.as_tensor(cache_len, dtype=torch.int64, device=q.device).reshape(-1).expand(B).contiguous()
+    bits = ops.tree_bits_from_parents(parents).to(q.device)
+    bits = bits.expand(B, n).contiguous()
+    positions = cache_len[:, None] + torch.arange(n, device=q.device, dtype=torch.int64)
+    return ops.prefill_forward(q, k, v, positions, scale, tree_bits=bits, tree_base=cache_len, sink=sink)
+
+
+__all__ = ["NAME", "WINDOW", "chosen_columns", "exact_attention", "window_attention", "tree_attention",
+           "forward_with_lse", "device_status", "LibraryMissing"]

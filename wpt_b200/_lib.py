@@ -1,0 +1,78 @@
+"""Loads libwpt_b200.so (built in-tree by wpt_b200/build.py) and declares
+the C ABI of include/wpt_attn.h for ctypes. There is no fallback: when the
+library is missing or was built for another GPU, every operation raises."""
+
+import ctypes
+import os
+
+import torch
+
+LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "libwpt_b200.so")
+
+OK, ERR_INVALID, ERR_UNSUPPORTED, ERR_CUDA = 0, 1, 2, 3
+
+_P = ctypes.c_void_p
+_I64 = ctypes.c_int64
+_I = ctypes.c_int
+_F = ctypes.c_float
+
+# name -> argument types, in include/wpt_attn.h's order
+SIGNATURES = {
+    "wpt_last_error": [],
+    "wpt_status": [ctypes.POINTER(ctypes.c_uint), _I],
+    "wpt_attn_prefill": [_P, _P, _P, _I64, _I64, _I64, _I64, _P, _P, _P, _P, _P, _P, _P, _P, _P, _I,
+                         _I, _I, _I, _I, _I, _I, _F, _P],
+    "wpt_attn_merge": [_P, _P, _I, _I64, _I64, _I, _I, _P, _P, _P, _P],
+}
+
+_lib = None
+
+
+class LibraryMissing(ImportError):
+    """libwpt_b200.so is not built: run `python -m wpt_b200.build`."""
+
+
+def lib():
+    """The loaded library (declared once)."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise LibraryMissing(f"{LIB_PATH} is not built: run `python -m wpt_b200.build`")
+        handle = ctypes.CDLL(LIB_PATH)
+        for name, args in SIGNATURES.items():
+            fn = getattr(handle, name)
+            fn.argtypes = args
+            fn.restype = ctypes.c_char_p if name == "wpt_last_error" else ctypes.c_int
+        _lib = handle
+    return _lib
+
+
+def check(rc):
+    """Raises for a non-zero status of a C-ABI call: NotImplementedError for
+    a shape the kernels do not compute (the reference's tests skip those),
+    ValueError for a broken contract, RuntimeError for a CUDA failure."""
+    if rc == OK:
+        return
+    message = lib().wpt_last_error().decode(errors="replace")
+    if rc == ERR_UNSUPPORTED:
+        raise NotImplementedError(message)
+    if rc == ERR_INVALID:
+        raise ValueError(message)
+    raise RuntimeError(message)
+
+
+def ptr(t):
+    """A tensor's device address for the C ABI, or NULL for None."""
+    return None if t is None else ctypes.c_void_p(t.data_ptr())
+
+
+def stream(device):
+    return ctypes.c_void_p(torch.cuda.current_stream(device).cuda_stream)
+
+
+def device_status(reset=True):
+    """The device-side status word (bit 0: a bounded wait ran out of time);
+    synchronises the device."""
+    value = ctypes.c_uint(0)
+    check(lib().wpt_status(ctypes.byref(value), 1 if reset else 0))
+    return value.value

@@ -1,0 +1,217 @@
+// The one translation unit of libwpt_b200.so: the kernels (headers beside
+// this file) and the extern "C" launchers declared in include/wpt_attn.h.
+#include <cstdarg>
+#include <cstdio>
+#include <string>
+
+#include "../../include/wpt_attn.h"
+#include "common.cuh"
+#include "merge.cuh"
+#include "prefill.cuh"
+
+namespace {
+
+thread_local std::string g_error;
+
+int fail(int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_error = buf;
+  return code;
+}
+
+int cuda_fail(cudaError_t e, const char* what) {
+  return fail(WPT_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+}
+
+__device__ unsigned g_status_word;
+
+// The device address of the status word on the current device.
+int status_word(unsigned** out) {
+  static unsigned* cached[64] = {};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  if (dev < 0 || dev >= 64) return fail(WPT_ERR_INVALID, "device %d out of range", dev);
+  if (cached[dev] == nullptr) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_status_word);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(status)");
+    cached[dev] = static_cast<unsigned*>(p);
+  }
+  *out = cached[dev];
+  return WPT_OK;
+}
+
+using EncodeTiled = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                 const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                 CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+int encoder(EncodeTiled* out) {
+  static EncodeTiled fn = nullptr;
+  if (fn == nullptr) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    cudaError_t e = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q);
+    if (e != cudaSuccess || q != cudaDriverEntryPointSuccess || p == nullptr)
+      return fail(WPT_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
+    fn = reinterpret_cast<EncodeTiled>(p);
+  }
+  *out = fn;
+  return WPT_OK;
+}
+
+// A bf16 tensor map with 128-byte swizzle and 64-element inner boxes.
+int tensor_map(CUtensorMap* map, const void* base, int rank, const cuuint64_t* dims, const cuuint64_t* strides_bytes,
+               const cuuint32_t* box) {
+  EncodeTiled encode;
+  if (int rc = encoder(&encode)) return rc;
+  cuuint32_t elem[3] = {1, 1, 1};
+  CUresult r = encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, rank, const_cast<void*>(base), dims, strides_bytes,
+                      box, elem, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                      CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(WPT_ERR_INVALID, "cuTensorMapEncodeTiled failed (%d)", static_cast<int>(r));
+  return WPT_OK;
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// A (B, N, C) table as a 3-D map {C, N, B} with boxes of {64, 128, 1}.
+int table_map(CUtensorMap* map, const void* base, int64_t stride_b, int64_t stride_n, int B, int N, int C) {
+  if (!aligned16(base)) return fail(WPT_ERR_INVALID, "a key/value table is not 16-byte aligned");
+  if (stride_n % 8 != 0 || (B > 1 && stride_b % 8 != 0) || stride_n < C)
+    return fail(WPT_ERR_INVALID, "key/value strides must be multiples of 8 elements (got %lld, %lld)",
+                static_cast<long long>(stride_b), static_cast<long long>(stride_n));
+  if (B == 1) stride_b = static_cast<int64_t>(N) * stride_n;
+  cuuint64_t dims[3] = {static_cast<cuuint64_t>(C), static_cast<cuuint64_t>(N), static_cast<cuuint64_t>(B)};
+  cuuint64_t strides[2] = {static_cast<cuuint64_t>(stride_n) * 2, static_cast<cuuint64_t>(stride_b) * 2};
+  cuuint32_t box[3] = {64, 128, 1};
+  return tensor_map(map, base, 3, dims, strides, box);
+}
+
+template <typename Kernel>
+int allow_smem(Kernel kernel, int bytes) {
+  cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(max dynamic shared memory)");
+  return WPT_OK;
+}
+
+template <int C>
+int launch_prefill(const wpt::PrefillParams& p, const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
+                   cudaStream_t stream) {
+  constexpr int STAGES = 2;
+  using L = wpt::PrefillLayout<C, STAGES>;
+  auto kernel = wpt::prefill_kernel<C, STAGES>;
+  if (int rc = allow_smem(kernel, L::BYTES)) return rc;
+  dim3 grid((p.T + p.TQ - 1) / p.TQ, p.B, p.splits);
+  kernel<<<grid, 192, L::BYTES, stream>>>(tq, tk, tv, p);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "prefill_kernel launch");
+  return WPT_OK;
+}
+
+template <int C>
+int launch_merge(const float* part_o, const float* part_lse, int splits, int64_t rows, int64_t split_stride, int H,
+                 const float* sink, void* out, float* lse, cudaStream_t stream) {
+  const int warps = 8;
+  const int64_t blocks = (rows + warps - 1) / warps;
+  wpt::merge_kernel<C><<<static_cast<unsigned>(blocks), warps * 32, 0, stream>>>(
+      part_o, part_lse, splits, rows, split_stride, H, sink, static_cast<__nv_bfloat16*>(out), lse);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "merge_kernel launch");
+  return WPT_OK;
+}
+
+}  // namespace
+
+extern "C" const char* wpt_last_error(void) { return g_error.c_str(); }
+
+extern "C" int wpt_status(unsigned* status, int reset) {
+  unsigned* word = nullptr;
+  if (int rc = status_word(&word)) return rc;
+  cudaError_t e = cudaDeviceSynchronize();
+  if (e != cudaSuccess) return cuda_fail(e, "cudaDeviceSynchronize");
+  unsigned value = 0;
+  e = cudaMemcpy(&value, word, sizeof(value), cudaMemcpyDeviceToHost);
+  if (e != cudaSuccess) return cuda_fail(e, "read status");
+  if (reset) {
+    e = cudaMemset(word, 0, sizeof(unsigned));
+    if (e != cudaSuccess) return cuda_fail(e, "reset status");
+    e = cudaDeviceSynchronize();
+    if (e != cudaSuccess) return cuda_fail(e, "cudaDeviceSynchronize");
+  }
+  if (status) *status = value;
+  return WPT_OK;
+}
+
+extern "C" int wpt_attn_prefill(const void* q, const void* k, const void* v, int64_t k_stride_b, int64_t k_stride_n,
+                                int64_t v_stride_b, int64_t v_stride_n, const int64_t* positions,
+                                const int64_t* floor_rows, const uint64_t* tree_bits, const int64_t* tree_base,
+                                const float* sink, void* out, float* lse, float* part_o, float* part_lse, int splits,
+                                int B, int T, int H, int C, int N, int window, float scale, void* stream) {
+  if (C != 64 && C != 128) return fail(WPT_ERR_UNSUPPORTED, "head width %d: the kernels take 64 or 128", C);
+  if (H < 1 || H > 128) return fail(WPT_ERR_UNSUPPORTED, "%d heads: the kernels take 1 to 128", H);
+  if (B < 1 || T < 1 || N < 1) return fail(WPT_ERR_INVALID, "empty shape B=%d T=%d N=%d", B, T, N);
+  if (static_cast<int64_t>(B) * T * H >= (int64_t(1) << 31)) return fail(WPT_ERR_UNSUPPORTED, "B*T*H too large");
+  if (splits < 1) return fail(WPT_ERR_INVALID, "splits must be >= 1");
+  if (splits > 1 && (part_o == nullptr || part_lse == nullptr))
+    return fail(WPT_ERR_INVALID, "splits > 1 needs part_o and part_lse scratch");
+  if (tree_bits != nullptr && tree_base == nullptr) return fail(WPT_ERR_INVALID, "tree_bits needs tree_base");
+  if (!q || !k || !v || !positions || !out || !lse) return fail(WPT_ERR_INVALID, "a required pointer is NULL");
+  if (!aligned16(q) || !aligned16(out)) return fail(WPT_ERR_INVALID, "q and out must be 16-byte aligned");
+  if (!(scale > 0.f)) return fail(WPT_ERR_INVALID, "scale must be positive");
+
+  CUtensorMap tq, tk, tv;
+  {
+    cuuint64_t dims[2] = {static_cast<cuuint64_t>(C), static_cast<cuuint64_t>(B) * T * H};
+    cuuint64_t strides[1] = {static_cast<cuuint64_t>(C) * 2};
+    cuuint32_t box[2] = {64, 128};
+    if (int rc = tensor_map(&tq, q, 2, dims, strides, box)) return rc;
+  }
+  if (int rc = table_map(&tk, k, k_stride_b, k_stride_n, B, N, C)) return rc;
+  if (int rc = table_map(&tv, v, v_stride_b, v_stride_n, B, N, C)) return rc;
+
+  wpt::PrefillParams p;
+  p.positions = positions;
+  p.floor_rows = floor_rows;
+  p.tree_bits = tree_bits;
+  p.tree_base = tree_base;
+  p.sink = splits > 1 ? nullptr : sink;
+  p.out = static_cast<__nv_bfloat16*>(out);
+  p.lse = lse;
+  p.part_o = part_o;
+  p.part_lse = part_lse;
+  if (int rc = status_word(&p.status)) return rc;
+  p.B = B;
+  p.T = T;
+  p.H = H;
+  p.N = N;
+  p.window = window > 0 ? window : 0;
+  p.TQ = 128 / H;
+  p.splits = splits;
+  p.scale_log2 = scale * wpt::LOG2E;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  int rc = C == 128 ? launch_prefill<128>(p, tq, tk, tv, s) : launch_prefill<64>(p, tq, tk, tv, s);
+  if (rc) return rc;
+  if (splits > 1) {
+    const int64_t rows = static_cast<int64_t>(B) * T * H;
+    rc = C == 128 ? launch_merge<128>(part_o, part_lse, splits, rows, rows, H, sink, out, lse, s)
+                  : launch_merge<64>(part_o, part_lse, splits, rows, rows, H, sink, out, lse, s);
+  }
+  return rc;
+}
+
+extern "C" int wpt_attn_merge(const float* part_o, const float* part_lse, int splits, int64_t rows,
+                              int64_t split_stride, int H, int C, const float* sink, void* out, float* lse,
+                              void* stream) {
+  if (C != 64 && C != 128) return fail(WPT_ERR_UNSUPPORTED, "head width %d: the kernels take 64 or 128", C);
+  if (splits < 1 || rows < 0 || split_stride < rows || H < 1)
+    return fail(WPT_ERR_INVALID, "bad merge shape splits=%d rows=%lld", splits, static_cast<long long>(rows));
+  if (rows == 0) return WPT_OK;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  return C == 128 ? launch_merge<128>(part_o, part_lse, splits, rows, split_stride, H, sink, out, lse, s)
+                  : launch_merge<64>(part_o, part_lse, splits, rows, split_stride, H, sink, out, lse, s);
+}

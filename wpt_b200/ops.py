@@ -1,0 +1,124 @@
+"""Forward operations over the C ABI (include/wpt_attn.h): tensor checks,
+output and scratch allocation through torch's caching allocator, and the
+choice of kernel and split count. Every function here launches CUDA
+kernels of libwpt_b200.so on the current stream; none has a CPU path.
+
+Kernel choice: queries x heads of one batch row fill the 128 rows of the
+prefill kernel's tiles (tcgen05, M = 128 rows); with few queries per row
+(decode, short extends) the key-stream kernel computes S^T = K Q^T with the
+keys as M instead, and splits long rows over many CTAs.
+"""
+
+import math
+
+import torch
+
+from . import _lib
+
+SM_COUNT = 148
+
+
+def _need_cuda(*tensors):
+    for t in tensors:
+        if t is not None and not t.is_cuda:
+            raise ValueError("wpt_b200 computes on a CUDA device only; got a tensor on " + str(t.device))
+
+
+def _bf16(x):
+    return x if x.dtype == torch.bfloat16 else x.to(torch.bfloat16)
+
+
+def _table(x):
+    """A (B, N, C) table whose last dimension is contiguous, strides in
+    multiples of 8 elements (16 bytes), at a 16-byte aligned address."""
+    x = _bf16(x)
+    ok = (x.stride(-1) == 1 and x.stride(1) % 8 == 0 and (x.shape[0] == 1 or x.stride(0) % 8 == 0)
+          and x.data_ptr() % 16 == 0)
+    return x if ok else x.contiguous()
+
+
+def _rows(x):
+    return x.to(torch.int64).contiguous()
+
+
+def _splits_for(ctas, tiles):
+    """Split count that gives at least about two CTAs per SM when the grid
+    is small, never more splits than key tiles."""
+    if ctas >= SM_COUNT or tiles <= 1:
+        return 1
+    return int(max(1, min(tiles, 32, math.ceil(2 * SM_COUNT / ctas))))
+
+
+def prefill_forward(q, k, v, positions, scale, window=0, floor=None, tree_bits=None, tree_base=None, sink=None,
+                    splits=None):
+    """(out (B, T, H, C) bf16, lse (B, T, H) fp32) from the tcgen05 prefill
+    kernel: each query reads rows max(0, p - window + 1, floor) ..
+    min(p, N - 1) of k and v, p its position; tree_bits/tree_base give the
+    tree mask; sink (H,) joins each head's denominator."""
+    _need_cuda(q, k, v, positions, floor, tree_bits, tree_base, sink)
+    q = _bf16(q).contiguous()
+    k, v = _table(k), _table(v)
+    B, T, H, C = q.shape
+    N = k.shape[1]
+    positions = _rows(positions)
+    floor = None if floor is None else _rows(floor)
+    if tree_bits is not None:
+        tree_bits = tree_bits.to(torch.int64).contiguous()
+        tree_base = _rows(tree_base)
+    if sink is not None:
+        sink = sink.float().contiguous()
+    out = torch.empty_like(q)
+    lse = torch.empty(B, T, H, dtype=torch.float32, device=q.device)
+    TQ = max(1, 128 // H)
+    if splits is None:
+        tiles = window // 128 + 2 if window else (N + 127) // 128
+        splits = _splits_for(B * math.ceil(T / TQ), tiles)
+    part_o = part_lse = None
+    if splits > 1:
+        part_o = torch.empty(splits, B * T * H, C, dtype=torch.float32, device=q.device)
+        part_lse = torch.empty(splits, B * T * H, dtype=torch.float32, device=q.device)
+    _lib.check(_lib.lib().wpt_attn_prefill(
+        _lib.ptr(q), _lib.ptr(k), _lib.ptr(v), k.stride(0), k.stride(1), v.stride(0), v.stride(1),
+        _lib.ptr(positions), _lib.ptr(floor), _lib.ptr(tree_bits), _lib.ptr(tree_base), _lib.ptr(sink),
+        _lib.ptr(out), _lib.ptr(lse), _lib.ptr(part_o), _lib.ptr(part_lse), int(splits),
+        B, T, H, C, N, int(window), float(scale), _lib.stream(q.device)))
+    return out, lse
+
+
+def merge_partials(part_o, part_lse, H, sink=None, out=None, lse=None):
+    """Log-sum-exp merge of split partials: part_o (S, rows, C) fp32,
+    part_lse (S, rows) -> (out (rows, C) bf16, lse (rows,) fp32)."""
+    _need_cuda(part_o, part_lse, sink)
+    S, rows, C = part_o.shape
+    part_o, part_lse = part_o.float().contiguous(), part_lse.float().contiguous()
+    if sink is not None:
+        sink = sink.float().contiguous()
+    out = torch.empty(rows, C, dtype=torch.bfloat16, device=part_o.device) if out is None else out
+    lse = torch.empty(rows, dtype=torch.float32, device=part_o.device) if lse is None else lse
+    _lib.check(_lib.lib().wpt_attn_merge(_lib.ptr(part_o), _lib.ptr(part_lse), S, rows, rows, H, C, _lib.ptr(sink),
+                                         _lib.ptr(out), _lib.ptr(lse), _lib.stream(part_o.device)))
+    return out, lse
+
+
+def tree_bits_from_parents(parents):
+    """(n,) or (B, n) parent indices (-1 for a root, parents[i] < i) ->
+    int64 bit masks: bit j of node i is set when node j is i or one of its
+    ancestors. Computed on the host (the tree is tiny) and returned on the
+    parents' device."""
+    device = parents.device if torch.is_tensor(parents) else torch.device("cpu")
+    par = torch.as_tensor(parents, dtype=torch.int64).cpu()
+    flat = par.reshape(-1, par.shape[-1])
+    n = flat.shape[-1]
+    if n > 64:
+        raise NotImplementedError(f"a tree of {n} nodes: the kernels take up to 64")
+    bits = torch.zeros_like(flat)
+    for r in range(flat.shape[0]):
+        masks = []
+        for i in range(n):
+            p = int(flat[r, i])
+            if p >= i:
+                raise ValueError("parents must come before their children (parents[i] < i)")
+            m = (1 << i) | (masks[p] if p >= 0 else 0)
+            masks.append(m)
+            bits[r, i] = m - (1 << 64) if m >= (1 << 63) else m
+    return bits.reshape(par.shape).to(device)
