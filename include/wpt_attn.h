@@ -76,6 +76,31 @@ int wpt_attn_prefill(const void* q, const void* k, const void* v, int64_t k_stri
                      float scale, void* stream);
 
 /*
+ * Attention of few queries per batch row (decode, short extends) or of
+ * gathered rows (sparse), on the tensor cores with the keys as the MMA's M
+ * (S^T = K Q^T), split over CTAs along the keys. Replaces exact_attention's
+ * decode use (pytorch_kernels.py:98-121 at T = 1; the Triton form's (1, B)
+ * grid, triton_kernels.py:216) and sparse_attention
+ * (pytorch_kernels.py:171-187,213-217; triton_kernels.py:681-716).
+ *   idx == NULL  range mode: as wpt_attn_prefill (positions, window,
+ *                floor_rows); up to 64 / H queries share a CTA
+ *   idx != NULL  gather mode: idx int64 (B, T, K), -1 for none; each query
+ *                reads its rows idx[b, t, :] and then its last `window`
+ *                rows (rows < 0 or >= N are skipped), with the sink
+ *   splits, chunk_tiles  each query group's rows are cut into chunks of
+ *                chunk_tiles * 128 and chunk s goes to split s; rows past
+ *                splits * chunk_tiles * 128 are not read, so splits must
+ *                cover the longest row. splits > 1 needs part_o
+ *                (splits, B*T*H, C) and part_lse (splits, B*T*H) fp32 scratch.
+ *   C must be 128 and H at most 64.
+ */
+int wpt_attn_decode(const void* q, const void* k, const void* v, int64_t k_stride_b, int64_t k_stride_n,
+                    int64_t v_stride_b, int64_t v_stride_n, const int64_t* positions, const int64_t* floor_rows,
+                    const int64_t* idx, int K, const float* sink, void* out, float* lse, float* part_o,
+                    float* part_lse, int splits, int chunk_tiles, int B, int T, int H, int C, int N, int window,
+                    float scale, void* stream);
+
+/*
  * Merge of split-KV partial results (o normalised per split, fp32; lse per
  * split, natural log, -inf for none) into out (bf16) and lse, adding the
  * sink. part_o (splits, rows, C) at split stride split_stride rows;

@@ -54,7 +54,7 @@ class _Exact(torch.autograd.Function):
         B, T, H, c = q.shape
         N = k.shape[1]
         positions = _positions(positions, B)
-        out, lse = ops.prefill_forward(q, k, v, positions, scale)
+        out, lse = ops.attention_forward(q, k, v, positions, scale)
         K = chosen_columns(top_k, window, N)
         if K:
             raise NotImplementedError("top-k selection kernel not built yet")
@@ -80,7 +80,47 @@ def exact_attention(q, k, v, positions, scale, top_k, window):
 
 def forward_with_lse(q, k, v, positions, scale, window=0, sink=None):
     """Forward only, with the log-sum-exp: (out bf16, lse fp32)."""
-    return ops.prefill_forward(q, k, v, _positions(positions, q.shape[0]), scale, window=window, sink=sink)
+    return ops.attention_forward(q, k, v, _positions(positions, q.shape[0]), scale, window=window, sink=sink)
+
+
+# ----------------------------------------------------------- sparse attention
+
+def _window_rows(positions, window, N):
+    """pytorch_kernels.py:149-153."""
+    rows = positions[..., None] - window + 1 + torch.arange(window, device=positions.device)
+    return rows.masked_fill((rows < 0) | (rows >= N), -1)
+
+
+class _Sparse(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, q, k, v, sink, idx, positions, scale, window):
+        B, T, H, c = q.shape
+        positions = _positions(positions, B)
+        if idx.shape[-1] == 0:
+            out, lse = ops.attention_forward(q, k, v, positions, scale, window=window, sink=sink)
+        elif ops.uses_stream(1, H, c):
+            out, lse = ops.stream_forward(q, k, v, positions, scale, window=window, idx=idx, sink=sink)
+        else:
+            raise NotImplementedError(f"sparse attention with {H} heads of width {c}: the gather kernel takes "
+                                      "head width 128 and up to 64 heads")
+        ctx.save_for_backward(q, k, v, sink, idx, positions, out, lse)
+        ctx.scale, ctx.window = scale, window
+        return out.to(q.dtype)
+
+    @staticmethod
+    def backward(ctx, d_out):
+        from .backward import sparse_backward
+        q, k, v, sink, idx, positions, out, lse = ctx.saved_tensors
+        rows = torch.cat([idx, _window_rows(positions, ctx.window, k.shape[1])], -1)
+        dq, dk, dv, d_sink = sparse_backward(q, k, v, sink, rows, out, lse, d_out, ctx.scale)
+        return dq, dk, dv, d_sink, None, None, None, None
+
+
+def sparse_attention(q, k, v, sink, idx, positions, scale, window):
+    """pytorch_kernels.sparse_attention's result: the output (B, T, H, c), in
+    q's dtype, over each query's rows idx (B, T, K) (-1 for none) and its
+    last `window` rows, with sink (H,) in each head's denominator."""
+    return _Sparse.apply(q, k, v, sink, idx, positions, scale, window)
 
 
 # ----------------------------------------------------------- window attention
@@ -97,7 +137,7 @@ def window_attention(q, k, v, sink, positions, scale, window=None):
     t = torch.arange(T, device=q.device, dtype=torch.int64)
     rows = (t + W - 1).expand(B, T).contiguous()  # each query's own row in the table
     floor = rows - positions  # the row of position 0: rows before it are before the text
-    out, _ = ops.prefill_forward(q, k, v, rows, scale, window=W, floor=floor, sink=sink)
+    out, _ = ops.attention_forward(q, k, v, rows, scale, window=W, floor=floor, sink=sink)
     return out.to(q.dtype)
 
 
@@ -117,5 +157,6 @@ def tree_attention(q, k, v, cache_len, parents, scale, sink=None):
     return ops.prefill_forward(q, k, v, positions, scale, tree_bits=bits, tree_base=cache_len, sink=sink)
 
 
-__all__ = ["NAME", "WINDOW", "chosen_columns", "exact_attention", "window_attention", "tree_attention",
+__all__ = ["NAME", "WINDOW", "chosen_columns", "exact_attention", "sparse_attention", "window_attention",
+           "tree_attention",
            "forward_with_lse", "device_status", "LibraryMissing"]

@@ -22,6 +22,8 @@ SIGNATURES = {
     "wpt_status": [ctypes.POINTER(ctypes.c_uint), _I],
     "wpt_attn_prefill": [_P, _P, _P, _I64, _I64, _I64, _I64, _P, _P, _P, _P, _P, _P, _P, _P, _P, _I,
                          _I, _I, _I, _I, _I, _I, _F, _P],
+    "wpt_attn_decode": [_P, _P, _P, _I64, _I64, _I64, _I64, _P, _P, _P, _I, _P, _P, _P, _P, _P, _I, _I,
+                        _I, _I, _I, _I, _I, _I, _F, _P],
     "wpt_attn_merge": [_P, _P, _I, _I64, _I64, _I, _I, _P, _P, _P, _P],
 }
 

@@ -1,0 +1,550 @@
+// Key-stream attention for few queries per batch row: decode, short
+// extends, and sparse attention over gathered rows. tcgen05 + TMEM on
+// sm_100a, with the keys as the MMA's M:
+//
+//   S^T  = K Q^T     M = 128 keys, N = NCOL columns (query x head), K = C
+//   O^T += V^T P^T   M = C,        N = NCOL,                        K = 128 keys
+//
+// so a single decode query's 32 heads still fill 128-row tensor-core tiles
+// (the keys), where the prefill kernel's rows would be three-quarters
+// empty. Replaces the decode use of exact_attention
+// (packages/wpt-model/src/wpt_model/pytorch_kernels.py:98-121 at T = 1;
+// the Triton form runs it on a (1, B) grid, triton_kernels.py:216) and
+// sparse_attention (pytorch_kernels.py:171-187,213-217; the Triton form's
+// _sparse_forward_kernel, triton_kernels.py:681-716).
+//
+// Keys. A CTA streams "slots" of one batch row. Range mode: slot i is row
+// lo + i of the union of its queries' ranges (each query masks its own
+// lo..hi). Gather mode (sparse): one query per CTA; slot i < K is
+// idx[b, t, i], then the query's window rows p - window + 1 .. p; -1, or a
+// row outside the table, is masked (pytorch_kernels.py:149-153,182).
+// Slots are split into chunks of chunk_tiles x 128 over gridDim.y; with
+// more than one split every CTA writes a partial result for the merge
+// kernel (merge.cuh).
+//
+// Loads: 2 loader warps copy each slot's 256-byte K and V rows with 16-byte
+// cp.async (coalesced: 16 lanes per row) into 128-byte-swizzled tiles, so
+// arbitrary row gathers cost the same as contiguous ones; they publish a
+// stage after cp.async.wait_group and a proxy fence. Warp 4 issues the MMAs.
+// Warps 0-3 do the softmax: thread r owns slot r of a tile, holds its
+// NCOL scores, and the per-column maximum and sum over the 128 slots come
+// from a 31-shuffle transpose reduction per warp plus shared memory across
+// the four warps. P^T is written to shared memory (bf16) as the second
+// MMA's B operand. The running maximum is lazy (raised only by more than
+// 8 in base 2), as in the prefill kernel.
+#pragma once
+
+#include <climits>
+
+#include "common.cuh"
+
+namespace wpt {
+
+struct StreamParams {
+  const __nv_bfloat16* q;  // (B, T, H, C) contiguous
+  const __nv_bfloat16* k;
+  const __nv_bfloat16* v;
+  int64_t ksb, ksn, vsb, vsn;  // table strides, elements
+  const int64_t* positions;    // (B, T)
+  const int64_t* floor_rows;   // (B, T) or null (range mode)
+  const int64_t* idx;          // (B, T, K) or null: gather mode
+  const float* sink;           // (H,) or null
+  __nv_bfloat16* out;          // (B, T, H, C)
+  float* lse;                  // (B, T, H)
+  float* part_o;               // (splits, B*T*H, C)
+  float* part_lse;             // (splits, B*T*H)
+  unsigned* status;
+  int B, T, H, N, K, window, TQ, groups_per_row, splits, chunk_tiles;
+  float scale_log2;
+};
+
+template <int NCOL, int STAGES>
+struct StreamLayout {
+  static constexpr int C = 128, BN = 128;
+  static constexpr int Q_BYTES = NCOL * C * 2;
+  static constexpr int KV_BYTES = BN * C * 2;
+  static constexpr int P_BYTES = NCOL * BN * 2;
+  static constexpr int OFF_Q = 0;
+  static constexpr int OFF_K = ((Q_BYTES + 1023) / 1024) * 1024;
+  static constexpr int OFF_V = OFF_K + STAGES * KV_BYTES;
+  static constexpr int OFF_P = OFF_V + STAGES * KV_BYTES;
+  static constexpr int OFF_ROW = OFF_P + 2 * P_BYTES;
+  static constexpr int OFF_RED = OFF_ROW + STAGES * BN * 4;
+  static constexpr int OFF_M = OFF_RED + 4 * 64 * 4;
+  static constexpr int OFF_ALPHA = OFF_M + 64 * 4;
+  static constexpr int OFF_L = OFF_ALPHA + 64 * 4;
+  static constexpr int OFF_QLO = OFF_L + 64 * 4;
+  static constexpr int OFF_QHI = OFF_QLO + 64 * 4;
+  static constexpr int OFF_COLQ = OFF_QHI + 64 * 4;
+  static constexpr int OFF_BAR = OFF_COLQ + 64 * 4;
+  static constexpr int NBAR = 1 + 2 * STAGES + 5;
+  static constexpr int OFF_MISC = OFF_BAR + NBAR * 8;
+  static constexpr int BYTES = OFF_MISC + 16 + 1024;
+  static constexpr int TMEM_COLS = 3 * NCOL <= 32 ? 32 : 3 * NCOL <= 64 ? 64 : 3 * NCOL <= 128 ? 128 : 256;
+};
+
+constexpr int STREAM_THREADS = 224;  // warps 0-3 softmax, 4 MMA, 5-6 loaders
+constexpr int STREAM_LOADERS = 64;
+
+__device__ __forceinline__ void stream_query_rows(const StreamParams& p, int b, int t, int& lo, int& hi) {
+  const int64_t pos = p.positions[static_cast<int64_t>(b) * p.T + t];
+  const int64_t top = pos < static_cast<int64_t>(p.N) - 1 ? pos : static_cast<int64_t>(p.N) - 1;
+  int64_t low = 0;
+  if (p.window > 0 && pos - p.window + 1 > low) low = pos - p.window + 1;
+  if (p.floor_rows) {
+    const int64_t f = p.floor_rows[static_cast<int64_t>(b) * p.T + t];
+    if (f > low) low = f;
+  }
+  hi = top < -1 ? -1 : static_cast<int>(top);
+  lo = low > INT_MAX ? INT_MAX : static_cast<int>(low);
+}
+
+template <int NCOL, int STAGES, bool GATHER>
+__global__ void __launch_bounds__(STREAM_THREADS, 1)
+    stream_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v,
+                  const StreamParams p) {
+  using L = StreamLayout<NCOL, STAGES>;
+  constexpr int C = L::C, BN = L::BN;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sQ = smem + L::OFF_Q;
+  uint8_t* sK = smem + L::OFF_K;
+  uint8_t* sV = smem + L::OFF_V;
+  uint8_t* sP = smem + L::OFF_P;
+  int* s_row = reinterpret_cast<int*>(smem + L::OFF_ROW);
+  float* s_red = reinterpret_cast<float*>(smem + L::OFF_RED);
+  float* s_m = reinterpret_cast<float*>(smem + L::OFF_M);
+  float* s_alpha = reinterpret_cast<float*>(smem + L::OFF_ALPHA);
+  float* s_l = reinterpret_cast<float*>(smem + L::OFF_L);
+  int* s_qlo = reinterpret_cast<int*>(smem + L::OFF_QLO);
+  int* s_qhi = reinterpret_cast<int*>(smem + L::OFF_QHI);
+  int* s_colq = reinterpret_cast<int*>(smem + L::OFF_COLQ);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::OFF_BAR);
+  uint64_t* q_full = bars;
+  uint64_t* full = bars + 1;
+  uint64_t* kv_empty = full + STAGES;
+  uint64_t* s_full = kv_empty + STAGES;
+  uint64_t* p_ready = s_full + 2;
+  uint64_t* o_done = p_ready + 2;
+  uint32_t* s_tmem = reinterpret_cast<uint32_t*>(smem + L::OFF_MISC);
+  int* s_range = reinterpret_cast<int*>(smem + L::OFF_MISC + 4);
+
+  const int warp = threadIdx.x >> 5;
+  const int group = blockIdx.x, split = blockIdx.y;
+  const int b = group / p.groups_per_row;
+  const int t0 = (group - b * p.groups_per_row) * p.TQ;
+  const int TQg = min(p.TQ, p.T - t0);  // queries of this group
+  constexpr bool gather = GATHER;
+  const int64_t rows_total = static_cast<int64_t>(p.B) * p.T * p.H;
+
+  if (threadIdx.x == 0) {
+    s_range[0] = INT_MAX;
+    s_range[1] = -1;
+  }
+  if (threadIdx.x < 64) {
+    s_m[threadIdx.x] = -INFINITY;
+    s_qlo[threadIdx.x] = 0;
+    s_qhi[threadIdx.x] = -1;
+    const int tq = static_cast<int>(threadIdx.x) / p.H;  // column -> its query in the group, -1 for padding
+    s_colq[threadIdx.x] = (static_cast<int>(threadIdx.x) < NCOL && tq < TQg) ? tq : -1;
+  }
+  __syncthreads();
+  if (static_cast<int>(threadIdx.x) < TQg) {
+    int lo, hi;
+    stream_query_rows(p, b, t0 + threadIdx.x, lo, hi);
+    s_qlo[threadIdx.x] = lo;
+    s_qhi[threadIdx.x] = hi;
+    if (!gather && hi >= lo) {
+      atomicMin(&s_range[0], lo);
+      atomicMax(&s_range[1], hi);
+    }
+  }
+  __syncthreads();
+  // this CTA's slots: [slot0, slot_end) of `total`
+  int64_t total;
+  int range_lo = 0;
+  if (gather) {
+    total = static_cast<int64_t>(p.K) + (p.window > 0 ? p.window : 0);
+  } else {
+    range_lo = s_range[0];
+    total = s_range[1] >= s_range[0] ? static_cast<int64_t>(s_range[1]) - s_range[0] + 1 : 0;
+  }
+  const int64_t tiles_total = (total + BN - 1) / BN;
+  const int64_t tile0 = static_cast<int64_t>(split) * p.chunk_tiles;
+  const int64_t left = tiles_total - tile0;
+  const int ntiles = static_cast<int>(left <= 0 ? 0 : (left < p.chunk_tiles ? left : p.chunk_tiles));
+
+  if (ntiles == 0) {  // nothing to read: an empty partial, or the sink alone
+    if (static_cast<int>(threadIdx.x) < NCOL) {
+      const int col = threadIdx.x, tq = col / p.H, h = col - tq * p.H;
+      if (tq < TQg) {
+        const int64_t orow = (static_cast<int64_t>(b) * p.T + t0 + tq) * p.H + h;
+        if (p.splits > 1) {
+          p.part_lse[split * rows_total + orow] = -INFINITY;
+        } else {
+          for (int c = 0; c < C; ++c) p.out[orow * C + c] = __float2bfloat16_rn(0.f);
+          p.lse[orow] = p.sink != nullptr ? p.sink[h] : -INFINITY;
+        }
+      }
+    }
+    return;
+  }
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, STREAM_LOADERS);
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(full + s, GATHER ? STREAM_LOADERS : 1);
+      mbar_init(kv_empty + s, 1);
+    }
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(s_full + s, 1);
+      mbar_init(p_ready + s, 128);
+    }
+    mbar_init(o_done, 1);
+    fence_mbar_init();
+  }
+  if (warp == 4) {
+    tmem_alloc(s_tmem, L::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *s_tmem;
+
+  if (warp >= 5) {
+    // ---------------------------------------------------------- loaders
+    const int lt = threadIdx.x - 160;
+    const __nv_bfloat16* kb = p.k + static_cast<int64_t>(b) * p.ksb;
+    const __nv_bfloat16* vb = p.v + static_cast<int64_t>(b) * p.vsb;
+    // Q: NCOL rows (query x head), zeros for padding columns
+    for (int it = lt; it < NCOL * 16; it += STREAM_LOADERS) {
+      const int col = it >> 4, ch = it & 15;
+      const int tq = col / p.H, h = col - tq * p.H;
+      const bool ok = tq < TQg;
+      const __nv_bfloat16* src = p.q + ((static_cast<int64_t>(b) * p.T + t0 + tq) * p.H + h) * C + ch * 8;
+      cp_async_16(smem_u32(sQ + (ch >> 3) * (NCOL * 128) + sw128_offset(col, ch & 7)), ok ? src : p.q, ok);
+    }
+    cp_async_commit();
+    cp_async_wait<0>();
+    fence_proxy_async();
+    mbar_arrive(q_full);
+    if constexpr (!GATHER) {
+      // range mode: whole 128-row tiles by TMA, one thread, completion by bytes
+      if (lt == 0) {
+        for (int j = 0; j < ntiles; ++j) {
+          const int st = j % STAGES;
+          if (j >= STAGES && !mbar_wait(kv_empty + st, ((j / STAGES) & 1) ^ 1, p.status)) break;
+          const int n0 = range_lo + static_cast<int>((tile0 + j) * BN);
+          mbar_expect_tx(full + st, 2 * L::KV_BYTES);
+          tma_load_3d(sK + st * L::KV_BYTES, &tm_k, full + st, 0, n0, b);
+          tma_load_3d(sK + st * L::KV_BYTES + BN * 128, &tm_k, full + st, 64, n0, b);
+          tma_load_3d(sV + st * L::KV_BYTES, &tm_v, full + st, 0, n0, b);
+          tma_load_3d(sV + st * L::KV_BYTES + BN * 128, &tm_v, full + st, 64, n0, b);
+        }
+      }
+      __syncwarp();
+    } else {
+      const int64_t pos_g = p.positions[static_cast<int64_t>(b) * p.T + t0];
+      const int64_t* idx_row = gather ? p.idx + (static_cast<int64_t>(b) * p.T + t0) * p.K : nullptr;
+      // A tile is published (full barrier) once this thread's copies for it
+      // have landed. Normally tile j - 1 is published right after tile j is
+      // issued, keeping two tiles in flight; before blocking on a free stage,
+      // every issued tile is published first, since the consumer may need one
+      // of them to free that stage.
+      bool ok = true;
+      int published = 0;
+      for (int j = 0; j < ntiles; ++j) {
+        const int st = j % STAGES;
+        if (j >= STAGES) {
+          const uint32_t parity = ((j / STAGES) & 1) ^ 1;
+          if (!mbar_try_wait(kv_empty + st, parity)) {
+            if (published < j) {
+              cp_async_wait<0>();
+              fence_proxy_async();
+              for (; published < j; ++published) mbar_arrive(full + published % STAGES);
+            }
+            ok = mbar_wait(kv_empty + st, parity, p.status);
+          }
+          if (!ok) break;
+        }
+        int* rows = s_row + st * BN;
+  #pragma unroll
+        for (int half = 0; half < 2; ++half) {
+          const int i = lt + half * 64;
+          const int64_t slot = (tile0 + j) * BN + i;
+          int64_t row = -1;
+          if (slot < total) {
+            if (!gather) {
+              row = range_lo + slot;
+            } else if (slot < p.K) {
+              row = idx_row[slot];
+            } else {
+              row = pos_g - p.window + 1 + (slot - p.K);
+            }
+            if (row < 0 || row >= p.N) row = -1;
+          }
+          rows[i] = static_cast<int>(row);
+        }
+        named_barrier(2, STREAM_LOADERS);
+        const uint32_t dk = smem_u32(sK + st * L::KV_BYTES), dv = smem_u32(sV + st * L::KV_BYTES);
+  #pragma unroll 4
+        for (int it = 0; it < (BN * 16) / STREAM_LOADERS; ++it) {
+          const int flat = it * STREAM_LOADERS + lt;
+          const int r = flat >> 4, ch = flat & 15;
+          const int row = rows[r];
+          const bool has = row >= 0;
+          const uint32_t off = (ch >> 3) * (BN * 128) + sw128_offset(r, ch & 7);
+          cp_async_16(dk + off, has ? kb + static_cast<int64_t>(row) * p.ksn + ch * 8 : p.k, has);
+          cp_async_16(dv + off, has ? vb + static_cast<int64_t>(row) * p.vsn + ch * 8 : p.v, has);
+        }
+        cp_async_commit();
+        if (published == j - 1) {
+          cp_async_wait<1>();
+          fence_proxy_async();
+          mbar_arrive(full + published % STAGES);
+          ++published;
+        }
+      }
+      cp_async_wait<0>();
+      fence_proxy_async();
+      if (ok) {
+        for (; published < ntiles; ++published) mbar_arrive(full + published % STAGES);
+      }
+    }
+  } else if (warp == 4) {
+    // ------------------------------------------------------- MMA issuer
+    if ((threadIdx.x & 31) == 0) {
+      constexpr uint32_t IDESC_S = idesc_bf16(128, NCOL, 0, 0);
+      constexpr uint32_t IDESC_O = idesc_bf16(128, NCOL, 1, 0);
+      const uint32_t tS = tmem, tO = tmem + 2 * NCOL;
+      const uint32_t q_addr = smem_u32(sQ), k_addr = smem_u32(sK), v_addr = smem_u32(sV), p_addr = smem_u32(sP);
+      bool ok = mbar_wait(q_full, 0, p.status);
+      for (int j = 0; ok && j <= ntiles; ++j) {
+        if (j < ntiles) {
+          const int st = j % STAGES;
+          if (!(ok = mbar_wait(full + st, (j / STAGES) & 1, p.status))) break;
+          tc_fence_after();
+#pragma unroll
+          for (int kk = 0; kk < C / 16; ++kk) {
+            mma_ss(tS + (j & 1) * NCOL,
+                   sdesc_sw128(k_addr + st * L::KV_BYTES + (kk >> 2) * (BN * 128) + (kk & 3) * 32, 16, 1024),
+                   sdesc_sw128(q_addr + (kk >> 2) * (NCOL * 128) + (kk & 3) * 32, 16, 1024), IDESC_S,
+                   kk > 0 ? 1u : 0u);
+          }
+          mma_commit(s_full + (j & 1));
+        }
+        if (j > 0) {
+          const int jp = j - 1, st = jp % STAGES;
+          if (!(ok = mbar_wait(p_ready + (jp & 1), (jp >> 1) & 1, p.status))) break;
+          tc_fence_after();
+          const uint32_t pb = p_addr + (jp & 1) * L::P_BYTES;
+#pragma unroll
+          for (int kk = 0; kk < BN / 16; ++kk) {
+            mma_ss(tO, sdesc_sw128(v_addr + st * L::KV_BYTES + kk * 16 * 128, BN * 128, 1024),
+                   sdesc_sw128(pb + (kk >> 2) * (NCOL * 128) + (kk & 3) * 32, 16, 1024), IDESC_O,
+                   (jp > 0 || kk > 0) ? 1u : 0u);
+          }
+          mma_commit(kv_empty + st);
+          mma_commit(o_done);
+        }
+      }
+    }
+    __syncwarp();
+  } else {
+    // ------------------------------------------ softmax: thread r = slot r
+    const int r = threadIdx.x, lane = r & 31;
+    const uint32_t lane_addr = tmem + (static_cast<uint32_t>(warp * 32) << 16);
+    const uint32_t tO = lane_addr + 2 * NCOL;
+    const float sl2 = p.scale_log2;
+    float lp[NCOL];
+#pragma unroll
+    for (int c = 0; c < NCOL; ++c) lp[c] = 0.f;
+    // Column masks, read once: column c belongs to query c / H; a tile row
+    // is visible to the columns of every query whose bounds contain it.
+    const uint64_t head_bits = p.H >= 64 ? ~0ull : ((1ull << p.H) - 1);
+    const uint64_t all_cols = TQg * p.H >= 64 ? ~0ull : ((1ull << (TQg * p.H)) - 1);
+    int qlo_r[4], qhi_r[4];
+#pragma unroll
+    for (int tq = 0; tq < 4; ++tq) {
+      qlo_r[tq] = tq < TQg ? s_qlo[tq] : 1;
+      qhi_r[tq] = tq < TQg ? s_qhi[tq] : 0;
+    }
+    bool ok = true;
+    for (int j = 0; j < ntiles; ++j) {
+      const int st = j % STAGES;
+      if constexpr (GATHER) ok = __all_sync(0xffffffffu, mbar_wait(full + st, (j / STAGES) & 1, p.status));
+      if (ok) ok = __all_sync(0xffffffffu, mbar_wait(s_full + (j & 1), (j >> 1) & 1, p.status));
+      if (!ok) break;
+      tc_fence_after();
+      float s[NCOL];
+      {
+        const uint32_t sa = lane_addr + (j & 1) * NCOL;
+        if constexpr (NCOL == 16) {
+          uint32_t x[16];
+          tmem_ld16(sa, x);
+#pragma unroll
+          for (int c = 0; c < 16; ++c) s[c] = __uint_as_float(x[c]);
+        } else {
+#pragma unroll
+          for (int c32 = 0; c32 < NCOL / 32; ++c32) {
+            uint32_t x[32];
+            tmem_ld32(sa + c32 * 32, x);
+#pragma unroll
+            for (int c = 0; c < 32; ++c) s[c32 * 32 + c] = __uint_as_float(x[c]);
+          }
+        }
+      }
+      uint64_t vis;
+      if constexpr (GATHER) {
+        vis = s_row[st * BN + r] >= 0 ? all_cols : 0ull;
+      } else {
+        const int row = range_lo + static_cast<int>((tile0 + j) * BN) + r;
+        vis = 0ull;
+        if (TQg <= 4) {
+#pragma unroll
+          for (int tq = 0; tq < 4; ++tq)
+            if (row >= qlo_r[tq] && row <= qhi_r[tq]) vis |= head_bits << (tq * p.H);
+        } else {
+          for (int tq = 0; tq < TQg; ++tq)
+            if (row >= s_qlo[tq] && row <= s_qhi[tq]) vis |= head_bits << (tq * p.H);
+        }
+      }
+#pragma unroll
+      for (int c = 0; c < NCOL; ++c) s[c] = ((vis >> c) & 1ull) ? s[c] * sl2 : -INFINITY;
+      // per-column maximum over the tile's 128 slots
+#pragma unroll
+      for (int c32 = 0; c32 < (NCOL + 31) / 32; ++c32) {
+        float tmp[32];
+#pragma unroll
+        for (int c = 0; c < 32; ++c) tmp[c] = (c32 * 32 + c < NCOL) ? s[(c32 * 32 + c) % NCOL] : -INFINITY;
+        const float m = transpose_reduce32(tmp, MaxOp());
+        if (c32 * 32 + lane < NCOL) s_red[warp * 64 + c32 * 32 + lane] = m;
+      }
+      named_barrier(1, 128);
+      if (r < NCOL) {
+        const float tmax = fmaxf(fmaxf(s_red[r], s_red[64 + r]), fmaxf(s_red[128 + r], s_red[192 + r]));
+        const float mo = s_m[r];
+        float a = 1.f;
+        if (tmax > mo + 8.f) {
+          a = fast_exp2(mo - tmax);
+          s_m[r] = tmax;
+        }
+        s_alpha[r] = a;
+      }
+      named_barrier(1, 128);
+      float mreg[NCOL], areg[NCOL];
+#pragma unroll
+      for (int c4 = 0; c4 < NCOL / 4; ++c4) {
+        const float4 m4 = reinterpret_cast<const float4*>(s_m)[c4];
+        const float4 a4 = reinterpret_cast<const float4*>(s_alpha)[c4];
+        mreg[4 * c4] = m4.x;
+        mreg[4 * c4 + 1] = m4.y;
+        mreg[4 * c4 + 2] = m4.z;
+        mreg[4 * c4 + 3] = m4.w;
+        areg[4 * c4] = a4.x;
+        areg[4 * c4 + 1] = a4.y;
+        areg[4 * c4 + 2] = a4.z;
+        areg[4 * c4 + 3] = a4.w;
+      }
+      bool any = false;
+#pragma unroll
+      for (int c = 0; c < NCOL; ++c) {
+        lp[c] *= areg[c];
+        any |= areg[c] != 1.f;
+      }
+      if (any && j > 0) {  // every thread read the same alphas: uniform
+        ok = __all_sync(0xffffffffu, mbar_wait(o_done, (j - 1) & 1, p.status));
+        if (!ok) break;
+        tc_fence_after();
+        if constexpr (NCOL == 16) {
+          uint32_t x[16];
+          tmem_ld16(tO, x);
+#pragma unroll
+          for (int c = 0; c < 16; ++c) x[c] = __float_as_uint(__uint_as_float(x[c]) * areg[c]);
+          tmem_st16(tO, x);
+        } else {
+#pragma unroll
+          for (int c32 = 0; c32 < NCOL / 32; ++c32) {
+            uint32_t x[32];
+            tmem_ld32(tO + c32 * 32, x);
+#pragma unroll
+            for (int c = 0; c < 32; ++c) x[c] = __float_as_uint(__uint_as_float(x[c]) * areg[c32 * 32 + c]);
+            tmem_st32(tO + c32 * 32, x);
+          }
+        }
+      }
+      uint8_t* pbuf = sP + (j & 1) * L::P_BYTES + (r >> 6) * (NCOL * 128) + (r & 7) * 2;
+      const uint32_t chunk = (r & 63) >> 3;
+#pragma unroll
+      for (int c = 0; c < NCOL; ++c) {
+        const float m = mreg[c];
+        const float e = fast_exp2(s[c] - (m == -INFINITY ? 0.f : m));
+        lp[c] += e;
+        *reinterpret_cast<__nv_bfloat16*>(pbuf + sw128_offset(c, chunk)) = __float2bfloat16_rn(e);
+      }
+      tmem_wait_st();
+      tc_fence_before();
+      fence_proxy_async();
+      mbar_arrive(p_ready + (j & 1));
+    }
+    if (ok) ok = __all_sync(0xffffffffu, mbar_wait(o_done, (ntiles - 1) & 1, p.status));
+    tc_fence_after();
+    // per-column sums over the 128 slots
+#pragma unroll
+    for (int c32 = 0; c32 < (NCOL + 31) / 32; ++c32) {
+      float tmp[32];
+#pragma unroll
+      for (int c = 0; c < 32; ++c) tmp[c] = (c32 * 32 + c < NCOL) ? lp[(c32 * 32 + c) % NCOL] : 0.f;
+      const float sum = transpose_reduce32(tmp, SumOp());
+      if (c32 * 32 + lane < NCOL) s_red[warp * 64 + c32 * 32 + lane] = sum;
+    }
+    named_barrier(1, 128);
+    if (r < NCOL) s_l[r] = (s_red[r] + s_red[64 + r]) + (s_red[128 + r] + s_red[192 + r]);
+    named_barrier(1, 128);
+    if (ok) {
+      float o[NCOL];
+      if constexpr (NCOL == 16) {
+        uint32_t x[16];
+        tmem_ld16(tO, x);
+#pragma unroll
+        for (int c = 0; c < 16; ++c) o[c] = __uint_as_float(x[c]);
+      } else {
+#pragma unroll
+        for (int c32 = 0; c32 < NCOL / 32; ++c32) {
+          uint32_t x[32];
+          tmem_ld32(tO + c32 * 32, x);
+#pragma unroll
+          for (int c = 0; c < 32; ++c) o[c32 * 32 + c] = __uint_as_float(x[c]);
+        }
+      }
+      // thread r holds column r of the head width for every (query, head)
+#pragma unroll
+      for (int c = 0; c < NCOL; ++c) {
+        const int tq = s_colq[c];
+        if (tq < 0) continue;
+        const int h = c - tq * p.H;
+        const int64_t orow = (static_cast<int64_t>(b) * p.T + t0 + tq) * p.H + h;
+        const float m = s_m[c], msub = m == -INFINITY ? 0.f : m, l = s_l[c];
+        if (p.splits == 1) {
+          float denom = l;
+          if (p.sink != nullptr) denom += fast_exp2(fmaf(p.sink[h], LOG2E, -msub));
+          p.out[orow * C + r] = __float2bfloat16_rn(denom > 0.f ? o[c] / denom : 0.f);
+          if (r == 0) p.lse[orow] = denom > 0.f ? (msub + log2f(denom)) * LN2 : -INFINITY;
+        } else {
+          const int64_t prow = split * rows_total + orow;
+          p.part_o[prow * C + r] = l > 0.f ? o[c] / l : 0.f;
+          if (r == 0) p.part_lse[prow] = l > 0.f ? (msub + log2f(l)) * LN2 : -INFINITY;
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 4) {
+    tc_fence_after();
+    tmem_dealloc(tmem, L::TMEM_COLS);
+  }
+}
+
+}  // namespace wpt

@@ -2,12 +2,14 @@
 // this file) and the extern "C" launchers declared in include/wpt_attn.h.
 #include <cstdarg>
 #include <cstdio>
+#include <cstring>
 #include <string>
 
 #include "../../include/wpt_attn.h"
 #include "common.cuh"
 #include "merge.cuh"
 #include "prefill.cuh"
+#include "stream.cuh"
 
 namespace {
 
@@ -104,6 +106,7 @@ int launch_prefill(const wpt::PrefillParams& p, const CUtensorMap& tq, const CUt
                    cudaStream_t stream) {
   constexpr int STAGES = 2;
   using L = wpt::PrefillLayout<C, STAGES>;
+  static_assert(L::BYTES <= 232448, "prefill kernel shared memory exceeds 227 KB");
   auto kernel = wpt::prefill_kernel<C, STAGES>;
   if (int rc = allow_smem(kernel, L::BYTES)) return rc;
   dim3 grid((p.T + p.TQ - 1) / p.TQ, p.B, p.splits);
@@ -111,6 +114,30 @@ int launch_prefill(const wpt::PrefillParams& p, const CUtensorMap& tq, const CUt
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "prefill_kernel launch");
   return WPT_OK;
+}
+
+template <int NCOL, int STAGES, bool GATHER>
+int launch_stream_n(const CUtensorMap& tk, const CUtensorMap& tv, const wpt::StreamParams& p, int groups,
+                    cudaStream_t stream) {
+  using L = wpt::StreamLayout<NCOL, STAGES>;
+  static_assert(L::BYTES <= 232448, "key-stream kernel shared memory exceeds 227 KB");
+  auto kernel = wpt::stream_kernel<NCOL, STAGES, GATHER>;
+  if (int rc = allow_smem(kernel, L::BYTES)) return rc;
+  dim3 grid(groups, p.splits);
+  kernel<<<grid, wpt::STREAM_THREADS, L::BYTES, stream>>>(tk, tv, p);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "stream_kernel launch");
+  return WPT_OK;
+}
+
+template <bool GATHER>
+int launch_stream_g(const CUtensorMap& tk, const CUtensorMap& tv, const wpt::StreamParams& p, int ncol, int groups,
+                    cudaStream_t stream) {
+  switch (ncol) {
+    case 16: return launch_stream_n<16, 3, GATHER>(tk, tv, p, groups, stream);
+    case 32: return launch_stream_n<32, 3, GATHER>(tk, tv, p, groups, stream);
+    default: return launch_stream_n<64, 2, GATHER>(tk, tv, p, groups, stream);
+  }
 }
 
 template <int C>
@@ -214,4 +241,74 @@ extern "C" int wpt_attn_merge(const float* part_o, const float* part_lse, int sp
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   return C == 128 ? launch_merge<128>(part_o, part_lse, splits, rows, split_stride, H, sink, out, lse, s)
                   : launch_merge<64>(part_o, part_lse, splits, rows, split_stride, H, sink, out, lse, s);
+}
+
+extern "C" int wpt_attn_decode(const void* q, const void* k, const void* v, int64_t k_stride_b, int64_t k_stride_n,
+                               int64_t v_stride_b, int64_t v_stride_n, const int64_t* positions,
+                               const int64_t* floor_rows, const int64_t* idx, int K, const float* sink, void* out,
+                               float* lse, float* part_o, float* part_lse, int splits, int chunk_tiles, int B, int T,
+                               int H, int C, int N, int window, float scale, void* stream) {
+  if (C != 128) return fail(WPT_ERR_UNSUPPORTED, "head width %d: the key-stream kernel takes 128", C);
+  if (H < 1 || H > 64) return fail(WPT_ERR_UNSUPPORTED, "%d heads: the key-stream kernel takes 1 to 64", H);
+  if (B < 1 || T < 1 || N < 1) return fail(WPT_ERR_INVALID, "empty shape B=%d T=%d N=%d", B, T, N);
+  if (static_cast<int64_t>(B) * T * H >= (int64_t(1) << 31)) return fail(WPT_ERR_UNSUPPORTED, "B*T*H too large");
+  if (splits < 1 || chunk_tiles < 1) return fail(WPT_ERR_INVALID, "splits and chunk_tiles must be >= 1");
+  if (splits > 65535) return fail(WPT_ERR_UNSUPPORTED, "%d splits: at most 65535", splits);
+  if (splits > 1 && (part_o == nullptr || part_lse == nullptr))
+    return fail(WPT_ERR_INVALID, "splits > 1 needs part_o and part_lse scratch");
+  if (idx != nullptr && K < 0) return fail(WPT_ERR_INVALID, "K must be >= 0");
+  if (!q || !k || !v || !positions || !out || !lse) return fail(WPT_ERR_INVALID, "a required pointer is NULL");
+  if (!aligned16(q) || !aligned16(k) || !aligned16(v)) return fail(WPT_ERR_INVALID, "q, k, v must be 16-byte aligned");
+  if (k_stride_n % 8 || v_stride_n % 8 || (B > 1 && (k_stride_b % 8 || v_stride_b % 8)))
+    return fail(WPT_ERR_INVALID, "key/value strides must be multiples of 8 elements");
+  if (!(scale > 0.f)) return fail(WPT_ERR_INVALID, "scale must be positive");
+  const bool gather = idx != nullptr;
+  const int cols = gather ? H : (T * H < 64 ? T * H : 64);
+  const int ncol = cols <= 16 ? 16 : cols <= 32 ? 32 : 64;
+  wpt::StreamParams p;
+  p.q = static_cast<const __nv_bfloat16*>(q);
+  p.k = static_cast<const __nv_bfloat16*>(k);
+  p.v = static_cast<const __nv_bfloat16*>(v);
+  p.ksb = k_stride_b;
+  p.ksn = k_stride_n;
+  p.vsb = v_stride_b;
+  p.vsn = v_stride_n;
+  p.positions = positions;
+  p.floor_rows = gather ? nullptr : floor_rows;
+  p.idx = idx;
+  p.K = gather ? K : 0;
+  p.sink = splits > 1 ? nullptr : sink;
+  p.out = static_cast<__nv_bfloat16*>(out);
+  p.lse = lse;
+  p.part_o = part_o;
+  p.part_lse = part_lse;
+  if (int rc = status_word(&p.status)) return rc;
+  p.B = B;
+  p.T = T;
+  p.H = H;
+  p.N = N;
+  p.window = window > 0 ? window : 0;
+  p.TQ = gather ? 1 : ncol / H;
+  p.groups_per_row = (T + p.TQ - 1) / p.TQ;
+  p.splits = splits;
+  p.chunk_tiles = chunk_tiles;
+  p.scale_log2 = scale * wpt::LOG2E;
+  const int64_t groups = static_cast<int64_t>(B) * p.groups_per_row;
+  if (groups >= (int64_t(1) << 31)) return fail(WPT_ERR_UNSUPPORTED, "too many query groups");
+  CUtensorMap tk, tv;  // range mode loads whole tiles by TMA; gather mode does not read the maps
+  memset(&tk, 0, sizeof(tk));
+  memset(&tv, 0, sizeof(tv));
+  if (!gather) {
+    if (int rc = table_map(&tk, k, k_stride_b, k_stride_n, B, N, C)) return rc;
+    if (int rc = table_map(&tv, v, v_stride_b, v_stride_n, B, N, C)) return rc;
+  }
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int rc = gather ? launch_stream_g<true>(tk, tv, p, ncol, static_cast<int>(groups), s)
+                        : launch_stream_g<false>(tk, tv, p, ncol, static_cast<int>(groups), s);
+  if (rc) return rc;
+  if (splits > 1) {
+    const int64_t rows = static_cast<int64_t>(B) * T * H;
+    return launch_merge<128>(part_o, part_lse, splits, rows, rows, H, sink, out, lse, s);
+  }
+  return WPT_OK;
 }

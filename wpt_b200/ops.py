@@ -10,6 +10,7 @@ keys as M instead, and splits long rows over many CTAs.
 """
 
 import math
+import os
 
 import torch
 
@@ -83,6 +84,72 @@ def prefill_forward(q, k, v, positions, scale, window=0, floor=None, tree_bits=N
         _lib.ptr(out), _lib.ptr(lse), _lib.ptr(part_o), _lib.ptr(part_lse), int(splits),
         B, T, H, C, N, int(window), float(scale), _lib.stream(q.device)))
     return out, lse
+
+
+def _stream_shape(T, H, gather):
+    """(columns per CTA, queries per CTA) of the key-stream kernel, as the C
+    launcher derives them."""
+    cols = H if gather else min(T * H, 64)
+    ncol = 16 if cols <= 16 else 32 if cols <= 32 else 64
+    return ncol, (1 if gather else ncol // H)
+
+
+def uses_stream(T, H, C):
+    """Whether the key-stream kernel computes this shape (few queries per row)."""
+    return C == 128 and H <= 64 and T * H <= 64
+
+
+def stream_forward(q, k, v, positions, scale, window=0, floor=None, idx=None, sink=None, chunk_tiles=None):
+    """(out (B, T, H, C) bf16, lse (B, T, H) fp32) from the key-stream
+    kernel. Range mode (idx None): as prefill_forward. Gather mode: each
+    query reads rows idx[b, t, :] (-1 for none) and its last `window` rows."""
+    _need_cuda(q, k, v, positions, floor, idx, sink)
+    q = _bf16(q).contiguous()
+    k, v = _table(k), _table(v)
+    B, T, H, C = q.shape
+    N = k.shape[1]
+    positions = _rows(positions)
+    floor = None if floor is None else _rows(floor)
+    gather = idx is not None
+    K = 0
+    if gather:
+        idx = _rows(idx)
+        K = idx.shape[-1]
+    if sink is not None:
+        sink = sink.float().contiguous()
+    _, TQ = _stream_shape(T, H, gather)
+    groups = B * math.ceil(T / TQ)
+    if gather:
+        slots = K + max(window, 0)
+    else:
+        slots = min(N, window + TQ - 1) if window > 0 else N
+    tiles = max(1, math.ceil(slots / 128))
+    if chunk_tiles is None:
+        chunk_tiles = int(os.environ.get("WPT_B200_CHUNK", "0")) or max(min(8, tiles),
+                                                                         math.ceil(tiles * groups / (4 * SM_COUNT)))
+    chunk_tiles = max(1, min(int(chunk_tiles), tiles))
+    splits = math.ceil(tiles / chunk_tiles)
+    out = torch.empty_like(q)
+    lse = torch.empty(B, T, H, dtype=torch.float32, device=q.device)
+    part_o = part_lse = None
+    if splits > 1:
+        part_o = torch.empty(splits, B * T * H, C, dtype=torch.float32, device=q.device)
+        part_lse = torch.empty(splits, B * T * H, dtype=torch.float32, device=q.device)
+    _lib.check(_lib.lib().wpt_attn_decode(
+        _lib.ptr(q), _lib.ptr(k), _lib.ptr(v), k.stride(0), k.stride(1), v.stride(0), v.stride(1),
+        _lib.ptr(positions), _lib.ptr(floor), _lib.ptr(idx), K, _lib.ptr(sink), _lib.ptr(out), _lib.ptr(lse),
+        _lib.ptr(part_o), _lib.ptr(part_lse), splits, chunk_tiles, B, T, H, C, N, int(window), float(scale),
+        _lib.stream(q.device)))
+    return out, lse
+
+
+def attention_forward(q, k, v, positions, scale, window=0, floor=None, sink=None):
+    """Range attention by the kernel that suits the shape: the key-stream
+    kernel for few queries per row, the prefill kernel otherwise."""
+    B, T, H, C = q.shape
+    if uses_stream(T, H, C):
+        return stream_forward(q, k, v, positions, scale, window=window, floor=floor, sink=sink)
+    return prefill_forward(q, k, v, positions, scale, window=window, floor=floor, sink=sink)
 
 
 def merge_partials(part_o, part_lse, H, sink=None, out=None, lse=None):
