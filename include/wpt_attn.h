@@ -101,6 +101,22 @@ int wpt_attn_decode(const void* q, const void* k, const void* v, int64_t k_strid
                     float scale, void* stream);
 
 /*
+ * Exact attention's choice of rows (HySparse2's oracle selection,
+ * pytorch_kernels.py:112-117; the Triton form's _exact_choice_kernel,
+ * triton_kernels.py:393-508): for each query at position p, the K rows
+ * among 0 .. min(p - window, N - 1) with the largest
+ * score(n) = max_h (q_h . k_n * scale - lse_h), written to chosen (B, T, K)
+ * int64: the rows above the K-th score first, then rows equal to it by
+ * row index; every candidate in row order, then -1, when a query has K or
+ * fewer. lse (B, T, H) fp32 is the forward pass's. scores is caller scratch
+ * of B * T * ld_scores fp32 (ld_scores >= N). C must be 128, H at most 128.
+ * K = chosen_columns(top_k, window, N) (pytorch_kernels.py:73-77).
+ */
+int wpt_attn_topk(const void* q, const void* k, int64_t k_stride_b, int64_t k_stride_n, const int64_t* positions,
+                  const float* lse, float* scores, int64_t ld_scores, int64_t* chosen, int K, int B, int T, int H,
+                  int C, int N, int window, float scale, void* stream);
+
+/*
  * Merge of split-KV partial results (o normalised per split, fp32; lse per
  * split, natural log, -inf for none) into out (bf16) and lse, adding the
  * sink. part_o (splits, rows, C) at split stride split_stride rows;
@@ -111,6 +127,31 @@ int wpt_attn_decode(const void* q, const void* k, const void* v, int64_t k_strid
  */
 int wpt_attn_merge(const float* part_o, const float* part_lse, int splits, int64_t rows, int64_t split_stride,
                    int H, int C, const float* sink, void* out, float* lse, void* stream);
+
+/*
+ * The acceptance step of speculative decoding, WPT's rule
+ * (packages/wpt-inference/src/wpt_inference/__init__.py:173-179 the
+ * probabilities, :210-222 the loop), for R rows at once:
+ *   p_j = softmax(mask(scores[i, j] / temperature)), the mask keeping the
+ *         top_k largest (ties kept) when top_k > 0;
+ *   draft j of row i is kept iff uniforms[i, j] * q[i, j, tok] < p_j[tok];
+ *   the first rejected draft is replaced by a token drawn from
+ *   normalize(max(0, p_j - q[i, j])); a row that keeps all its drafts adds
+ *   one drawn from p_{n_i}.
+ * The reference draws with torch.rand and torch.multinomial; here the draws
+ * are explicit: uniforms (R, n) for the tests and resample (R,) for the
+ * last token, which is the first index whose float64 running sum of the
+ * weights exceeds resample[i] times their total.
+ *   scores    fp32 (R, n + 1, V) target logits at each draft's place and one after
+ *   drafted   int64 (R, n);  q  fp32 (R, n, V) the drafter's probabilities
+ *   lengths   int64 (R,) drafts verified per row, or NULL for n
+ *   stats     fp32 (R, n + 1, 3) caller scratch
+ *   tokens    int64 (R, n + 1): kept drafts then the drawn token, -1 padded
+ *   accepted  int64 (R,): drafts kept per row
+ */
+int wpt_accept(const float* scores, const int64_t* drafted, const float* q, const float* uniforms,
+               const float* resample, const int64_t* lengths, float* stats, int64_t* tokens, int64_t* accepted,
+               int R, int n, int V, float temperature, int top_k, void* stream);
 
 #ifdef __cplusplus
 }

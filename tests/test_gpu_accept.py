@@ -1,0 +1,70 @@
+"""The acceptance step on the GPU (wpt_inference/__init__.py:173-179,210-222):
+accepted counts and tokens bit-exact against the reference's own
+Writer._speculate (the golden fixtures, made with explicit draws) and
+against the CPU oracle at BASELINE config 4's shape (32 rows, 16 drafts,
+vocabulary 65536, logits ~ N(0, 2)): stochastic, greedy (top_k 1) and top_k
+40 at temperature 0.8, and rows verifying fewer drafts."""
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import accept as oa
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def wb():
+    import wpt_b200
+    from wpt_b200 import build
+    build.build()
+    return wpt_b200
+
+
+@pytest.mark.parametrize("name", ["stochastic", "topk", "greedy"])
+def test_accept_matches_reference_writer(wb, gold, name):
+    d = gold(f"accept_{name}.npz")
+    top_k = None if int(d["top_k"]) < 0 else int(d["top_k"])
+    dev = lambda a: torch.from_numpy(np.ascontiguousarray(a)).cuda()  # noqa: E731
+    tokens, accepted = wb.accept(dev(d["scores"]), dev(d["drafted"]), dev(d["q"]), dev(d["uniforms"]),
+                                 dev(d["resample"]), float(d["temperature"]), top_k)
+    assert np.array_equal(accepted.cpu().numpy(), d["accepted"])
+    assert np.array_equal(tokens.cpu().numpy(), d["tokens"])
+
+
+def _config4(seed, temperature, top_k, near=True):
+    g = torch.Generator().manual_seed(seed)
+    R, n, V = 32, 16, 65536
+    scores = torch.randn(R, n + 1, V, generator=g) * 2.0
+    q_logits = torch.randn(R, n, V, generator=g) * 2.0
+    if near:  # half of the rows draft close to the target, so that drafts are kept
+        q_logits[: R // 2] = scores[: R // 2, :n] + 0.3 * q_logits[: R // 2]
+    q = torch.from_numpy(oa.probabilities(q_logits.numpy(), temperature, top_k))
+    drafted = torch.multinomial(q.reshape(-1, V), 1, generator=g).view(R, n)
+    uniforms = torch.rand(R, n, generator=g)
+    resample = torch.rand(R, generator=g)
+    return scores, drafted, q, uniforms, resample
+
+
+@pytest.mark.parametrize("temperature,top_k", [(1.0, None), (1.0, 1), (0.8, 40)])
+def test_accept_matches_oracle_at_config4(wb, temperature, top_k):
+    scores, drafted, q, uniforms, resample = _config4(4, temperature, top_k)
+    tokens, accepted = wb.accept(scores.cuda(), drafted.cuda(), q.cuda(), uniforms.cuda(), resample.cuda(),
+                                 temperature, top_k)
+    ref_tokens, ref_accepted = oa.accept(scores.numpy(), drafted.numpy(), q.numpy(), uniforms.numpy(),
+                                         resample.numpy(), temperature, top_k)
+    assert np.array_equal(accepted.cpu().numpy(), ref_accepted)
+    assert np.array_equal(tokens.cpu().numpy(), ref_tokens)
+    assert ref_accepted.max() > 0 and ref_accepted.min() < 16  # both outcomes exercised
+
+
+def test_rows_verifying_fewer_drafts(wb):
+    scores, drafted, q, uniforms, resample = _config4(5, 1.0, None)
+    lengths = torch.randint(0, 17, (32,), generator=torch.Generator().manual_seed(6))
+    tokens, accepted = wb.accept(scores.cuda(), drafted.cuda(), q.cuda(), uniforms.cuda(), resample.cuda(), 1.0,
+                                 None, lengths=lengths.cuda())
+    ref_tokens, ref_accepted = oa.accept(scores.numpy(), drafted.numpy(), q.numpy(), uniforms.numpy(),
+                                         resample.numpy(), 1.0, None, lengths=lengths.numpy())
+    assert np.array_equal(accepted.cpu().numpy(), ref_accepted)
+    assert np.array_equal(tokens.cpu().numpy(), ref_tokens)

@@ -152,3 +152,34 @@ def test_split_kv_equals_unsplit(wb, splits):
     ref_out, ref_lse = oat.sparse_over_rows(_np(q), _np(e[..., :C]), _np(e[..., C:]), sink.double().cpu().numpy(),
                                             rows, C ** -0.5)
     _check(wb, parts[0], parts[1], ref_out, ref_lse)
+
+
+@pytest.mark.parametrize("splits", [2, 4])
+def test_split_kv_with_a_partly_filled_last_query_tile(wb, splits):
+    # the last query tile of each row holds 12 of 16 tokens (H = 8): every
+    # split's partial must be complete before its epilogue reads it
+    from wpt_b200 import ops
+    B, T, H, C = 2, 700, 8, 128
+    q, e = _inputs(B, T, H, C, T, seed=708)
+    positions = torch.arange(T).expand(B, T).contiguous()
+    out, lse = ops.prefill_forward(q.cuda(), e.cuda()[..., :C], e.cuda()[..., C:], positions.cuda(), C ** -0.5,
+                                   splits=splits)
+    ref_out, ref_lse, _ = oat.exact_attention(_np(q), _np(e[..., :C]), _np(e[..., C:]), positions.numpy(),
+                                              C ** -0.5, 0, 0)
+    _check(wb, out, lse, ref_out, ref_lse)
+
+
+def test_growing_scores_force_rescales(wb):
+    # scores that grow along the row raise each row's running maximum by far
+    # more than the lazy threshold in every tile, so O is rescaled each time
+    B, T, H, C = 1, 640, 16, 128
+    g = torch.Generator().manual_seed(31)
+    u = torch.randn(C, generator=g)
+    u = u / u.norm()
+    q = (u * 3.0 + 0.1 * torch.randn(B, T, H, C, generator=g)).bfloat16()
+    k = (u * (torch.arange(T)[:, None] / 16.0) + 0.1 * torch.randn(B, T, C, generator=g)).bfloat16()
+    v = torch.randn(B, T, C, generator=g).bfloat16()
+    positions = torch.arange(T).expand(B, T).contiguous()
+    out, lse = wb.forward_with_lse(q.cuda(), k.cuda(), v.cuda(), positions.cuda(), C ** -0.5)
+    ref_out, ref_lse, _ = oat.exact_attention(_np(q), _np(k), _np(v), positions.numpy(), C ** -0.5, 0, 0)
+    _check(wb, out, lse, ref_out, ref_lse)

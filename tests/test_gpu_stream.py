@@ -137,3 +137,24 @@ def test_sparse_golden_shape_through_both_paths_agree(wb):
                                idx=torch.from_numpy(window_rows).cuda(), sink=sink.cuda())
     assert (a.float() - b.float()).abs().max().item() < 1e-2
     assert (la - lb).abs().max().item() < 1e-4
+
+
+def test_decode_growing_scores_force_rescales(wb):
+    # the running maximum is raised by far more than the lazy threshold in
+    # every tile, so the key-stream kernel rescales O^T each time
+    from wpt_b200 import ops
+    B, H, C, N = 4, 32, 128, 3000
+    g = torch.Generator().manual_seed(32)
+    u = torch.randn(C, generator=g)
+    u = u / u.norm()
+    q = (u * 3.0 + 0.1 * torch.randn(B, 1, H, C, generator=g)).bfloat16()
+    e = torch.randn(B, N, 2 * C, generator=g)
+    e[..., :C] = u * (torch.arange(N)[:, None] / 16.0) + 0.1 * e[..., :C]
+    e = e.bfloat16()
+    positions = torch.tensor([[2999], [2000], [1300], [300]])
+    for chunk in (1, 4, 100):
+        out, lse = ops.stream_forward(q.cuda(), e.cuda()[..., :C], e.cuda()[..., C:], positions.cuda(), C ** -0.5,
+                                      chunk_tiles=chunk)
+        ref_out, ref_lse, _ = oat.exact_attention(_np(q), _np(e[..., :C]), _np(e[..., C:]), positions.numpy(),
+                                                  C ** -0.5, 0, 0)
+        _check(wb, out, lse, ref_out, ref_lse)

@@ -56,9 +56,7 @@ class _Exact(torch.autograd.Function):
         positions = _positions(positions, B)
         out, lse = ops.attention_forward(q, k, v, positions, scale)
         K = chosen_columns(top_k, window, N)
-        if K:
-            raise NotImplementedError("top-k selection kernel not built yet")
-        chosen = torch.empty(B, T, 0, dtype=torch.long, device=q.device)
+        chosen = ops.select_rows(q, k, positions, lse, scale, K, window)
         ctx.save_for_backward(q, k, v, positions, out, lse)
         ctx.scale = scale
         ctx.mark_non_differentiable(chosen)
@@ -157,6 +155,18 @@ def tree_attention(q, k, v, cache_len, parents, scale, sink=None):
     return ops.prefill_forward(q, k, v, positions, scale, tree_bits=bits, tree_base=cache_len, sink=sink)
 
 
-__all__ = ["NAME", "WINDOW", "chosen_columns", "exact_attention", "sparse_attention", "window_attention",
+# ------------------------------------------------------------ acceptance step
+
+def accept(scores, drafted, q, uniforms, resample, temperature=1.0, top_k=None, lengths=None):
+    """WPT's speculative acceptance (wpt_inference/__init__.py:173-179,
+    210-222) for R rows on the GPU, with the draws as inputs: scores
+    (R, n + 1, V) target logits, drafted (R, n), q (R, n, V) the drafter's
+    probabilities, uniforms (R, n) the accept tests' draws, resample (R,) the
+    last token's draw (inverse CDF). Returns (tokens (R, n + 1), -1 padded;
+    accepted (R,))."""
+    return ops.accept(scores, drafted, q, uniforms, resample, temperature, top_k, lengths)
+
+
+__all__ = ["accept", "NAME", "WINDOW", "chosen_columns", "exact_attention", "sparse_attention", "window_attention",
            "tree_attention",
            "forward_with_lse", "device_status", "LibraryMissing"]

@@ -68,7 +68,7 @@ struct PrefillLayout {
   static constexpr int OFF_K = Q_BYTES;
   static constexpr int OFF_V = OFF_K + STAGES * KV_BYTES;
   static constexpr int OFF_BAR = OFF_V + STAGES * KV_BYTES;
-  static constexpr int NBAR = 1 + 3 * STAGES + 5;
+  static constexpr int NBAR = 1 + 3 * STAGES + 6;
   static constexpr int OFF_MISC = OFF_BAR + NBAR * 8;
   static constexpr int BYTES = OFF_MISC + 16 + 1024;  // + slack to align the base to 1024
 };
@@ -105,6 +105,7 @@ __global__ void __launch_bounds__(192, 1)
   uint64_t* s_full = kv_empty + STAGES;
   uint64_t* p_ready = s_full + 2;
   uint64_t* o_done = p_ready + 2;
+  uint64_t* o_final = o_done + 1;  // one phase: the last P V product has completed
   uint32_t* s_tmem = reinterpret_cast<uint32_t*>(smem + L::OFF_MISC);
   int* s_range = reinterpret_cast<int*>(smem + L::OFF_MISC + 4);
 
@@ -125,6 +126,7 @@ __global__ void __launch_bounds__(192, 1)
       mbar_init(p_ready + s, 128);
     }
     mbar_init(o_done, 1);
+    mbar_init(o_final, 1);
     fence_mbar_init();
     s_range[0] = INT_MAX;
     s_range[1] = -1;
@@ -226,6 +228,7 @@ __global__ void __launch_bounds__(192, 1)
           }
           mma_commit(kv_empty + st);
           mma_commit(o_done);
+          if (j == ntiles) mma_commit(o_final);
         }
       }
     }
@@ -317,7 +320,10 @@ __global__ void __launch_bounds__(192, 1)
       tc_fence_before();
       mbar_arrive(p_ready + (j & 1));
     }
-    if (ok && ntiles > 0) ok = __all_sync(0xffffffffu, mbar_wait(o_done, (ntiles - 1) & 1, p.status));
+    // o_done's parity cannot name the last product here (the MMA may still be
+    // two products behind, and phase ntiles - 3 has the same parity), so the
+    // epilogue waits on o_final, which completes once, after the last one
+    if (ok && ntiles > 0) ok = __all_sync(0xffffffffu, mbar_wait(o_final, 0, p.status));
     tc_fence_after();
     if (ok) {
       const int64_t orow = (static_cast<int64_t>(b) * p.T + t) * p.H + h;

@@ -77,7 +77,7 @@ struct StreamLayout {
   static constexpr int OFF_QHI = OFF_QLO + 64 * 4;
   static constexpr int OFF_COLQ = OFF_QHI + 64 * 4;
   static constexpr int OFF_BAR = OFF_COLQ + 64 * 4;
-  static constexpr int NBAR = 1 + 2 * STAGES + 5;
+  static constexpr int NBAR = 1 + 2 * STAGES + 6;
   static constexpr int OFF_MISC = OFF_BAR + NBAR * 8;
   static constexpr int BYTES = OFF_MISC + 16 + 1024;
   static constexpr int TMEM_COLS = 3 * NCOL <= 32 ? 32 : 3 * NCOL <= 64 ? 64 : 3 * NCOL <= 128 ? 128 : 256;
@@ -126,6 +126,7 @@ __global__ void __launch_bounds__(STREAM_THREADS, 1)
   uint64_t* s_full = kv_empty + STAGES;
   uint64_t* p_ready = s_full + 2;
   uint64_t* o_done = p_ready + 2;
+  uint64_t* o_final = o_done + 1;  // one phase: the last P V product has completed
   uint32_t* s_tmem = reinterpret_cast<uint32_t*>(smem + L::OFF_MISC);
   int* s_range = reinterpret_cast<int*>(smem + L::OFF_MISC + 4);
 
@@ -201,6 +202,7 @@ __global__ void __launch_bounds__(STREAM_THREADS, 1)
       mbar_init(p_ready + s, 128);
     }
     mbar_init(o_done, 1);
+    mbar_init(o_final, 1);
     fence_mbar_init();
   }
   if (warp == 4) {
@@ -347,6 +349,7 @@ __global__ void __launch_bounds__(STREAM_THREADS, 1)
           }
           mma_commit(kv_empty + st);
           mma_commit(o_done);
+          if (j == ntiles) mma_commit(o_final);
         }
       }
     }
@@ -488,7 +491,10 @@ __global__ void __launch_bounds__(STREAM_THREADS, 1)
       fence_proxy_async();
       mbar_arrive(p_ready + (j & 1));
     }
-    if (ok) ok = __all_sync(0xffffffffu, mbar_wait(o_done, (ntiles - 1) & 1, p.status));
+    // o_done's parity cannot name the last product here (the MMA may still be
+    // two products behind, and phase ntiles - 3 has the same parity), so the
+    // epilogue waits on o_final, which completes once, after the last one
+    if (ok) ok = __all_sync(0xffffffffu, mbar_wait(o_final, 0, p.status));
     tc_fence_after();
     // per-column sums over the 128 slots
 #pragma unroll

@@ -6,9 +6,11 @@
 #include <string>
 
 #include "../../include/wpt_attn.h"
+#include "accept.cuh"
 #include "common.cuh"
 #include "merge.cuh"
 #include "prefill.cuh"
+#include "select.cuh"
 #include "stream.cuh"
 
 namespace {
@@ -138,6 +140,20 @@ int launch_stream_g(const CUtensorMap& tk, const CUtensorMap& tv, const wpt::Str
     case 32: return launch_stream_n<32, 3, GATHER>(tk, tv, p, groups, stream);
     default: return launch_stream_n<64, 2, GATHER>(tk, tv, p, groups, stream);
   }
+}
+
+template <int NCOL>
+int launch_score(const CUtensorMap& tq, const CUtensorMap& tk, const wpt::ScoreParams& p, int groups, int splits,
+                 cudaStream_t stream) {
+  constexpr int STAGES = 4;
+  using L = wpt::ScoreLayout<NCOL, STAGES>;
+  static_assert(L::BYTES <= 232448, "score kernel shared memory exceeds 227 KB");
+  auto kernel = wpt::score_kernel<NCOL, STAGES>;
+  if (int rc = allow_smem(kernel, L::BYTES)) return rc;
+  kernel<<<dim3(groups, splits), 192, L::BYTES, stream>>>(tq, tk, p);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "score_kernel launch");
+  return WPT_OK;
 }
 
 template <int C>
@@ -310,5 +326,104 @@ extern "C" int wpt_attn_decode(const void* q, const void* k, const void* v, int6
     const int64_t rows = static_cast<int64_t>(B) * T * H;
     return launch_merge<128>(part_o, part_lse, splits, rows, rows, H, sink, out, lse, s);
   }
+  return WPT_OK;
+}
+
+extern "C" int wpt_attn_topk(const void* q, const void* k, int64_t k_stride_b, int64_t k_stride_n,
+                             const int64_t* positions, const float* lse, float* scores, int64_t ld_scores,
+                             int64_t* chosen, int K, int B, int T, int H, int C, int N, int window, float scale,
+                             void* stream) {
+  if (C != 128) return fail(WPT_ERR_UNSUPPORTED, "head width %d: the selection kernel takes 128", C);
+  if (H < 1 || H > 128) return fail(WPT_ERR_UNSUPPORTED, "%d heads: the selection kernel takes 1 to 128", H);
+  if (B < 1 || T < 1 || N < 1 || K < 0) return fail(WPT_ERR_INVALID, "bad shape B=%d T=%d N=%d K=%d", B, T, N, K);
+  if (K == 0) return WPT_OK;
+  if (ld_scores < N) return fail(WPT_ERR_INVALID, "ld_scores %lld < N %d", static_cast<long long>(ld_scores), N);
+  if (!q || !k || !positions || !lse || !scores || !chosen) return fail(WPT_ERR_INVALID, "a required pointer is NULL");
+  if (!aligned16(q)) return fail(WPT_ERR_INVALID, "q must be 16-byte aligned");
+  if (static_cast<int64_t>(B) * T * H >= (int64_t(1) << 31)) return fail(WPT_ERR_UNSUPPORTED, "B*T*H too large");
+  const int cols = T * H < 256 ? T * H : 256;
+  const int ncol = cols <= 16 ? 16 : cols <= 32 ? 32 : cols <= 64 ? 64 : cols <= 128 ? 128 : 256;
+  wpt::ScoreParams p;
+  p.positions = positions;
+  p.lse = lse;
+  p.scores = scores;
+  p.ld = ld_scores;
+  if (int rc = status_word(&p.status)) return rc;
+  p.B = B;
+  p.T = T;
+  p.H = H;
+  p.N = N;
+  p.window = window;
+  p.TQ = ncol / H;
+  if (p.TQ < 1) return fail(WPT_ERR_UNSUPPORTED, "%d heads exceed the selection kernel's columns", H);
+  p.groups_per_row = (T + p.TQ - 1) / p.TQ;
+  p.scale = scale;
+  const int64_t groups = static_cast<int64_t>(B) * p.groups_per_row;
+  const int tiles = (N + 127) / 128;
+  int64_t chunk = (static_cast<int64_t>(tiles) * groups + 4 * 148 - 1) / (4 * 148);
+  if (chunk < 4) chunk = 4;
+  if (chunk > tiles) chunk = tiles;
+  p.chunk_tiles = static_cast<int>(chunk);
+  const int splits = (tiles + p.chunk_tiles - 1) / p.chunk_tiles;
+  if (groups >= (int64_t(1) << 31) || splits > 65535) return fail(WPT_ERR_UNSUPPORTED, "selection grid too large");
+  CUtensorMap tq, tk;
+  {
+    cuuint64_t dims[2] = {static_cast<cuuint64_t>(C), static_cast<cuuint64_t>(B) * T * H};
+    cuuint64_t strides[1] = {static_cast<cuuint64_t>(C) * 2};
+    cuuint32_t box[2] = {64, static_cast<cuuint32_t>(ncol)};
+    if (int rc = tensor_map(&tq, q, 2, dims, strides, box)) return rc;
+  }
+  if (int rc = table_map(&tk, k, k_stride_b, k_stride_n, B, N, C)) return rc;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  int rc;
+  switch (ncol) {
+    case 16: rc = launch_score<16>(tq, tk, p, static_cast<int>(groups), splits, s); break;
+    case 32: rc = launch_score<32>(tq, tk, p, static_cast<int>(groups), splits, s); break;
+    case 64: rc = launch_score<64>(tq, tk, p, static_cast<int>(groups), splits, s); break;
+    case 128: rc = launch_score<128>(tq, tk, p, static_cast<int>(groups), splits, s); break;
+    default: rc = launch_score<256>(tq, tk, p, static_cast<int>(groups), splits, s); break;
+  }
+  if (rc) return rc;
+  const int cap = N < 49152 ? N : 49152;
+  const int smem = (cap + 256 + 32) * 4;
+  if (int rc2 = allow_smem(wpt::topk_kernel, smem)) return rc2;
+  wpt::topk_kernel<<<static_cast<unsigned>(static_cast<int64_t>(B) * T), wpt::TOPK_THREADS, smem, s>>>(
+      scores, ld_scores, positions, chosen, T, N, K, window, cap);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "topk_kernel launch");
+  return WPT_OK;
+}
+
+extern "C" int wpt_accept(const float* scores, const int64_t* drafted, const float* q, const float* uniforms,
+                          const float* resample, const int64_t* lengths, float* stats, int64_t* tokens,
+                          int64_t* accepted, int R, int n, int V, float temperature, int top_k, void* stream) {
+  if (R < 0 || n < 0 || V < 1) return fail(WPT_ERR_INVALID, "bad accept shape R=%d n=%d V=%d", R, n, V);
+  if (R == 0) return WPT_OK;
+  if (R > 65535 || n + 1 > 65535) return fail(WPT_ERR_UNSUPPORTED, "accept grid too large (R=%d, n=%d)", R, n);
+  if (!(temperature > 0.f)) return fail(WPT_ERR_INVALID, "temperature must be positive");
+  if (!scores || !stats || !tokens || !accepted || !resample || (n > 0 && (!drafted || !q || !uniforms)))
+    return fail(WPT_ERR_INVALID, "a required pointer is NULL");
+  wpt::AcceptParams p;
+  p.scores = scores;
+  p.drafted = drafted;
+  p.q = q;
+  p.uniforms = uniforms;
+  p.resample = resample;
+  p.lengths = lengths;
+  p.stats = stats;
+  p.tokens = tokens;
+  p.accepted = accepted;
+  p.R = R;
+  p.n = n;
+  p.V = V;
+  p.top_k = top_k;
+  p.temperature = temperature;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  wpt::accept_stats_kernel<<<dim3(n + 1, R), wpt::ACCEPT_THREADS, 0, s>>>(p);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "accept_stats_kernel launch");
+  wpt::accept_draw_kernel<<<R, wpt::ACCEPT_THREADS, 0, s>>>(p);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "accept_draw_kernel launch");
   return WPT_OK;
 }

@@ -152,6 +152,28 @@ def attention_forward(q, k, v, positions, scale, window=0, floor=None, sink=None
     return prefill_forward(q, k, v, positions, scale, window=window, floor=floor, sink=sink)
 
 
+def select_rows(q, k, positions, lse, scale, K, window):
+    """Each query's K chosen rows (B, T, K) int64 (pytorch_kernels.py:112-117):
+    the top K by max_h (q_h . k_n * scale - lse_h) among rows 0 .. p - window,
+    -1 padded. lse is the forward pass's (B, T, H)."""
+    _need_cuda(q, k, positions, lse)
+    q = _bf16(q).contiguous()
+    k = _table(k)
+    B, T, H, C = q.shape
+    N = k.shape[1]
+    positions = _rows(positions)
+    lse = lse.float().contiguous()
+    chosen = torch.empty(B, T, K, dtype=torch.int64, device=q.device)
+    if K == 0:
+        return chosen
+    ld = (N + 3) // 4 * 4
+    scores = torch.empty(B * T, ld, dtype=torch.float32, device=q.device)
+    _lib.check(_lib.lib().wpt_attn_topk(
+        _lib.ptr(q), _lib.ptr(k), k.stride(0), k.stride(1), _lib.ptr(positions), _lib.ptr(lse), _lib.ptr(scores),
+        ld, _lib.ptr(chosen), int(K), B, T, H, C, N, int(window), float(scale), _lib.stream(q.device)))
+    return chosen
+
+
 def merge_partials(part_o, part_lse, H, sink=None, out=None, lse=None):
     """Log-sum-exp merge of split partials: part_o (S, rows, C) fp32,
     part_lse (S, rows) -> (out (rows, C) bf16, lse (rows,) fp32)."""
@@ -189,3 +211,27 @@ def tree_bits_from_parents(parents):
             masks.append(m)
             bits[r, i] = m - (1 << 64) if m >= (1 << 63) else m
     return bits.reshape(par.shape).to(device)
+
+
+def accept(scores, drafted, q, uniforms, resample, temperature=1.0, top_k=None, lengths=None):
+    """The acceptance step for R rows (wpt_inference/__init__.py:173-179,
+    210-222) with explicit draws: returns (tokens (R, n + 1) int64, -1
+    padded: each row's kept drafts then its drawn token; accepted (R,)
+    int64: the drafts each row kept)."""
+    _need_cuda(scores, drafted, q, uniforms, resample, lengths)
+    scores = scores.float().contiguous()
+    R, n1, V = scores.shape
+    n = n1 - 1
+    drafted = drafted.to(torch.int64).contiguous()
+    q = q.float().contiguous()
+    uniforms = uniforms.float().contiguous()
+    resample = resample.float().reshape(R).contiguous()
+    lengths = None if lengths is None else lengths.to(torch.int64).contiguous()
+    stats = torch.empty(R, n + 1, 3, dtype=torch.float32, device=scores.device)
+    tokens = torch.empty(R, n + 1, dtype=torch.int64, device=scores.device)
+    accepted = torch.empty(R, dtype=torch.int64, device=scores.device)
+    _lib.check(_lib.lib().wpt_accept(
+        _lib.ptr(scores), _lib.ptr(drafted), _lib.ptr(q), _lib.ptr(uniforms), _lib.ptr(resample), _lib.ptr(lengths),
+        _lib.ptr(stats), _lib.ptr(tokens), _lib.ptr(accepted), R, n, V, float(temperature),
+        0 if top_k is None else int(top_k), _lib.stream(scores.device)))
+    return tokens, accepted
