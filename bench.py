@@ -1,0 +1,427 @@
+"""Benchmark of the B200 attention hot path (WPT's MQA attention) on the
+headline configuration BASELINE.json quotes first for one GPU, config 2:
+prefill attention, bf16, B=8, T=4096, 16 query heads, 1 KV head, head
+width 128, a causal pass (exact_attention) then a window-1024 pass with a
+sink (sparse_attention with no chosen rows), inputs ~ N(0,1)*0.5 from
+seeds 1 and 2. One step = both passes over one batch. Metric: prefill
+attention TFLOP/s of algorithmic work (4*H*c per visible (query, key) pair).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
+
+With N > 1 it runs under torchrun, one rank per GPU; each rank takes its
+own batch of 8 rows (weak scaling, no collective on the data path) and the
+timed region is bracketed by barriers, its time the maximum over ranks.
+Secondary lines in the same JSON: decode attention GB/s (config 3, global
+and window-1024 rows; with N > 1 also the 262,144-token row split along its
+keys over the ranks with an NCCL combine), tree verification (config 4)
+and the acceptance step (config 4).
+
+--impl reference times the reference's CPU path: the CPU restatement of
+the reference's PyTorch attention (oracle/, pinned to the reference's own
+outputs by tests/test_oracle.py) in float32 with BLAS on the host cores,
+each step a bounded sample (one batch row of config 2, both passes).
+"""
+
+import argparse
+import datetime
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+import numpy as np
+import torch
+import torch.distributed as dist
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+METRIC = "prefill attention TFLOP/s (config 2: causal + window-1024 passes)"
+B2, T2, H2, C2, W2 = 8, 4096, 16, 128, 1024
+
+
+def peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            d = json.load(f)
+        return {k: float(d[k]) for k in FALLBACK_PEAKS}, "measured"
+    return dict(FALLBACK_PEAKS), "fallback"
+
+
+def config2_flops(B=B2, T=T2, H=H2, C=C2, W=W2):
+    causal = 4.0 * B * H * C * T * (T + 1) / 2
+    window = 4.0 * B * H * C * sum(min(p + 1, W) for p in range(T))
+    return causal, window
+
+
+# ------------------------------------------------------------------ clocks
+
+class Clocks:
+    """nvidia-smi samples of one GPU during the timed region."""
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, local_rank):
+        visible = os.environ.get("CUDA_VISIBLE_DEVICES", "")
+        ids = [x for x in visible.split(",") if x.strip()]
+        self.index = ids[local_rank] if local_rank < len(ids) and ids[local_rank].strip().isdigit() else str(local_rank)
+        self.proc = None
+        self.file = None
+
+    def start(self):
+        try:
+            self.file = tempfile.TemporaryFile(mode="w+")
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                                          "-i", self.index, "-lms", "200"], stdout=self.file,
+                                         stderr=subprocess.DEVNULL)
+        except (OSError, ValueError):
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        time.sleep(0.25)
+        self.proc.terminate()
+        self.proc.wait(timeout=10)
+        self.file.seek(0)
+        rows = [r.split(",") for r in self.file.read().strip().splitlines() if r.count(",") >= 8]
+        sm = [float(r[1]) for r in rows if r[1].strip().replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if r[2].strip().replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if "Active" in r[5 + i] and "Not" not in r[5 + i]})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(rows)}
+
+
+# -------------------------------------------------------------- workloads
+
+def config2_inputs(device, rank):
+    g = torch.Generator(device=device).manual_seed(1 + 1000 * rank)
+    q = (torch.randn(B2, T2, H2, C2, generator=g, device=device) * 0.5).bfloat16()
+    entries = (torch.randn(B2, T2, 2 * C2, generator=g, device=device) * 0.5).bfloat16()
+    sink = torch.randn(H2, generator=torch.Generator(device=device).manual_seed(2), device=device) * 0.5
+    positions = torch.arange(T2, device=device).expand(B2, T2).contiguous()
+    return q, entries, positions, sink
+
+
+def prefill_step(wb, q, entries, positions, sink):
+    C = q.shape[-1]
+    k, v = entries[..., :C], entries[..., C:]
+    empty = torch.empty(q.shape[0], q.shape[1], 0, dtype=torch.int64, device=q.device)
+    causal, _ = wb.exact_attention(q, k, v, positions, C ** -0.5, 0, W2)
+    window = wb.sparse_attention(q, k, v, sink, empty, positions, C ** -0.5, W2)
+    return causal, window
+
+
+def config3_lengths():
+    return torch.randint(1024, 32769, (64,), generator=torch.Generator().manual_seed(0))
+
+
+def tree_parents(n=16, seed=3):
+    """§8(d) config 4's draft tree: node 0 the root at depth 1; node i's parent
+    drawn uniformly among earlier nodes of depth < 4 with fewer than 2
+    children (the root may take 3)."""
+    g = torch.Generator().manual_seed(seed)
+    parents, depth, kids = [-1], [1], [0]
+    for i in range(1, n):
+        eligible = [j for j in range(i) if depth[j] < 4 and kids[j] < (3 if j == 0 else 2)]
+        j = eligible[int(torch.randint(len(eligible), (1,), generator=g))]
+        parents.append(j)
+        depth.append(depth[j] + 1)
+        kids.append(0)
+        kids[j] += 1
+    return parents, depth
+
+
+def timed(fn, steps, warmup, stream=None):
+    """Mean milliseconds per call of fn over `steps` calls, CUDA events on the
+    launching stream, synchronised on both sides."""
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    s = torch.cuda.Event(enable_timing=True)
+    e = torch.cuda.Event(enable_timing=True)
+    stream = stream or torch.cuda.current_stream()
+    s.record(stream)
+    for _ in range(steps):
+        fn()
+    e.record(stream)
+    torch.cuda.synchronize()
+    return s.elapsed_time(e) / steps
+
+
+def secondary(wb, ops, device, rank, world, hbm):
+    """Decode, verification and acceptance lines (each rank runs its own)."""
+    out = {}
+    C, H = 128, 32
+    # config 3: 64 ragged decode rows
+    L = config3_lengths()
+    g = torch.Generator(device=device).manual_seed(10 + rank)
+    table = (torch.randn(64, 32768, 2 * C, generator=g, device=device) * 0.5).bfloat16()
+    q = (torch.randn(64, 1, H, C, generator=g, device=device) * 0.5).bfloat16()
+    sink = torch.randn(H, generator=g, device=device) * 0.5
+    pos = (L - 1).to(device)[:, None].contiguous()
+    k, v = table[..., :C], table[..., C:]
+    empty = torch.empty(64, 1, 0, dtype=torch.int64, device=device)
+    ms_g = timed(lambda: wb.exact_attention(q, k, v, pos, C ** -0.5, 0, 128), 20, 3)
+    ms_w = timed(lambda: wb.sparse_attention(q, k, v, sink, empty, pos, C ** -0.5, 1024), 20, 3)
+    qo = 2 * 64 * H * C * 2
+    bytes_g = int(L.sum()) * 2 * C * 2 + qo
+    bytes_w = int(L.clamp(max=1024).sum()) * 2 * C * 2 + qo
+    out["decode_global"] = {"metric": "decode attention HBM GB/s (config 3, global rows)", "unit": "GB/s",
+                            "value": round(bytes_g / ms_g / 1e6, 1), "frac_of_hbm": round(bytes_g / ms_g / 1e6 / hbm, 3),
+                            "ms": round(ms_g, 4), "algorithmic_bytes": bytes_g}
+    out["decode_window"] = {"metric": "decode attention HBM GB/s (config 3, window-1024 rows)", "unit": "GB/s",
+                            "value": round(bytes_w / ms_w / 1e6, 1), "frac_of_hbm": round(bytes_w / ms_w / 1e6 / hbm, 3),
+                            "ms": round(ms_w, 4), "algorithmic_bytes": bytes_w}
+    del table
+    # the 262,144-token row, split along its keys over the ranks
+    from wpt_b200 import multi
+    N = 262144
+    start, stop = multi.key_shard(N, world, rank)
+    gl = torch.Generator(device=device).manual_seed(20 + rank)
+    shard = (torch.randn(1, stop - start, 2 * C, generator=gl, device=device) * 0.5).bfloat16()
+    ql = (torch.randn(1, 1, H, C, generator=torch.Generator(device=device).manual_seed(21), device=device) * 0.5
+          ).bfloat16()
+    pl = torch.full((1, 1), N - 1, dtype=torch.int64, device=device)
+
+    def long_row():
+        return multi.long_decode(ql, shard[..., :C], shard[..., C:], start, pl, C ** -0.5)
+    if world > 1:
+        dist.barrier()
+    ms_l = timed(long_row, 20, 3)
+    if world > 1:
+        t = torch.tensor([ms_l], device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms_l = float(t)
+    bytes_l = N * 2 * C * 2
+    out["decode_long_row"] = {"metric": f"decode attention HBM GB/s (262,144-token row over {world} GPU(s))",
+                              "unit": "GB/s", "value": round(bytes_l / ms_l / 1e6, 1),
+                              "frac_of_hbm": round(bytes_l / ms_l / 1e6 / (hbm * world), 3), "ms": round(ms_l, 4)}
+    del shard
+    # config 4: tree verification
+    parents, depth = tree_parents()
+    B4, L4, n4 = 32, 8192, 16
+    g4 = torch.Generator(device=device).manual_seed(3 + rank)
+    t4 = (torch.randn(B4, L4 + n4, 2 * C, generator=g4, device=device) * 0.5).bfloat16()
+    q4 = (torch.randn(B4, n4, H, C, generator=g4, device=device) * 0.5).bfloat16()
+    cl = torch.full((B4,), L4, dtype=torch.int64, device=device)
+    bits = ops.tree_bits_from_parents(torch.tensor(parents)).to(device).expand(B4, n4).contiguous()
+    vpos = cl[:, None] + torch.arange(n4, device=device)
+    ms_v = timed(lambda: ops.prefill_forward(q4, t4[..., :C], t4[..., C:], vpos, C ** -0.5, tree_bits=bits,
+                                             tree_base=cl), 20, 3)
+    flops_v = 4.0 * B4 * H * C * sum(L4 + d for d in depth)
+    out["verify_tree"] = {"metric": "tree verification attention TFLOP/s (config 4)", "unit": "TFLOP/s",
+                          "value": round(flops_v / ms_v / 1e9, 1), "ms": round(ms_v, 4), "algorithmic_flops": flops_v}
+    del t4
+    # config 4: acceptance step
+    R, n, V = 32, 16, 65536
+    ga = torch.Generator(device=device).manual_seed(4)
+    scores = torch.randn(R, n + 1, V, generator=ga, device=device) * 2.0
+    qprob = torch.softmax(torch.randn(R, n, V, generator=ga, device=device) * 2.0, -1)
+    drafted = torch.multinomial(qprob.reshape(-1, V), 1, generator=ga).view(R, n)
+    uniforms = torch.rand(R, n, generator=ga, device=device)
+    resample = torch.rand(R, generator=ga, device=device)
+    ms_a = timed(lambda: wb.accept(scores, drafted, qprob, uniforms, resample, 1.0, None), 20, 3)
+    _, accepted = wb.accept(scores, drafted, qprob, uniforms, resample, 1.0, None)
+    written = int(accepted.sum()) + R
+    bytes_a = 2 * R * (n + 1) * V * 4
+    out["accept"] = {"metric": "speculative acceptance, accepted tokens/s (config 4, stochastic)", "unit": "tokens/s",
+                     "value": round(written / ms_a * 1e3, 1), "ms": round(ms_a, 4),
+                     "logit_GB/s": round(bytes_a / ms_a / 1e6, 1), "tokens_per_call": written}
+    return out
+
+
+# ----------------------------------------------------------- CPU baseline
+
+def cpu_rows(seconds=10.0, max_rows=B2, dtype=np.float32):
+    """The CPU restatement on config-2 rows (both passes), until `seconds`
+    have passed (at least one row). Returns (TFLOP/s, rows, seconds, threads)."""
+    from oracle import attention as oat
+    causal, window = config2_flops(B=1)
+    g = torch.Generator().manual_seed(1)
+    done, flops, t0 = 0, 0.0, time.perf_counter()
+    while done < max_rows and (done == 0 or time.perf_counter() - t0 < seconds):
+        q = (torch.randn(1, T2, H2, C2, generator=g) * 0.5).bfloat16().float().numpy()
+        e = (torch.randn(1, T2, 2 * C2, generator=g) * 0.5).bfloat16().float().numpy()
+        sink = (torch.randn(H2, generator=torch.Generator().manual_seed(2)) * 0.5).numpy()
+        pos = np.arange(T2)[None]
+        oat.range_attention(q, e[..., :C2], e[..., C2:], pos, C2 ** -0.5, dtype=dtype)
+        oat.range_attention(q, e[..., :C2], e[..., C2:], pos, C2 ** -0.5, window=W2, sink=sink, dtype=dtype)
+        done += 1
+        flops += causal + window
+    dt = time.perf_counter() - t0
+    return flops / dt / 1e12, done, dt
+
+
+def reference_arm(args, rank, world):
+    """--impl reference: the CPU restatement timed on the host cores."""
+    if rank != 0:
+        return
+    causal, window = config2_flops(B=1)
+    for _ in range(args.warmup):
+        cpu_rows(seconds=0.0, max_rows=1)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        cpu_rows(seconds=0.0, max_rows=1)
+    dt = time.perf_counter() - t0
+    value = (causal + window) * args.steps / dt / 1e12
+    cores = os.cpu_count()
+    line = {"impl": "reference", "metric": METRIC, "value": round(value, 4), "unit": "TFLOP/s", "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(dt / args.steps * 1e3, 2),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": "config 2 prefill (B=8, T=4096, 16q/1kv, c=128; causal + window 1024 + sink)",
+                       "global_batch": B2 * args.gpus, "seq_len": T2, "parallelism": "cpu"},
+            "cpu_baseline": {"value": round(value, 4), "unit": "TFLOP/s", "cores": cores, "kind": "port",
+                             "sample": "one batch row of config 2 per step (causal + window passes), float32 BLAS"},
+            "e2e": {"value": round(value, 4), "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+# ------------------------------------------------------------------- main
+
+def main():
+    parser = argparse.ArgumentParser()
+    parser.add_argument("--gpus", type=int, default=1)
+    parser.add_argument("--steps", type=int, default=50)
+    parser.add_argument("--warmup", type=int, default=5)
+    parser.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    parser.add_argument("--no-secondary", action="store_true")
+    parser.add_argument("--e2e-steps", type=int, default=10)
+    args = parser.parse_args()
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        reference_arm(args, rank, world)
+        return
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=device)
+    import wpt_b200
+    from wpt_b200 import build, ops
+    if rank == 0 or not os.path.exists(os.path.join(ROOT, "wpt_b200", "libwpt_b200.so")):
+        build.build()
+    if world > 1:
+        dist.barrier()
+    pk, pk_kind = peaks()
+    torch.set_grad_enabled(False)
+    q, entries, positions, sink = config2_inputs(device, rank)
+    causal_flop, window_flop = config2_flops()
+    step_flop = causal_flop + window_flop
+    for _ in range(args.warmup):
+        prefill_step(wpt_b200, q, entries, positions, sink)
+    torch.cuda.synchronize()
+    if wpt_b200.device_status() != 0:
+        raise RuntimeError("kernel status error during warm-up")
+    stream = torch.cuda.current_stream()
+    marks = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    clocks = Clocks(local)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    clocks.start()
+    launches0 = ops.LAUNCHES[0]
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record(stream)
+    C = C2
+    k, v = entries[..., :C], entries[..., C:]
+    empty = torch.empty(B2, T2, 0, dtype=torch.int64, device=device)
+    for i in range(args.steps):
+        marks[i][0].record(stream)
+        wpt_b200.exact_attention(q, k, v, positions, C ** -0.5, 0, W2)  # the dominant kernel: causal prefill
+        marks[i][1].record(stream)
+        wpt_b200.sparse_attention(q, k, v, sink, empty, positions, C ** -0.5, W2)
+    stop.record(stream)
+    torch.cuda.synchronize()
+    launches = ops.LAUNCHES[0] - launches0
+    if world > 1:
+        dist.barrier()
+    clock = clocks.stop()
+    ms = start.elapsed_time(stop)
+    causal_ms = sum(a.elapsed_time(b) for a, b in marks) / args.steps
+    if world > 1:
+        t = torch.tensor([ms], device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t)
+    ms_step = ms / args.steps
+    value = step_flop * world / (ms_step * 1e-3) / 1e12
+    achieved = causal_flop / (causal_ms * 1e-3) / 1e12
+    status = wpt_b200.device_status()
+
+    # end to end through the public API: pinned host inputs in, outputs back, every step
+    q_h = q.cpu().pin_memory()
+    e_h = entries.cpu().pin_memory()
+    p_h = positions.cpu().pin_memory()
+    s_h = sink.cpu().pin_memory()
+    o1_h = torch.empty(q.shape, dtype=q.dtype).pin_memory()
+    o2_h = torch.empty(q.shape, dtype=q.dtype).pin_memory()
+    q_d, e_d, p_d, s_d = torch.empty_like(q), torch.empty_like(entries), torch.empty_like(positions), torch.empty_like(sink)
+
+    def e2e_step():
+        q_d.copy_(q_h, non_blocking=True)
+        e_d.copy_(e_h, non_blocking=True)
+        p_d.copy_(p_h, non_blocking=True)
+        s_d.copy_(s_h, non_blocking=True)
+        a, b = prefill_step(wpt_b200, q_d, e_d, p_d, s_d)
+        o1_h.copy_(a, non_blocking=True)
+        o2_h.copy_(b, non_blocking=True)
+    if world > 1:
+        dist.barrier()
+    e2e_ms = timed(e2e_step, args.e2e_steps, 2, stream)
+    if world > 1:
+        t = torch.tensor([e2e_ms], device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_ms = float(t)
+    h2d = q.numel() * 2 + entries.numel() * 2 + positions.numel() * 8 + sink.numel() * 4
+    d2h = 2 * q.numel() * 2
+    e2e_value = step_flop * world / (e2e_ms * 1e-3) / 1e12
+
+    extra = {} if args.no_secondary else secondary(wpt_b200, ops, device, rank, world, pk["hbm_gbs"])
+    status |= wpt_b200.device_status()
+    cpu = None
+    if rank == 0 and world == 1:
+        tf, rows, secs = cpu_rows(seconds=10.0)
+        cpu = {"value": round(tf, 4), "unit": "TFLOP/s", "cores": os.cpu_count(), "kind": "port",
+               "sample": f"{rows} batch row(s) of config 2 (causal + window passes), float32 BLAS, {secs:.1f} s"}
+    if rank == 0:
+        peak = pk["bf16_tflops_sustained"]
+        line = {
+            "metric": METRIC, "value": round(value, 2), "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms_step, 4), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded N(0,1)*0.5, config 2 shapes)",
+            "config": {"workload": "config 2 prefill: B=8 per GPU, T=4096, 16q/1kv heads, c=128; causal pass + "
+                                   "window-1024 pass with sink", "global_batch": B2 * world, "seq_len": T2,
+                       "parallelism": f"batch-sharded x{world} (weak)",
+                       "l2": "inputs larger than L2 (q 134 MB + kv 17 MB + outputs 268 MB per step)"},
+            "e2e": {"value": round(e2e_value, 2), "unit": "TFLOP/s", "h2d_bytes_per_step": int(h2d),
+                    "d2h_bytes_per_step": int(d2h), "ms_per_step": round(e2e_ms, 3)},
+            "gpu_launches": int(launches),
+            "roofline": {"bound": "tensor", "kernel": "prefill_kernel (causal pass)", "achieved": round(achieved, 2),
+                         "peak": peak, "peak_kind": f"bf16_tflops_sustained of {pk_kind}", "unit": "TFLOP/s",
+                         "frac": round(achieved / peak, 4), "ms_per_launch": round(causal_ms, 4),
+                         "algorithmic_flops_per_launch": causal_flop,
+                         "traffic": None},
+            "clocks": clock,
+            "status": status,
+        }
+        if cpu is not None:
+            line["cpu_baseline"] = cpu
+        if extra:
+            line["secondary"] = extra
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

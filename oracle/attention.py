@@ -90,6 +90,48 @@ def exact_attention(q, k, v, positions, scale, top_k, window, dtype=np.float64):
     return out, lse, chosen
 
 
+def range_attention(q, k, v, positions, scale, window=0, sink=None, dtype=np.float64):
+    """Attention over contiguous rows, the exact path (pytorch_kernels.py
+    :98-121, no choice) and the window path (sparse_attention with no chosen
+    rows, :171-187 over the rows of :149-153) in one: query at position p
+    reads rows max(0, p - window + 1) .. min(p, N - 1) (every row up to p when
+    window is 0), sink (H,) or None in each head's denominator. Blocks of
+    queries go through matrix products (BLAS), so this is also the timed CPU
+    baseline. Returns (out, lse)."""
+    q = np.asarray(q, dtype)
+    k = np.asarray(k, dtype)
+    v = np.asarray(v, dtype)
+    positions = np.asarray(positions, np.int64)
+    B, T, H, c = q.shape
+    N = k.shape[1]
+    out = np.empty((B, T, H, c), dtype)
+    lse = np.empty((B, T, H), dtype)
+    step = max(1, (1 << 22) // max(1, H * (window if window else N)))
+    for b in range(B):
+        for t0 in range(0, T, step):
+            part = slice(t0, min(T, t0 + step))
+            p = positions[b, part]
+            hi = np.minimum(p, N - 1)
+            lo = np.maximum(p - window + 1, 0) if window else np.zeros_like(p)
+            a, e = int(lo.min()), int(hi.max()) + 1
+            R = len(p)
+            if e <= a:
+                out[b, part] = 0
+                lse[b, part] = -np.inf if sink is None else np.asarray(sink, dtype)[None, :]
+                continue
+            rows = np.arange(a, e)
+            z = (q[b, part].reshape(R * H, c) @ k[b, a:e].T).reshape(R, H, e - a) * dtype(scale)
+            seen = (rows[None, :] >= lo[:, None]) & (rows[None, :] <= hi[:, None])
+            z = np.where(seen[:, None, :], z, NEG_INF)
+            l = _logsumexp(z)
+            if sink is not None:
+                l = np.logaddexp(l, np.asarray(sink, dtype)[None, :])
+            lse[b, part] = l
+            w = np.exp(z - l[..., None])
+            out[b, part] = (w.reshape(R * H, e - a) @ v[b, a:e]).reshape(R, H, c)
+    return out, lse
+
+
 def window_rows(positions, window, N):
     """pytorch_kernels.py:149-153: (B, T, window) each query's last window
     rows, -1 before the text and past the table."""

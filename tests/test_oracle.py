@@ -132,3 +132,18 @@ def test_greedy_accept_is_argmax_agreement():
     tokens, accepted = oa.accept(scores, drafted, q, rng.random((R, n)), rng.random(R), 1.0, 1)
     assert accepted.tolist() == [n, 2, n, n]
     assert tokens[1, 2] == scores[1, 2].argmax()
+
+
+def test_range_attention_equals_exact_and_sparse_window():
+    # the BLAS range path (the timed CPU baseline) against the two pinned restatements
+    rng = np.random.default_rng(2)
+    B, T, H, c, N = 2, 90, 3, 16, 130
+    q, k, v = rng.normal(size=(B, T, H, c)), rng.normal(size=(B, N, c)), rng.normal(size=(B, N, c))
+    sink = rng.normal(size=H)
+    positions = np.stack([N - T + np.arange(T), 7 + np.arange(T)])
+    out, lse = oat.range_attention(q, k, v, positions, 0.3)
+    ref_out, ref_lse, _ = oat.exact_attention(q, k, v, positions, 0.3, 0, 0)
+    assert np.abs(out - ref_out).max() < 1e-10 and np.abs(lse - ref_lse).max() < 1e-10
+    out, lse = oat.range_attention(q, k, v, positions, 0.3, window=17, sink=sink)
+    ref_out, ref_lse = oat.sparse_attention(q, k, v, sink, np.zeros((B, T, 0), np.int64), positions, 0.3, 17)
+    assert np.abs(out - ref_out).max() < 1e-10 and np.abs(lse - ref_lse).max() < 1e-10

@@ -17,6 +17,7 @@ import torch
 from . import _lib
 
 SM_COUNT = 148
+LAUNCHES = [0]  # kernels this module has launched (read by bench.py around its timed region)
 
 
 def _need_cuda(*tensors):
@@ -83,6 +84,7 @@ def prefill_forward(q, k, v, positions, scale, window=0, floor=None, tree_bits=N
         _lib.ptr(positions), _lib.ptr(floor), _lib.ptr(tree_bits), _lib.ptr(tree_base), _lib.ptr(sink),
         _lib.ptr(out), _lib.ptr(lse), _lib.ptr(part_o), _lib.ptr(part_lse), int(splits),
         B, T, H, C, N, int(window), float(scale), _lib.stream(q.device)))
+    LAUNCHES[0] += 1 + (splits > 1)
     return out, lse
 
 
@@ -140,6 +142,7 @@ def stream_forward(q, k, v, positions, scale, window=0, floor=None, idx=None, si
         _lib.ptr(positions), _lib.ptr(floor), _lib.ptr(idx), K, _lib.ptr(sink), _lib.ptr(out), _lib.ptr(lse),
         _lib.ptr(part_o), _lib.ptr(part_lse), splits, chunk_tiles, B, T, H, C, N, int(window), float(scale),
         _lib.stream(q.device)))
+    LAUNCHES[0] += 1 + (splits > 1)
     return out, lse
 
 
@@ -171,6 +174,7 @@ def select_rows(q, k, positions, lse, scale, K, window):
     _lib.check(_lib.lib().wpt_attn_topk(
         _lib.ptr(q), _lib.ptr(k), k.stride(0), k.stride(1), _lib.ptr(positions), _lib.ptr(lse), _lib.ptr(scores),
         ld, _lib.ptr(chosen), int(K), B, T, H, C, N, int(window), float(scale), _lib.stream(q.device)))
+    LAUNCHES[0] += 2
     return chosen
 
 
@@ -186,6 +190,7 @@ def merge_partials(part_o, part_lse, H, sink=None, out=None, lse=None):
     lse = torch.empty(rows, dtype=torch.float32, device=part_o.device) if lse is None else lse
     _lib.check(_lib.lib().wpt_attn_merge(_lib.ptr(part_o), _lib.ptr(part_lse), S, rows, rows, H, C, _lib.ptr(sink),
                                          _lib.ptr(out), _lib.ptr(lse), _lib.stream(part_o.device)))
+    LAUNCHES[0] += 1
     return out, lse
 
 
@@ -234,4 +239,5 @@ def accept(scores, drafted, q, uniforms, resample, temperature=1.0, top_k=None, 
         _lib.ptr(scores), _lib.ptr(drafted), _lib.ptr(q), _lib.ptr(uniforms), _lib.ptr(resample), _lib.ptr(lengths),
         _lib.ptr(stats), _lib.ptr(tokens), _lib.ptr(accepted), R, n, V, float(temperature),
         0 if top_k is None else int(top_k), _lib.stream(scores.device)))
+    LAUNCHES[0] += 2
     return tokens, accepted
