@@ -117,6 +117,29 @@ int wpt_attn_topk(const void* q, const void* k, int64_t k_stride_b, int64_t k_st
                   int C, int N, int window, float scale, void* stream);
 
 /*
+ * wpt_attn_decode without caller scratch: the same computation and
+ * arguments, but the split partials go to a static 8 MiB device array the
+ * library holds on every GPU that loads it, so the call allocates nothing.
+ * No counterpart in the reference. It serves callers that cannot allocate
+ * device memory per call: a decode loop captured in a CUDA graph (a
+ * cudaMalloc cannot be captured), a host behind an FFI (Go, Java, Rust) with
+ * no caching allocator, where a cudaFree per step would synchronise the
+ * device, or a serving process that must not grow its footprint mid-run.
+ * Limit: splits * B * T * H * (C + 1) floats must fit in 2^21 (8 MiB);
+ * larger calls return WPT_ERR_UNSUPPORTED and launch nothing. The first call
+ * on a device looks up the array's device address (cudaGetSymbolAddress);
+ * make that first call before any stream capture. Every call shares the
+ * array: calls that overlap on the GPU (other streams, other threads) race
+ * on it, so serialise them. Nothing in the array needs to start at zero:
+ * each call writes every partial its merge reads.
+ */
+int wpt_attn_decode_noalloc(const void* q, const void* k, const void* v, int64_t k_stride_b, int64_t k_stride_n,
+                            int64_t v_stride_b, int64_t v_stride_n, const int64_t* positions,
+                            const int64_t* floor_rows, const int64_t* idx, int K, const float* sink, void* out,
+                            float* lse, int splits, int chunk_tiles, int B, int T, int H, int C, int N, int window,
+                            float scale, void* stream);
+
+/*
  * Merge of split-KV partial results (o normalised per split, fp32; lse per
  * split, natural log, -inf for none) into out (bf16) and lse, adding the
  * sink. part_o (splits, rows, C) at split stride split_stride rows;

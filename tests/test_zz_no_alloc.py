@@ -1,0 +1,78 @@
+"""wpt_attn_decode_noalloc, the decode entry point that allocates nothing:
+its split partials live in the library's static device array instead of
+caller buffers. It is for callers that cannot allocate device memory on
+the hot path (a decode step captured in a CUDA graph, an FFI host without a
+caching allocator, a serving loop that must not synchronise on cudaFree).
+
+Called through the C ABI, twice in a row with different inputs, its output
+must match wpt_attn_decode's (given torch-allocated scratch) within the
+tolerances of the other GPU tests; an oversized call must be refused before
+anything launches. This file is collected last so that a run stopping at
+its first failure has already run every other test; it also passes alone
+in a fresh process."""
+
+import ctypes
+
+import numpy as np
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+OUT_TOL, LSE_TOL = 2e-2, 1e-3
+
+
+@pytest.fixture(scope="module")
+def lib():
+    from wpt_b200 import _lib, build
+    build.build()
+    return _lib
+
+
+def _case(seed, B=6, H=32, C=128, N=5000):
+    g = torch.Generator().manual_seed(seed)
+    q = (torch.randn(B, 1, H, C, generator=g) * 0.5).bfloat16().cuda()
+    e = (torch.randn(B, N, 2 * C, generator=g) * 0.5).bfloat16().cuda()
+    lengths = torch.randint(1, N + 1, (B,), generator=g)
+    positions = (lengths - 1)[:, None].contiguous().cuda()
+    sink = (torch.randn(H, generator=g) * 0.5).cuda()
+    return q, e, positions, sink
+
+
+def _decode(L, q, e, positions, sink, splits, chunk, noalloc):
+    B, T, H, C = q.shape
+    N = e.shape[1]
+    k, v = e[..., :C], e[..., C:]
+    out = torch.empty_like(q)
+    lse = torch.empty(B, T, H, dtype=torch.float32, device=q.device)
+    common = (L.ptr(q), L.ptr(k), L.ptr(v), k.stride(0), k.stride(1), v.stride(0), v.stride(1), L.ptr(positions),
+              None, None, 0, L.ptr(sink), L.ptr(out), L.ptr(lse))
+    tail = (splits, chunk, B, T, H, C, N, 0, C ** -0.5, L.stream(q.device))
+    if noalloc:
+        rc = L.lib().wpt_attn_decode_noalloc(*common, *tail)
+    else:
+        part_o = torch.empty(splits, B * T * H, C, dtype=torch.float32, device=q.device)
+        part_lse = torch.empty(splits, B * T * H, dtype=torch.float32, device=q.device)
+        rc = L.lib().wpt_attn_decode(*common, L.ptr(part_o), L.ptr(part_lse), *tail)
+    L.check(rc)
+    torch.cuda.synchronize()
+    return out, lse
+
+
+def test_noalloc_decode_matches_the_allocating_entry_point_twice(lib):
+    splits, chunk = 5, 8  # 5 x 8 x 128 = 5120 rows per query, more than N
+    for seed in (1, 2):  # two calls in a row share (and overwrite) the static scratch
+        q, e, positions, sink = _case(seed)
+        want, want_lse = _decode(lib, q, e, positions, sink, splits, chunk, noalloc=False)
+        got, got_lse = _decode(lib, q, e, positions, sink, splits, chunk, noalloc=True)
+        assert np.isfinite(got.float().cpu().numpy()).all()
+        assert (got.float() - want.float()).abs().max().item() < OUT_TOL
+        assert (got_lse - want_lse).abs().max().item() < LSE_TOL
+    assert lib.device_status() == 0
+
+
+def test_noalloc_decode_refuses_more_than_its_scratch(lib):
+    # 64 rows x 32 heads x 129 floats per split: 1024 splits need far more than 8 MiB
+    q, e, positions, sink = _case(3, B=64, N=1000)
+    with pytest.raises(NotImplementedError, match="static scratch"):
+        _decode(lib, q, e, positions, sink, 1024, 1, noalloc=True)

@@ -3,6 +3,7 @@
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
+#include <mutex>
 #include <string>
 
 #include "../../include/wpt_attn.h"
@@ -426,4 +427,62 @@ extern "C" int wpt_accept(const float* scores, const int64_t* drafted, const flo
   e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "accept_draw_kernel launch");
   return WPT_OK;
+}
+
+// ---------------------------------------------------------------- no-alloc
+// Scratch of wpt_attn_decode_noalloc: the per-split partial outputs and
+// log-sum-exps live in this file-scope device array instead of buffers the
+// caller allocates. Every GPU that loads the library holds these 8 MiB
+// until the process exits. In host code the array's name is only a
+// host-side stand-in: its device address comes from cudaGetSymbolAddress,
+// once per device, with that device current.
+constexpr size_t WPT_NOALLOC_SCRATCH_FLOATS = size_t(1) << 21;  // 8 MiB of fp32
+static __device__ __align__(256) float g_noalloc_scratch[WPT_NOALLOC_SCRATCH_FLOATS];
+
+namespace {
+
+int noalloc_scratch(float** out) {
+  static std::mutex lock;
+  static float* cached[64] = {};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  if (dev < 0 || dev >= 64) return fail(WPT_ERR_INVALID, "device %d out of range", dev);
+  std::lock_guard<std::mutex> guard(lock);
+  if (cached[dev] == nullptr) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(no-alloc scratch)");
+    cached[dev] = static_cast<float*>(p);
+  }
+  *out = cached[dev];
+  return WPT_OK;
+}
+
+}  // namespace
+
+extern "C" int wpt_attn_decode_noalloc(const void* q, const void* k, const void* v, int64_t k_stride_b,
+                                       int64_t k_stride_n, int64_t v_stride_b, int64_t v_stride_n,
+                                       const int64_t* positions, const int64_t* floor_rows, const int64_t* idx,
+                                       int K, const float* sink, void* out, float* lse, int splits, int chunk_tiles,
+                                       int B, int T, int H, int C, int N, int window, float scale, void* stream) {
+  float* part_o = nullptr;
+  float* part_lse = nullptr;
+  if (splits > 1) {
+    if (B < 1 || T < 1 || H < 1 || C < 1) return fail(WPT_ERR_INVALID, "empty shape B=%d T=%d H=%d C=%d", B, T, H, C);
+    const int64_t rows = static_cast<int64_t>(B) * T * H;
+    const int64_t need = static_cast<int64_t>(splits) * rows * (C + 1);
+    if (need > static_cast<int64_t>(WPT_NOALLOC_SCRATCH_FLOATS))
+      return fail(WPT_ERR_UNSUPPORTED,
+                  "no-alloc decode: %d splits x %lld rows x (%d + 1) floats = %lld floats exceed the %lld-float "
+                  "(8 MiB) static scratch; use fewer splits or rows, or wpt_attn_decode with caller buffers",
+                  splits, static_cast<long long>(rows), C, static_cast<long long>(need),
+                  static_cast<long long>(WPT_NOALLOC_SCRATCH_FLOATS));
+    float* scratch = nullptr;
+    if (int rc = noalloc_scratch(&scratch)) return rc;
+    part_o = scratch;                                   // (splits, rows, C), 256-byte aligned
+    part_lse = scratch + static_cast<int64_t>(splits) * rows * C;  // (splits, rows)
+  }
+  return wpt_attn_decode(q, k, v, k_stride_b, k_stride_n, v_stride_b, v_stride_n, positions, floor_rows, idx, K, sink,
+                         out, lse, part_o, part_lse, splits, chunk_tiles, B, T, H, C, N, window, scale, stream);
 }
