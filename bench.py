@@ -285,6 +285,46 @@ def reference_arm(args, rank, world):
     print(json.dumps(line), flush=True)
 
 
+# --------------------------------------------------------- profile cases
+
+def profile_case(args):
+    """--case NAME: only one kernel, on a bounded case, `--warmup` then
+    `--steps` launches: the command profiles/ summaries are captured with
+    (ncu needs small, self-contained runs)."""
+    torch.cuda.set_device(0)
+    device = torch.device("cuda", 0)
+    import wpt_b200
+    from wpt_b200 import build, ops
+    build.build()
+    torch.set_grad_enabled(False)
+    B = args.case_batch
+    C = 128
+    if args.case == "prefill":  # config 2's causal pass on B rows
+        q, entries, positions, sink = config2_inputs(device, 0)
+        q, entries, positions = q[:B].contiguous(), entries[:B].contiguous(), positions[:B].contiguous()
+        fn = lambda: ops.prefill_forward(q, entries[..., :C], entries[..., C:], positions, C ** -0.5)  # noqa: E731
+    elif args.case == "window":  # config 2's window pass on B rows
+        q, entries, positions, sink = config2_inputs(device, 0)
+        q, entries, positions = q[:B].contiguous(), entries[:B].contiguous(), positions[:B].contiguous()
+        fn = lambda: ops.prefill_forward(q, entries[..., :C], entries[..., C:], positions, C ** -0.5,  # noqa: E731
+                                         window=W2, sink=sink)
+    elif args.case == "decode":  # config 3's global rows, the first B of them
+        L = config3_lengths()[:B]
+        g = torch.Generator(device=device).manual_seed(10)
+        table = (torch.randn(B, 32768, 2 * C, generator=g, device=device) * 0.5).bfloat16()
+        q = (torch.randn(B, 1, 32, C, generator=g, device=device) * 0.5).bfloat16()
+        pos = (L - 1).to(device)[:, None].contiguous()
+        fn = lambda: ops.stream_forward(q, table[..., :C], table[..., C:], pos, C ** -0.5)  # noqa: E731
+    else:
+        raise SystemExit(f"unknown case {args.case}")
+    for _ in range(args.warmup):
+        fn()
+    torch.cuda.synchronize()
+    ms = timed(fn, args.steps, 0)
+    print(json.dumps({"case": args.case, "batch": B, "ms_per_call": round(ms, 4),
+                      "status": wpt_b200.device_status()}), flush=True)
+
+
 # ------------------------------------------------------------------- main
 
 def main():
@@ -295,7 +335,12 @@ def main():
     parser.add_argument("--impl", default="b200", choices=["b200", "reference"])
     parser.add_argument("--no-secondary", action="store_true")
     parser.add_argument("--e2e-steps", type=int, default=10)
+    parser.add_argument("--case", default=None, help="profile one kernel: prefill, window or decode")
+    parser.add_argument("--case-batch", type=int, default=4)
     args = parser.parse_args()
+    if args.case:
+        profile_case(args)
+        return
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))

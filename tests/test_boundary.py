@@ -1,0 +1,105 @@
+"""The drop-in boundary without a GPU: the C-ABI library builds, loads and
+exports every function include/wpt_attn.h declares, the ctypes table
+declares the same set, and the host-side logic of the kernel-form module
+(column counts, tree masks, kernel choice, refusal of CPU tensors) follows
+the reference's contract (pytorch_kernels.py:18-26,73-77)."""
+
+import ctypes
+import os
+import re
+
+import pytest
+import torch
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def _declared():
+    text = open(os.path.join(ROOT, "include", "wpt_attn.h")).read()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(wpt_\w+)\s*\(", text)))
+
+
+@pytest.fixture(scope="module")
+def library():
+    from wpt_b200 import build
+    build.build()
+    return ctypes.CDLL(build.TARGET)
+
+
+def test_library_exports_every_declared_symbol(library):
+    names = _declared()
+    assert "wpt_attn_prefill" in names and "wpt_accept" in names
+    for name in names:
+        assert hasattr(library, name), name
+
+
+def test_ctypes_table_matches_the_header():
+    from wpt_b200 import _lib
+    assert sorted(_lib.SIGNATURES) == _declared()
+
+
+def test_last_error_is_callable_without_a_gpu(library):
+    library.wpt_last_error.restype = ctypes.c_char_p
+    assert isinstance(library.wpt_last_error(), bytes)
+
+
+def test_invalid_shapes_are_refused_before_any_launch(library):
+    # argument checks run on the host: an unsupported head width is WPT_ERR_UNSUPPORTED (2)
+    from wpt_b200 import _lib
+    lib = _lib.lib()
+    rc = lib.wpt_attn_prefill(None, None, None, 0, 0, 0, 0, None, None, None, None, None, None, None, None, None, 1,
+                              1, 1, 1, 96, 1, 0, 1.0, None)
+    assert rc == _lib.ERR_UNSUPPORTED
+    with pytest.raises(NotImplementedError, match="head width 96"):
+        _lib.check(rc)
+
+
+def test_chosen_columns_follows_the_reference():
+    import wpt_b200
+    assert wpt_b200.chosen_columns(1024, 128, 100) == 0
+    assert wpt_b200.chosen_columns(1024, 128, 500) == 372
+    assert wpt_b200.chosen_columns(1024, 128, 5000) == 1024
+
+
+def test_tree_bits_from_parents():
+    from wpt_b200 import ops
+    bits = ops.tree_bits_from_parents(torch.tensor([-1, 0, 0, 1, 1, 2, 4]))
+    assert bits.tolist() == [0b1, 0b11, 0b101, 0b1011, 0b10011, 0b100101, 0b1010011]
+    chain = ops.tree_bits_from_parents(torch.arange(64) - 1)
+    assert chain[0].item() == 1 and chain[-1].item() == -1  # all 64 bits, as a signed int64
+    with pytest.raises(ValueError):
+        ops.tree_bits_from_parents(torch.tensor([-1, 2, 0]))
+    with pytest.raises(NotImplementedError):
+        ops.tree_bits_from_parents(torch.arange(65) - 1)
+
+
+def test_kernel_choice_by_shape():
+    from wpt_b200 import ops
+    assert ops.uses_stream(1, 32, 128) and ops.uses_stream(2, 32, 128) and ops.uses_stream(4, 16, 128)
+    assert not ops.uses_stream(3, 32, 128)  # 96 columns: the prefill kernel
+    assert not ops.uses_stream(1, 32, 64)   # head width 64: the prefill kernel
+    assert ops._stream_shape(1, 32, False) == (32, 1)
+    assert ops._stream_shape(3, 12, False) == (64, 5)
+    assert ops._stream_shape(7, 12, True) == (16, 1)
+
+
+def test_cpu_tensors_are_refused_not_computed():
+    import wpt_b200
+    q = torch.zeros(1, 4, 2, 128, dtype=torch.bfloat16)
+    k = torch.zeros(1, 4, 128, dtype=torch.bfloat16)
+    with pytest.raises(ValueError, match="CUDA device only"):
+        wpt_b200.exact_attention(q, k, k, torch.arange(4), 0.1, 0, 2)
+
+
+def test_module_has_the_reference_contract():
+    import inspect
+
+    import wpt_b200
+    assert isinstance(wpt_b200.NAME, str)
+    assert list(inspect.signature(wpt_b200.exact_attention).parameters) == [
+        "q", "k", "v", "positions", "scale", "top_k", "window"]
+    assert list(inspect.signature(wpt_b200.sparse_attention).parameters) == [
+        "q", "k", "v", "sink", "idx", "positions", "scale", "window"]
+    assert list(inspect.signature(wpt_b200.window_attention).parameters)[:6] == [
+        "q", "k", "v", "sink", "positions", "scale"]
