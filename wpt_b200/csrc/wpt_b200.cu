@@ -2,6 +2,7 @@
 // this file) and the extern "C" launchers declared in include/wpt_attn.h.
 #include <cstdarg>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 #include <string>
@@ -104,19 +105,43 @@ int allow_smem(Kernel kernel, int bytes) {
   return WPT_OK;
 }
 
-template <int C>
-int launch_prefill(const wpt::PrefillParams& p, const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
-                   cudaStream_t stream) {
-  constexpr int STAGES = 2;
-  using L = wpt::PrefillLayout<C, STAGES>;
+template <int C, int SLICES>
+int launch_prefill_s(const wpt::PrefillParams& p, const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
+                     cudaStream_t stream) {
+  constexpr int QB = 2, KST = 2, VST = 2;
+  using L = wpt::PrefillLayout<C, QB, KST, VST, SLICES>;
   static_assert(L::BYTES <= 232448, "prefill kernel shared memory exceeds 227 KB");
-  auto kernel = wpt::prefill_kernel<C, STAGES>;
+  auto kernel = wpt::prefill_kernel<C, QB, KST, VST, SLICES>;
   if (int rc = allow_smem(kernel, L::BYTES)) return rc;
-  dim3 grid((p.T + p.TQ - 1) / p.TQ, p.B, p.splits);
-  kernel<<<grid, 192, L::BYTES, stream>>>(tq, tk, tv, p);
+  int sms = 148;
+  int dev = 0;
+  if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int grid = p.items < sms ? p.items : sms;  // persistent: one CTA per SM walks the items
+  kernel<<<grid, L::THREADS, L::BYTES, stream>>>(tq, tk, tv, p);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "prefill_kernel launch");
   return WPT_OK;
+}
+
+// Softmax warps per row quadrant (WPT_B200_SLICES = 1, 2 or 4 overrides the default).
+int prefill_slices() {
+  static int slices = 0;
+  if (slices == 0) {
+    const char* env = getenv("WPT_B200_SLICES");
+    const int v = env ? atoi(env) : 0;
+    slices = (v == 1 || v == 2 || v == 4) ? v : 2;
+  }
+  return slices;
+}
+
+template <int C>
+int launch_prefill(const wpt::PrefillParams& p, const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
+                   cudaStream_t stream) {
+  switch (prefill_slices()) {
+    case 1: return launch_prefill_s<C, 1>(p, tq, tk, tv, stream);
+    case 4: return launch_prefill_s<C, 4>(p, tq, tk, tv, stream);
+    default: return launch_prefill_s<C, 2>(p, tq, tk, tv, stream);
+  }
 }
 
 template <int NCOL, int STAGES, bool GATHER>
@@ -236,6 +261,11 @@ extern "C" int wpt_attn_prefill(const void* q, const void* k, const void* v, int
   p.window = window > 0 ? window : 0;
   p.TQ = 128 / H;
   p.splits = splits;
+  {
+    const int64_t items = static_cast<int64_t>((T + p.TQ - 1) / p.TQ) * B * splits;
+    if (items >= (int64_t(1) << 31)) return fail(WPT_ERR_UNSUPPORTED, "too many prefill work items");
+    p.items = static_cast<int>(items);
+  }
   p.scale_log2 = scale * wpt::LOG2E;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   int rc = C == 128 ? launch_prefill<128>(p, tq, tk, tv, s) : launch_prefill<64>(p, tq, tk, tv, s);
