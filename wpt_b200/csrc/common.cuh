@@ -86,6 +86,13 @@ __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, u
       "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y), "r"(z)
       : "memory");
 }
+// Brings a tile of a 2D tensor map into L2 (no shared memory, no barrier).
+__device__ __forceinline__ void tma_prefetch_l2_2d(const CUtensorMap* map, int x, int y) {
+  asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(x), "r"(y)
+               : "memory");
+}
 
 // ------------------------------------------------------ cp.async (16 bytes)
 __device__ __forceinline__ void cp_async_16(uint32_t dst, const void* src, bool fill) {
@@ -138,6 +145,30 @@ __device__ __forceinline__ void mma_ts(uint32_t d, uint32_t a, uint64_t b, uint3
       "r"(a), "l"(b), "r"(idesc), "r"(accumulate)
       : "memory");
 }
+// mma_ss / mma_ts with the descriptors given as a base plus a constant
+// offset (in descriptor units), added inside the statement so that a run of
+// issues keeps only the bases in registers.
+template <uint32_t OFF_A, uint32_t OFF_B>
+__device__ __forceinline__ void mma_ss_off(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t.reg .b64 da, db;\n\t"
+      "add.s64 da, %1, %5;\n\tadd.s64 db, %2, %6;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], da, db, %3, p;\n\t}\n" ::"r"(d),
+      "l"(a), "l"(b), "r"(idesc), "r"(accumulate), "n"(OFF_A), "n"(OFF_B)
+      : "memory");
+}
+template <uint32_t OFF_A, uint32_t OFF_B>
+__device__ __forceinline__ void mma_ts_off(uint32_t d, uint32_t a, uint64_t b, uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t.reg .b32 ta;\n\t.reg .b64 db;\n\t"
+      "add.u32 ta, %1, %5;\n\tadd.s64 db, %2, %6;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [ta], db, %3, p;\n\t}\n" ::"r"(d),
+      "r"(a), "l"(b), "r"(idesc), "r"(accumulate), "n"(OFF_A), "n"(OFF_B)
+      : "memory");
+}
+
 // Arrives on bar once every tcgen05 operation this thread issued before has completed.
 __device__ __forceinline__ void mma_commit(uint64_t* bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
@@ -255,6 +286,18 @@ __device__ __forceinline__ float fast_exp2(float x) {
   return y;
 }
 
+// Register limit of this warpgroup's threads (all its warps execute the
+// same instruction): dec returns registers to the block's pool, inc waits
+// until the pool has them.
+template <int N>
+__device__ __forceinline__ void setmaxnreg_dec() {
+  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;\n" ::"n"(N) : "memory");
+}
+template <int N>
+__device__ __forceinline__ void setmaxnreg_inc() {
+  asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;\n" ::"n"(N) : "memory");
+}
+
 // Named barrier over `count` threads (a multiple of 32) of this CTA.
 __device__ __forceinline__ void named_barrier(int id, int count) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
@@ -285,6 +328,55 @@ struct MaxOp {
 struct SumOp {
   __device__ __forceinline__ float operator()(float a, float b) const { return a + b; }
 };
+
+// ---------------------------------------------------- packed fp32 pairs
+__device__ __forceinline__ uint64_t f2_pack(float a, float b) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
+  return r;
+}
+__device__ __forceinline__ void f2_unpack(uint64_t v, float& a, float& b) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(v));
+}
+__device__ __forceinline__ uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+__device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+
+// 2^x for a pair of floats on the FMA pipe, leaving the exp unit (MUFU) to
+// other elements. Method: 2^x = 2^r * 2^f with r = round(x) and
+// f = x - r in [-1/2, 1/2]; r comes from adding 1.5 * 2^23, which leaves it
+// in the low mantissa bits, and 2^r is applied by adding r to the result's
+// exponent field (an integer multiply-add of those bits by 2^23). 2^f is a
+// cubic fitted by least squares for relative error on Chebyshev nodes of
+// [-1/2, 1/2] (fit made for this library): max relative error 7.8e-5 over
+// x in [-120, 20], far below the bf16 rounding (3.9e-3) the weights take
+// next. x is clamped at -127: there 2^f < 1 and the exponent sum goes
+// negative, which the final integer maximum turns into +0, so -inf (a
+// masked score) gives exactly 0; results below 2^-126 come out as 0 or a
+// denormal.
+__device__ __forceinline__ void exp2_poly_pair(float x0, float x1, float& y0, float& y1) {
+  constexpr float MAGIC = 12582912.0f;  // 1.5 * 2^23
+  const uint64_t x = f2_pack(fmaxf(x0, -127.f), fmaxf(x1, -127.f));
+  const uint64_t t = f2_add(x, f2_pack(MAGIC, MAGIC));
+  const uint64_t r = f2_add(t, f2_pack(-MAGIC, -MAGIC));
+  const uint64_t f = f2_fma(r, f2_pack(-1.f, -1.f), x);
+  uint64_t q = f2_fma(f2_pack(0.05508868396282196f, 0.05508868396282196f), f,
+                      f2_pack(0.24260404706001282f, 0.24260404706001282f));
+  q = f2_fma(q, f, f2_pack(0.6932762265205383f, 0.6932762265205383f));
+  q = f2_fma(q, f, f2_pack(0.9999289512634277f, 0.9999289512634277f));
+  float p0, p1, t0, t1;
+  f2_unpack(q, p0, p1);
+  f2_unpack(t, t0, t1);
+  y0 = __int_as_float(max(__float_as_int(p0) + __float_as_int(t0) * (1 << 23), 0));
+  y1 = __int_as_float(max(__float_as_int(p1) + __float_as_int(t1) * (1 << 23), 0));
+}
 
 constexpr float LOG2E = 1.4426950408889634f;
 constexpr float LN2 = 0.6931471805599453f;

@@ -6,50 +6,57 @@
 // queries per row, the window/sink form (pytorch_kernels.py:171-187 over a
 // contiguous window; attention.py:85-107) and tree-masked verification.
 //
-// Tiles. A work item is BM = 128 "rows": TQ = 128 / H consecutive query
+// Tiles. A query tile is BM = 128 "rows": TQ = 128 / H consecutive query
 // tokens of one batch row, each with its H heads (row r = token r / H, head
 // r % H). All heads of MQA read the same keys, so one K/V tile serves every
 // row, and the 128 rows are the M of both products:
 //   S  = Q K^T   M=128 rows, N=128 keys, K=C    A=Q (smem), B=K (smem)
 //   O += P V     M=128 rows, N=C,       K=128  A=P (TMEM),  B=V (smem, MN-major)
+// A work item is a pair of consecutive query tiles, A (tokens t0 ..) and B
+// (tokens t0 + TQ ..), of one batch row and key split: both read the same
+// key tiles, so each K and V tile is loaded once for 256 rows.
 //
-// Persistent schedule. One CTA per SM walks the work items (query tile,
-// batch row, key split) from the most expensive (the last query tiles) down,
-// item c, c + gridDim.x, ... The loader keeps prefetching across item
-// boundaries: Q has QB shared-memory buffers, and K and V stream through
-// separate rings (KST and VST stages) so a K stage is released as soon as
-// its S product completes and a V stage once its P V product does. TMEM
-// holds S twice (2 x 128 columns, one per key tile in flight) and O twice
-// (one per item in flight, 2 x C columns), so an item's epilogue overlaps
-// the next item's products. P (bf16) overwrites the first 64 columns of its
-// S buffer.
+// Warps. Softmax warpgroup A (warps 0-3) owns tile A, warpgroup B (warps
+// 4-7) tile B: warp w reads TMEM lane quadrant w % 4 and each thread owns
+// one row and all 128 keys of a key tile, so no thread exchanges anything
+// with another. Warp 8 issues the tcgen05 products (one lane), warp 9 runs
+// the TMA loads (one lane) and publishes each item's key-tile range to the
+// other warps through a small shared-memory ring.
 //
-// Warps: 4 x SLICES softmax warps, then the tcgen05 issuer (one lane) and the
-// TMA loader (one lane). Warp w reads TMEM lane quadrant w % 4 (rows
-// 32 (w % 4) ..), so SLICES warps share each quadrant: each thread owns one
-// row and a slice of 128 / SLICES of its keys. The slices of a row exchange
-// their maxima through shared memory once per tile and all take the same
-// lazy-maximum decision; each rescales and writes its slice of O.
+// Pipeline. TMEM holds S_A, S_B (128 columns each, P as bf16 pairs over the
+// first 64 columns of its S) and O_A, O_B (C columns each). Per key tile j
+// the issuer runs PV_A(j-1), S_A(j), PV_B(j-1), S_B(j): while warpgroup A
+// turns S_A(j) into P the tensor pipe works on B's products and the other
+// way round. tcgen05 products of one thread run in issue order, so S_A(j)
+// overwrites P_A(j-1) only after PV_A(j-1) has read it, and the commit that
+// says S_A(j) is ready also says PV_A(j-1) is done, which is what a rescale
+// of O_A needs. Q pairs have QB buffers; K and V tiles stream through one
+// ring of NS stages in the order K(0), V(0), K(1), V(1), ...
 //
 // Online softmax in base 2 with a lazy maximum: a row's running maximum is
 // only raised (and O rescaled) when a tile's maximum exceeds it by more
-// than 8, so P stays below 2^8 and O is rarely touched. The rescale waits
-// for the previous P V product to finish (o_done) and is done by every lane
-// of a warp when any lane needs it (tcgen05.ld/st are warp-collective).
+// than 8, so P stays below 2^8 and O is rarely touched. The rescale is done
+// by every lane of a warp when any lane needs it (tcgen05.ld/st are
+// warp-collective). P is handed to the issuer in two halves of 64 keys
+// (p_half, then p_ready), so the first half of P V runs while the second
+// half of P is computed. Exponentials: POLY8 of every 8 pairs of weights
+// are computed on the FMA pipe (exp2_poly_pair), the rest with ex2.approx,
+// so the two pipes share the work.
 //
 // Masks. Query t at position p (its own table row) reads rows lo..hi:
 //   hi = min(p, N - 1); lo = max(0, p - window + 1 when window > 0, floor[b,t]).
 // Tree mode adds: rows tree_base[b] + i (0 <= i < 64) are visible only when
 // bit i of tree_bits[b, t] is set (node t sees itself and its ancestors).
-// Key slices wholly inside a row's range skip the per-element mask.
+// Key tiles wholly inside a row's range skip the per-element mask.
 //
 // Split-KV: an item's key tiles may be split; with splits > 1 each split
 // writes its normalised partial output and LSE (no sink) for the merge
 // kernel, which adds the sink.
 //
 // Barrier phases run on across items: key tile g (counted over the CTA's
-// items) uses K stage g % KST, V stage g % VST and S buffer g % 2; the n-th
-// item with any key tile uses Q buffer n % QB and O buffer n % 2.
+// items) is ring entries 2g (K) and 2g + 1 (V); the n-th item with any key
+// tile uses Q buffer n % QB; the idx-th item of the CTA uses ring slot
+// idx % IR of the item ring.
 #pragma once
 
 #include <climits>
@@ -73,25 +80,30 @@ struct PrefillParams {
   float scale_log2;  // softmax scale * log2(e)
 };
 
-template <int C, int QB, int KST, int VST, int SLICES>
+template <int C, int QB, int NS>
 struct PrefillLayout {
   static constexpr int BM = 128, BN = 128;
-  static constexpr int SUB = C / 64;  // 64-element (128-byte) column chunks
-  static constexpr int Q_BYTES = BM * C * 2;
+  static constexpr int SUB = C / 64;           // 64-element (128-byte) column chunks
+  static constexpr int QT_BYTES = BM * C * 2;  // one query tile
+  static constexpr int Q_BYTES = 2 * QT_BYTES; // a pair
   static constexpr int KV_BYTES = BN * C * 2;  // one K or V tile
+  static constexpr int IR = 4;                 // item ring slots
   static constexpr int OFF_Q = 0;
-  static constexpr int OFF_K = QB * Q_BYTES;
-  static constexpr int OFF_V = OFF_K + KST * KV_BYTES;
-  static constexpr int OFF_BAR = OFF_V + VST * KV_BYTES;
-  // q_full[QB], q_empty[QB], k_full[KST], k_empty[KST], v_full[VST], v_empty[VST],
-  // s_full[2], p_ready[2], o_done, o_final[2], o_free[2]
-  static constexpr int NBAR = 2 * QB + 2 * KST + 2 * VST + 4 + 1 + 4;
-  // row maxima for two tiles, then row sums: (3, SLICES, 128) floats
-  static constexpr int OFF_RED = OFF_BAR + NBAR * 8;
-  static constexpr int OFF_MISC = OFF_RED + 3 * SLICES * 128 * 4;
+  static constexpr int OFF_KV = QB * Q_BYTES;
+  static constexpr int OFF_BAR = OFF_KV + NS * KV_BYTES;
+  // q_full[QB], q_empty[QB], kv_full[NS], kv_empty[NS], s_full[2], p_half[2],
+  // p_ready[2], o_final[2], o_free[2], item_full[IR], item_empty[IR]
+  static constexpr int NBAR = 2 * QB + 2 * NS + 10 + 2 * IR;
+  static constexpr int OFF_ITEM = OFF_BAR + NBAR * 8;  // IR x (first key tile, key tiles)
+  static constexpr int OFF_MISC = OFF_ITEM + IR * 8;
   static constexpr int BYTES = OFF_MISC + 16 + 1024;  // + slack to align the base to 1024
-  static constexpr int THREADS = 32 * (4 * SLICES + 2);
-  static constexpr int MMA_WARP = 4 * SLICES, LOAD_WARP = 4 * SLICES + 1;
+  // warpgroups 0 and 1: softmax; warpgroup 2: the issuer, the loader and two idle warps
+  static constexpr int THREADS = 384;
+  static constexpr int MMA_WARP = 8, LOAD_WARP = 9;
+  // registers per thread after setmaxnreg: 168 at launch (65536 / 384), then
+  // 128 x 56 + 256 x 224 = 384 x 168, the block's whole allocation
+  static constexpr int REGS_CONTROL = 56, REGS_SOFTMAX = 224;
+  static constexpr int ITEM_READERS = 9;  // the issuer warp and the 8 softmax warps
 };
 
 __device__ __forceinline__ void prefill_query_rows(const PrefillParams& p, int b, int t, int& lo, int& hi) {
@@ -107,26 +119,33 @@ __device__ __forceinline__ void prefill_query_rows(const PrefillParams& p, int b
   lo = low > INT_MAX ? INT_MAX : static_cast<int>(low);
 }
 
-// Work item k: the most expensive query tiles first, then batch row, then split.
+// Work item k: the most expensive query-tile pairs first, then batch row, then split.
 struct PrefillItem {
   int b, t0, split, tile0, ntiles;
 };
 
-// Called by all 32 lanes of a warp: lane i reads the positions of tokens
-// t0 + i, t0 + i + 32, ... and warp reductions give the item's key range,
-// one global-load round trip for the usual TQ <= 32.
-__device__ __forceinline__ PrefillItem prefill_item(const PrefillParams& p, int k) {
+__device__ __forceinline__ PrefillItem prefill_place(const PrefillParams& p, int k) {
   PrefillItem it;
-  const int lane = threadIdx.x & 31;
-  const int per_tile = p.B * p.splits;
-  const int nq = (p.T + p.TQ - 1) / p.TQ;
-  const int qtile = nq - 1 - k / per_tile;
-  const int rem = k - (k / per_tile) * per_tile;
+  const int per_pair = p.B * p.splits;
+  const int np = (p.T + 2 * p.TQ - 1) / (2 * p.TQ);
+  const int qpair = np - 1 - k / per_pair;
+  const int rem = k - (k / per_pair) * per_pair;
   it.b = rem / p.splits;
   it.split = rem - it.b * p.splits;
-  it.t0 = qtile * p.TQ;
+  it.t0 = qpair * 2 * p.TQ;
+  it.tile0 = 0;
+  it.ntiles = 0;
+  return it;
+}
+
+// The key tiles of item k. Called by all 32 lanes of a warp: lane i reads
+// the positions of tokens t0 + i, t0 + i + 32, ... and warp reductions give
+// the pair's key range.
+__device__ __forceinline__ PrefillItem prefill_item(const PrefillParams& p, int k) {
+  PrefillItem it = prefill_place(p, k);
+  const int lane = threadIdx.x & 31;
   int row_lo = INT_MAX, row_hi = -1;
-  const int tq_end = min(p.TQ, p.T - it.t0);
+  const int tq_end = min(2 * p.TQ, p.T - it.t0);
   for (int tq = lane; tq < tq_end; tq += 32) {
     int lo, hi;
     prefill_query_rows(p, it.b, it.t0 + tq, lo, hi);
@@ -137,8 +156,6 @@ __device__ __forceinline__ PrefillItem prefill_item(const PrefillParams& p, int 
   }
   row_lo = __reduce_min_sync(0xffffffffu, row_lo);
   row_hi = __reduce_max_sync(0xffffffffu, row_hi);
-  it.tile0 = 0;
-  it.ntiles = 0;
   if (row_hi >= row_lo) {
     const int first = row_lo / 128, last = row_hi / 128, total = last - first + 1;
     const int per = (total + p.splits - 1) / p.splits;
@@ -149,48 +166,163 @@ __device__ __forceinline__ PrefillItem prefill_item(const PrefillParams& p, int 
   return it;
 }
 
-// N consecutive TMEM columns of this warp's lanes into registers (one wait).
-template <int N>
-__device__ __forceinline__ void tmem_cols(uint32_t taddr, uint32_t (&r)[N]) {
-  if constexpr (N == 128) {
-    tmem_ld128(taddr, r);
-  } else if constexpr (N == 64) {
-    tmem_ld64(taddr, r);
-  } else if constexpr (N == 32) {
-    tmem_ld32(taddr, r);
-  } else {
-    static_assert(N == 16, "16, 32, 64 or 128 columns");
-    tmem_ld16(taddr, r);
+// Visibility of 32 consecutive tile columns (bit i: column c0 + i) for a
+// row that sees columns a..b (relative to c0) and, in a tree tile, only the
+// tree rows whose bits are set: sh is the tree-bit index of column c0.
+__device__ __forceinline__ uint32_t prefill_visible_word(int a, int b, bool in_tree, int sh, uint64_t tbits) {
+  const int lo = a < 0 ? 0 : (a > 32 ? 32 : a);
+  const int hi = b < -1 ? 0 : (b >= 31 ? 32 : b + 1);  // columns lo .. hi - 1
+  uint32_t m = hi <= lo ? 0u : ((hi == 32 ? 0xFFFFFFFFu : ((1u << hi) - 1u)) & ~((1u << lo) - 1u));
+  if (in_tree && sh > -32 && sh < 64) {
+    uint32_t t;  // tree bits of the columns inside the tree, ones outside it
+    if (sh >= 0) {
+      t = static_cast<uint32_t>(tbits >> sh);
+      if (sh > 32) t |= 0xFFFFFFFFu << (64 - sh);
+    } else {
+      t = (static_cast<uint32_t>(tbits) << -sh) | ((1u << -sh) - 1u);
+    }
+    m &= t;
+  }
+  return m;
+}
+
+__device__ __forceinline__ float max3f(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
+// Weights of 64 scores (one half of a row's key tile) as 32 bf16 pairs
+// against msub, their fp32 sum, and (rmax) the maximum of s * sl2 - msub
+// over them, found in the same pass.
+template <int POLY8>
+__device__ __forceinline__ float prefill_half_weights(const uint32_t (&r)[64], float sl2, float msub,
+                                                      uint32_t (&pk)[32], float& rmax) {
+  const uint64_t s2 = f2_pack(sl2, sl2), nm = f2_pack(-msub, -msub);
+  uint64_t acc[2] = {f2_pack(0.f, 0.f), f2_pack(0.f, 0.f)};
+  float m[2] = {-INFINITY, -INFINITY};
+#pragma unroll
+  for (int i = 0; i < 32; ++i) {
+    const uint64_t x = f2_fma(f2_pack(__uint_as_float(r[2 * i]), __uint_as_float(r[2 * i + 1])), s2, nm);
+    float x0, x1, e0, e1;
+    f2_unpack(x, x0, x1);
+    m[i & 1] = max3f(m[i & 1], x0, x1);
+    if ((i & 7) < POLY8) {
+      exp2_poly_pair(x0, x1, e0, e1);
+    } else {
+      e0 = fast_exp2(x0);
+      e1 = fast_exp2(x1);
+    }
+    pk[i] = pack_bf16(e0, e1);
+    acc[i & 1] = f2_add(acc[i & 1], f2_pack(e0, e1));
+  }
+  rmax = fmaxf(m[0], m[1]);
+  float a0, a1, b0, b1;
+  f2_unpack(acc[0], a0, a1);
+  f2_unpack(acc[1], b0, b1);
+  return (a0 + a1) + (b0 + b1);
+}
+
+// Maximum of 128 values: eight independent chains of three-input maxima.
+__device__ __forceinline__ float max128(const uint32_t (&r)[128]) {
+  float m[8];
+#pragma unroll
+  for (int c = 0; c < 8; ++c) m[c] = __uint_as_float(r[c]);
+#pragma unroll
+  for (int i = 8; i < 128; i += 16) {
+#pragma unroll
+    for (int c = 0; c < 8; ++c) m[c] = max3f(m[c], __uint_as_float(r[i + 2 * c]), __uint_as_float(r[i + 2 * c + 1]));
+  }
+  return max3f(max3f(m[0], m[1], m[2]), max3f(m[3], m[4], m[5]), fmaxf(m[6], m[7]));
+}
+
+// Multiplies this warp's rows of O (C TMEM columns from oAddr) by alpha.
+template <int C>
+__device__ __forceinline__ void prefill_rescale_o(uint32_t oAddr, float alpha) {
+#pragma unroll
+  for (int c = 0; c < C; c += 32) {
+    uint32_t o[32];
+    tmem_ld32(oAddr + c, o);
+#pragma unroll
+    for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+    tmem_st32(oAddr + c, o);
   }
 }
 
-template <int C, int QB, int KST, int VST, int SLICES>
-__global__ void __launch_bounds__(PrefillLayout<C, QB, KST, VST, SLICES>::THREADS, 1)
+// Sets the scores of the tile columns c0 .. c0 + 63 this row may not read
+// to -inf (a, b: the row's visible tile columns; tb: the tree's first tile
+// column).
+__device__ __forceinline__ void prefill_mask_half(uint32_t (&r)[64], int c0, int a, int b, bool in_tree, int tb,
+                                                  uint64_t tbits) {
+#pragma unroll
+  for (int wd = 0; wd < 2; ++wd) {
+    const int cw = c0 + 32 * wd;
+    const uint32_t vis = prefill_visible_word(a - cw, b - cw, in_tree, cw - tb, tbits);
+#pragma unroll
+    for (int i = 0; i < 32; ++i)
+      if (!((vis >> i) & 1u)) r[32 * wd + i] = __float_as_uint(-INFINITY);
+  }
+}
+
+// S_w = Q_w K^T for key tile gs into S buffer w (TMEM column 128 w), then
+// a commit on s_full[w]. qa: the Q pair's shared-memory address. One thread
+// issues back to back with the tensor pipe, so each descriptor is a base
+// plus a constant offset (addresses are in 16-byte units in the low 14
+// bits, and no shared-memory address carries out of them).
+template <int KK>
+__device__ __forceinline__ void prefill_s_steps(uint32_t d, uint64_t dq, uint64_t dk, uint32_t idesc) {
+  if constexpr (KK > 0) prefill_s_steps<KK - 1>(d, dq, dk, idesc);
+  constexpr uint32_t off = ((KK >> 2) * (128 * 128) + (KK & 3) * 32) >> 4;
+  mma_ss_off<off, off>(d, dq, dk, idesc, KK > 0 ? 1u : 0u);
+}
+template <int C, int NS, int QT_BYTES, int KV_BYTES>
+__device__ __forceinline__ void prefill_issue_s(uint32_t tmem, uint32_t qa, uint32_t kv_addr, int w, int gs,
+                                                uint64_t* s_full) {
+  const uint64_t dq = sdesc_sw128(qa + w * QT_BYTES, 16, 1024);
+  const uint64_t dk = sdesc_sw128(kv_addr + ((2 * gs) % NS) * KV_BYTES, 16, 1024);
+  prefill_s_steps<C / 16 - 1>(tmem + w * 128, dq, dk, idesc_bf16(128, 128, 0, 0));
+  mma_commit(s_full + w);
+}
+
+// O_w += P_w V for key tile gp over its keys 64 HALF .. 64 HALF + 63 (first:
+// O_w = P_w V). P_w is bf16 pairs over the first 64 columns of S buffer w;
+// V is MN-major in its ring stage.
+template <int KK, int KK0>
+__device__ __forceinline__ void prefill_pv_steps(uint32_t d, uint32_t a, uint64_t dv, uint32_t idesc, uint32_t acc0) {
+  if constexpr (KK > KK0) prefill_pv_steps<KK - 1, KK0>(d, a, dv, idesc, acc0);
+  constexpr uint32_t off = (KK * 16 * 128) >> 4;
+  mma_ts_off<KK * 8, off>(d, a, dv, idesc, KK > 0 ? 1u : acc0);
+}
+template <int C, int NS, int KV_BYTES, int HALF>
+__device__ __forceinline__ void prefill_issue_pv(uint32_t tmem, uint32_t kv_addr, int w, int gp, bool first) {
+  const uint64_t dv = sdesc_sw128(kv_addr + ((2 * gp + 1) % NS) * KV_BYTES, 128 * 128, 1024);
+  prefill_pv_steps<4 * HALF + 3, 4 * HALF>(tmem + 256 + w * C, tmem + w * 128, dv, idesc_bf16(128, C, 0, 1),
+                                           first ? 0u : 1u);
+}
+
+template <int C, int QB, int NS, int POLY8>
+__global__ void __launch_bounds__(PrefillLayout<C, QB, NS>::THREADS, 1)
     prefill_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                    const __grid_constant__ CUtensorMap tm_v, const PrefillParams p) {
-  using L = PrefillLayout<C, QB, KST, VST, SLICES>;
-  constexpr int BM = L::BM, BN = L::BN, SUB = L::SUB;
-  constexpr int KS = BN / SLICES;  // keys per softmax thread
-  constexpr int OS = C / SLICES;   // output columns per softmax thread
-  constexpr int NSOFT = 128 * SLICES;
+  using L = PrefillLayout<C, QB, NS>;
+  constexpr int BM = L::BM, BN = L::BN, SUB = L::SUB, IR = L::IR;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sQ = smem + L::OFF_Q;
-  uint8_t* sK = smem + L::OFF_K;
-  uint8_t* sV = smem + L::OFF_V;
+  uint8_t* sKV = smem + L::OFF_KV;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::OFF_BAR);
   uint64_t* q_full = bars;
   uint64_t* q_empty = q_full + QB;
-  uint64_t* k_full = q_empty + QB;
-  uint64_t* k_empty = k_full + KST;
-  uint64_t* v_full = k_empty + KST;
-  uint64_t* v_empty = v_full + VST;
-  uint64_t* s_full = v_empty + VST;
-  uint64_t* p_ready = s_full + 2;
-  uint64_t* o_done = p_ready + 2;  // one phase per P V product
-  uint64_t* o_final = o_done + 1;  // [O buffer]: one phase per item, after its last P V
-  uint64_t* o_free = o_final + 2;  // [O buffer]: the epilogue has read it
-  float* s_red = reinterpret_cast<float*>(smem + L::OFF_RED);
+  uint64_t* kv_full = q_empty + QB;
+  uint64_t* kv_empty = kv_full + NS;
+  uint64_t* s_full = kv_empty + NS;  // [warpgroup]: one phase per key tile
+  uint64_t* p_half = s_full + 2;     // [warpgroup]: the first 64 keys' P of the tile is in TMEM
+  uint64_t* p_ready = p_half + 2;    // [warpgroup]: all of the tile's P is in TMEM
+  uint64_t* o_final = p_ready + 2;   // [warpgroup]: one phase per item, after its last P V
+  uint64_t* o_free = o_final + 2;    // [warpgroup]: the epilogue has read O
+  uint64_t* item_full = o_free + 2;
+  uint64_t* item_empty = item_full + IR;
+  int2* s_items = reinterpret_cast<int2*>(smem + L::OFF_ITEM);
   uint32_t* s_tmem = reinterpret_cast<uint32_t*>(smem + L::OFF_MISC);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -200,21 +332,21 @@ __global__ void __launch_bounds__(PrefillLayout<C, QB, KST, VST, SLICES>::THREAD
       mbar_init(q_full + s, 1);
       mbar_init(q_empty + s, 1);
     }
+    for (int s = 0; s < NS; ++s) {
+      mbar_init(kv_full + s, 1);
+      mbar_init(kv_empty + s, 1);
+    }
     for (int s = 0; s < 2; ++s) {
       mbar_init(s_full + s, 1);
-      mbar_init(p_ready + s, NSOFT);
+      mbar_init(p_half + s, 128);
+      mbar_init(p_ready + s, 128);
       mbar_init(o_final + s, 1);
-      mbar_init(o_free + s, NSOFT);
+      mbar_init(o_free + s, 128);
     }
-    for (int s = 0; s < KST; ++s) {
-      mbar_init(k_full + s, 1);
-      mbar_init(k_empty + s, 1);
+    for (int s = 0; s < IR; ++s) {
+      mbar_init(item_full + s, 1);
+      mbar_init(item_empty + s, L::ITEM_READERS);
     }
-    for (int s = 0; s < VST; ++s) {
-      mbar_init(v_full + s, 1);
-      mbar_init(v_empty + s, 1);
-    }
-    mbar_init(o_done, 1);
     fence_mbar_init();
   }
   if (warp == L::MMA_WARP) {
@@ -229,112 +361,167 @@ __global__ void __launch_bounds__(PrefillLayout<C, QB, KST, VST, SLICES>::THREAD
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  const uint32_t tmem = *s_tmem;  // S buffers at columns 0 and 128, O buffers at 256 and 256 + C
+  const uint32_t tmem = *s_tmem;  // S_A at column 0, S_B at 128, O_A at 256, O_B at 256 + C
 
+  // Each role ends with its own __syncthreads (the CTA's last barrier), so
+  // no code runs under two different register limits.
+  if (warp >= 8) {
+  setmaxnreg_dec<L::REGS_CONTROL>();
   if (warp == L::LOAD_WARP) {
     // ------------------------------------------------------------ TMA loader
     bool ok = true;
-    int g = 0, n = 0;  // key tiles issued so far, items with key tiles so far
-    for (int k = blockIdx.x; ok && k < p.items; k += gridDim.x) {
+    int idx = 0, g = 0, n = 0;  // items seen, key tiles issued, items with key tiles
+    for (int k = blockIdx.x; ok && k < p.items; k += gridDim.x, ++idx) {
       const PrefillItem it = prefill_item(p, k);  // the whole warp
-      if (it.ntiles == 0) continue;
       if (lane == 0) {
-        const int qb = n % QB;
-        if (n >= QB) ok = mbar_wait(q_empty + qb, ((n / QB) & 1) ^ 1, p.status);
+        const int slot = idx % IR;
+        if (idx >= IR) ok = mbar_wait(item_empty + slot, ((idx / IR) & 1) ^ 1, p.status);
         if (ok) {
-          mbar_expect_tx(q_full + qb, L::Q_BYTES);
-          const int qrow0 = (it.b * p.T + it.t0) * p.H;
-          for (int s = 0; s < SUB; ++s)
-            tma_load_2d(sQ + qb * L::Q_BYTES + s * BM * 128, &tm_q, q_full + qb, s * 64, qrow0);
+          s_items[slot] = make_int2(it.tile0, it.ntiles);
+          mbar_arrive(item_full + slot);
         }
-        for (int j = 0; ok && j < it.ntiles; ++j) {
-          const int gg = g + j, n0 = (it.tile0 + j) * BN;
-          const int ks = gg % KST, vs = gg % VST;
-          if (gg >= KST && !(ok = mbar_wait(k_empty + ks, ((gg / KST) & 1) ^ 1, p.status))) break;
-          mbar_expect_tx(k_full + ks, L::KV_BYTES);
-          for (int s = 0; s < SUB; ++s)
-            tma_load_3d(sK + ks * L::KV_BYTES + s * BN * 128, &tm_k, k_full + ks, s * 64, n0, it.b);
-          if (gg >= VST && !(ok = mbar_wait(v_empty + vs, ((gg / VST) & 1) ^ 1, p.status))) break;
-          mbar_expect_tx(v_full + vs, L::KV_BYTES);
-          for (int s = 0; s < SUB; ++s)
-            tma_load_3d(sV + vs * L::KV_BYTES + s * BN * 128, &tm_v, v_full + vs, s * 64, n0, it.b);
+        if (ok && it.ntiles > 0) {
+          // the next item's Q pair into L2 now, so that its load below is an L2 hit
+          const int kn = k + static_cast<int>(gridDim.x);
+          if (kn < p.items) {
+            const PrefillItem nx = prefill_place(p, kn);
+            for (int w = 0; w < 2; ++w)
+              for (int s = 0; s < SUB; ++s)
+                tma_prefetch_l2_2d(&tm_q, s * 64, (nx.b * p.T + nx.t0 + w * p.TQ) * p.H);
+          }
+          const int qb = n % QB;
+          if (n >= QB) ok = mbar_wait(q_empty + qb, ((n / QB) & 1) ^ 1, p.status);
+          if (ok) {
+            mbar_expect_tx(q_full + qb, L::Q_BYTES);
+            for (int w = 0; w < 2; ++w) {
+              const int qrow0 = (it.b * p.T + it.t0 + w * p.TQ) * p.H;
+              for (int s = 0; s < SUB; ++s)
+                tma_load_2d(sQ + qb * L::Q_BYTES + w * L::QT_BYTES + s * BM * 128, &tm_q, q_full + qb, s * 64,
+                            qrow0);
+            }
+          }
+          for (int j = 0; ok && j < it.ntiles; ++j) {
+            const int n0 = (it.tile0 + j) * BN;
+            for (int kv = 0; ok && kv < 2; ++kv) {
+              const int u = 2 * (g + j) + kv, slot = u % NS;
+              if (u >= NS && !(ok = mbar_wait(kv_empty + slot, ((u / NS) & 1) ^ 1, p.status))) break;
+              mbar_expect_tx(kv_full + slot, L::KV_BYTES);
+              for (int s = 0; s < SUB; ++s)
+                tma_load_3d(sKV + slot * L::KV_BYTES + s * BN * 128, kv ? &tm_v : &tm_k, kv_full + slot, s * 64,
+                            n0, it.b);
+            }
+          }
         }
       }
       ok = __shfl_sync(0xffffffffu, ok, 0);
-      g += it.ntiles;
-      ++n;
+      if (it.ntiles > 0) {
+        g += it.ntiles;
+        ++n;
+      }
     }
     // the consumers wait for every copy issued here before the CTA leaves
     // (or time out together with this thread), so nothing lands after exit
+    tc_fence_before();
+    __syncthreads();
   } else if (warp == L::MMA_WARP) {
     // ------------------------------------------------------ tcgen05 issuer
-    constexpr uint32_t IDESC_S = idesc_bf16(BM, BN, 0, 0);
-    constexpr uint32_t IDESC_O = idesc_bf16(BM, C, 0, 1);
-    const uint32_t q_addr = smem_u32(sQ), k_addr = smem_u32(sK), v_addr = smem_u32(sV);
+    const uint32_t q_addr = smem_u32(sQ), kv_addr = smem_u32(sKV);
     bool ok = true;
-    int g = 0, n = 0;
-    for (int k = blockIdx.x; ok && k < p.items; k += gridDim.x) {
-      const PrefillItem it = prefill_item(p, k);  // the whole warp
-      if (it.ntiles == 0) continue;
+    int idx = 0, g = 0, n = 0;
+    for (int k = blockIdx.x; ok && k < p.items; k += gridDim.x, ++idx) {
+      const int slot = idx % IR;
+      ok = mbar_wait(item_full + slot, (idx / IR) & 1, p.status);
+      const int2 info = s_items[slot];
+      __syncwarp();
+      if (lane == 0) mbar_arrive(item_empty + slot);
+      ok = __all_sync(0xffffffffu, ok);
+      if (!ok) break;
+      const int nt = info.y;
+      if (nt == 0) continue;
       if (lane == 0) {
-        const int qb = n % QB, ob = n & 1;
-        const uint32_t tO = tmem + 256 + ob * C;
-        ok = mbar_wait(q_full + qb, (n / QB) & 1, p.status);
-        if (ok && n >= 2) ok = mbar_wait(o_free + ob, ((n >> 1) & 1) ^ 1, p.status);
-        for (int j = 0; ok && j <= it.ntiles; ++j) {
-          if (j < it.ntiles) {  // S(g + j) = Q K^T
-            const int gs = g + j, ks = gs % KST;
-            if (!(ok = mbar_wait(k_full + ks, (gs / KST) & 1, p.status))) break;
-            tc_fence_after();
-            const uint32_t d = tmem + (gs & 1) * 128;
-#pragma unroll
-            for (int kk = 0; kk < C / 16; ++kk) {
-              const uint32_t off = (kk >> 2) * (128 * 128) + (kk & 3) * 32;
-              mma_ss(d, sdesc_sw128(q_addr + qb * L::Q_BYTES + off, 16, 1024),
-                     sdesc_sw128(k_addr + ks * L::KV_BYTES + off, 16, 1024), IDESC_S, kk > 0 ? 1u : 0u);
-            }
-            mma_commit(k_empty + ks);
-            mma_commit(s_full + (gs & 1));
-            if (j == it.ntiles - 1) mma_commit(q_empty + qb);  // the item's last reader of Q
+        const int qb = n % QB;
+        const uint32_t qa = q_addr + qb * L::Q_BYTES;
+        ok = mbar_wait(q_full + qb, (n / QB) & 1, p.status) &&
+             mbar_wait(kv_full + (2 * g) % NS, ((2 * g) / NS) & 1, p.status);
+        if (ok) {
+          tc_fence_after();
+          prefill_issue_s<C, NS, L::QT_BYTES, L::KV_BYTES>(tmem, qa, kv_addr, 0, g, s_full);
+          prefill_issue_s<C, NS, L::QT_BYTES, L::KV_BYTES>(tmem, qa, kv_addr, 1, g, s_full);
+          mma_commit(kv_empty + (2 * g) % NS);
+          if (nt == 1) mma_commit(q_empty + qb);  // the item's last reader of Q
+        }
+        for (int j = 1; ok && j <= nt; ++j) {
+          const int gp = g + j - 1, gs = g + j;
+          // warpgroup A: P V of tile j - 1, then S of tile j
+          if (!(ok = mbar_wait(p_half, gp & 1, p.status))) break;
+          if (j == 1 && n >= 1 && !(ok = mbar_wait(o_free, (n - 1) & 1, p.status))) break;
+          if (!(ok = mbar_wait(kv_full + (2 * gp + 1) % NS, ((2 * gp + 1) / NS) & 1, p.status))) break;
+          if (j < nt && !(ok = mbar_wait(kv_full + (2 * gs) % NS, ((2 * gs) / NS) & 1, p.status))) break;
+          tc_fence_after();
+          prefill_issue_pv<C, NS, L::KV_BYTES, 0>(tmem, kv_addr, 0, gp, j == 1);
+          if (!(ok = mbar_wait(p_ready, gp & 1, p.status))) break;
+          tc_fence_after();
+          prefill_issue_pv<C, NS, L::KV_BYTES, 1>(tmem, kv_addr, 0, gp, j == 1);
+          if (j == nt) mma_commit(o_final);
+          if (j < nt) {
+            prefill_issue_s<C, NS, L::QT_BYTES, L::KV_BYTES>(tmem, qa, kv_addr, 0, gs, s_full);
           }
-          if (j > 0) {  // O += P V for key tile g + j - 1
-            const int gp = g + j - 1, vs = gp % VST;
-            if (!(ok = mbar_wait(p_ready + (gp & 1), (gp >> 1) & 1, p.status))) break;
-            if (!(ok = mbar_wait(v_full + vs, (gp / VST) & 1, p.status))) break;
-            tc_fence_after();
-            const uint32_t a = tmem + (gp & 1) * 128;
-#pragma unroll
-            for (int kk = 0; kk < BN / 16; ++kk) {
-              mma_ts(tO, a + kk * 8, sdesc_sw128(v_addr + vs * L::KV_BYTES + kk * 16 * 128, BN * 128, 1024), IDESC_O,
-                     (j > 1 || kk > 0) ? 1u : 0u);
-            }
-            mma_commit(v_empty + vs);
-            mma_commit(o_done);
-            if (j == it.ntiles) mma_commit(o_final + ob);
+          // warpgroup B
+          if (!(ok = mbar_wait(p_half + 1, gp & 1, p.status))) break;
+          if (j == 1 && n >= 1 && !(ok = mbar_wait(o_free + 1, (n - 1) & 1, p.status))) break;
+          tc_fence_after();
+          prefill_issue_pv<C, NS, L::KV_BYTES, 0>(tmem, kv_addr, 1, gp, j == 1);
+          if (!(ok = mbar_wait(p_ready + 1, gp & 1, p.status))) break;
+          tc_fence_after();
+          prefill_issue_pv<C, NS, L::KV_BYTES, 1>(tmem, kv_addr, 1, gp, j == 1);
+          mma_commit(kv_empty + (2 * gp + 1) % NS);
+          if (j == nt) mma_commit(o_final + 1);
+          if (j < nt) {
+            prefill_issue_s<C, NS, L::QT_BYTES, L::KV_BYTES>(tmem, qa, kv_addr, 1, gs, s_full);
+            mma_commit(kv_empty + (2 * gs) % NS);
+            if (j == nt - 1) mma_commit(q_empty + qb);
           }
         }
       }
       ok = __shfl_sync(0xffffffffu, ok, 0);
-      g += it.ntiles;
+      g += nt;
       ++n;
     }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
   } else {
-    // ---------------- softmax: one row and a slice of its keys per thread
-    const int quad = warp & 3, slice = warp >> 2;
+    tc_fence_before();
+    __syncthreads();
+  }
+  } else {
+    setmaxnreg_inc<L::REGS_SOFTMAX>();
+    // ------------------- softmax: warpgroup w owns query tile w of the pair
+    const int quad = warp & 3, w = warp >> 2;
     const int row = quad * 32 + lane;
     const int tq = row / p.H, h = row - tq * p.H;
     const uint32_t lane_addr = tmem + (static_cast<uint32_t>(quad * 32) << 16);
+    const uint32_t sAddr = lane_addr + w * 128, oAddr = lane_addr + 256 + w * C;
     const float sl2 = p.scale_log2;
     const int64_t rows_all = static_cast<int64_t>(p.B) * p.T * p.H;
     bool ok = true;
-    int g = 0, n = 0;
-    for (int k = blockIdx.x; ok && k < p.items; k += gridDim.x) {
-      const PrefillItem it = prefill_item(p, k);
-      const int t = it.t0 + tq;
+    int idx = 0, g = 0, n = 0;
+    for (int k = blockIdx.x; ok && k < p.items; k += gridDim.x, ++idx) {
+      const int slot = idx % IR;
+      ok = mbar_wait(item_full + slot, (idx / IR) & 1, p.status);
+      const int2 info = s_items[slot];
+      __syncwarp();
+      if (lane == 0) mbar_arrive(item_empty + slot);
+      ok = __all_sync(0xffffffffu, ok);
+      if (!ok) break;
+      const PrefillItem it = prefill_place(p, k);
+      const int tile0 = info.x, nt = info.y;
+      const int t = it.t0 + w * p.TQ + tq;
       const bool valid = tq < p.TQ && t < p.T;
       const int64_t orow = (static_cast<int64_t>(it.b) * p.T + t) * p.H + h;
-      if (it.ntiles == 0) {  // an empty split: nothing to read
-        if (valid && slice == 0) {
+      if (nt == 0) {  // an empty split: nothing to read
+        if (valid) {
           if (p.splits > 1) {
             p.part_lse[static_cast<int64_t>(it.split) * rows_all + orow] = -INFINITY;
           } else {
@@ -344,9 +531,7 @@ __global__ void __launch_bounds__(PrefillLayout<C, QB, KST, VST, SLICES>::THREAD
         }
         continue;
       }
-      const int ob = n & 1;
-      const uint32_t tO = lane_addr + 256 + ob * C + slice * OS;
-      int lo = 0, hi = -1;
+      int lo = 1, hi = 0;  // an invalid row sees nothing
       if (valid) prefill_query_rows(p, it.b, t, lo, hi);
       int64_t tbase = int64_t(1) << 62;  // no tree: a base no row reaches
       uint64_t tbits = ~0ull;
@@ -355,146 +540,90 @@ __global__ void __launch_bounds__(PrefillLayout<C, QB, KST, VST, SLICES>::THREAD
         tbits = p.tree_bits[static_cast<int64_t>(it.b) * p.T + t];
       }
       float m_used = -INFINITY, l = 0.f;
-      for (int j = 0; j < it.ntiles; ++j) {
+      for (int j = 0; j < nt; ++j) {
         const int gs = g + j;
-        ok = __all_sync(0xffffffffu, mbar_wait(s_full + (gs & 1), (gs >> 1) & 1, p.status));
+        ok = __all_sync(0xffffffffu, mbar_wait(s_full + w, gs & 1, p.status));
         if (!ok) break;
         tc_fence_after();
-        const int n0 = (it.tile0 + j) * BN + slice * KS;  // this thread's first key
-        const uint32_t sAddr = lane_addr + (gs & 1) * 128;
-        uint32_t r[KS];
-        tmem_cols<KS>(sAddr + slice * KS, r);
-        const bool whole = valid && n0 >= lo && n0 + KS - 1 <= hi &&
-                           (static_cast<int64_t>(n0) + KS - 1 < tbase || static_cast<int64_t>(n0) >= tbase + 64);
-        float tmax = -INFINITY;
-        if (whole) {
-#pragma unroll
-          for (int i = 0; i < KS; ++i) tmax = fmaxf(tmax, __uint_as_float(r[i]));
-        } else {
-#pragma unroll
-          for (int i = 0; i < KS; ++i) {
-            const int nn = n0 + i;
-            bool vis = valid && nn >= lo && nn <= hi;
-            const int64_t d = static_cast<int64_t>(nn) - tbase;
-            if (d >= 0 && d < 64) vis = vis && ((tbits >> d) & 1ull);
-            if (!vis) r[i] = __float_as_uint(-INFINITY);
-            tmax = fmaxf(tmax, __uint_as_float(r[i]));
-          }
+        uint32_t r[128];
+        tmem_ld128(sAddr, r);
+        const int n0 = (tile0 + j) * BN;  // the tile's first key
+        const int a = lo - n0, b = hi - n0;  // the row sees tile columns a..b
+        const bool in_tree = static_cast<int64_t>(n0) + BN > tbase && static_cast<int64_t>(n0) < tbase + 64;
+        if (a > 0 || b < BN - 1 || in_tree) {
+          const int tb = in_tree ? static_cast<int>(tbase - n0) : 0;  // the tree's first tile column
+          prefill_mask_half(*reinterpret_cast<uint32_t(*)[64]>(r), 0, a, b, in_tree, tb, tbits);
+          prefill_mask_half(*reinterpret_cast<uint32_t(*)[64]>(r + 64), 64, a, b, in_tree, tb, tbits);
         }
-        if constexpr (SLICES > 1) {  // the row's maximum over its slices (double-buffered by tile parity)
-          float* red = s_red + (gs & 1) * SLICES * 128;
-          red[slice * 128 + row] = tmax;
-          named_barrier(1, NSOFT);
-#pragma unroll
-          for (int o = 0; o < SLICES; ++o)
-            if (o != slice) tmax = fmaxf(tmax, red[o * 128 + row]);
-        }
-        tmax *= sl2;
+        const float tmax = max128(r) * sl2;
         const bool need = tmax > m_used + 8.f;
         const float alpha = need ? fast_exp2(m_used - tmax) : 1.f;
-        if (__any_sync(0xffffffffu, need) && j > 0) {  // every slice's warp votes alike: same rows, same maxima
-          ok = __all_sync(0xffffffffu, mbar_wait(o_done, (gs - 1) & 1, p.status));
-          if (!ok) break;
-          tc_fence_after();
-#pragma unroll
-          for (int c = 0; c < OS; c += 16) {
-            uint32_t o[16];
-            tmem_ld16(tO + c, o);
-#pragma unroll
-            for (int i = 0; i < 16; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
-            tmem_st16(tO + c, o);
-          }
-        }
         if (need) {
           l *= alpha;
           m_used = tmax;
         }
+        // S_w(gs) complete means P_w V of the tile before is too: O_w may be
+        // rescaled (before p_half lets the next product accumulate into it)
+        if (__any_sync(0xffffffffu, need) && j > 0) prefill_rescale_o<C>(oAddr, alpha);
         const float msub = m_used == -INFINITY ? 0.f : m_used;
-        // the weights of this slice as bf16 pairs, over columns [slice KS / 2, (slice + 1) KS / 2) of S
+        // P in two halves of 64 keys: the issuer starts on the first half's
+        // product while the second half is computed
 #pragma unroll
-        for (int c = 0; c < KS / 2; c += 32 < KS / 2 ? 32 : KS / 2) {
-          constexpr int NP = 32 < KS / 2 ? 32 : KS / 2;
-          uint32_t pk[NP];
-#pragma unroll
-          for (int i = 0; i < NP; ++i) {
-            const float e0 = fast_exp2(fmaf(__uint_as_float(r[2 * (c + i)]), sl2, -msub));
-            const float e1 = fast_exp2(fmaf(__uint_as_float(r[2 * (c + i) + 1]), sl2, -msub));
-            l += e0 + e1;
-            pk[i] = pack_bf16(e0, e1);
-          }
-          if constexpr (NP == 32) {
-            tmem_st32(sAddr + slice * (KS / 2) + c, pk);
-          } else {
-            tmem_st16(sAddr + slice * (KS / 2) + c, pk);
-          }
+        for (int hf = 0; hf < 2; ++hf) {
+          uint32_t pk[32];
+          float hmax;
+          l += prefill_half_weights<POLY8>(*reinterpret_cast<const uint32_t(*)[64]>(r + 64 * hf), sl2, msub, pk, hmax);
+          tmem_st32(sAddr + 32 * hf, pk);
+          tmem_wait_st();
+          tc_fence_before();
+          mbar_arrive((hf == 0 ? p_half : p_ready) + w);
         }
-        tmem_wait_st();
-        tc_fence_before();
-        mbar_arrive(p_ready + (gs & 1));
       }
       if (!ok) break;
-      // o_done's parity cannot name the item's last product (the MMA may still
-      // be two products behind), so the epilogue waits on o_final, which
-      // completes once per item and O buffer, after the item's last product
-      ok = __all_sync(0xffffffffu, mbar_wait(o_final + ob, (n >> 1) & 1, p.status));
+      // o_final completes once per item, after the item's last P V product
+      ok = __all_sync(0xffffffffu, mbar_wait(o_final + w, n & 1, p.status));
       if (!ok) break;
       tc_fence_after();
-      if constexpr (SLICES > 1) {  // the row's sum over its slices
-        float* lred = s_red + 2 * SLICES * 128;
-        lred[slice * 128 + row] = l;
-        named_barrier(1, NSOFT);
-        l = 0.f;
-#pragma unroll
-        for (int o = 0; o < SLICES; ++o) l += lred[o * 128 + row];
+      uint32_t o[C];
+      if constexpr (C == 128) {
+        tmem_ld128(oAddr, o);
+      } else {
+        tmem_ld64(oAddr, o);
       }
+      tc_fence_before();
+      mbar_arrive(o_free + w);  // O_w may be overwritten by the next item
       const float msub = m_used == -INFINITY ? 0.f : m_used;
       float denom = l;
       if (p.splits == 1 && p.sink != nullptr && valid) denom += fast_exp2(fmaf(p.sink[h], LOG2E, -msub));
       const float inv = denom > 0.f ? 1.f / denom : 0.f;
-#pragma unroll
-      for (int c = 0; c < OS; c += 16) {
-        uint32_t o16[16];
-        tmem_ld16(tO + c, o16);
-        if (!valid) continue;
+      if (valid) {
         if (p.splits == 1) {
-          uint4* dst = reinterpret_cast<uint4*>(p.out + orow * C + slice * OS + c);
+          uint4* dst = reinterpret_cast<uint4*>(p.out + orow * C);
 #pragma unroll
-          for (int v4 = 0; v4 < 2; ++v4) {
-            uint4 w;
-            w.x = pack_bf16(__uint_as_float(o16[v4 * 8 + 0]) * inv, __uint_as_float(o16[v4 * 8 + 1]) * inv);
-            w.y = pack_bf16(__uint_as_float(o16[v4 * 8 + 2]) * inv, __uint_as_float(o16[v4 * 8 + 3]) * inv);
-            w.z = pack_bf16(__uint_as_float(o16[v4 * 8 + 4]) * inv, __uint_as_float(o16[v4 * 8 + 5]) * inv);
-            w.w = pack_bf16(__uint_as_float(o16[v4 * 8 + 6]) * inv, __uint_as_float(o16[v4 * 8 + 7]) * inv);
-            dst[v4] = w;
+          for (int v4 = 0; v4 < C / 8; ++v4) {
+            uint4 u;
+            u.x = pack_bf16(__uint_as_float(o[v4 * 8 + 0]) * inv, __uint_as_float(o[v4 * 8 + 1]) * inv);
+            u.y = pack_bf16(__uint_as_float(o[v4 * 8 + 2]) * inv, __uint_as_float(o[v4 * 8 + 3]) * inv);
+            u.z = pack_bf16(__uint_as_float(o[v4 * 8 + 4]) * inv, __uint_as_float(o[v4 * 8 + 5]) * inv);
+            u.w = pack_bf16(__uint_as_float(o[v4 * 8 + 6]) * inv, __uint_as_float(o[v4 * 8 + 7]) * inv);
+            dst[v4] = u;
           }
-        } else {
-          const int64_t prow = static_cast<int64_t>(it.split) * rows_all + orow;
-          float4* dst = reinterpret_cast<float4*>(p.part_o + prow * C + slice * OS + c);
-#pragma unroll
-          for (int v4 = 0; v4 < 4; ++v4)
-            dst[v4] = make_float4(__uint_as_float(o16[v4 * 4]) * inv, __uint_as_float(o16[v4 * 4 + 1]) * inv,
-                                  __uint_as_float(o16[v4 * 4 + 2]) * inv, __uint_as_float(o16[v4 * 4 + 3]) * inv);
-        }
-      }
-      tc_fence_before();
-      mbar_arrive(o_free + ob);  // O buffer ob may be overwritten by the item after next
-      if (valid && slice == 0) {
-        if (p.splits == 1) {
           p.lse[orow] = denom > 0.f ? (msub + log2f(denom)) * LN2 : -INFINITY;
         } else {
-          p.part_lse[static_cast<int64_t>(it.split) * rows_all + orow] =
-              l > 0.f ? (msub + log2f(l)) * LN2 : -INFINITY;
+          const int64_t prow = static_cast<int64_t>(it.split) * rows_all + orow;
+          float4* dst = reinterpret_cast<float4*>(p.part_o + prow * C);
+#pragma unroll
+          for (int v4 = 0; v4 < C / 4; ++v4)
+            dst[v4] = make_float4(__uint_as_float(o[v4 * 4]) * inv, __uint_as_float(o[v4 * 4 + 1]) * inv,
+                                  __uint_as_float(o[v4 * 4 + 2]) * inv, __uint_as_float(o[v4 * 4 + 3]) * inv);
+          p.part_lse[prow] = l > 0.f ? (msub + log2f(l)) * LN2 : -INFINITY;
         }
       }
-      g += it.ntiles;
+      g += nt;
       ++n;
     }
-  }
-  tc_fence_before();
-  __syncthreads();
-  if (warp == L::MMA_WARP) {
-    tc_fence_after();
-    tmem_dealloc(tmem, 512);
+    tc_fence_before();
+    __syncthreads();
   }
 }
 

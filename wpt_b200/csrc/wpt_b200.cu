@@ -105,13 +105,32 @@ int allow_smem(Kernel kernel, int bytes) {
   return WPT_OK;
 }
 
-template <int C, int SLICES>
-int launch_prefill_s(const wpt::PrefillParams& p, const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
+// Q-pair buffers and K/V ring stages of the prefill kernel: the ring gets
+// what 227 KB leaves after the Q buffers (the next item's Q is prefetched
+// into L2 instead of a second buffer when C = 128).
+template <int C>
+struct PrefillShape {
+  static constexpr int QB = C == 128 ? 1 : 2, NS = C == 128 ? 5 : 8;
+};
+
+// Pairs of weights in every 8 computed on the FMA pipe (WPT_B200_POLY8 = 0..4 overrides).
+int prefill_poly8() {
+  static int v = -1;
+  if (v < 0) {
+    const char* env = getenv("WPT_B200_POLY8");
+    const int e = env ? atoi(env) : 2;
+    v = (e >= 0 && e <= 4) ? e : 2;
+  }
+  return v;
+}
+
+template <int C, int POLY8>
+int launch_prefill_p(const wpt::PrefillParams& p, const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
                      cudaStream_t stream) {
-  constexpr int QB = 2, KST = 2, VST = 2;
-  using L = wpt::PrefillLayout<C, QB, KST, VST, SLICES>;
+  constexpr int QB = PrefillShape<C>::QB, NS = PrefillShape<C>::NS;
+  using L = wpt::PrefillLayout<C, QB, NS>;
   static_assert(L::BYTES <= 232448, "prefill kernel shared memory exceeds 227 KB");
-  auto kernel = wpt::prefill_kernel<C, QB, KST, VST, SLICES>;
+  auto kernel = wpt::prefill_kernel<C, QB, NS, POLY8>;
   if (int rc = allow_smem(kernel, L::BYTES)) return rc;
   int sms = 148;
   int dev = 0;
@@ -123,24 +142,15 @@ int launch_prefill_s(const wpt::PrefillParams& p, const CUtensorMap& tq, const C
   return WPT_OK;
 }
 
-// Softmax warps per row quadrant (WPT_B200_SLICES = 1, 2 or 4 overrides the default).
-int prefill_slices() {
-  static int slices = 0;
-  if (slices == 0) {
-    const char* env = getenv("WPT_B200_SLICES");
-    const int v = env ? atoi(env) : 0;
-    slices = (v == 1 || v == 2 || v == 4) ? v : 2;
-  }
-  return slices;
-}
-
 template <int C>
 int launch_prefill(const wpt::PrefillParams& p, const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
                    cudaStream_t stream) {
-  switch (prefill_slices()) {
-    case 1: return launch_prefill_s<C, 1>(p, tq, tk, tv, stream);
-    case 4: return launch_prefill_s<C, 4>(p, tq, tk, tv, stream);
-    default: return launch_prefill_s<C, 2>(p, tq, tk, tv, stream);
+  switch (prefill_poly8()) {
+    case 0: return launch_prefill_p<C, 0>(p, tq, tk, tv, stream);
+    case 1: return launch_prefill_p<C, 1>(p, tq, tk, tv, stream);
+    case 3: return launch_prefill_p<C, 3>(p, tq, tk, tv, stream);
+    case 4: return launch_prefill_p<C, 4>(p, tq, tk, tv, stream);
+    default: return launch_prefill_p<C, 2>(p, tq, tk, tv, stream);
   }
 }
 
@@ -224,7 +234,7 @@ extern "C" int wpt_attn_prefill(const void* q, const void* k, const void* v, int
   if (C != 64 && C != 128) return fail(WPT_ERR_UNSUPPORTED, "head width %d: the kernels take 64 or 128", C);
   if (H < 1 || H > 128) return fail(WPT_ERR_UNSUPPORTED, "%d heads: the kernels take 1 to 128", H);
   if (B < 1 || T < 1 || N < 1) return fail(WPT_ERR_INVALID, "empty shape B=%d T=%d N=%d", B, T, N);
-  if (static_cast<int64_t>(B) * T * H >= (int64_t(1) << 31)) return fail(WPT_ERR_UNSUPPORTED, "B*T*H too large");
+  if (static_cast<int64_t>(B) * T * H + 256 >= (int64_t(1) << 31)) return fail(WPT_ERR_UNSUPPORTED, "B*T*H too large");
   if (splits < 1) return fail(WPT_ERR_INVALID, "splits must be >= 1");
   if (splits > 1 && (part_o == nullptr || part_lse == nullptr))
     return fail(WPT_ERR_INVALID, "splits > 1 needs part_o and part_lse scratch");
@@ -262,7 +272,7 @@ extern "C" int wpt_attn_prefill(const void* q, const void* k, const void* v, int
   p.TQ = 128 / H;
   p.splits = splits;
   {
-    const int64_t items = static_cast<int64_t>((T + p.TQ - 1) / p.TQ) * B * splits;
+    const int64_t items = static_cast<int64_t>((T + 2 * p.TQ - 1) / (2 * p.TQ)) * B * splits;  // query-tile pairs
     if (items >= (int64_t(1) << 31)) return fail(WPT_ERR_UNSUPPORTED, "too many prefill work items");
     p.items = static_cast<int>(items);
   }

@@ -74,7 +74,7 @@ def prefill_forward(q, k, v, positions, scale, window=0, floor=None, tree_bits=N
     TQ = max(1, 128 // H)
     if splits is None:
         tiles = window // 128 + 2 if window else (N + 127) // 128
-        splits = _splits_for(B * math.ceil(T / TQ), tiles)
+        splits = _splits_for(B * math.ceil(T / (2 * TQ)), tiles)  # one CTA item per pair of query tiles
     part_o = part_lse = None
     if splits > 1:
         part_o = torch.empty(splits, B * T * H, C, dtype=torch.float32, device=q.device)
