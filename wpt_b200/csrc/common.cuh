@@ -169,6 +169,42 @@ __device__ __forceinline__ void mma_ts_off(uint32_t d, uint32_t a, uint64_t b, u
       : "memory");
 }
 
+// Warp-wide forms of the two above and of mma_commit: all 32 lanes execute
+// them with the same operands and the elected lane (always the lowest, so
+// one thread issues every product and commit) issues. The operand
+// arithmetic stays warp-uniform, which keeps it off the per-thread path.
+template <uint32_t OFF_A, uint32_t OFF_B>
+__device__ __forceinline__ void mma_ss_off_warp(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc,
+                                                uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p, e;\n\t.reg .b64 da, db;\n\t"
+      "add.s64 da, %1, %5;\n\tadd.s64 db, %2, %6;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "elect.sync _|e, 0xffffffff;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], da, db, %3, p;\n\t}\n" ::"r"(d),
+      "l"(a), "l"(b), "r"(idesc), "r"(accumulate), "n"(OFF_A), "n"(OFF_B)
+      : "memory");
+}
+template <uint32_t OFF_A, uint32_t OFF_B>
+__device__ __forceinline__ void mma_ts_off_warp(uint32_t d, uint32_t a, uint64_t b, uint32_t idesc,
+                                                uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p, e;\n\t.reg .b32 ta;\n\t.reg .b64 db;\n\t"
+      "add.u32 ta, %1, %5;\n\tadd.s64 db, %2, %6;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "elect.sync _|e, 0xffffffff;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [ta], db, %3, p;\n\t}\n" ::"r"(d),
+      "r"(a), "l"(b), "r"(idesc), "r"(accumulate), "n"(OFF_A), "n"(OFF_B)
+      : "memory");
+}
+__device__ __forceinline__ void mma_commit_warp(uint64_t* bar) {
+  asm volatile(
+      "{\n\t.reg .pred e;\n\telect.sync _|e, 0xffffffff;\n\t"
+      "@e tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n\t}\n" ::"r"(
+          smem_u32(bar))
+      : "memory");
+}
+
 // Arrives on bar once every tcgen05 operation this thread issued before has completed.
 __device__ __forceinline__ void mma_commit(uint64_t* bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(

@@ -31,7 +31,7 @@
 // overwrites P_A(j-1) only after PV_A(j-1) has read it, and the commit that
 // says S_A(j) is ready also says PV_A(j-1) is done, which is what a rescale
 // of O_A needs. Q pairs have QB buffers; K and V tiles stream through one
-// ring of NS stages in the order K(0), V(0), K(1), V(1), ...
+// ring of NS stages, K one tile ahead: K(0), K(1), V(0), K(2), V(1), ...
 //
 // Online softmax in base 2 with a lazy maximum: a row's running maximum is
 // only raised (and O rescaled) when a tile's maximum exceeds it by more
@@ -54,9 +54,9 @@
 // kernel, which adds the sink.
 //
 // Barrier phases run on across items: key tile g (counted over the CTA's
-// items) is ring entries 2g (K) and 2g + 1 (V); the n-th item with any key
-// tile uses Q buffer n % QB; the idx-th item of the CTA uses ring slot
-// idx % IR of the item ring.
+// items) is ring entries prefill_k_entry(g) (K) and prefill_v_entry(g) (V);
+// the n-th item with any key tile uses Q buffer n % QB; the idx-th item of
+// the CTA uses ring slot idx % IR of the item ring.
 #pragma once
 
 #include <climits>
@@ -186,6 +186,14 @@ __device__ __forceinline__ uint32_t prefill_visible_word(int a, int b, bool in_t
   return m;
 }
 
+// Ring entries of key tile g (counted over the CTA's items): the loader
+// runs K one tile ahead of V, K(0) K(1) V(0) K(2) V(1) ..., which gives
+// each K load about two and a half rounds of the issue loop before it is
+// read and each V load one and a half. Entry 2G - 1 (a K(G) after the last
+// tile) is never used.
+__device__ __forceinline__ int prefill_k_entry(int g) { return g == 0 ? 0 : 2 * g - 1; }
+__device__ __forceinline__ int prefill_v_entry(int g) { return 2 * g + 2; }
+
 __device__ __forceinline__ float max3f(float a, float b, float c) {
   float d;
   asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
@@ -265,23 +273,23 @@ __device__ __forceinline__ void prefill_mask_half(uint32_t (&r)[64], int c0, int
 }
 
 // S_w = Q_w K^T for key tile gs into S buffer w (TMEM column 128 w), then
-// a commit on s_full[w]. qa: the Q pair's shared-memory address. One thread
-// issues back to back with the tensor pipe, so each descriptor is a base
-// plus a constant offset (addresses are in 16-byte units in the low 14
-// bits, and no shared-memory address carries out of them).
+// a commit on s_full[w]. qa: the Q pair's shared-memory address. Called by
+// the whole issuer warp (one elected lane issues): each descriptor is a
+// warp-uniform base plus a constant offset (addresses are in 16-byte units
+// in the low 14 bits, and no shared-memory address carries out of them).
 template <int KK>
 __device__ __forceinline__ void prefill_s_steps(uint32_t d, uint64_t dq, uint64_t dk, uint32_t idesc) {
   if constexpr (KK > 0) prefill_s_steps<KK - 1>(d, dq, dk, idesc);
   constexpr uint32_t off = ((KK >> 2) * (128 * 128) + (KK & 3) * 32) >> 4;
-  mma_ss_off<off, off>(d, dq, dk, idesc, KK > 0 ? 1u : 0u);
+  mma_ss_off_warp<off, off>(d, dq, dk, idesc, KK > 0 ? 1u : 0u);
 }
 template <int C, int NS, int QT_BYTES, int KV_BYTES>
 __device__ __forceinline__ void prefill_issue_s(uint32_t tmem, uint32_t qa, uint32_t kv_addr, int w, int gs,
                                                 uint64_t* s_full) {
   const uint64_t dq = sdesc_sw128(qa + w * QT_BYTES, 16, 1024);
-  const uint64_t dk = sdesc_sw128(kv_addr + ((2 * gs) % NS) * KV_BYTES, 16, 1024);
+  const uint64_t dk = sdesc_sw128(kv_addr + (prefill_k_entry(gs) % NS) * KV_BYTES, 16, 1024);
   prefill_s_steps<C / 16 - 1>(tmem + w * 128, dq, dk, idesc_bf16(128, 128, 0, 0));
-  mma_commit(s_full + w);
+  mma_commit_warp(s_full + w);
 }
 
 // O_w += P_w V for key tile gp over its keys 64 HALF .. 64 HALF + 63 (first:
@@ -291,11 +299,11 @@ template <int KK, int KK0>
 __device__ __forceinline__ void prefill_pv_steps(uint32_t d, uint32_t a, uint64_t dv, uint32_t idesc, uint32_t acc0) {
   if constexpr (KK > KK0) prefill_pv_steps<KK - 1, KK0>(d, a, dv, idesc, acc0);
   constexpr uint32_t off = (KK * 16 * 128) >> 4;
-  mma_ts_off<KK * 8, off>(d, a, dv, idesc, KK > 0 ? 1u : acc0);
+  mma_ts_off_warp<KK * 8, off>(d, a, dv, idesc, KK > 0 ? 1u : acc0);
 }
 template <int C, int NS, int KV_BYTES, int HALF>
 __device__ __forceinline__ void prefill_issue_pv(uint32_t tmem, uint32_t kv_addr, int w, int gp, bool first) {
-  const uint64_t dv = sdesc_sw128(kv_addr + ((2 * gp + 1) % NS) * KV_BYTES, 128 * 128, 1024);
+  const uint64_t dv = sdesc_sw128(kv_addr + (prefill_v_entry(gp) % NS) * KV_BYTES, 128 * 128, 1024);
   prefill_pv_steps<4 * HALF + 3, 4 * HALF>(tmem + 256 + w * C, tmem + w * 128, dv, idesc_bf16(128, C, 0, 1),
                                            first ? 0u : 1u);
 }
@@ -371,6 +379,15 @@ __global__ void __launch_bounds__(PrefillLayout<C, QB, NS>::THREADS, 1)
     // ------------------------------------------------------------ TMA loader
     bool ok = true;
     int idx = 0, g = 0, n = 0;  // items seen, key tiles issued, items with key tiles
+    int pend_g = -1, pend_n0 = 0, pend_b = 0;  // (lane 0) the V tile not yet issued
+    // ring entry u: K or V of a key tile starting at row n0 of batch row b
+    auto load = [&](int u, bool v, int n0, int b) {
+      const int slot = u % NS;
+      if (u >= NS && !(ok = mbar_wait(kv_empty + slot, ((u / NS) & 1) ^ 1, p.status))) return;
+      mbar_expect_tx(kv_full + slot, L::KV_BYTES);
+      for (int s = 0; s < SUB; ++s)
+        tma_load_3d(sKV + slot * L::KV_BYTES + s * BN * 128, v ? &tm_v : &tm_k, kv_full + slot, s * 64, n0, b);
+    };
     for (int k = blockIdx.x; ok && k < p.items; k += gridDim.x, ++idx) {
       const PrefillItem it = prefill_item(p, k);  // the whole warp
       if (lane == 0) {
@@ -380,35 +397,31 @@ __global__ void __launch_bounds__(PrefillLayout<C, QB, NS>::THREADS, 1)
           s_items[slot] = make_int2(it.tile0, it.ntiles);
           mbar_arrive(item_full + slot);
         }
-        if (ok && it.ntiles > 0) {
-          // the next item's Q pair into L2 now, so that its load below is an L2 hit
-          const int kn = k + static_cast<int>(gridDim.x);
-          if (kn < p.items) {
-            const PrefillItem nx = prefill_place(p, kn);
-            for (int w = 0; w < 2; ++w)
-              for (int s = 0; s < SUB; ++s)
-                tma_prefetch_l2_2d(&tm_q, s * 64, (nx.b * p.T + nx.t0 + w * p.TQ) * p.H);
-          }
-          const int qb = n % QB;
-          if (n >= QB) ok = mbar_wait(q_empty + qb, ((n / QB) & 1) ^ 1, p.status);
-          if (ok) {
-            mbar_expect_tx(q_full + qb, L::Q_BYTES);
-            for (int w = 0; w < 2; ++w) {
-              const int qrow0 = (it.b * p.T + it.t0 + w * p.TQ) * p.H;
-              for (int s = 0; s < SUB; ++s)
-                tma_load_2d(sQ + qb * L::Q_BYTES + w * L::QT_BYTES + s * BM * 128, &tm_q, q_full + qb, s * 64,
-                            qrow0);
+        for (int j = 0; ok && j < it.ntiles; ++j) {
+          const int n0 = (it.tile0 + j) * BN;
+          load(prefill_k_entry(g + j), false, n0, it.b);
+          if (ok && pend_g >= 0) load(prefill_v_entry(pend_g), true, pend_n0, pend_b);
+          pend_g = g + j;
+          pend_n0 = n0;
+          pend_b = it.b;
+          if (ok && j == 0) {  // the Q pair, once the previous item's last V is on its way
+            const int kn = k + static_cast<int>(gridDim.x);
+            if (kn < p.items) {  // the next item's Q pair into L2 now, so that its load is an L2 hit
+              const PrefillItem nx = prefill_place(p, kn);
+              for (int w = 0; w < 2; ++w)
+                for (int s = 0; s < SUB; ++s)
+                  tma_prefetch_l2_2d(&tm_q, s * 64, (nx.b * p.T + nx.t0 + w * p.TQ) * p.H);
             }
-          }
-          for (int j = 0; ok && j < it.ntiles; ++j) {
-            const int n0 = (it.tile0 + j) * BN;
-            for (int kv = 0; ok && kv < 2; ++kv) {
-              const int u = 2 * (g + j) + kv, slot = u % NS;
-              if (u >= NS && !(ok = mbar_wait(kv_empty + slot, ((u / NS) & 1) ^ 1, p.status))) break;
-              mbar_expect_tx(kv_full + slot, L::KV_BYTES);
-              for (int s = 0; s < SUB; ++s)
-                tma_load_3d(sKV + slot * L::KV_BYTES + s * BN * 128, kv ? &tm_v : &tm_k, kv_full + slot, s * 64,
-                            n0, it.b);
+            const int qb = n % QB;
+            if (n >= QB) ok = mbar_wait(q_empty + qb, ((n / QB) & 1) ^ 1, p.status);
+            if (ok) {
+              mbar_expect_tx(q_full + qb, L::Q_BYTES);
+              for (int w = 0; w < 2; ++w) {
+                const int qrow0 = (it.b * p.T + it.t0 + w * p.TQ) * p.H;
+                for (int s = 0; s < SUB; ++s)
+                  tma_load_2d(sQ + qb * L::Q_BYTES + w * L::QT_BYTES + s * BM * 128, &tm_q, q_full + qb, s * 64,
+                              qrow0);
+              }
             }
           }
         }
@@ -419,6 +432,7 @@ __global__ void __launch_bounds__(PrefillLayout<C, QB, NS>::THREADS, 1)
         ++n;
       }
     }
+    if (lane == 0 && ok && pend_g >= 0) load(prefill_v_entry(pend_g), true, pend_n0, pend_b);
     // the consumers wait for every copy issued here before the CTA leaves
     // (or time out together with this thread), so nothing lands after exit
     tc_fence_before();
@@ -438,52 +452,50 @@ __global__ void __launch_bounds__(PrefillLayout<C, QB, NS>::THREADS, 1)
       if (!ok) break;
       const int nt = info.y;
       if (nt == 0) continue;
-      if (lane == 0) {
-        const int qb = n % QB;
-        const uint32_t qa = q_addr + qb * L::Q_BYTES;
-        ok = mbar_wait(q_full + qb, (n / QB) & 1, p.status) &&
-             mbar_wait(kv_full + (2 * g) % NS, ((2 * g) / NS) & 1, p.status);
-        if (ok) {
-          tc_fence_after();
-          prefill_issue_s<C, NS, L::QT_BYTES, L::KV_BYTES>(tmem, qa, kv_addr, 0, g, s_full);
-          prefill_issue_s<C, NS, L::QT_BYTES, L::KV_BYTES>(tmem, qa, kv_addr, 1, g, s_full);
-          mma_commit(kv_empty + (2 * g) % NS);
-          if (nt == 1) mma_commit(q_empty + qb);  // the item's last reader of Q
-        }
-        for (int j = 1; ok && j <= nt; ++j) {
-          const int gp = g + j - 1, gs = g + j;
-          // warpgroup A: P V of tile j - 1, then S of tile j
-          if (!(ok = mbar_wait(p_half, gp & 1, p.status))) break;
-          if (j == 1 && n >= 1 && !(ok = mbar_wait(o_free, (n - 1) & 1, p.status))) break;
-          if (!(ok = mbar_wait(kv_full + (2 * gp + 1) % NS, ((2 * gp + 1) / NS) & 1, p.status))) break;
-          if (j < nt && !(ok = mbar_wait(kv_full + (2 * gs) % NS, ((2 * gs) / NS) & 1, p.status))) break;
-          tc_fence_after();
-          prefill_issue_pv<C, NS, L::KV_BYTES, 0>(tmem, kv_addr, 0, gp, j == 1);
-          if (!(ok = mbar_wait(p_ready, gp & 1, p.status))) break;
-          tc_fence_after();
-          prefill_issue_pv<C, NS, L::KV_BYTES, 1>(tmem, kv_addr, 0, gp, j == 1);
-          if (j == nt) mma_commit(o_final);
-          if (j < nt) {
-            prefill_issue_s<C, NS, L::QT_BYTES, L::KV_BYTES>(tmem, qa, kv_addr, 0, gs, s_full);
-          }
-          // warpgroup B
-          if (!(ok = mbar_wait(p_half + 1, gp & 1, p.status))) break;
-          if (j == 1 && n >= 1 && !(ok = mbar_wait(o_free + 1, (n - 1) & 1, p.status))) break;
-          tc_fence_after();
-          prefill_issue_pv<C, NS, L::KV_BYTES, 0>(tmem, kv_addr, 1, gp, j == 1);
-          if (!(ok = mbar_wait(p_ready + 1, gp & 1, p.status))) break;
-          tc_fence_after();
-          prefill_issue_pv<C, NS, L::KV_BYTES, 1>(tmem, kv_addr, 1, gp, j == 1);
-          mma_commit(kv_empty + (2 * gp + 1) % NS);
-          if (j == nt) mma_commit(o_final + 1);
-          if (j < nt) {
-            prefill_issue_s<C, NS, L::QT_BYTES, L::KV_BYTES>(tmem, qa, kv_addr, 1, gs, s_full);
-            mma_commit(kv_empty + (2 * gs) % NS);
-            if (j == nt - 1) mma_commit(q_empty + qb);
-          }
+      // the whole warp runs the issue loop; one elected lane issues
+      auto wait = [&](uint64_t* bar, int parity) {
+        return __all_sync(0xffffffffu, mbar_wait(bar, parity, p.status));
+      };
+      const int qb = n % QB;
+      const uint32_t qa = q_addr + qb * L::Q_BYTES;
+      ok = wait(q_full + qb, (n / QB) & 1) && wait(kv_full + prefill_k_entry(g) % NS, (prefill_k_entry(g) / NS) & 1);
+      if (ok) {
+        tc_fence_after();
+        prefill_issue_s<C, NS, L::QT_BYTES, L::KV_BYTES>(tmem, qa, kv_addr, 0, g, s_full);
+        prefill_issue_s<C, NS, L::QT_BYTES, L::KV_BYTES>(tmem, qa, kv_addr, 1, g, s_full);
+        mma_commit_warp(kv_empty + prefill_k_entry(g) % NS);
+        if (nt == 1) mma_commit_warp(q_empty + qb);  // the item's last reader of Q
+      }
+      for (int j = 1; ok && j <= nt; ++j) {
+        const int gp = g + j - 1, gs = g + j;
+        // warpgroup A: P V of tile j - 1 (by halves of P), then S of tile j
+        if (!(ok = wait(p_half, gp & 1))) break;
+        if (j == 1 && n >= 1 && !(ok = wait(o_free, (n - 1) & 1))) break;
+        if (!(ok = wait(kv_full + prefill_v_entry(gp) % NS, (prefill_v_entry(gp) / NS) & 1))) break;
+        if (j < nt && !(ok = wait(kv_full + prefill_k_entry(gs) % NS, (prefill_k_entry(gs) / NS) & 1))) break;
+        tc_fence_after();
+        prefill_issue_pv<C, NS, L::KV_BYTES, 0>(tmem, kv_addr, 0, gp, j == 1);
+        if (!(ok = wait(p_ready, gp & 1))) break;
+        tc_fence_after();
+        prefill_issue_pv<C, NS, L::KV_BYTES, 1>(tmem, kv_addr, 0, gp, j == 1);
+        if (j == nt) mma_commit_warp(o_final);
+        if (j < nt) prefill_issue_s<C, NS, L::QT_BYTES, L::KV_BYTES>(tmem, qa, kv_addr, 0, gs, s_full);
+        // warpgroup B
+        if (!(ok = wait(p_half + 1, gp & 1))) break;
+        if (j == 1 && n >= 1 && !(ok = wait(o_free + 1, (n - 1) & 1))) break;
+        tc_fence_after();
+        prefill_issue_pv<C, NS, L::KV_BYTES, 0>(tmem, kv_addr, 1, gp, j == 1);
+        if (!(ok = wait(p_ready + 1, gp & 1))) break;
+        tc_fence_after();
+        prefill_issue_pv<C, NS, L::KV_BYTES, 1>(tmem, kv_addr, 1, gp, j == 1);
+        mma_commit_warp(kv_empty + prefill_v_entry(gp) % NS);
+        if (j == nt) mma_commit_warp(o_final + 1);
+        if (j < nt) {
+          prefill_issue_s<C, NS, L::QT_BYTES, L::KV_BYTES>(tmem, qa, kv_addr, 1, gs, s_full);
+          mma_commit_warp(kv_empty + prefill_k_entry(gs) % NS);
+          if (j == nt - 1) mma_commit_warp(q_empty + qb);
         }
       }
-      ok = __shfl_sync(0xffffffffu, ok, 0);
       g += nt;
       ++n;
     }

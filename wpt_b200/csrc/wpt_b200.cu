@@ -118,8 +118,8 @@ int prefill_poly8() {
   static int v = -1;
   if (v < 0) {
     const char* env = getenv("WPT_B200_POLY8");
-    const int e = env ? atoi(env) : 2;
-    v = (e >= 0 && e <= 4) ? e : 2;
+    const int e = env ? atoi(env) : 1;
+    v = (e >= 0 && e <= 4) ? e : 1;
   }
   return v;
 }
@@ -147,10 +147,10 @@ int launch_prefill(const wpt::PrefillParams& p, const CUtensorMap& tq, const CUt
                    cudaStream_t stream) {
   switch (prefill_poly8()) {
     case 0: return launch_prefill_p<C, 0>(p, tq, tk, tv, stream);
-    case 1: return launch_prefill_p<C, 1>(p, tq, tk, tv, stream);
     case 3: return launch_prefill_p<C, 3>(p, tq, tk, tv, stream);
     case 4: return launch_prefill_p<C, 4>(p, tq, tk, tv, stream);
-    default: return launch_prefill_p<C, 2>(p, tq, tk, tv, stream);
+    case 2: return launch_prefill_p<C, 2>(p, tq, tk, tv, stream);
+    default: return launch_prefill_p<C, 1>(p, tq, tk, tv, stream);
   }
 }
 
