@@ -458,21 +458,23 @@ __global__ void __launch_bounds__(PrefillLayout<C, QB, NS>::THREADS, 1)
       };
       const int qb = n % QB;
       const uint32_t qa = q_addr + qb * L::Q_BYTES;
-      ok = wait(q_full + qb, (n / QB) & 1) && wait(kv_full + prefill_k_entry(g) % NS, (prefill_k_entry(g) / NS) & 1);
+      // the ring entries a round reads are waited for at the end of the round
+      // before, while the tensor pipe still has that round's products queued
+      auto wait_kv = [&](int u) { return wait(kv_full + u % NS, (u / NS) & 1); };
+      ok = wait(q_full + qb, (n / QB) & 1) && wait_kv(prefill_k_entry(g));
       if (ok) {
         tc_fence_after();
         prefill_issue_s<C, NS, L::QT_BYTES, L::KV_BYTES>(tmem, qa, kv_addr, 0, g, s_full);
         prefill_issue_s<C, NS, L::QT_BYTES, L::KV_BYTES>(tmem, qa, kv_addr, 1, g, s_full);
         mma_commit_warp(kv_empty + prefill_k_entry(g) % NS);
         if (nt == 1) mma_commit_warp(q_empty + qb);  // the item's last reader of Q
+        ok = wait_kv(prefill_v_entry(g)) && (nt == 1 || wait_kv(prefill_k_entry(g + 1)));
       }
       for (int j = 1; ok && j <= nt; ++j) {
         const int gp = g + j - 1, gs = g + j;
         // warpgroup A: P V of tile j - 1 (by halves of P), then S of tile j
         if (!(ok = wait(p_half, gp & 1))) break;
         if (j == 1 && n >= 1 && !(ok = wait(o_free, (n - 1) & 1))) break;
-        if (!(ok = wait(kv_full + prefill_v_entry(gp) % NS, (prefill_v_entry(gp) / NS) & 1))) break;
-        if (j < nt && !(ok = wait(kv_full + prefill_k_entry(gs) % NS, (prefill_k_entry(gs) / NS) & 1))) break;
         tc_fence_after();
         prefill_issue_pv<C, NS, L::KV_BYTES, 0>(tmem, kv_addr, 0, gp, j == 1);
         if (!(ok = wait(p_ready, gp & 1))) break;
@@ -494,6 +496,7 @@ __global__ void __launch_bounds__(PrefillLayout<C, QB, NS>::THREADS, 1)
           prefill_issue_s<C, NS, L::QT_BYTES, L::KV_BYTES>(tmem, qa, kv_addr, 1, gs, s_full);
           mma_commit_warp(kv_empty + prefill_k_entry(gs) % NS);
           if (j == nt - 1) mma_commit_warp(q_empty + qb);
+          ok = wait_kv(prefill_v_entry(gs)) && (j + 1 == nt || wait_kv(prefill_k_entry(gs + 1)));
         }
       }
       g += nt;
