@@ -13,7 +13,7 @@
 // accept_stats_kernel, one CTA per (row, position): x = scores / temperature;
 // with top_k, the top_k-th largest x by a 4 x 8-bit radix select
 // (ties kept, as `scores < v[..., [-1]]` keeps them); the maximum m and the
-// sum Z of exp(x - m) over the kept x.
+// sum Z of exp(x - m) over the kept x, in one pass over the row.
 // accept_draw_kernel, one CTA per row: the decisions (one thread, a handful
 // of lookups), then the draw: each thread sums its contiguous slice of the
 // weights in float64, a block scan finds the slice where the running sum
@@ -152,18 +152,34 @@ __global__ void __launch_bounds__(ACCEPT_THREADS) accept_stats_kernel(const Acce
     }
     thr = accept_unkey(prefix);
   }
-  float m = -INFINITY;
-  for (int v = threadIdx.x; v < p.V; v += blockDim.x) {
-    const float y = x[v] / temp;
-    if (y >= thr) m = fmaxf(m, y);
+  // the maximum and the sum of exp(x - m) over the kept x in one pass: each
+  // thread keeps a running (maximum, sum) and rescales its sum when its
+  // maximum rises; the block combines them (16-byte loads when rows allow)
+  float m = -INFINITY, z = 0.f;
+  auto take = [&](float y) {
+    if (!(y >= thr)) return;
+    if (y > m) {
+      z = z * expf(m - y) + 1.f;
+      m = y;
+    } else {
+      z += expf(y - m);
+    }
+  };
+  if ((p.V & 3) == 0) {
+    const float4* x4 = reinterpret_cast<const float4*>(x);
+    for (int v = threadIdx.x; v < p.V / 4; v += blockDim.x) {
+      const float4 f = __ldg(x4 + v);
+      take(f.x / temp);
+      take(f.y / temp);
+      take(f.z / temp);
+      take(f.w / temp);
+    }
+  } else {
+    for (int v = threadIdx.x; v < p.V; v += blockDim.x) take(__ldg(x + v) / temp);
   }
-  m = block_max(m, s_red);
-  float z = 0.f;
-  for (int v = threadIdx.x; v < p.V; v += blockDim.x) {
-    const float y = x[v] / temp;
-    if (y >= thr) z += expf(y - m);
-  }
-  z = block_sum(z, s_red);
+  const float mb = block_max(m, s_red);
+  z = block_sum(m == -INFINITY ? 0.f : z * expf(m - mb), s_red);
+  m = mb;
   if (threadIdx.x == 0) {
     float* st = p.stats + (static_cast<int64_t>(i) * (p.n + 1) + j) * 3;
     st[0] = m;

@@ -231,17 +231,22 @@ __device__ __forceinline__ float prefill_half_weights(const uint32_t (&r)[64], f
   return (a0 + a1) + (b0 + b1);
 }
 
-// Maximum of 128 values: eight independent chains of three-input maxima.
+// Maximum of 128 values as a tree of three-input maxima (depth 5: 43, 15,
+// 5, 2, 1 nodes), so the latency is a few instructions, not a chain.
 __device__ __forceinline__ float max128(const uint32_t (&r)[128]) {
-  float m[8];
+  float a[43];
 #pragma unroll
-  for (int c = 0; c < 8; ++c) m[c] = __uint_as_float(r[c]);
+  for (int i = 0; i < 42; ++i)
+    a[i] = max3f(__uint_as_float(r[3 * i]), __uint_as_float(r[3 * i + 1]), __uint_as_float(r[3 * i + 2]));
+  a[42] = fmaxf(__uint_as_float(r[126]), __uint_as_float(r[127]));
+  float b[15];
 #pragma unroll
-  for (int i = 8; i < 128; i += 16) {
+  for (int i = 0; i < 14; ++i) b[i] = max3f(a[3 * i], a[3 * i + 1], a[3 * i + 2]);
+  b[14] = a[42];
+  float c[5];
 #pragma unroll
-    for (int c = 0; c < 8; ++c) m[c] = max3f(m[c], __uint_as_float(r[i + 2 * c]), __uint_as_float(r[i + 2 * c + 1]));
-  }
-  return max3f(max3f(m[0], m[1], m[2]), max3f(m[3], m[4], m[5]), fmaxf(m[6], m[7]));
+  for (int i = 0; i < 5; ++i) c[i] = max3f(b[3 * i], b[3 * i + 1], b[3 * i + 2]);
+  return max3f(max3f(c[0], c[1], c[2]), c[3], c[4]);
 }
 
 // Multiplies this warp's rows of O (C TMEM columns from oAddr) by alpha.
