@@ -99,6 +99,25 @@ __device__ __forceinline__ void stream_query_rows(const StreamParams& p, int b, 
   lo = low > INT_MAX ? INT_MAX : static_cast<int>(low);
 }
 
+// S^T (+)= K Q^T over head-width steps 0..KK: A = the K tile (K-major,
+// 64-element chunks BN * 128 bytes apart), B = Q (K-major, NCOL rows).
+template <int NCOL, int KK>
+__device__ __forceinline__ void stream_s_steps(uint32_t d, uint64_t dk, uint64_t dq, uint32_t idesc) {
+  if constexpr (KK > 0) stream_s_steps<NCOL, KK - 1>(d, dk, dq, idesc);
+  constexpr uint32_t off_k = ((KK >> 2) * (128 * 128) + (KK & 3) * 32) >> 4;
+  constexpr uint32_t off_q = ((KK >> 2) * (NCOL * 128) + (KK & 3) * 32) >> 4;
+  mma_ss_off_warp<off_k, off_q>(d, dk, dq, idesc, KK > 0 ? 1u : 0u);
+}
+// O^T (+)= V^T P^T over key steps 0..KK: A = V^T (MN-major), B = P^T
+// (K-major, NCOL rows); acc0 = 0 makes the first step overwrite O^T.
+template <int NCOL, int KK>
+__device__ __forceinline__ void stream_pv_steps(uint32_t d, uint64_t dv, uint64_t dp, uint32_t idesc, uint32_t acc0) {
+  if constexpr (KK > 0) stream_pv_steps<NCOL, KK - 1>(d, dv, dp, idesc, acc0);
+  constexpr uint32_t off_v = (KK * 16 * 128) >> 4;
+  constexpr uint32_t off_p = ((KK >> 2) * (NCOL * 128) + (KK & 3) * 32) >> 4;
+  mma_ss_off_warp<off_v, off_p>(d, dv, dp, idesc, KK > 0 ? 1u : acc0);
+}
+
 template <int NCOL, int STAGES, bool GATHER>
 __global__ void __launch_bounds__(STREAM_THREADS, 1)
     stream_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v,
@@ -316,44 +335,36 @@ __global__ void __launch_bounds__(STREAM_THREADS, 1)
     }
   } else if (warp == 4) {
     // ------------------------------------------------------- MMA issuer
-    if ((threadIdx.x & 31) == 0) {
-      constexpr uint32_t IDESC_S = idesc_bf16(128, NCOL, 0, 0);
-      constexpr uint32_t IDESC_O = idesc_bf16(128, NCOL, 1, 0);
-      const uint32_t tS = tmem, tO = tmem + 2 * NCOL;
-      const uint32_t q_addr = smem_u32(sQ), k_addr = smem_u32(sK), v_addr = smem_u32(sV), p_addr = smem_u32(sP);
-      bool ok = mbar_wait(q_full, 0, p.status);
-      for (int j = 0; ok && j <= ntiles; ++j) {
-        if (j < ntiles) {
-          const int st = j % STAGES;
-          if (!(ok = mbar_wait(full + st, (j / STAGES) & 1, p.status))) break;
-          tc_fence_after();
-#pragma unroll
-          for (int kk = 0; kk < C / 16; ++kk) {
-            mma_ss(tS + (j & 1) * NCOL,
-                   sdesc_sw128(k_addr + st * L::KV_BYTES + (kk >> 2) * (BN * 128) + (kk & 3) * 32, 16, 1024),
-                   sdesc_sw128(q_addr + (kk >> 2) * (NCOL * 128) + (kk & 3) * 32, 16, 1024), IDESC_S,
-                   kk > 0 ? 1u : 0u);
-          }
-          mma_commit(s_full + (j & 1));
-        }
-        if (j > 0) {
-          const int jp = j - 1, st = jp % STAGES;
-          if (!(ok = mbar_wait(p_ready + (jp & 1), (jp >> 1) & 1, p.status))) break;
-          tc_fence_after();
-          const uint32_t pb = p_addr + (jp & 1) * L::P_BYTES;
-#pragma unroll
-          for (int kk = 0; kk < BN / 16; ++kk) {
-            mma_ss(tO, sdesc_sw128(v_addr + st * L::KV_BYTES + kk * 16 * 128, BN * 128, 1024),
-                   sdesc_sw128(pb + (kk >> 2) * (NCOL * 128) + (kk & 3) * 32, 16, 1024), IDESC_O,
-                   (jp > 0 || kk > 0) ? 1u : 0u);
-          }
-          mma_commit(kv_empty + st);
-          mma_commit(o_done);
-          if (j == ntiles) mma_commit(o_final);
-        }
+    // the whole warp runs the loop and one elected lane issues; descriptors
+    // are warp-uniform bases plus constant offsets
+    constexpr uint32_t IDESC_S = idesc_bf16(128, NCOL, 0, 0);
+    constexpr uint32_t IDESC_O = idesc_bf16(128, NCOL, 1, 0);
+    const uint32_t tS = tmem, tO = tmem + 2 * NCOL;
+    const uint32_t q_addr = smem_u32(sQ), k_addr = smem_u32(sK), v_addr = smem_u32(sV), p_addr = smem_u32(sP);
+    const uint64_t dq = sdesc_sw128(q_addr, 16, 1024);
+    auto wait = [&](uint64_t* bar, int parity) { return __all_sync(0xffffffffu, mbar_wait(bar, parity, p.status)); };
+    bool ok = wait(q_full, 0);
+    for (int j = 0; ok && j <= ntiles; ++j) {
+      if (j < ntiles) {
+        const int st = j % STAGES;
+        if (!(ok = wait(full + st, (j / STAGES) & 1))) break;
+        tc_fence_after();
+        stream_s_steps<NCOL, C / 16 - 1>(tS + (j & 1) * NCOL, sdesc_sw128(k_addr + st * L::KV_BYTES, 16, 1024), dq,
+                                         IDESC_S);
+        mma_commit_warp(s_full + (j & 1));
+      }
+      if (j > 0) {
+        const int jp = j - 1, st = jp % STAGES;
+        if (!(ok = wait(p_ready + (jp & 1), (jp >> 1) & 1))) break;
+        tc_fence_after();
+        stream_pv_steps<NCOL, BN / 16 - 1>(tO, sdesc_sw128(v_addr + st * L::KV_BYTES, BN * 128, 1024),
+                                           sdesc_sw128(p_addr + (jp & 1) * L::P_BYTES, 16, 1024), IDESC_O,
+                                           jp > 0 ? 1u : 0u);
+        mma_commit_warp(kv_empty + st);
+        mma_commit_warp(o_done);
+        if (j == ntiles) mma_commit_warp(o_final);
       }
     }
-    __syncwarp();
   } else {
     // ------------------------------------------ softmax: thread r = slot r
     const int r = threadIdx.x, lane = r & 31;

@@ -129,8 +129,8 @@ def stream_forward(q, k, v, positions, scale, window=0, floor=None, idx=None, si
     if chunk_tiles is None:
         # at least 16 key tiles per CTA (a CTA's start-up costs about as much
         # as streaming a few tiles), more when that still gives two CTAs per SM
-        chunk_tiles = int(os.environ.get("WPT_B200_CHUNK", "0")) or max(min(16, tiles),
-                                                                         math.ceil(tiles * groups / (2 * SM_COUNT)))
+        chunk_tiles = int(os.environ.get("WPT_B200_CHUNK", "0")) or max(
+            min(16, tiles), 16 * math.ceil(tiles * groups / (2 * SM_COUNT) / 16))
     chunk_tiles = max(1, min(int(chunk_tiles), tiles))
     splits = math.ceil(tiles / chunk_tiles)
     out = torch.empty_like(q)
