@@ -55,6 +55,20 @@ def peaks():
     return dict(FALLBACK_PEAKS), "fallback"
 
 
+def profiled_traffic():
+    """DRAM bytes per causal-pass launch at B=8 from the committed ncu summary
+    (the line `traffic_bytes_per_launch_b8: N`), or None."""
+    path = os.path.join(ROOT, "profiles", "prefill_kernel_config2.md")
+    try:
+        with open(path) as f:
+            for line in f:
+                if line.startswith("traffic_bytes_per_launch_b8:"):
+                    return int(line.split(":", 1)[1])
+    except (OSError, ValueError):
+        pass
+    return None
+
+
 def config2_flops(B=B2, T=T2, H=H2, C=C2, W=W2):
     causal = 4.0 * B * H * C * T * (T + 1) / 2
     window = 4.0 * B * H * C * sum(min(p + 1, W) for p in range(T))
@@ -470,7 +484,9 @@ def main():
                          "peak": peak, "peak_kind": f"bf16_tflops_sustained of {pk_kind}", "unit": "TFLOP/s",
                          "frac": round(achieved / peak, 4), "ms_per_launch": round(causal_ms, 4),
                          "algorithmic_flops_per_launch": causal_flop,
-                         "traffic": None},
+                         "traffic": profiled_traffic(),
+                         "traffic_source": "ncu dram__bytes_read+write of the causal pass at B=4, x2 for B=8 "
+                                           "(profiles/prefill_kernel_config2.md)"},
             "clocks": clock,
             "status": status,
         }
