@@ -93,6 +93,19 @@ def test_long_single_row_over_many_splits(wb):
     _check(wb, out, lse, ref_out, ref_lse)
 
 
+@pytest.mark.parametrize("chunk", [2, 7])
+def test_long_row_merged_from_many_splits(wb, chunk):
+    # 157 or 23 splits of one 32-head row: the merge's one-CTA-per-row form
+    from wpt_b200 import ops
+    q, e, positions = _decode_case(1, 1, 32, 40000, seed=6, lengths=torch.tensor([39999]))
+    C = 128
+    out, lse = ops.stream_forward(q.cuda(), e.cuda()[..., :C], e.cuda()[..., C:], positions.cuda(), C ** -0.5,
+                                  chunk_tiles=chunk)
+    ref_out, ref_lse, _ = oat.exact_attention(_np(q), _np(e[..., :C]), _np(e[..., C:]), positions.numpy(),
+                                              C ** -0.5, 0, 0)
+    _check(wb, out, lse, ref_out, ref_lse)
+
+
 def _sparse_case(B, T, H, N, K, W, seed):
     g = torch.Generator().manual_seed(seed)
     C = 128

@@ -70,11 +70,12 @@ def long_decode(q, k_shard, v_shard, shard_start, positions, scale, sink=None, g
     out, lse = partial(q, k_shard, v_shard, local, scale)
     o = out.float().reshape(1, B * T * H, C)
     s = lse.float().reshape(1, B * T * H)
-    if world > 1:
-        parts_o = torch.empty(world, B * T * H, C, dtype=torch.float32, device=o.device)
-        parts_s = torch.empty(world, B * T * H, dtype=torch.float32, device=o.device)
-        dist.all_gather_into_tensor(parts_o, o.contiguous(), group=group)
-        dist.all_gather_into_tensor(parts_s, s.contiguous(), group=group)
+    if world > 1:  # one collective: each rank's (output, log-sum) rows packed side by side
+        packed = torch.cat([o, s.unsqueeze(-1)], dim=-1).contiguous()
+        gathered = torch.empty(world, B * T * H, C + 1, dtype=torch.float32, device=o.device)
+        dist.all_gather_into_tensor(gathered, packed, group=group)
+        parts_o = gathered[..., :C].contiguous()
+        parts_s = gathered[..., C].contiguous()
     else:
         parts_o, parts_s = o, s
     merged, merged_lse = merge(parts_o, parts_s, H, sink)
