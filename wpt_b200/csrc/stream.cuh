@@ -517,7 +517,22 @@ __global__ void __launch_bounds__(STREAM_THREADS, 1)
       if (c32 * 32 + lane < NCOL) s_red[warp * 64 + c32 * 32 + lane] = sum;
     }
     named_barrier(1, 128);
-    if (r < NCOL) s_l[r] = (s_red[r] + s_red[64 + r]) + (s_red[128 + r] + s_red[192 + r]);
+    // thread c < NCOL finishes column c: its normaliser (into s_l) and log-sum
+    const int ncols = TQg * p.H;  // columns with a query; the rest are padding
+    const int64_t row0 = (static_cast<int64_t>(b) * p.T + t0) * p.H;  // column c is row row0 + c
+    if (r < ncols) {
+      const float l = (s_red[r] + s_red[64 + r]) + (s_red[128 + r] + s_red[192 + r]);
+      const float m = s_m[r], msub = m == -INFINITY ? 0.f : m;
+      if (p.splits == 1) {
+        float denom = l;
+        if (p.sink != nullptr) denom += fast_exp2(fmaf(p.sink[r % p.H], LOG2E, -msub));
+        s_l[r] = denom > 0.f ? 1.f / denom : 0.f;
+        if (ok) p.lse[row0 + r] = denom > 0.f ? (msub + log2f(denom)) * LN2 : -INFINITY;
+      } else {
+        s_l[r] = l > 0.f ? 1.f / l : 0.f;
+        if (ok) p.part_lse[split * rows_total + row0 + r] = l > 0.f ? (msub + log2f(l)) * LN2 : -INFINITY;
+      }
+    }
     named_barrier(1, 128);
     if (ok) {
       float o[NCOL];
@@ -535,24 +550,17 @@ __global__ void __launch_bounds__(STREAM_THREADS, 1)
           for (int c = 0; c < 32; ++c) o[c32 * 32 + c] = __uint_as_float(x[c]);
         }
       }
-      // thread r holds column r of the head width for every (query, head)
+      // thread r holds element r of the head width for every column (query, head)
+      if (p.splits == 1) {
+        __nv_bfloat16* dst = p.out + row0 * C + r;
 #pragma unroll
-      for (int c = 0; c < NCOL; ++c) {
-        const int tq = s_colq[c];
-        if (tq < 0) continue;
-        const int h = c - tq * p.H;
-        const int64_t orow = (static_cast<int64_t>(b) * p.T + t0 + tq) * p.H + h;
-        const float m = s_m[c], msub = m == -INFINITY ? 0.f : m, l = s_l[c];
-        if (p.splits == 1) {
-          float denom = l;
-          if (p.sink != nullptr) denom += fast_exp2(fmaf(p.sink[h], LOG2E, -msub));
-          p.out[orow * C + r] = __float2bfloat16_rn(denom > 0.f ? o[c] / denom : 0.f);
-          if (r == 0) p.lse[orow] = denom > 0.f ? (msub + log2f(denom)) * LN2 : -INFINITY;
-        } else {
-          const int64_t prow = split * rows_total + orow;
-          p.part_o[prow * C + r] = l > 0.f ? o[c] / l : 0.f;
-          if (r == 0) p.part_lse[prow] = l > 0.f ? (msub + log2f(l)) * LN2 : -INFINITY;
-        }
+        for (int c = 0; c < NCOL; ++c)
+          if (c < ncols) dst[static_cast<int64_t>(c) * C] = __float2bfloat16_rn(o[c] * s_l[c]);
+      } else {
+        float* dst = p.part_o + (split * rows_total + row0) * C + r;
+#pragma unroll
+        for (int c = 0; c < NCOL; ++c)
+          if (c < ncols) dst[static_cast<int64_t>(c) * C] = o[c] * s_l[c];
       }
     }
   }
