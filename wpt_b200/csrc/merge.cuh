@@ -53,59 +53,79 @@ __global__ void __launch_bounds__(256) merge_kernel(const float* __restrict__ pa
 }
 
 // The same merge for few rows with many splits (a long row split over many
-// CTAs or GPUs): one CTA of MERGE_WARPS warps per row, warp w taking splits
-// w, w + MERGE_WARPS, ..., the warps' maxima, sums and columns combined in
-// shared memory, so the split loop is MERGE_WARPS times shorter.
-constexpr int MERGE_WARPS = 8;
+// CTAs or GPUs): one CTA of MERGE_THREADS per row. Its threads first take
+// the splits' log-sums in parallel (maximum, weights into shared memory,
+// their sum), then MERGE_THREADS / C groups of C threads each add a share of
+// the splits' output rows (coalesced, several loads in flight per thread),
+// and the groups' sums are combined in shared memory.
+constexpr int MERGE_THREADS = 512, MERGE_MAX_SPLITS = 2048;
 template <int C>
-__global__ void __launch_bounds__(MERGE_WARPS * 32) merge_wide_kernel(
+__global__ void __launch_bounds__(MERGE_THREADS) merge_wide_kernel(
     const float* __restrict__ part_o, const float* __restrict__ part_lse, int splits, int64_t split_stride, int H,
     const float* __restrict__ sink, __nv_bfloat16* __restrict__ out, float* __restrict__ lse_out) {
-  __shared__ float s_m[MERGE_WARPS], s_d[MERGE_WARPS];
-  __shared__ float s_acc[MERGE_WARPS][C];
+  constexpr int GROUPS = MERGE_THREADS / C;
+  __shared__ float s_w[MERGE_MAX_SPLITS];
+  __shared__ float s_red[MERGE_THREADS / 32 + 1];
+  __shared__ float s_acc[GROUPS][C];
   const int64_t row = blockIdx.x;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
   const int h = static_cast<int>(row % H);
+  // maximum of the log-sums (and the sink)
   float m = -INFINITY;
-  for (int s = warp; s < splits; s += MERGE_WARPS) m = fmaxf(m, part_lse[s * split_stride + row]);
-  if (lane == 0) s_m[warp] = m;
+  for (int s = t; s < splits; s += MERGE_THREADS) m = fmaxf(m, part_lse[s * split_stride + row]);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+  if (lane == 0) s_red[warp] = m;
   __syncthreads();
   const float sk = sink != nullptr ? sink[h] : -INFINITY;
   m = sk;
 #pragma unroll
-  for (int w = 0; w < MERGE_WARPS; ++w) m = fmaxf(m, s_m[w]);
-  float acc[C / 32];
-#pragma unroll
-  for (int i = 0; i < C / 32; ++i) acc[i] = 0.f;
-  float denom = 0.f;
-  if (m != -INFINITY) {
-    for (int s = warp; s < splits; s += MERGE_WARPS) {
-      const float ls = part_lse[s * split_stride + row];
-      if (ls == -INFINITY) continue;
-      const float wgt = __expf(ls - m);
-      denom += wgt;
-      const float* o = part_o + (s * split_stride + row) * C;
-#pragma unroll
-      for (int i = 0; i < C / 32; ++i) acc[i] = fmaf(wgt, o[lane + 32 * i], acc[i]);
-    }
+  for (int w = 0; w < MERGE_THREADS / 32; ++w) m = fmaxf(m, s_red[w]);
+  __syncthreads();
+  // weights exp(lse_s - m) and their sum
+  float d = 0.f;
+  for (int s = t; s < splits; s += MERGE_THREADS) {
+    const float ls = part_lse[s * split_stride + row];
+    const float w = (m == -INFINITY || ls == -INFINITY) ? 0.f : __expf(ls - m);
+    s_w[s] = w;
+    d += w;
   }
 #pragma unroll
-  for (int i = 0; i < C / 32; ++i) s_acc[warp][lane + 32 * i] = acc[i];
-  if (lane == 0) s_d[warp] = denom;
+  for (int o = 16; o > 0; o >>= 1) d += __shfl_xor_sync(0xffffffffu, d, o);
+  if (lane == 0) s_red[warp] = d;
   __syncthreads();
-  if (warp == 0) {
-    float d = (m != -INFINITY && sink != nullptr) ? __expf(sk - m) : 0.f;
+  // group g adds splits g, g + GROUPS, ...: thread c of the group, column c
+  const int g = t / C, c = t - g * C;
+  float acc0 = 0.f, acc1 = 0.f, acc2 = 0.f, acc3 = 0.f;
+  const float* o = part_o + row * C + c;
+  int s = g;
+  for (; s + 3 * GROUPS < splits; s += 4 * GROUPS) {
+    const float w0 = s_w[s], w1 = s_w[s + GROUPS], w2 = s_w[s + 2 * GROUPS], w3 = s_w[s + 3 * GROUPS];
+    const float o0 = w0 != 0.f ? o[s * split_stride * C] : 0.f;
+    const float o1 = w1 != 0.f ? o[(s + GROUPS) * split_stride * C] : 0.f;
+    const float o2 = w2 != 0.f ? o[(s + 2 * GROUPS) * split_stride * C] : 0.f;
+    const float o3 = w3 != 0.f ? o[(s + 3 * GROUPS) * split_stride * C] : 0.f;
+    acc0 = fmaf(w0, o0, acc0);
+    acc1 = fmaf(w1, o1, acc1);
+    acc2 = fmaf(w2, o2, acc2);
+    acc3 = fmaf(w3, o3, acc3);
+  }
+  for (; s < splits; s += GROUPS) {
+    const float w = s_w[s];
+    if (w != 0.f) acc0 = fmaf(w, o[s * split_stride * C], acc0);
+  }
+  s_acc[g][c] = (acc0 + acc1) + (acc2 + acc3);
+  __syncthreads();
+  if (t < C) {
+    float denom = (m != -INFINITY && sink != nullptr) ? __expf(sk - m) : 0.f;
 #pragma unroll
-    for (int w = 0; w < MERGE_WARPS; ++w) d += s_d[w];
-    const float inv = d > 0.f ? 1.f / d : 0.f;
+    for (int w = 0; w < MERGE_THREADS / 32; ++w) denom += s_red[w];
+    float a = 0.f;
 #pragma unroll
-    for (int i = 0; i < C / 32; ++i) {
-      float a = 0.f;
-#pragma unroll
-      for (int w = 0; w < MERGE_WARPS; ++w) a += s_acc[w][lane + 32 * i];
-      out[row * C + lane + 32 * i] = __float2bfloat16_rn(a * inv);
-    }
-    if (lane == 0) lse_out[row] = d > 0.f ? m + __logf(d) : -INFINITY;
+    for (int k = 0; k < GROUPS; ++k) a += s_acc[k][t];
+    const float inv = denom > 0.f ? 1.f / denom : 0.f;
+    out[row * C + t] = __float2bfloat16_rn(a * inv);
+    if (t == 0) lse_out[row] = denom > 0.f ? m + __logf(denom) : -INFINITY;
   }
 }
 

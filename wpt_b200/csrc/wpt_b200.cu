@@ -195,8 +195,8 @@ int launch_score(const CUtensorMap& tq, const CUtensorMap& tk, const wpt::ScoreP
 template <int C>
 int launch_merge(const float* part_o, const float* part_lse, int splits, int64_t rows, int64_t split_stride, int H,
                  const float* sink, void* out, float* lse, cudaStream_t stream) {
-  if (splits >= 16 && rows <= 4096) {  // few rows, many splits: a CTA per row splits the split loop
-    wpt::merge_wide_kernel<C><<<static_cast<unsigned>(rows), wpt::MERGE_WARPS * 32, 0, stream>>>(
+  if (splits >= 16 && splits <= wpt::MERGE_MAX_SPLITS && rows <= 4096) {  // few rows, many splits: a CTA per row
+    wpt::merge_wide_kernel<C><<<static_cast<unsigned>(rows), wpt::MERGE_THREADS, 0, stream>>>(
         part_o, part_lse, splits, split_stride, H, sink, static_cast<__nv_bfloat16*>(out), lse);
   } else {
     const int warps = 8;
