@@ -68,12 +68,21 @@ def check(rc):
 
 
 def ptr(t):
-    """A tensor's device address for the C ABI, or NULL for None."""
-    return None if t is None else ctypes.c_void_p(t.data_ptr())
+    """A tensor's device address for the C ABI, or NULL for None (the
+    declared argument types convert plain integers)."""
+    return None if t is None else t.data_ptr()
+
+
+_raw_stream = getattr(torch._C, "_cuda_getCurrentRawStream", None)
 
 
 def stream(device):
-    return ctypes.c_void_p(torch.cuda.current_stream(device).cuda_stream)
+    """The current CUDA stream of `device` as a handle (the raw query skips
+    building a torch Stream object on every call)."""
+    if _raw_stream is not None:
+        index = device.index if device.index is not None else torch.cuda.current_device()
+        return _raw_stream(index)
+    return torch.cuda.current_stream(device).cuda_stream
 
 
 def device_status(reset=True):

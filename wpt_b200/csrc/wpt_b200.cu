@@ -4,7 +4,9 @@
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
+#include <map>
 #include <mutex>
+#include <utility>
 #include <string>
 
 #include "../../include/wpt_attn.h"
@@ -98,10 +100,41 @@ int table_map(CUtensorMap* map, const void* base, int64_t stride_b, int64_t stri
   return tensor_map(map, base, 3, dims, strides, box);
 }
 
+// The current device (and its SM count), asked of the runtime once per
+// thread and device change rather than on every launch.
+int current_device(int* sms = nullptr) {
+  static thread_local int cached_sms[64] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) dev = 0;
+  if (sms) {
+    if (cached_sms[dev] == 0) {
+      int v = 148;
+      if (cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) v = 148;
+      cached_sms[dev] = v;
+    }
+    *sms = cached_sms[dev];
+  }
+  return dev;
+}
+
+// Raises a kernel's dynamic shared memory limit to `bytes` on the current
+// device, once per (kernel, device, size): the attribute call costs
+// microseconds that a decode step should not pay on every launch.
 template <typename Kernel>
 int allow_smem(Kernel kernel, int bytes) {
+  static std::mutex mu;
+  static std::map<std::pair<const void*, int>, int> done;
+  const int dev = current_device();
+  const auto key = std::make_pair(reinterpret_cast<const void*>(kernel), dev);
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    auto it = done.find(key);
+    if (it != done.end() && it->second >= bytes) return WPT_OK;
+  }
   cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
   if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(max dynamic shared memory)");
+  std::lock_guard<std::mutex> lock(mu);
+  done[key] = bytes;
   return WPT_OK;
 }
 
@@ -133,8 +166,7 @@ int launch_prefill_p(const wpt::PrefillParams& p, const CUtensorMap& tq, const C
   auto kernel = wpt::prefill_kernel<C, QB, NS, POLY8>;
   if (int rc = allow_smem(kernel, L::BYTES)) return rc;
   int sms = 148;
-  int dev = 0;
-  if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  current_device(&sms);
   const int grid = p.items < sms ? p.items : sms;  // persistent: one CTA per SM walks the items
   kernel<<<grid, L::THREADS, L::BYTES, stream>>>(tq, tk, tv, p);
   cudaError_t e = cudaGetLastError();

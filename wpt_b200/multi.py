@@ -62,11 +62,13 @@ def long_decode(q, k_shard, v_shard, shard_start, positions, scale, sink=None, g
     sink) -> (out rows, lse rows) combines the gathered shares (default: the
     merge kernel). Tests substitute CPU versions to check the partitioning
     with gloo ranks."""
-    partial = partial or (lambda q_, k_, v_, p_, s_: ops.stream_forward(q_, k_, v_, p_, s_))
-    merge = merge or ops.merge_partials
     B, T, H, C = q.shape
     world = dist.get_world_size(group) if dist.is_initialized() else 1
     local = positions - shard_start  # rows of this shard the query sees: 0 .. local (none when negative)
+    if world == 1 and partial is None and merge is None:  # the whole row is here: one kernel call
+        return ops.stream_forward(q, k_shard, v_shard, local, scale, sink=sink)
+    partial = partial or (lambda q_, k_, v_, p_, s_: ops.stream_forward(q_, k_, v_, p_, s_))
+    merge = merge or ops.merge_partials
     out, lse = partial(q, k_shard, v_shard, local, scale)
     o = out.float().reshape(1, B * T * H, C)
     s = lse.float().reshape(1, B * T * H)

@@ -40,6 +40,8 @@ def _table(x):
 
 
 def _rows(x):
+    if x.dtype == torch.int64 and x.is_contiguous():
+        return x
     return x.to(torch.int64).contiguous()
 
 
