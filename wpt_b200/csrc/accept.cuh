@@ -14,11 +14,13 @@
 // with top_k, the top_k-th largest x by a 4 x 8-bit radix select
 // (ties kept, as `scores < v[..., [-1]]` keeps them); the maximum m and the
 // sum Z of exp(x - m) over the kept x, in one pass over the row.
-// accept_draw_kernel, one CTA per row: the decisions (one thread, a handful
-// of lookups), then the draw: each thread sums its contiguous slice of the
-// weights in float64, a block scan finds the slice where the running sum
-// crosses resample * total, and that thread walks its slice.
+// accept_draw_kernel, one CTA per row: the decisions (one thread per draft,
+// the first rejection by an atomic minimum), then the draw: float64 sums of
+// 256-entry chunks of the weights (coalesced), a block scan finds the chunk
+// where the running sum crosses resample * total, and one warp walks it.
 #pragma once
+
+#include <type_traits>
 
 #include "common.cuh"
 
@@ -165,17 +167,40 @@ __global__ void __launch_bounds__(ACCEPT_THREADS) accept_stats_kernel(const Acce
       z += expf(y - m);
     }
   };
-  if ((p.V & 3) == 0) {
-    const float4* x4 = reinterpret_cast<const float4*>(x);
-    for (int v = threadIdx.x; v < p.V / 4; v += blockDim.x) {
-      const float4 f = __ldg(x4 + v);
-      take(f.x / temp);
-      take(f.y / temp);
-      take(f.z / temp);
-      take(f.w / temp);
+  // x / temperature is x itself at temperature 1: that case skips the division
+  auto pass = [&](auto unit) {
+    auto scaled = [&](float v) { return decltype(unit)::value ? v : v / temp; };
+    if ((p.V & 3) == 0) {  // four 16-byte loads in flight per thread
+      const float4* x4 = reinterpret_cast<const float4*>(x);
+      const int n4 = p.V / 4;
+      int v = threadIdx.x;
+      for (; v + 3 * ACCEPT_THREADS < n4; v += 4 * ACCEPT_THREADS) {
+        float4 f[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) f[u] = __ldg(x4 + v + u * ACCEPT_THREADS);
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          take(scaled(f[u].x));
+          take(scaled(f[u].y));
+          take(scaled(f[u].z));
+          take(scaled(f[u].w));
+        }
+      }
+      for (; v < n4; v += ACCEPT_THREADS) {
+        const float4 f = __ldg(x4 + v);
+        take(scaled(f.x));
+        take(scaled(f.y));
+        take(scaled(f.z));
+        take(scaled(f.w));
+      }
+    } else {
+      for (int v = threadIdx.x; v < p.V; v += blockDim.x) take(scaled(__ldg(x + v)));
     }
+  };
+  if (temp == 1.f) {
+    pass(std::true_type());
   } else {
-    for (int v = threadIdx.x; v < p.V; v += blockDim.x) take(__ldg(x + v) / temp);
+    pass(std::false_type());
   }
   const float mb = block_max(m, s_red);
   z = block_sum(m == -INFINITY ? 0.f : z * expf(m - mb), s_red);
@@ -190,51 +215,101 @@ __global__ void __launch_bounds__(ACCEPT_THREADS) accept_stats_kernel(const Acce
 
 // p_j[v] as the reference's float32 softmax gives it
 __device__ __forceinline__ float accept_prob(const float* x, const float* st, int v, float temp) {
-  const float y = x[v] / temp;
+  const float y = temp == 1.f ? x[v] : x[v] / temp;
   return y >= st[2] ? expf(y - st[0]) / st[1] : 0.f;
 }
 
+// The draw's weight of vocabulary entry v: p_j[v], or max(0, p_j[v] - q_j[v])
+// after a rejection (qv non-null). The row's statistics come in registers
+// (m, 1 / Z, threshold); the weight scales by 1 / Z instead of dividing,
+// which only moves the inverse CDF's boundaries by float32 rounding.
+struct DrawRow {
+  const float* x;
+  const float* qv;
+  float m, rz, thr, temp;
+  __device__ __forceinline__ float weight(int v) const {
+    const float y = temp == 1.f ? x[v] : x[v] / temp;
+    float w = y >= thr ? expf(y - m) * rz : 0.f;
+    if (qv) w = fmaxf(w - qv[v], 0.f);
+    return w;
+  }
+};
+
+// One CTA per row. The decisions: thread j < drafts tests draft j
+// (u_j q_j[tok] < p_j[tok]) and a block vote finds the first rejection.
+// The draw: the row's weights in chunks of DRAW_CHUNK consecutive entries
+// (lane l of a warp takes entries 8l .. 8l + 7 of a chunk, so the warp's
+// loads are coalesced), each chunk's float64 sum into shared memory; a
+// block scan over the chunks finds the one where the running sum crosses
+// resample * total, and one warp rescans that chunk to the entry.
+constexpr int DRAW_CHUNK = 256;
 __global__ void __launch_bounds__(ACCEPT_THREADS) accept_draw_kernel(const AcceptParams p) {
+  extern __shared__ double s_chunk[];  // ceil(V / DRAW_CHUNK) chunk sums
   __shared__ double s_scan[33];
-  __shared__ int s_pick[2];
-  const int i = blockIdx.x;
+  __shared__ int s_pick[3];
+  const int i = blockIdx.x, t = threadIdx.x, lane = t & 31, warp = t >> 5;
+  constexpr int WARPS = ACCEPT_THREADS / 32;
   const int ni = accept_row_drafts(p, i);
   const float temp = p.temperature;
   int64_t* tokens = p.tokens + static_cast<int64_t>(i) * (p.n + 1);
-  if (threadIdx.x == 0) {
-    int reject = -1;
-    for (int j = 0; j < ni; ++j) {
-      const int64_t tok = p.drafted[static_cast<int64_t>(i) * p.n + j];
-      const float* x = p.scores + (static_cast<int64_t>(i) * (p.n + 1) + j) * p.V;
-      const float* st = p.stats + (static_cast<int64_t>(i) * (p.n + 1) + j) * 3;
-      const float pj = (tok >= 0 && tok < p.V) ? accept_prob(x, st, static_cast<int>(tok), temp) : 0.f;
-      const float qj = (tok >= 0 && tok < p.V) ? p.q[(static_cast<int64_t>(i) * p.n + j) * p.V + tok] : 0.f;
-      if (p.uniforms[static_cast<int64_t>(i) * p.n + j] * qj < pj) {
-        tokens[j] = tok;
-      } else {
-        reject = j;
-        break;
-      }
-    }
-    s_pick[0] = reject;
+  if (t == 0) {
+    s_pick[0] = ni;  // the first rejected draft, ni when every draft is kept
+    s_pick[1] = p.V - 1;  // the drawn entry (the last when rounding leaves the target past the end)
+    s_pick[2] = -1;  // the chunk the running sum crosses the target in
   }
   __syncthreads();
-  const int reject = s_pick[0];
-  const int jd = reject >= 0 ? reject : ni;  // the position the last token is drawn at
-  const float* x = p.scores + (static_cast<int64_t>(i) * (p.n + 1) + jd) * p.V;
-  const float* st = p.stats + (static_cast<int64_t>(i) * (p.n + 1) + jd) * 3;
-  const float* qv = reject >= 0 ? p.q + (static_cast<int64_t>(i) * p.n + jd) * p.V : nullptr;
-  const int per = (p.V + ACCEPT_THREADS - 1) / ACCEPT_THREADS;
-  const int v0 = threadIdx.x * per, v1 = min(p.V, v0 + per);
-  double part = 0.0;
-  for (int v = v0; v < v1; ++v) {
-    float w = accept_prob(x, st, v, temp);
-    if (qv) w = fmaxf(w - qv[v], 0.f);
-    part += static_cast<double>(w);
+  for (int j = t; j < ni; j += ACCEPT_THREADS) {
+    const int64_t tok = p.drafted[static_cast<int64_t>(i) * p.n + j];
+    const float* xj = p.scores + (static_cast<int64_t>(i) * (p.n + 1) + j) * p.V;
+    const float* stj = p.stats + (static_cast<int64_t>(i) * (p.n + 1) + j) * 3;
+    const bool in = tok >= 0 && tok < p.V;
+    const float pj = in ? accept_prob(xj, stj, static_cast<int>(tok), temp) : 0.f;
+    const float qj = in ? p.q[(static_cast<int64_t>(i) * p.n + j) * p.V + tok] : 0.f;
+    if (!(p.uniforms[static_cast<int64_t>(i) * p.n + j] * qj < pj)) atomicMin(&s_pick[0], j);
   }
-  // block exclusive scan of the slices' sums (float64)
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  double incl = part;
+  __syncthreads();
+  const int kept = s_pick[0];
+  const int reject = kept < ni ? kept : -1;
+  for (int j = t; j < kept; j += ACCEPT_THREADS) tokens[j] = p.drafted[static_cast<int64_t>(i) * p.n + j];
+  const float* st = p.stats + (static_cast<int64_t>(i) * (p.n + 1) + kept) * 3;
+  DrawRow row;
+  row.x = p.scores + (static_cast<int64_t>(i) * (p.n + 1) + kept) * p.V;
+  row.qv = reject >= 0 ? p.q + (static_cast<int64_t>(i) * p.n + kept) * p.V : nullptr;
+  row.m = st[0];
+  row.rz = 1.f / st[1];
+  row.thr = st[2];
+  row.temp = temp;
+  const int chunks = (p.V + DRAW_CHUNK - 1) / DRAW_CHUNK;
+  // each warp sums its chunks, two at a time: lane l takes entries 8l .. 8l + 7
+  for (int c = warp; c < chunks; c += 2 * WARPS) {
+    double part[2];
+#pragma unroll
+    for (int u = 0; u < 2; ++u) {
+      const int v0 = (c + u * WARPS) * DRAW_CHUNK + 8 * lane;
+      float w[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) w[e] = v0 + e < p.V ? row.weight(v0 + e) : 0.f;
+      part[u] = 0.0;
+#pragma unroll
+      for (int e = 0; e < 8; ++e) part[u] += static_cast<double>(w[e]);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      part[0] += __shfl_xor_sync(0xffffffffu, part[0], o);
+      part[1] += __shfl_xor_sync(0xffffffffu, part[1], o);
+    }
+    if (lane == 0) {
+      s_chunk[c] = part[0];
+      if (c + WARPS < chunks) s_chunk[c + WARPS] = part[1];
+    }
+  }
+  __syncthreads();
+  // block scan over the chunk sums: thread t takes chunks [t * per, (t + 1) * per)
+  const int per = (chunks + ACCEPT_THREADS - 1) / ACCEPT_THREADS;
+  const int c0 = t * per, c1 = min(chunks, c0 + per);
+  double mine = 0.0;
+  for (int c = c0; c < c1; ++c) mine += s_chunk[c];
+  double incl = mine;
 #pragma unroll
   for (int o = 1; o < 32; o <<= 1) {
     const double y = __shfl_up_sync(0xffffffffu, incl, o);
@@ -243,34 +318,65 @@ __global__ void __launch_bounds__(ACCEPT_THREADS) accept_draw_kernel(const Accep
   if (lane == 31) s_scan[warp] = incl;
   __syncthreads();
   if (warp == 0) {
-    double w = lane < ACCEPT_THREADS / 32 ? s_scan[lane] : 0.0;
+    double w = lane < WARPS ? s_scan[lane] : 0.0;
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
       const double y = __shfl_up_sync(0xffffffffu, w, o);
       if (lane >= o) w += y;
     }
-    if (lane < ACCEPT_THREADS / 32) s_scan[lane] = w;
+    if (lane < WARPS) s_scan[lane] = w;
   }
-  if (threadIdx.x == 0) s_pick[1] = p.V - 1;
   __syncthreads();
-  const double before = (warp > 0 ? s_scan[warp - 1] : 0.0) + incl - part;
-  const double total = s_scan[ACCEPT_THREADS / 32 - 1];
+  const double total = s_scan[WARPS - 1];
   const double target = static_cast<double>(p.resample[i]) * total;
-  if (before <= target && before + part > target) {  // the crossing is in this slice
-    double cs = before;
-    for (int v = v0; v < v1; ++v) {
-      float w = accept_prob(x, st, v, temp);
-      if (qv) w = fmaxf(w - qv[v], 0.f);
-      cs += static_cast<double>(w);
-      if (cs > target) {
-        s_pick[1] = v;
+  double before = (warp > 0 ? s_scan[warp - 1] : 0.0) + incl - mine;
+  if (c0 < c1 && before <= target && before + mine > target) {  // the crossing is in one of these chunks
+    for (int c = c0; c < c1; ++c) {
+      if (before + s_chunk[c] > target) {
+        s_pick[2] = c;
+        s_scan[32] = before;
         break;
+      }
+      before += s_chunk[c];
+    }
+  }
+  __syncthreads();
+  // one warp walks the crossing chunk
+  if (warp == 0 && (total > target)) {
+    const int c = s_pick[2];
+    if (c >= 0) {
+      const int v0 = c * DRAW_CHUNK + 8 * lane;
+      double w8[8];
+      double part = 0.0;
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        w8[e] = v0 + e < p.V ? static_cast<double>(row.weight(v0 + e)) : 0.0;
+        part += w8[e];
+      }
+      double lincl = part;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const double y = __shfl_up_sync(0xffffffffu, lincl, o);
+        if (lane >= o) lincl += y;
+      }
+      double cs = s_scan[32] + lincl - part;
+      const unsigned hit = __ballot_sync(0xffffffffu, cs <= target && cs + part > target);
+      if (hit != 0 && lane == __ffs(hit) - 1) {
+        int pick = v0 + 7;
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          cs += w8[e];
+          if (cs > target) {
+            pick = v0 + e;
+            break;
+          }
+        }
+        s_pick[1] = pick < p.V ? pick : p.V - 1;
       }
     }
   }
   __syncthreads();
-  if (threadIdx.x == 0) {
-    const int kept = reject >= 0 ? reject : ni;
+  if (t == 0) {
     tokens[kept] = s_pick[1];
     for (int j = kept + 1; j <= p.n; ++j) tokens[j] = -1;
     p.accepted[i] = kept;

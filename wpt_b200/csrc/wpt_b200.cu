@@ -479,6 +479,7 @@ extern "C" int wpt_accept(const float* scores, const int64_t* drafted, const flo
   if (R == 0) return WPT_OK;
   if (R > 65535 || n + 1 > 65535) return fail(WPT_ERR_UNSUPPORTED, "accept grid too large (R=%d, n=%d)", R, n);
   if (!(temperature > 0.f)) return fail(WPT_ERR_INVALID, "temperature must be positive");
+  if (V > 48 * 1024 / 8 * 256) return fail(WPT_ERR_UNSUPPORTED, "vocabulary of %d entries exceeds 1,572,864", V);
   if (!scores || !stats || !tokens || !accepted || !resample || (n > 0 && (!drafted || !q || !uniforms)))
     return fail(WPT_ERR_INVALID, "a required pointer is NULL");
   wpt::AcceptParams p;
@@ -500,7 +501,8 @@ extern "C" int wpt_accept(const float* scores, const int64_t* drafted, const flo
   wpt::accept_stats_kernel<<<dim3(n + 1, R), wpt::ACCEPT_THREADS, 0, s>>>(p);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "accept_stats_kernel launch");
-  wpt::accept_draw_kernel<<<R, wpt::ACCEPT_THREADS, 0, s>>>(p);
+  const int draw_smem = (V + wpt::DRAW_CHUNK - 1) / wpt::DRAW_CHUNK * 8;  // one float64 per chunk
+  wpt::accept_draw_kernel<<<R, wpt::ACCEPT_THREADS, draw_smem, s>>>(p);
   e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "accept_draw_kernel launch");
   return WPT_OK;
