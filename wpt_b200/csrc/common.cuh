@@ -334,6 +334,22 @@ __device__ __forceinline__ void setmaxnreg_inc() {
   asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;\n" ::"n"(N) : "memory");
 }
 
+// Named barrier over `count` threads that also ANDs a flag across them, so
+// that every thread leaves with the same decision (a wait that timed out in
+// one warp stops all of them together, none is left waiting at a barrier).
+__device__ __forceinline__ bool named_barrier_and(int id, int count, bool flag) {
+  uint32_t out;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.u32 p, %1, 0;\n\t"
+      "barrier.red.and.pred q, %2, %3, p;\n\t"
+      "selp.u32 %0, 1, 0, q;\n\t}\n"
+      : "=r"(out)
+      : "r"(flag ? 1u : 0u), "r"(id), "r"(count)
+      : "memory");
+  return out != 0;
+}
+
 // Named barrier over `count` threads (a multiple of 32) of this CTA.
 __device__ __forceinline__ void named_barrier(int id, int count) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");

@@ -387,9 +387,9 @@ __global__ void __launch_bounds__(STREAM_THREADS, 1)
     bool ok = true;
     for (int j = 0; j < ntiles; ++j) {
       const int st = j % STAGES;
+      // a failed wait is carried to the tile's first barrier, where the four warps agree on it
       if constexpr (GATHER) ok = __all_sync(0xffffffffu, mbar_wait(full + st, (j / STAGES) & 1, p.status));
       if (ok) ok = __all_sync(0xffffffffu, mbar_wait(s_full + (j & 1), (j >> 1) & 1, p.status));
-      if (!ok) break;
       tc_fence_after();
       float s[NCOL];
       {
@@ -435,7 +435,8 @@ __global__ void __launch_bounds__(STREAM_THREADS, 1)
         const float m = transpose_reduce32(tmp, MaxOp());
         if (c32 * 32 + lane < NCOL) s_red[warp * 64 + c32 * 32 + lane] = m;
       }
-      named_barrier(1, 128);
+      ok = named_barrier_and(1, 128, ok);
+      if (!ok) break;
       if (r < NCOL) {
         const float tmax = fmaxf(fmaxf(s_red[r], s_red[64 + r]), fmaxf(s_red[128 + r], s_red[192 + r]));
         const float mo = s_m[r];
@@ -468,8 +469,10 @@ __global__ void __launch_bounds__(STREAM_THREADS, 1)
         any |= areg[c] != 1.f;
       }
       if (any && j > 0) {  // every thread read the same alphas: uniform
-        ok = __all_sync(0xffffffffu, mbar_wait(o_done, (j - 1) & 1, p.status));
-        if (!ok) break;
+        // (a failed wait skips the rescale; the next tile's barrier stops every warp)
+        ok = __all_sync(0xffffffffu, mbar_wait(o_done, (j - 1) & 1, p.status)) && ok;
+      }
+      if (ok && any && j > 0) {
         tc_fence_after();
         if constexpr (NCOL == 16) {
           uint32_t x[16];
