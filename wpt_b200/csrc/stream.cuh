@@ -287,11 +287,12 @@ __global__ void __launch_bounds__(STREAM_THREADS, 1)
             }
             ok = mbar_wait(kv_empty + st, parity, p.status);
           }
-          if (!ok) break;
         }
+        // a failed wait is carried to the barrier below, where the two loader
+        // warps agree on it, and the stage's rows are left alone
         int* rows = s_row + st * BN;
   #pragma unroll
-        for (int half = 0; half < 2; ++half) {
+        for (int half = 0; half < 2 && ok; ++half) {
           const int i = lt + half * 64;
           const int64_t slot = (tile0 + j) * BN + i;
           int64_t row = -1;
@@ -307,7 +308,8 @@ __global__ void __launch_bounds__(STREAM_THREADS, 1)
           }
           rows[i] = static_cast<int>(row);
         }
-        named_barrier(2, STREAM_LOADERS);
+        ok = named_barrier_and(2, STREAM_LOADERS, ok);
+        if (!ok) break;
         const uint32_t dk = smem_u32(sK + st * L::KV_BYTES), dv = smem_u32(sV + st * L::KV_BYTES);
   #pragma unroll 4
         for (int it = 0; it < (BN * 16) / STREAM_LOADERS; ++it) {
