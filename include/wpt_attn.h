@@ -92,6 +92,11 @@ int wpt_attn_prefill(const void* q, const void* k, const void* v, int64_t k_stri
  *                splits * chunk_tiles * 128 are not read, so splits must
  *                cover the longest row. splits > 1 needs part_o
  *                (splits, B*T*H, C) and part_lse (splits, B*T*H) fp32 scratch.
+ *   out == lse == NULL with splits > 1: the call stops at the partials
+ *                (each split's output normalised by its own sum, and the
+ *                natural log of that sum; no sink), for a caller that merges
+ *                them with other partials (wpt_attn_merge), e.g. those of
+ *                the other GPUs holding the rest of a long row.
  *   C must be 128 and H at most 64.
  */
 int wpt_attn_decode(const void* q, const void* k, const void* v, int64_t k_stride_b, int64_t k_stride_n,

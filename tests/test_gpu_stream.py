@@ -171,3 +171,21 @@ def test_decode_growing_scores_force_rescales(wb):
         ref_out, ref_lse, _ = oat.exact_attention(_np(q), _np(e[..., :C]), _np(e[..., C:]), positions.numpy(),
                                                   C ** -0.5, 0, 0)
         _check(wb, out, lse, ref_out, ref_lse)
+
+
+def test_partials_merged_by_the_caller_equal_the_whole_call(wb):
+    # out = lse = NULL: the kernel stops at its split partials; merging two
+    # halves' partials (as two GPUs of a long row would) gives the whole row
+    from wpt_b200 import ops
+    q, e, positions = _decode_case(1, 1, 32, 20000, seed=7, lengths=torch.tensor([19999]))
+    C = 128
+    qd, ed, pd = q.cuda(), e.cuda(), positions.cuda()
+    half = 10240
+    parts = [ops.stream_partials(qd, ed[:, a:b, :C], ed[:, a:b, C:], pd - a, C ** -0.5)
+             for a, b in ((0, half), (half, 20000))]
+    part_o = torch.cat([p[0] for p in parts])
+    part_lse = torch.cat([p[1] for p in parts])
+    out, lse = ops.merge_partials(part_o, part_lse, 32)
+    ref_out, ref_lse, _ = oat.exact_attention(_np(q), _np(e[..., :C]), _np(e[..., C:]), positions.numpy(),
+                                              C ** -0.5, 0, 0)
+    _check(wb, out.reshape(1, 1, 32, C), lse.reshape(1, 1, 32), ref_out, ref_lse)

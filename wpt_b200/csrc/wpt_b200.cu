@@ -351,7 +351,10 @@ extern "C" int wpt_attn_decode(const void* q, const void* k, const void* v, int6
   if (splits > 1 && (part_o == nullptr || part_lse == nullptr))
     return fail(WPT_ERR_INVALID, "splits > 1 needs part_o and part_lse scratch");
   if (idx != nullptr && K < 0) return fail(WPT_ERR_INVALID, "K must be >= 0");
-  if (!q || !k || !v || !positions || !out || !lse) return fail(WPT_ERR_INVALID, "a required pointer is NULL");
+  // out and lse both NULL with splits > 1: partials only, merged by the caller
+  const bool partials_only = splits > 1 && out == nullptr && lse == nullptr;
+  if (!q || !k || !v || !positions || ((!out || !lse) && !partials_only))
+    return fail(WPT_ERR_INVALID, "a required pointer is NULL");
   if (!aligned16(q) || !aligned16(k) || !aligned16(v)) return fail(WPT_ERR_INVALID, "q, k, v must be 16-byte aligned");
   if (k_stride_n % 8 || v_stride_n % 8 || (B > 1 && (k_stride_b % 8 || v_stride_b % 8)))
     return fail(WPT_ERR_INVALID, "key/value strides must be multiples of 8 elements");
@@ -400,7 +403,7 @@ extern "C" int wpt_attn_decode(const void* q, const void* k, const void* v, int6
   const int rc = gather ? launch_stream_g<true>(tk, tv, p, ncol, static_cast<int>(groups), s)
                         : launch_stream_g<false>(tk, tv, p, ncol, static_cast<int>(groups), s);
   if (rc) return rc;
-  if (splits > 1) {
+  if (splits > 1 && !partials_only) {
     const int64_t rows = static_cast<int64_t>(B) * T * H;
     return launch_merge<128>(part_o, part_lse, splits, rows, rows, H, sink, out, lse, s);
   }

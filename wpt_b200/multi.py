@@ -65,8 +65,19 @@ def long_decode(q, k_shard, v_shard, shard_start, positions, scale, sink=None, g
     B, T, H, C = q.shape
     world = dist.get_world_size(group) if dist.is_initialized() else 1
     local = positions - shard_start  # rows of this shard the query sees: 0 .. local (none when negative)
-    if world == 1 and partial is None and merge is None:  # the whole row is here: one kernel call
-        return ops.stream_forward(q, k_shard, v_shard, local, scale, sink=sink)
+    if partial is None and merge is None:
+        if world == 1:  # the whole row is here: one kernel call
+            return ops.stream_forward(q, k_shard, v_shard, local, scale, sink=sink)
+        # the kernel's own split partials go straight into the collective and
+        # one merge combines every rank's splits (no local merge, no copies)
+        part_o, part_lse = ops.stream_partials(q, k_shard, v_shard, local, scale)
+        S = part_o.shape[0]
+        parts_o = torch.empty(world * S, B * T * H, C, dtype=torch.float32, device=q.device)
+        parts_s = torch.empty(world * S, B * T * H, dtype=torch.float32, device=q.device)
+        dist.all_gather_into_tensor(parts_o, part_o, group=group)
+        dist.all_gather_into_tensor(parts_s, part_lse, group=group)
+        merged, merged_lse = ops.merge_partials(parts_o, parts_s, H, sink)
+        return merged.reshape(B, T, H, C), merged_lse.reshape(B, T, H)
     partial = partial or (lambda q_, k_, v_, p_, s_: ops.stream_forward(q_, k_, v_, p_, s_))
     merge = merge or ops.merge_partials
     out, lse = partial(q, k_shard, v_shard, local, scale)

@@ -150,6 +150,35 @@ def stream_forward(q, k, v, positions, scale, window=0, floor=None, idx=None, si
     return out, lse
 
 
+def stream_partials(q, k, v, positions, scale, window=0):
+    """The key-stream kernel's split partials without the merge: (part_o
+    (S, B*T*H, C) fp32, each split's output normalised by its own sum;
+    part_lse (S, B*T*H) fp32, the natural log of that sum, -inf for a split
+    with no visible row), S >= 2. For callers that merge them with partials
+    computed elsewhere (merge_partials), e.g. on the other GPUs of a long row."""
+    _need_cuda(q, k, v, positions)
+    q = _bf16(q).contiguous()
+    k, v = _table(k), _table(v)
+    B, T, H, C = q.shape
+    N = k.shape[1]
+    positions = _rows(positions)
+    _, TQ = _stream_shape(T, H, False)
+    groups = B * math.ceil(T / TQ)
+    slots = min(N, window + TQ - 1) if window > 0 else N
+    tiles = max(1, math.ceil(slots / 128))
+    chunk_tiles = max(min(16, tiles), 16 * math.ceil(tiles * groups / (2 * SM_COUNT) / 16))
+    chunk_tiles = max(1, min(chunk_tiles, tiles))
+    splits = max(2, math.ceil(tiles / chunk_tiles))
+    part_o = torch.empty(splits, B * T * H, C, dtype=torch.float32, device=q.device)
+    part_lse = torch.empty(splits, B * T * H, dtype=torch.float32, device=q.device)
+    _lib.check(_lib.lib().wpt_attn_decode(
+        _lib.ptr(q), _lib.ptr(k), _lib.ptr(v), k.stride(0), k.stride(1), v.stride(0), v.stride(1),
+        _lib.ptr(positions), None, None, 0, None, None, None, _lib.ptr(part_o), _lib.ptr(part_lse), splits,
+        chunk_tiles, B, T, H, C, N, int(window), float(scale), _lib.stream(q.device)))
+    LAUNCHES[0] += 1
+    return part_o, part_lse
+
+
 def attention_forward(q, k, v, positions, scale, window=0, floor=None, sink=None):
     """Range attention by the kernel that suits the shape: the key-stream
     kernel for few queries per row, the prefill kernel otherwise."""
