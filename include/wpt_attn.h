@@ -32,6 +32,7 @@
 #ifndef WPT_ATTN_H_
 #define WPT_ATTN_H_
 
+#include <stddef.h>
 #include <stdint.h>
 
 #ifdef __cplusplus
@@ -173,13 +174,18 @@ int wpt_attn_merge(const float* part_o, const float* part_lse, int splits, int64
  *   scores    fp32 (R, n + 1, V) target logits at each draft's place and one after
  *   drafted   int64 (R, n);  q  fp32 (R, n, V) the drafter's probabilities
  *   lengths   int64 (R,) drafts verified per row, or NULL for n
- *   stats     fp32 (R, n + 1, 3) caller scratch
+ *   scratch   caller scratch of wpt_accept_scratch_bytes(R, n, V) bytes, 16-byte
+ *             aligned (segment statistics, chunk sums, per-row counters)
  *   tokens    int64 (R, n + 1): kept drafts then the drawn token, -1 padded
  *   accepted  int64 (R,): drafts kept per row
  */
 int wpt_accept(const float* scores, const int64_t* drafted, const float* q, const float* uniforms,
-               const float* resample, const int64_t* lengths, float* stats, int64_t* tokens, int64_t* accepted,
+               const float* resample, const int64_t* lengths, void* scratch, int64_t* tokens, int64_t* accepted,
                int R, int n, int V, float temperature, int top_k, void* stream);
+
+/* Bytes of scratch wpt_accept needs for R rows of n drafts over V entries
+ * (0 for a bad shape). */
+size_t wpt_accept_scratch_bytes(int R, int n, int V);
 
 #ifdef __cplusplus
 }

@@ -68,3 +68,25 @@ def test_rows_verifying_fewer_drafts(wb):
                                          resample.numpy(), 1.0, None, lengths=lengths.numpy())
     assert np.array_equal(accepted.cpu().numpy(), ref_accepted)
     assert np.array_equal(tokens.cpu().numpy(), ref_tokens)
+
+
+@pytest.mark.parametrize("V,temperature", [(1000, 1.0), (50257, 0.7), (152067, 1.0), (4096, 1.3)])
+def test_vocabularies_of_any_size(wb, V, temperature):
+    """Vocabularies that are not a multiple of the statistics segment, the
+    draw chunk or four entries (the scalar path), with masked (-inf) logits."""
+    g = torch.Generator().manual_seed(V)
+    R, n = 6, 5
+    scores = torch.randn(R, n + 1, V, generator=g) * 2.0
+    scores[:, :, V // 3: V // 3 + 17] = float("-inf")
+    q_logits = scores[:, :n] + 0.5 * torch.randn(R, n, V, generator=g)
+    q = torch.from_numpy(oa.probabilities(q_logits.numpy(), temperature, None))
+    drafted = torch.multinomial(q.reshape(-1, V), 1, generator=g).view(R, n)
+    uniforms = torch.rand(R, n, generator=g)
+    resample = torch.rand(R, generator=g)
+    tokens, accepted = wb.accept(scores.cuda(), drafted.cuda(), q.cuda(), uniforms.cuda(), resample.cuda(),
+                                 temperature, None)
+    ref_tokens, ref_accepted = oa.accept(scores.numpy(), drafted.numpy(), q.numpy(), uniforms.numpy(),
+                                         resample.numpy(), temperature, None)
+    assert np.array_equal(accepted.cpu().numpy(), ref_accepted)
+    assert np.array_equal(tokens.cpu().numpy(), ref_tokens)
+    assert wb.device_status() == 0

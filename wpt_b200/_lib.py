@@ -26,10 +26,13 @@ SIGNATURES = {
                         _I, _I, _I, _I, _I, _I, _F, _P],
     "wpt_attn_topk": [_P, _P, _I64, _I64, _P, _P, _P, _I64, _P, _I, _I, _I, _I, _I, _I, _I, _F, _P],
     "wpt_accept": [_P, _P, _P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _F, _I, _P],
+    "wpt_accept_scratch_bytes": [_I, _I, _I],
     "wpt_attn_decode_noalloc": [_P, _P, _P, _I64, _I64, _I64, _I64, _P, _P, _P, _I, _P, _P, _P, _I, _I, _I, _I,
                                 _I, _I, _I, _I, _F, _P],
     "wpt_attn_merge": [_P, _P, _I, _I64, _I64, _I, _I, _P, _P, _P, _P],
 }
+
+RESTYPES = {"wpt_last_error": ctypes.c_char_p, "wpt_accept_scratch_bytes": ctypes.c_size_t}
 
 _lib = None
 
@@ -48,7 +51,7 @@ def lib():
         for name, args in SIGNATURES.items():
             fn = getattr(handle, name)
             fn.argtypes = args
-            fn.restype = ctypes.c_char_p if name == "wpt_last_error" else ctypes.c_int
+            fn.restype = RESTYPES.get(name, ctypes.c_int)
         _lib = handle
     return _lib
 

@@ -1,5 +1,6 @@
 // The one translation unit of libwpt_b200.so: the kernels (headers beside
 // this file) and the extern "C" launchers declared in include/wpt_attn.h.
+#include <algorithm>
 #include <cstdarg>
 #include <cstdio>
 #include <cstdlib>
@@ -475,16 +476,23 @@ extern "C" int wpt_attn_topk(const void* q, const void* k, int64_t k_stride_b, i
   return WPT_OK;
 }
 
+extern "C" size_t wpt_accept_scratch_bytes(int R, int n, int V) {
+  if (R < 0 || n < 0 || V < 1) return 0;
+  return wpt::accept_scratch(R, n, V).bytes;
+}
+
 extern "C" int wpt_accept(const float* scores, const int64_t* drafted, const float* q, const float* uniforms,
-                          const float* resample, const int64_t* lengths, float* stats, int64_t* tokens,
+                          const float* resample, const int64_t* lengths, void* scratch, int64_t* tokens,
                           int64_t* accepted, int R, int n, int V, float temperature, int top_k, void* stream) {
   if (R < 0 || n < 0 || V < 1) return fail(WPT_ERR_INVALID, "bad accept shape R=%d n=%d V=%d", R, n, V);
   if (R == 0) return WPT_OK;
   if (R > 65535 || n + 1 > 65535) return fail(WPT_ERR_UNSUPPORTED, "accept grid too large (R=%d, n=%d)", R, n);
   if (!(temperature > 0.f)) return fail(WPT_ERR_INVALID, "temperature must be positive");
-  if (V > 48 * 1024 / 8 * 256) return fail(WPT_ERR_UNSUPPORTED, "vocabulary of %d entries exceeds 1,572,864", V);
-  if (!scores || !stats || !tokens || !accepted || !resample || (n > 0 && (!drafted || !q || !uniforms)))
+  if (!scores || !scratch || !tokens || !accepted || !resample || (n > 0 && (!drafted || !q || !uniforms)))
     return fail(WPT_ERR_INVALID, "a required pointer is NULL");
+  if (reinterpret_cast<uintptr_t>(scratch) % 16 != 0) return fail(WPT_ERR_INVALID, "accept scratch not 16-byte aligned");
+  const wpt::AcceptScratch layout = wpt::accept_scratch(R, n, V);
+  char* base = static_cast<char*>(scratch);
   wpt::AcceptParams p;
   p.scores = scores;
   p.drafted = drafted;
@@ -492,20 +500,49 @@ extern "C" int wpt_accept(const float* scores, const int64_t* drafted, const flo
   p.uniforms = uniforms;
   p.resample = resample;
   p.lengths = lengths;
-  p.stats = stats;
+  p.part = reinterpret_cast<float2*>(base + layout.part);
+  p.thr = reinterpret_cast<float*>(base + layout.thr);
+  p.chunk_sum = reinterpret_cast<double*>(base + layout.chunk_sum);
+  p.count = reinterpret_cast<unsigned*>(base + layout.count);
   p.tokens = tokens;
   p.accepted = accepted;
   p.R = R;
   p.n = n;
   p.V = V;
   p.top_k = top_k;
+  p.S = (V + wpt::STAT_SEG - 1) / wpt::STAT_SEG;
+  p.chunks = (V + wpt::DRAW_CHUNK - 1) / wpt::DRAW_CHUNK;
   p.temperature = temperature;
+  const int slices = (p.chunks + wpt::DRAW_CPS - 1) / wpt::DRAW_CPS;
+  if (slices > 65535) return fail(WPT_ERR_UNSUPPORTED, "vocabulary of %d entries is too large", V);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  wpt::accept_stats_kernel<<<dim3(n + 1, R), wpt::ACCEPT_THREADS, 0, s>>>(p);
-  cudaError_t e = cudaGetLastError();
-  if (e != cudaSuccess) return cuda_fail(e, "accept_stats_kernel launch");
-  const int draw_smem = (V + wpt::DRAW_CHUNK - 1) / wpt::DRAW_CHUNK * 8;  // one float64 per chunk
-  wpt::accept_draw_kernel<<<R, wpt::ACCEPT_THREADS, draw_smem, s>>>(p);
+  cudaError_t e;
+  if (top_k > 1 && top_k < V) {
+    wpt::accept_topk_stats_kernel<<<dim3(n + 1, R), wpt::ACCEPT_THREADS, 0, s>>>(p);
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return cuda_fail(e, "accept_topk_stats_kernel launch");
+  } else {
+    // a grid the SMs hold at once: its warps take the units in turn
+    const bool greedy = top_k == 1 && V > 1;
+    auto kernel = greedy ? wpt::accept_stats_kernel<true> : wpt::accept_stats_kernel<false>;
+    static int resident[2][64] = {};
+    int sms = 148;
+    const int dev = current_device(&sms);
+    if (resident[greedy][dev] == 0) {
+      int per_sm = 0;
+      e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, wpt::STAT_THREADS, 0);
+      if (e != cudaSuccess) return cuda_fail(e, "cudaOccupancyMaxActiveBlocksPerMultiprocessor");
+      resident[greedy][dev] = per_sm > 0 ? per_sm : 1;
+    }
+    const int64_t units = static_cast<int64_t>(R) * (n + 1) * p.S;
+    const int64_t want = (units + wpt::STAT_THREADS / 32 - 1) / (wpt::STAT_THREADS / 32);
+    const int blocks = static_cast<int>(
+        std::max<int64_t>(1, std::min<int64_t>(want, static_cast<int64_t>(sms) * resident[greedy][dev])));
+    kernel<<<blocks, wpt::STAT_THREADS, 0, s>>>(p);
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return cuda_fail(e, "accept_stats_kernel launch");
+  }
+  wpt::accept_draw_kernel<<<dim3(R, slices), wpt::DRAW_THREADS, 0, s>>>(p);
   e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "accept_draw_kernel launch");
   return WPT_OK;

@@ -265,12 +265,12 @@ def accept(scores, drafted, q, uniforms, resample, temperature=1.0, top_k=None, 
     uniforms = uniforms.float().contiguous()
     resample = resample.float().reshape(R).contiguous()
     lengths = None if lengths is None else lengths.to(torch.int64).contiguous()
-    stats = torch.empty(R, n + 1, 3, dtype=torch.float32, device=scores.device)
+    scratch = torch.empty(_lib.lib().wpt_accept_scratch_bytes(R, n, V), dtype=torch.uint8, device=scores.device)
     tokens = torch.empty(R, n + 1, dtype=torch.int64, device=scores.device)
     accepted = torch.empty(R, dtype=torch.int64, device=scores.device)
     _lib.check(_lib.lib().wpt_accept(
         _lib.ptr(scores), _lib.ptr(drafted), _lib.ptr(q), _lib.ptr(uniforms), _lib.ptr(resample), _lib.ptr(lengths),
-        _lib.ptr(stats), _lib.ptr(tokens), _lib.ptr(accepted), R, n, V, float(temperature),
+        _lib.ptr(scratch), _lib.ptr(tokens), _lib.ptr(accepted), R, n, V, float(temperature),
         0 if top_k is None else int(top_k), _lib.stream(scores.device)))
     LAUNCHES[0] += 2
     return tokens, accepted
