@@ -90,3 +90,29 @@ def test_vocabularies_of_any_size(wb, V, temperature):
     assert np.array_equal(accepted.cpu().numpy(), ref_accepted)
     assert np.array_equal(tokens.cpu().numpy(), ref_tokens)
     assert wb.device_status() == 0
+
+
+@pytest.mark.parametrize("V,top_k,tied", [(1000, 5, False), (65536, 1500, False), (65536, 40, True),
+                                          (32000, 200, False)])
+def test_top_k_thresholds(wb, V, top_k, tied):
+    """The top-k threshold's paths: a bound from the thread maxima and a
+    sort of the few entries above it; and the radix passes over the whole
+    row when top_k exceeds the thread count or thousands of entries tie
+    (logits rounded to halves) at the bound."""
+    g = torch.Generator().manual_seed(top_k)
+    R, n = 4, 6
+    scores = torch.randn(R, n + 1, V, generator=g) * 2.0
+    if tied:
+        scores = torch.round(scores * 2.0) / 2.0
+    q_logits = scores[:, :n] + 0.5 * torch.randn(R, n, V, generator=g)
+    q = torch.from_numpy(oa.probabilities(q_logits.numpy(), 0.9, top_k))
+    drafted = torch.multinomial(q.reshape(-1, V), 1, generator=g).view(R, n)
+    uniforms = torch.rand(R, n, generator=g)
+    resample = torch.rand(R, generator=g)
+    tokens, accepted = wb.accept(scores.cuda(), drafted.cuda(), q.cuda(), uniforms.cuda(), resample.cuda(),
+                                 0.9, top_k)
+    ref_tokens, ref_accepted = oa.accept(scores.numpy(), drafted.numpy(), q.numpy(), uniforms.numpy(),
+                                         resample.numpy(), 0.9, top_k)
+    assert np.array_equal(accepted.cpu().numpy(), ref_accepted)
+    assert np.array_equal(tokens.cpu().numpy(), ref_tokens)
+    assert wb.device_status() == 0

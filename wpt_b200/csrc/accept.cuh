@@ -17,14 +17,15 @@
 // HBM through every SM with no tail of whole rows. top_k 1 (greedy) keeps
 // the maxima: the units reduce to (maximum, count of maxima). A larger
 // top_k's threshold needs the position's whole row: one CTA per
-// (row, position) finds it by a 4 x 8-bit radix select (ties kept, as
-// `scores < v[..., [-1]]` keeps them) and writes the row's (m, Z) as its
-// first segment. The draw: DRAW_CPS-chunk slices of each row, one CTA per
-// slice. Every CTA of a row makes the row's decisions (one warp per draft,
-// the first rejection by an atomic minimum; all CTAs get the same answer),
-// sums its slice of the draw's weights in DRAW_CHUNK-entry float64 chunk
-// sums, and the row's last CTA to finish (an arrival counter) scans the
-// chunk sums to the crossing chunk and walks it to the entry with one warp.
+// (row, position) finds it (ties kept, as `scores < v[..., [-1]]` keeps
+// them), reduces the kept x to (m, Z) and makes the draft's accept test.
+// Of the segment units, the last of a position to finish (an arrival
+// counter) combines its segments into (m, Z) and makes the accept test.
+// The draw: DRAW_CPS-chunk slices of each row, one CTA per slice. Every CTA
+// of a row finds the first failed test, sums its slice of the draw's
+// weights in DRAW_CHUNK-entry float64 chunk sums, and the row's last CTA to
+// finish (an arrival counter) scans the chunk sums to the crossing chunk and
+// walks it to the entry with one warp.
 #pragma once
 
 #include <type_traits>
@@ -49,9 +50,13 @@ struct AcceptParams {
   const float* resample;  // (R,)
   const int64_t* lengths; // (R,) drafts verified per row, or null (all n)
   float2* part;           // (R, n + 1, S) scratch: each segment's (maximum, sum of exp(x - maximum))
-  float* thr;             // (R, n + 1) scratch: the top_k-th largest x (top-k mode)
+  float2* pos_stat;       // (R, n + 1) scratch: each position's (m, Z)
+  float* thr;             // (R, n + 1) scratch: each position's threshold (top-k and greedy modes)
+  int* keep;              // (R, n + 1) scratch: draft j's accept test passed (j < drafts of the row)
   double* chunk_sum;      // (R, chunks) scratch: the draw's chunk sums
-  unsigned* count;        // (R,) scratch: draw CTAs of the row that finished
+  unsigned* pos_count;    // (R, n + 1) scratch, zeroed before the launches: segments of the position done
+  unsigned* count;        // (R,) scratch, zeroed before the launches: draw CTAs of the row done
+  unsigned long long* ticket;  // scratch, zeroed before the launches: statistics units taken
   int64_t* tokens;        // (R, n + 1), -1 padded
   int64_t* accepted;      // (R,)
   int R, n, V, top_k;
@@ -62,7 +67,7 @@ struct AcceptParams {
 // Byte offsets of the scratch regions inside the caller's buffer (each
 // region 256-byte aligned); the last value is the buffer's size.
 struct AcceptScratch {
-  size_t part, thr, chunk_sum, count, bytes;
+  size_t part, pos_stat, thr, keep, chunk_sum, pos_count, count, ticket, bytes;
 };
 inline size_t accept_align(size_t x) { return (x + 255) / 256 * 256; }
 inline AcceptScratch accept_scratch(int R, int n, int V) {
@@ -71,10 +76,14 @@ inline AcceptScratch accept_scratch(int R, int n, int V) {
   const size_t chunks = (static_cast<size_t>(V) + DRAW_CHUNK - 1) / DRAW_CHUNK;
   AcceptScratch a;
   a.part = 0;
-  a.thr = a.part + accept_align(positions * S * sizeof(float2));
-  a.chunk_sum = a.thr + accept_align(positions * sizeof(float));
-  a.count = a.chunk_sum + accept_align(static_cast<size_t>(R) * chunks * sizeof(double));
-  a.bytes = a.count + accept_align(static_cast<size_t>(R) * sizeof(unsigned));
+  a.pos_stat = a.part + accept_align(positions * S * sizeof(float2));
+  a.thr = a.pos_stat + accept_align(positions * sizeof(float2));
+  a.keep = a.thr + accept_align(positions * sizeof(float));
+  a.chunk_sum = a.keep + accept_align(positions * sizeof(int));
+  a.pos_count = a.chunk_sum + accept_align(static_cast<size_t>(R) * chunks * sizeof(double));
+  a.count = a.pos_count + positions * sizeof(unsigned);  // the counters are one zeroed range
+  a.ticket = (a.count + static_cast<size_t>(R) * sizeof(unsigned) + 7) / 8 * 8;
+  a.bytes = accept_align(a.ticket + sizeof(unsigned long long));
   return a;
 }
 
@@ -180,29 +189,83 @@ __device__ __forceinline__ void accept_stat_batch(float& m, float& z, const floa
   z += acc;
 }
 
-// Top-k mode: one CTA per (row, position) selects the threshold and reduces
-// the kept x of the whole row; the row's (m, Z) becomes segment 0 and the
-// other segments are empty.
-__global__ void __launch_bounds__(ACCEPT_THREADS) accept_topk_stats_kernel(const AcceptParams p) {
-  __shared__ uint32_t s_hist[256];
-  __shared__ float s_red[33];
-  __shared__ uint32_t s_sel[2];
-  const int j = blockIdx.x, i = blockIdx.y;
-  if (blockIdx.x == 0 && blockIdx.y == 0)
-    for (int r = threadIdx.x; r < p.R; r += blockDim.x) p.count[r] = 0u;
-  const int ni = accept_row_drafts(p, i);
-  if (j > ni) return;
-  const int64_t ij = static_cast<int64_t>(i) * (p.n + 1) + j;
-  const float* x = p.scores + ij * p.V;
-  const float temp = p.temperature;
-  // the top_k-th largest x (radix select over order keys)
+// The statistics (m, Z) of position ij from its S segments, by one warp:
+// the maximum, then the segments' sums rescaled to it (greedy: the counts
+// of the segments whose maximum is it), summed in a fixed order and
+// broadcast from lane 0, so every warp of every CTA gets the same bits for
+// the same position.
+__device__ __forceinline__ float2 accept_position_stats(const AcceptParams& p, int64_t ij, int lane) {
+  const float2* part = p.part + ij * p.S;
+  float m = -INFINITY;
+  for (int s = lane; s < p.S; s += 32) m = fmaxf(m, __ldcg(&part[s]).x);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+  float z = 0.f;
+  if (accept_greedy(p)) {
+    for (int s = lane; s < p.S; s += 32) {
+      const float2 e = __ldcg(&part[s]);
+      z += e.x == m ? e.y : 0.f;
+    }
+  } else if (m != -INFINITY) {
+    for (int s = lane; s < p.S; s += 32) {
+      const float2 e = __ldcg(&part[s]);
+      z += e.y * expf(e.x - m);
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) z += __shfl_xor_sync(0xffffffffu, z, o);
+  return make_float2(m, __shfl_sync(0xffffffffu, z, 0));
+}
+
+// x / temperature as the reference's float32 division gives it, from the
+// reciprocal r = 1 / t (correctly rounded) and Markstein's correction of
+// the product: q0 = x r, then q0 + (x - q0 t) r with the remainder exact by
+// fma (P. Markstein, IBM J. Res. Dev. 34(1), 1990). An infinite or NaN q0
+// (masked -inf logits) is the quotient itself.
+struct TempScale {
+  float t, r;
+  bool unit;
+  __device__ __forceinline__ float operator()(float x) const {
+    if (unit) return x;
+    const float q0 = x * r;
+    const float y = fmaf(fmaf(-q0, t, x), r, q0);
+    return fabsf(q0) < INFINITY ? y : q0;
+  }
+};
+__device__ __forceinline__ TempScale temp_scale(float t) {
+  TempScale s;
+  s.t = t;
+  s.r = 1.f / t;
+  s.unit = t == 1.f;
+  return s;
+}
+
+// Draft j's accept test, u_j q_j[tok] < p_j[tok], from its position's
+// statistics: p_j[tok] = exp(y - m) / Z when y = x[tok] / temperature
+// passes the threshold, else 0. A token outside the vocabulary fails.
+__device__ __forceinline__ int accept_test(const AcceptParams& p, int64_t ij, int i, int j, float m, float z,
+                                           float thr) {
+  const int64_t tok = p.drafted[static_cast<int64_t>(i) * p.n + j];
+  float pj = 0.f, qj = 0.f;
+  if (tok >= 0 && tok < p.V) {
+    const float y = temp_scale(p.temperature)(p.scores[ij * p.V + tok]);
+    pj = y >= thr ? expf(y - m) / z : 0.f;
+    qj = p.q[(static_cast<int64_t>(i) * p.n + j) * p.V + tok];
+  }
+  return p.uniforms[static_cast<int64_t>(i) * p.n + j] * qj < pj ? 1 : 0;
+}
+
+// The k-th largest of n order keys get(0) .. get(n - 1) by four 8-bit radix
+// passes (every thread of the block calls it).
+template <typename Get>
+__device__ uint32_t block_radix_kth(Get get, int n, int k, uint32_t* s_hist, uint32_t* s_sel) {
   uint32_t prefix = 0, mask = 0;
-  int remaining = p.top_k;
+  int remaining = k;
   for (int shift = 24; shift >= 0; shift -= 8) {
     for (int b = threadIdx.x; b < 256; b += blockDim.x) s_hist[b] = 0;
     __syncthreads();
-    for (int v = threadIdx.x; v < p.V; v += blockDim.x) {
-      const uint32_t key = accept_key(x[v] / temp);
+    for (int v = threadIdx.x; v < n; v += blockDim.x) {
+      const uint32_t key = get(v);
       if ((key & mask) == prefix) atomicAdd(&s_hist[(key >> shift) & 255u], 1u);
     }
     __syncthreads();
@@ -241,76 +304,181 @@ __global__ void __launch_bounds__(ACCEPT_THREADS) accept_topk_stats_kernel(const
     remaining -= static_cast<int>(s_sel[1]);
     __syncthreads();
   }
-  const float thr = accept_unkey(prefix);
-  // the maximum and the sum of exp(x - m) over the kept x: a running
-  // (maximum, sum) per thread, rescaled when its maximum rises
-  float m = -INFINITY, z = 0.f;
-  for (int v = threadIdx.x; v < p.V; v += blockDim.x) {
-    const float y = x[v] / temp;
-    if (!(y >= thr)) continue;
-    if (y > m) {
-      z = z * expf(m - y) + 1.f;
-      m = y;
-    } else {
-      z += expf(y - m);
+  return prefix;
+}
+
+// Top-k mode (1 < top_k < V): one CTA per (row, position). Pass 1 takes
+// each thread's maximum of its strided share of x and the row's maximum m;
+// the top_k-th largest thread maximum t0 is a lower bound of the threshold
+// (the maxima are some of the x). Pass 2 (from L2) gathers every x >= t0
+// into shared memory, usually about top_k of them; a bitonic sort of their
+// keys gives the threshold (the top_k-th largest, ties kept as
+// `scores < v[..., [-1]]` keeps them) and Z = sum of exp(x - m) over the
+// kept x, summed in sorted order. When more than TOPK_CAND pass t0 (or
+// top_k exceeds the thread count), the threshold comes from radix passes
+// over the whole row and (m, Z) from one more pass. The CTA writes the
+// position's (m, Z), threshold and accept test.
+constexpr int TOPK_CAND = 2048;
+__global__ void __launch_bounds__(ACCEPT_THREADS) accept_topk_stats_kernel(const AcceptParams p) {
+  __shared__ uint32_t s_hist[256];
+  __shared__ float s_red[33];
+  __shared__ uint32_t s_sel[2];
+  __shared__ uint32_t s_keys[TOPK_CAND];
+  __shared__ int s_count;
+  const int j = blockIdx.x, i = blockIdx.y, t = threadIdx.x;
+  griddep_launch();
+  const int ni = accept_row_drafts(p, i);
+  if (j > ni) return;
+  const int64_t ij = static_cast<int64_t>(i) * (p.n + 1) + j;
+  const float* x = p.scores + ij * p.V;
+  const float temp = p.temperature;
+  const TempScale scale = temp_scale(temp);
+  auto y_at = [&](int v) { return scale(x[v]); };
+  const int k = p.top_k;
+  if (t == 0) s_count = 0;
+  // pass 1: thread maxima and the row maximum
+  float tm = -INFINITY;
+  for (int v = t; v < p.V; v += ACCEPT_THREADS) tm = fmaxf(tm, y_at(v));
+  const float m = block_max(tm, s_red);
+  bool fast = k <= ACCEPT_THREADS;
+  int count = 0;
+  if (fast) {
+    s_keys[t] = accept_key(tm);
+    __syncthreads();
+    const float t0 = accept_unkey(block_radix_kth([&](int v) { return s_keys[v]; }, ACCEPT_THREADS, k, s_hist, s_sel));
+    // pass 2: every x at or above the bound (compared as floats, as the mask compares)
+    for (int v = t; v < p.V; v += ACCEPT_THREADS) {
+      const float y = y_at(v);
+      if (y >= t0) {
+        const int at = atomicAdd(&s_count, 1);
+        if (at < TOPK_CAND) s_keys[at] = accept_key(y);
+      }
     }
+    __syncthreads();
+    count = s_count;
+    fast = count <= TOPK_CAND;
   }
-  const float mb = block_max(m, s_red);
-  z = block_sum(m == -INFINITY ? 0.f : z * expf(m - mb), s_red);
-  for (int s = threadIdx.x; s < p.S; s += blockDim.x)
-    p.part[ij * p.S + s] = s == 0 ? make_float2(mb, z) : make_float2(-INFINITY, 0.f);
-  if (threadIdx.x == 0) p.thr[ij] = thr;
+  float thr, z;
+  if (fast) {
+    int size = 2;
+    while (size < count) size <<= 1;
+    for (int e = count + t; e < size; e += ACCEPT_THREADS) s_keys[e] = 0u;  // below every key
+    __syncthreads();
+    // bitonic sort, descending
+    for (int span = 2; span <= size; span <<= 1) {
+      for (int stride = span >> 1; stride > 0; stride >>= 1) {
+        for (int pr = t; pr < size / 2; pr += ACCEPT_THREADS) {
+          const int a = 2 * stride * (pr / stride) + (pr % stride), b = a + stride;
+          const uint32_t ka = s_keys[a], kb = s_keys[b];
+          const bool desc = (a & span) == 0;
+          if (desc ? ka < kb : ka > kb) {
+            s_keys[a] = kb;
+            s_keys[b] = ka;
+          }
+        }
+        __syncthreads();
+      }
+    }
+    thr = accept_unkey(s_keys[k - 1]);
+    float part = 0.f;
+    for (int e = t; e < count; e += ACCEPT_THREADS) {
+      const float y = accept_unkey(s_keys[e]);
+      if (y >= thr) part += expf(y - m);
+    }
+    z = block_sum(part, s_red);
+  } else {
+    thr = accept_unkey(block_radix_kth([&](int v) { return accept_key(y_at(v)); }, p.V, k, s_hist, s_sel));
+    // the sum of exp(x - m) over the kept x: a running (maximum, sum) per
+    // thread, rescaled when its maximum rises
+    float tmax = -INFINITY, tz = 0.f;
+    for (int v = t; v < p.V; v += ACCEPT_THREADS) {
+      const float y = y_at(v);
+      if (!(y >= thr)) continue;
+      if (y > tmax) {
+        tz = tz * expf(tmax - y) + 1.f;
+        tmax = y;
+      } else {
+        tz += expf(y - tmax);
+      }
+    }
+    z = block_sum(tmax == -INFINITY ? 0.f : tz * expf(tmax - m), s_red);
+  }
+  if (t == 0) {
+    p.pos_stat[ij] = make_float2(m, z);
+    p.thr[ij] = thr;
+    if (j < ni) p.keep[ij] = accept_test(p, ij, i, j, m, z, thr);
+  }
 }
 
 // Segment statistics: warp w of the grid reduces units w, w + warps, ...;
 // unit u is segment u % S of position u / S. Lane l reads 16-byte vectors
 // l, l + 32, ... of the segment, four in flight, in batches of 16 values.
-template <bool GREEDY>
+template <bool GREEDY, bool UNIT_TEMP>
 __global__ void __launch_bounds__(STAT_THREADS) accept_stats_kernel(const AcceptParams p) {
   const int lane = threadIdx.x & 31;
   const int warp = (blockIdx.x * STAT_THREADS + threadIdx.x) >> 5;
   const int warps = (gridDim.x * STAT_THREADS) >> 5;
-  if (blockIdx.x == 0)
-    for (int r = threadIdx.x; r < p.R; r += blockDim.x) p.count[r] = 0u;
   const int64_t units = static_cast<int64_t>(p.R) * (p.n + 1) * p.S;
-  const float temp = p.temperature;
-  const bool unit_temp = temp == 1.f;
+  griddep_launch();
+  const TempScale scale = temp_scale(p.temperature);
   const bool vec = (p.V & 3) == 0 && (reinterpret_cast<uintptr_t>(p.scores) & 15) == 0;
-  for (int64_t u = warp; u < units; u += warps) {
+  // units: warp w starts with unit w, then takes tickets (one atomic per
+  // unit, taken a unit ahead) so that warps on faster SMs take more units
+  int64_t u = warp;
+  while (u < units) {
+    unsigned long long ticket = 0;
+    if (lane == 0) ticket = atomicAdd(p.ticket, 1ull);
     const int64_t ij = u / p.S;
     const int s = static_cast<int>(u - ij * p.S);
     const int i = static_cast<int>(ij / (p.n + 1)), j = static_cast<int>(ij - static_cast<int64_t>(i) * (p.n + 1));
-    if (j > accept_row_drafts(p, i)) continue;  // a position past the row's drafts: never read
+    const int ni = accept_row_drafts(p, i);
+    const int64_t next = warps + static_cast<int64_t>(__shfl_sync(0xffffffffu, ticket, 0));
+    if (j > ni) {  // a position past the row's drafts: never read
+      u = next;
+      continue;
+    }
     const float* x = p.scores + ij * p.V;
     const int v0 = s * STAT_SEG, v1 = min(p.V, v0 + STAT_SEG);
     float m = -INFINITY, z = 0.f;
-    if (vec) {
+    if (vec) {  // lane l: 16-byte vectors l, l + 32, ... of the unit, in batches of four,
+                // the next batch's loads in flight while a batch is reduced
       const float4* x4 = reinterpret_cast<const float4*>(x);
-      for (int b = v0 / 4 + lane; b < v1 / 4; b += 4 * 32) {
-        float y[16];
+      const int e1 = v1 / 4;
+      auto fetch = [&](int b, float4 (&f)[4]) {
 #pragma unroll
         for (int k = 0; k < 4; ++k) {
           const int e = b + 32 * k;
-          const float4 f = e < v1 / 4 ? __ldg(x4 + e) : make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
-          y[4 * k] = f.x;
-          y[4 * k + 1] = f.y;
-          y[4 * k + 2] = f.z;
-          y[4 * k + 3] = f.w;
+          f[k] = e < e1 ? __ldg(x4 + e) : make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
         }
-        // x / temperature; at temperature 1 the division is skipped (x itself)
-        if (!unit_temp) {
+      };
+      float4 cur[4], nxt[4];
+      int b = v0 / 4 + lane;
+      fetch(b, cur);
+      for (; b < e1; b += 4 * 32) {
+        fetch(b + 4 * 32, nxt);
+        float y[16];
 #pragma unroll
-          for (int k = 0; k < 16; ++k) y[k] = y[k] / temp;
+        for (int k = 0; k < 4; ++k) {
+          y[4 * k] = cur[k].x;
+          y[4 * k + 1] = cur[k].y;
+          y[4 * k + 2] = cur[k].z;
+          y[4 * k + 3] = cur[k].w;
+        }
+        if (!UNIT_TEMP) {
+#pragma unroll
+          for (int k = 0; k < 16; ++k) y[k] = scale(y[k]);
         }
         accept_stat_batch<GREEDY>(m, z, y);
+#pragma unroll
+        for (int k = 0; k < 4; ++k) cur[k] = nxt[k];
       }
-    } else {
+    } else {  // lane l: entries l, l + 32, ...
       for (int b = v0 + lane; b < v1; b += 4 * 32) {
         float y[4];
 #pragma unroll
         for (int k = 0; k < 4; ++k) {
           const int e = b + 32 * k;
-          y[k] = e < v1 ? (unit_temp ? __ldg(x + e) : __ldg(x + e) / temp) : -INFINITY;
+          y[k] = e < v1 ? scale(__ldg(x + e)) : -INFINITY;
         }
         accept_stat_batch<GREEDY>(m, z, y);
       }
@@ -322,57 +490,69 @@ __global__ void __launch_bounds__(STAT_THREADS) accept_stats_kernel(const Accept
       const float2 b = make_float2(__shfl_xor_sync(0xffffffffu, a.x, o), __shfl_xor_sync(0xffffffffu, a.y, o));
       a = GREEDY ? accept_count_merge(a, b) : accept_stat_merge(a, b);
     }
-    if (lane == 0) p.part[u] = a;
-  }
-}
-
-// The statistics (m, Z) of position ij from its S segments, by one warp:
-// the maximum, then the segments' sums rescaled to it (greedy: the counts
-// of the segments whose maximum is it), summed in a fixed order and
-// broadcast from lane 0, so every warp of every CTA gets the same bits for
-// the same position.
-__device__ __forceinline__ float2 accept_position_stats(const AcceptParams& p, int64_t ij, int lane) {
-  const float2* part = p.part + ij * p.S;
-  float m = -INFINITY;
-  for (int s = lane; s < p.S; s += 32) m = fmaxf(m, part[s].x);
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-  float z = 0.f;
-  if (accept_greedy(p)) {
-    for (int s = lane; s < p.S; s += 32) {
-      const float2 e = part[s];
-      z += e.x == m ? e.y : 0.f;
+    // the position's last segment to finish combines them and makes the
+    // draft's accept test
+    unsigned done = 0;
+    if (lane == 0) {
+      p.part[u] = a;
+      __threadfence();
+      done = atomicAdd(p.pos_count + ij, 1u);
     }
-  } else if (m != -INFINITY) {
-    for (int s = lane; s < p.S; s += 32) {
-      const float2 e = part[s];
-      z += e.y * expf(e.x - m);
+    if (__shfl_sync(0xffffffffu, done, 0) == static_cast<unsigned>(p.S - 1)) {
+      __threadfence();
+      const float2 st = accept_position_stats(p, ij, lane);
+      if (lane == 0) {
+        const float thr = GREEDY ? st.x : -INFINITY;
+        p.pos_stat[ij] = st;
+        p.thr[ij] = thr;
+        if (j < ni) p.keep[ij] = accept_test(p, ij, i, j, st.x, st.y, thr);
+      }
     }
+    u = next;
   }
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) z += __shfl_xor_sync(0xffffffffu, z, o);
-  return make_float2(m, __shfl_sync(0xffffffffu, z, 0));
 }
 
 // The draw's weight of vocabulary entry v: p_j[v], or max(0, p_j[v] - q_j[v])
 // after a rejection (qv non-null). The row's statistics come in registers
 // (m, 1 / Z, threshold); the weight scales by 1 / Z instead of dividing,
 // which only moves the inverse CDF's boundaries by float32 rounding.
+// load8 reads entries v0 .. v0 + 7 (v0 a multiple of 8; two 16-byte loads
+// each of x and q when the rows are 16-byte aligned); entries past the
+// vocabulary read as x = -inf, q = 0, which weigh 0.
 struct DrawRow {
   const float* x;
   const float* qv;
-  float m, rz, thr, temp;
-  __device__ __forceinline__ float weight(int v) const {
-    const float y = temp == 1.f ? x[v] : x[v] / temp;
+  float m, rz, thr;
+  TempScale scale;
+  bool vec;
+  __device__ __forceinline__ void load8(int v0, int V, float (&xv)[8], float (&qq)[8]) const {
+    if (vec && v0 + 8 <= V) {
+      const float4 a = __ldg(reinterpret_cast<const float4*>(x + v0));
+      const float4 b = __ldg(reinterpret_cast<const float4*>(x + v0) + 1);
+      xv[0] = a.x, xv[1] = a.y, xv[2] = a.z, xv[3] = a.w, xv[4] = b.x, xv[5] = b.y, xv[6] = b.z, xv[7] = b.w;
+      if (qv) {
+        const float4 c = __ldg(reinterpret_cast<const float4*>(qv + v0));
+        const float4 d = __ldg(reinterpret_cast<const float4*>(qv + v0) + 1);
+        qq[0] = c.x, qq[1] = c.y, qq[2] = c.z, qq[3] = c.w, qq[4] = d.x, qq[5] = d.y, qq[6] = d.z, qq[7] = d.w;
+      }
+    } else {
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        xv[e] = v0 + e < V ? __ldg(x + v0 + e) : -INFINITY;
+        if (qv) qq[e] = v0 + e < V ? __ldg(qv + v0 + e) : 0.f;
+      }
+    }
+  }
+  __device__ __forceinline__ float weight(float xe, float qe) const {
+    const float y = scale(xe);
     float w = y >= thr ? expf(y - m) * rz : 0.f;
-    if (qv) w = fmaxf(w - qv[v], 0.f);
+    if (qv) w = fmaxf(w - qe, 0.f);
     return w;
   }
 };
 
-// grid (R, slices). The decisions: warp w tests drafts w, w + DRAW_WARPS, ...
-// (u_j q_j[tok] < p_j[tok]) and an atomic minimum finds the first
-// rejection. The slice: chunks [y * DRAW_CPS, (y + 1) * DRAW_CPS) of the
+// grid (R, slices). The first failed accept test (a ballot over the tests
+// the statistics kernels made) gives the draw's position. The slice: chunks [y * DRAW_CPS, (y + 1) * DRAW_CPS) of the
 // draw's weights, lane l of a warp taking entries 8l .. 8l + 7 of a chunk
 // (coalesced), each chunk's float64 sum to the row's chunk sums. The row's
 // last CTA to arrive scans the chunk sums for the one where the running sum
@@ -384,76 +564,79 @@ __global__ void __launch_bounds__(DRAW_THREADS) accept_draw_kernel(const AcceptP
   const int i = blockIdx.x, t = threadIdx.x, lane = t & 31, warp = t >> 5;
   const int ni = accept_row_drafts(p, i);
   const float temp = p.temperature;
-  const bool radix = accept_radix(p), greedy = accept_greedy(p);
+  const int64_t row0 = static_cast<int64_t>(i) * (p.n + 1);
   if (t == 0) {
-    s_pick[0] = ni;       // the first rejected draft, ni when every draft is kept
     s_pick[1] = p.V - 1;  // the drawn entry (the last when rounding leaves the target past the end)
     s_pick[2] = -1;       // the chunk the running sum crosses the target in
     s_pick[3] = 0;        // this CTA is the row's last to finish its slice
   }
-  __syncthreads();
-  for (int j = warp; j < ni; j += DRAW_WARPS) {
-    const int64_t ij = static_cast<int64_t>(i) * (p.n + 1) + j;
-    const float2 st = accept_position_stats(p, ij, lane);
-    if (lane == 0) {
-      const int64_t tok = p.drafted[static_cast<int64_t>(i) * p.n + j];
-      float pj = 0.f, qj = 0.f;
-      if (tok >= 0 && tok < p.V) {
-        const float x = p.scores[ij * p.V + tok];
-        const float y = temp == 1.f ? x : x / temp;
-        const float thr = radix ? p.thr[ij] : (greedy ? st.x : -INFINITY);
-        pj = y >= thr ? expf(y - st.x) / st.y : 0.f;
-        qj = p.q[(static_cast<int64_t>(i) * p.n + j) * p.V + tok];
+  griddep_wait();  // the statistics kernel's results
+  // the first draft whose accept test failed (ni when every draft passed)
+  if (warp == 0) {
+    int first = ni;
+    for (int j0 = 0; j0 < ni; j0 += 32) {
+      const int j = j0 + lane;
+      const unsigned failed = __ballot_sync(0xffffffffu, j < ni && p.keep[row0 + j] == 0);
+      if (failed != 0) {
+        first = j0 + __ffs(failed) - 1;
+        break;
       }
-      if (!(p.uniforms[static_cast<int64_t>(i) * p.n + j] * qj < pj)) atomicMin(&s_pick[0], j);
+    }
+    if (lane == 0) {
+      const float2 st = p.pos_stat[row0 + first];
+      s_pick[0] = first;
+      s_stat[0] = st.x;
+      s_stat[1] = 1.f / st.y;
+      s_stat[2] = p.thr[row0 + first];
     }
   }
   __syncthreads();
   const int kept = s_pick[0];
   const int reject = kept < ni ? kept : -1;
-  const int64_t ik = static_cast<int64_t>(i) * (p.n + 1) + kept;
-  if (warp == 0) {
-    const float2 st = accept_position_stats(p, ik, lane);
-    if (lane == 0) {
-      s_stat[0] = st.x;
-      s_stat[1] = 1.f / st.y;
-      s_stat[2] = radix ? p.thr[ik] : (greedy ? st.x : -INFINITY);
-    }
-  }
-  __syncthreads();
+  const int64_t ik = row0 + kept;
   DrawRow row;
   row.x = p.scores + ik * p.V;
   row.qv = reject >= 0 ? p.q + (static_cast<int64_t>(i) * p.n + kept) * p.V : nullptr;
   row.m = s_stat[0];
   row.rz = s_stat[1];
   row.thr = s_stat[2];
-  row.temp = temp;
+  row.scale = temp_scale(temp);
+  row.vec = (p.V & 3) == 0 && (reinterpret_cast<uintptr_t>(p.scores) & 15) == 0 &&
+            (reinterpret_cast<uintptr_t>(p.q) & 15) == 0;
   double* sums = p.chunk_sum + static_cast<int64_t>(i) * p.chunks;
   const int c_begin = blockIdx.y * DRAW_CPS, c_end = min(p.chunks, c_begin + DRAW_CPS);
-  // each warp sums its chunks of the slice, two at a time
-  for (int c = c_begin + warp; c < c_end; c += 2 * DRAW_WARPS) {
-    double part[2];
+  // warp w sums chunks w, w + DRAW_WARPS, ... of the slice: every load first
+  constexpr int CPW = DRAW_CPS / DRAW_WARPS;
+  float xv[CPW][8], qq[CPW][8];
 #pragma unroll
-    for (int u = 0; u < 2; ++u) {
-      const int cu = c + u * DRAW_WARPS;
-      const int v0 = cu * DRAW_CHUNK + 8 * lane;
-      float w[8];
+  for (int u = 0; u < CPW; ++u) {
+    const int c = c_begin + warp + u * DRAW_WARPS;
+    if (c < c_end) {
+      row.load8(c * DRAW_CHUNK + 8 * lane, p.V, xv[u], qq[u]);
+    } else {
 #pragma unroll
-      for (int e = 0; e < 8; ++e) w[e] = cu < c_end && v0 + e < p.V ? row.weight(v0 + e) : 0.f;
-      part[u] = 0.0;
-#pragma unroll
-      for (int e = 0; e < 8; ++e) part[u] += static_cast<double>(w[e]);
+      for (int e = 0; e < 8; ++e) xv[u][e] = -INFINITY, qq[u][e] = 0.f;
     }
+  }
+  double part[CPW];
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-      part[0] += __shfl_xor_sync(0xffffffffu, part[0], o);
-      part[1] += __shfl_xor_sync(0xffffffffu, part[1], o);
+  for (int u = 0; u < CPW; ++u) {
+    part[u] = 0.0;
+#pragma unroll
+    for (int e = 0; e < 8; ++e) part[u] += static_cast<double>(row.weight(xv[u][e], qq[u][e]));
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+#pragma unroll
+    for (int u = 0; u < CPW; ++u) part[u] += __shfl_xor_sync(0xffffffffu, part[u], o);
+  }
+  if (lane == 0) {
+#pragma unroll
+    for (int u = 0; u < CPW; ++u) {
+      const int c = c_begin + warp + u * DRAW_WARPS;
+      if (c < c_end) sums[c] = part[u];
     }
-    if (lane == 0) {
-      sums[c] = part[0];
-      if (c + DRAW_WARPS < c_end) sums[c + DRAW_WARPS] = part[1];
-      __threadfence();
-    }
+    __threadfence();
   }
   __syncthreads();
   if (t == 0) {
@@ -507,11 +690,13 @@ __global__ void __launch_bounds__(DRAW_THREADS) accept_draw_kernel(const AcceptP
     const int c = s_pick[2];
     if (c >= 0) {
       const int v0 = c * DRAW_CHUNK + 8 * lane;
+      float cx[8], cq[8];
+      row.load8(v0, p.V, cx, cq);
       double w8[8];
       double part = 0.0;
 #pragma unroll
       for (int e = 0; e < 8; ++e) {
-        w8[e] = v0 + e < p.V ? static_cast<double>(row.weight(v0 + e)) : 0.0;
+        w8[e] = static_cast<double>(row.weight(cx[e], cq[e]));
         part += w8[e];
       }
       double lincl = part;

@@ -325,6 +325,14 @@ __device__ __forceinline__ float fast_exp2(float x) {
 // Register limit of this warpgroup's threads (all its warps execute the
 // same instruction): dec returns registers to the block's pool, inc waits
 // until the pool has them.
+// Programmatic dependent launch: a kernel launched with programmatic stream
+// serialisation may start while the kernel before it on the stream still
+// runs; griddep_wait blocks until that kernel has finished and its memory
+// writes are visible (a no-op for a kernel launched without the attribute).
+// griddep_launch lets the next kernel start launching its CTAs early.
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void griddep_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 template <int N>
 __device__ __forceinline__ void setmaxnreg_dec() {
   asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;\n" ::"n"(N) : "memory");

@@ -501,9 +501,13 @@ extern "C" int wpt_accept(const float* scores, const int64_t* drafted, const flo
   p.resample = resample;
   p.lengths = lengths;
   p.part = reinterpret_cast<float2*>(base + layout.part);
+  p.pos_stat = reinterpret_cast<float2*>(base + layout.pos_stat);
   p.thr = reinterpret_cast<float*>(base + layout.thr);
+  p.keep = reinterpret_cast<int*>(base + layout.keep);
   p.chunk_sum = reinterpret_cast<double*>(base + layout.chunk_sum);
+  p.pos_count = reinterpret_cast<unsigned*>(base + layout.pos_count);
   p.count = reinterpret_cast<unsigned*>(base + layout.count);
+  p.ticket = reinterpret_cast<unsigned long long*>(base + layout.ticket);
   p.tokens = tokens;
   p.accepted = accepted;
   p.R = R;
@@ -516,7 +520,9 @@ extern "C" int wpt_accept(const float* scores, const int64_t* drafted, const flo
   const int slices = (p.chunks + wpt::DRAW_CPS - 1) / wpt::DRAW_CPS;
   if (slices > 65535) return fail(WPT_ERR_UNSUPPORTED, "vocabulary of %d entries is too large", V);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  cudaError_t e;
+  // the arrival counters (positions', rows') and the unit ticket start at zero
+  cudaError_t e = cudaMemsetAsync(base + layout.pos_count, 0, layout.bytes - layout.pos_count, s);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaMemsetAsync(accept counters)");
   if (top_k > 1 && top_k < V) {
     wpt::accept_topk_stats_kernel<<<dim3(n + 1, R), wpt::ACCEPT_THREADS, 0, s>>>(p);
     e = cudaGetLastError();
@@ -524,26 +530,41 @@ extern "C" int wpt_accept(const float* scores, const int64_t* drafted, const flo
   } else {
     // a grid the SMs hold at once: its warps take the units in turn
     const bool greedy = top_k == 1 && V > 1;
-    auto kernel = greedy ? wpt::accept_stats_kernel<true> : wpt::accept_stats_kernel<false>;
-    static int resident[2][64] = {};
+    const int variant = (greedy ? 2 : 0) + (temperature == 1.f ? 1 : 0);
+    void (*const kernels[4])(const wpt::AcceptParams) = {
+        wpt::accept_stats_kernel<false, false>, wpt::accept_stats_kernel<false, true>,
+        wpt::accept_stats_kernel<true, false>, wpt::accept_stats_kernel<true, true>};
+    auto kernel = kernels[variant];
+    static int resident[4][64] = {};
     int sms = 148;
     const int dev = current_device(&sms);
-    if (resident[greedy][dev] == 0) {
+    if (resident[variant][dev] == 0) {
       int per_sm = 0;
       e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, wpt::STAT_THREADS, 0);
       if (e != cudaSuccess) return cuda_fail(e, "cudaOccupancyMaxActiveBlocksPerMultiprocessor");
-      resident[greedy][dev] = per_sm > 0 ? per_sm : 1;
+      resident[variant][dev] = per_sm > 0 ? per_sm : 1;
     }
     const int64_t units = static_cast<int64_t>(R) * (n + 1) * p.S;
     const int64_t want = (units + wpt::STAT_THREADS / 32 - 1) / (wpt::STAT_THREADS / 32);
     const int blocks = static_cast<int>(
-        std::max<int64_t>(1, std::min<int64_t>(want, static_cast<int64_t>(sms) * resident[greedy][dev])));
+        std::max<int64_t>(1, std::min<int64_t>(want, static_cast<int64_t>(sms) * resident[variant][dev])));
     kernel<<<blocks, wpt::STAT_THREADS, 0, s>>>(p);
     e = cudaGetLastError();
     if (e != cudaSuccess) return cuda_fail(e, "accept_stats_kernel launch");
   }
-  wpt::accept_draw_kernel<<<dim3(R, slices), wpt::DRAW_THREADS, 0, s>>>(p);
-  e = cudaGetLastError();
+  // the draw launches while the statistics finish (programmatic dependent
+  // launch) and waits for them on the device
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(R, slices);
+  cfg.blockDim = dim3(wpt::DRAW_THREADS);
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  e = cudaLaunchKernelEx(&cfg, wpt::accept_draw_kernel, p);
   if (e != cudaSuccess) return cuda_fail(e, "accept_draw_kernel launch");
   return WPT_OK;
 }
