@@ -187,6 +187,11 @@ int wpt_accept(const float* scores, const int64_t* drafted, const float* q, cons
  * (0 for a bad shape). */
 size_t wpt_accept_scratch_bytes(int R, int n, int V);
 
+/* out[i] = x[i] / temperature as the acceptance kernels compute it (the
+ * reference's float32 `scores / temperature`, wpt_inference/__init__.py:174):
+ * exposed so that tests can compare it with IEEE division. fp32, n entries. */
+int wpt_temperature_scale(const float* x, int64_t n, float temperature, float* out, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

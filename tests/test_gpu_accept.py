@@ -116,3 +116,31 @@ def test_top_k_thresholds(wb, V, top_k, tied):
     assert np.array_equal(accepted.cpu().numpy(), ref_accepted)
     assert np.array_equal(tokens.cpu().numpy(), ref_tokens)
     assert wb.device_status() == 0
+
+
+@pytest.mark.parametrize("temperature", [0.7, 0.8, 0.9, 1.3, 0.3, 2.5, 0.123456])
+def test_temperature_scaling_is_ieee_division(wb, temperature):
+    """The kernels' x / temperature (reciprocal, product and Markstein's
+    correction) against numpy's IEEE float32 division on 2^22 random bit
+    patterns plus logits' usual range, +-0 and +-inf: bit for bit for
+    quotients of magnitude 2^-100 and up and for zeros and infinities,
+    within one unit in the last place below."""
+    from wpt_b200 import _lib
+    rng = np.random.default_rng(int(temperature * 1e6))
+    bits = rng.integers(0, 2 ** 32, 1 << 22, dtype=np.uint64).astype(np.uint32)
+    x = bits.view(np.float32)
+    x = x[np.isfinite(x)]
+    x = np.concatenate([x, rng.normal(0.0, 4.0, 1 << 20).astype(np.float32),
+                        np.array([0.0, -0.0, np.inf, -np.inf], np.float32)])
+    with np.errstate(over="ignore", under="ignore"):
+        ref = x / np.float32(temperature)
+    xd = torch.from_numpy(x).cuda()
+    out = torch.empty_like(xd)
+    _lib.check(_lib.lib().wpt_temperature_scale(_lib.ptr(xd), xd.numel(), float(temperature), _lib.ptr(out),
+                                                _lib.stream(xd.device)))
+    got = out.cpu().numpy()
+    normal = (np.abs(ref) >= np.float32(2.0 ** -100)) | (x == 0)
+    differ = got[normal].view(np.uint32) != ref[normal].view(np.uint32)
+    assert not differ.any(), (x[normal][differ][:8], got[normal][differ][:8], ref[normal][differ][:8])
+    ulps = np.abs(got[~normal].view(np.int32).astype(np.int64) - ref[~normal].view(np.int32).astype(np.int64))
+    assert ulps.max(initial=0) <= 1

@@ -220,8 +220,11 @@ __device__ __forceinline__ float2 accept_position_stats(const AcceptParams& p, i
 // x / temperature as the reference's float32 division gives it, from the
 // reciprocal r = 1 / t (correctly rounded) and Markstein's correction of
 // the product: q0 = x r, then q0 + (x - q0 t) r with the remainder exact by
-// fma (P. Markstein, IBM J. Res. Dev. 34(1), 1990). An infinite or NaN q0
-// (masked -inf logits) is the quotient itself.
+// fma (P. Markstein, IBM J. Res. Dev. 34(1), 1990). The remainder is exact,
+// and the quotient the IEEE one, while it stays clear of float32's
+// subnormal range: for quotients of magnitude 2^-100 and up. Below that it
+// is within one unit in the last place (and exp(y - m) cannot tell). A zero,
+// infinite or NaN q0 (signed zeros, masked -inf logits) is the quotient.
 struct TempScale {
   float t, r;
   bool unit;
@@ -229,7 +232,8 @@ struct TempScale {
     if (unit) return x;
     const float q0 = x * r;
     const float y = fmaf(fmaf(-q0, t, x), r, q0);
-    return fabsf(q0) < INFINITY ? y : q0;
+    const float a = fabsf(q0);
+    return a < INFINITY && a > 0.f ? y : q0;
   }
 };
 __device__ __forceinline__ TempScale temp_scale(float t) {
@@ -238,6 +242,13 @@ __device__ __forceinline__ TempScale temp_scale(float t) {
   s.r = 1.f / t;
   s.unit = t == 1.f;
   return s;
+}
+
+__global__ void temperature_scale_kernel(const float* x, int64_t n, float t, float* out) {
+  const TempScale scale = temp_scale(t);
+  for (int64_t k = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; k < n;
+       k += static_cast<int64_t>(gridDim.x) * blockDim.x)
+    out[k] = scale(x[k]);
 }
 
 // Draft j's accept test, u_j q_j[tok] < p_j[tok], from its position's

@@ -476,6 +476,20 @@ extern "C" int wpt_attn_topk(const void* q, const void* k, int64_t k_stride_b, i
   return WPT_OK;
 }
 
+extern "C" int wpt_temperature_scale(const float* x, int64_t n, float temperature, float* out, void* stream) {
+  if (n < 0 || (n > 0 && (!x || !out))) return fail(WPT_ERR_INVALID, "bad temperature_scale arguments");
+  if (!(temperature > 0.f)) return fail(WPT_ERR_INVALID, "temperature must be positive");
+  if (n == 0) return WPT_OK;
+  int sms = 148;
+  current_device(&sms);
+  const int64_t want = (n + 255) / 256;
+  const int blocks = static_cast<int>(std::min<int64_t>(want, static_cast<int64_t>(sms) * 8));
+  wpt::temperature_scale_kernel<<<blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(x, n, temperature, out);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "temperature_scale_kernel launch");
+  return WPT_OK;
+}
+
 extern "C" size_t wpt_accept_scratch_bytes(int R, int n, int V) {
   if (R < 0 || n < 0 || V < 1) return 0;
   return wpt::accept_scratch(R, n, V).bytes;
