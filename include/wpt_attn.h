@@ -127,10 +127,10 @@ int wpt_attn_topk(const void* q, const void* k, int64_t k_stride_b, int64_t k_st
  * arguments, but the split partials go to a static 8 MiB device array the
  * library holds on every GPU that loads it, so the call allocates nothing.
  * No counterpart in the reference. It serves callers that cannot allocate
- * device memory per call: a decode loop captured in a CUDA graph (a
- * cudaMalloc cannot be captured), a host behind an FFI (Go, Java, Rust) with
- * no caching allocator, where a cudaFree per step would synchronise the
- * device, or a serving process that must not grow its footprint mid-run.
+ * device memory per call: a host behind an FFI (Go, Java, Rust) with no
+ * caching allocator, where a cudaMalloc and cudaFree per step would
+ * synchronise the device, or a serving process that must not grow its
+ * footprint mid-run.
  * Limit: splits * B * T * H * (C + 1) floats must fit in 2^21 (8 MiB);
  * larger calls return WPT_ERR_UNSUPPORTED and launch nothing. The first call
  * on a device looks up the array's device address (cudaGetSymbolAddress);

@@ -1,8 +1,8 @@
 """wpt_attn_decode_noalloc, the decode entry point that allocates nothing:
 its split partials live in the library's static device array instead of
 caller buffers. It is for callers that cannot allocate device memory on
-the hot path (a decode step captured in a CUDA graph, an FFI host without a
-caching allocator, a serving loop that must not synchronise on cudaFree).
+the hot path (an FFI host without a caching allocator, a serving loop that
+must not synchronise on cudaMalloc/cudaFree or grow its footprint).
 
 Called through the C ABI, twice in a row with different inputs, its output
 must match wpt_attn_decode's (given torch-allocated scratch) within the
