@@ -234,6 +234,25 @@ def secondary(wb, ops, device, rank, world, hbm):
                             "ms": round(ms_w, 4), "graph_value": round(bytes_w / gms_w / 1e6, 1),
                             "graph_frac_of_hbm": round(bytes_w / gms_w / 1e6 / hbm, 3), "graph_ms": round(gms_w, 4),
                             "algorithmic_bytes": bytes_w}
+    # A4 + A5 (the model's exact layer with its top-1024 selection, window 128; then the sparse layer
+    # over those rows plus each query's last 1024 rows, with the sink)
+    f_s = lambda: wb.exact_attention(q, k, v, pos, C ** -0.5, 1024, 128)  # noqa: E731
+    ms_s, gms_s = timed(f_s, 20, 3), graph_timed(f_s, 20, 3)
+    _, chosen = f_s()
+    f_p = lambda: wb.sparse_attention(q, k, v, sink, chosen, pos, C ** -0.5, 1024)  # noqa: E731
+    ms_p, gms_p = timed(f_p, 20, 3), graph_timed(f_p, 20, 3)
+    bytes_s = bytes_g + int(L.sum()) * C * 2  # the attention's K and V, then K once more for the scores
+    bytes_p = 64 * (1024 + 1024) * 2 * C * 2 + qo  # chosen + window rows, K and V, gathered
+    out["exact_top1024"] = {"metric": "exact attention + top-1024 row selection, HBM GB/s (config 3 rows)",
+                            "unit": "GB/s", "value": round(bytes_s / ms_s / 1e6, 1), "ms": round(ms_s, 4),
+                            "graph_value": round(bytes_s / gms_s / 1e6, 1),
+                            "graph_frac_of_hbm": round(bytes_s / gms_s / 1e6 / hbm, 3), "graph_ms": round(gms_s, 4),
+                            "algorithmic_bytes": bytes_s}
+    out["sparse_gather"] = {"metric": "sparse attention over 1024 chosen + 1024 window rows, GB/s (config 3)",
+                            "unit": "GB/s", "value": round(bytes_p / ms_p / 1e6, 1), "ms": round(ms_p, 4),
+                            "graph_value": round(bytes_p / gms_p / 1e6, 1),
+                            "graph_frac_of_hbm": round(bytes_p / gms_p / 1e6 / hbm, 3), "graph_ms": round(gms_p, 4),
+                            "algorithmic_bytes": bytes_p}
     del table
     # the 262,144-token row, split along its keys over the ranks
     from wpt_b200 import multi

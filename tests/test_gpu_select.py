@@ -129,3 +129,26 @@ def test_choice_feeds_sparse_attention(wb):
     ref, _ = oat.sparse_attention(_np(q), _np(e[..., :C]), _np(e[..., C:]), sink.double().numpy(),
                                   chosen.cpu().numpy(), positions.numpy(), C ** -0.5, window)
     assert np.abs(out.float().cpu().numpy() - ref).max() < 2e-2
+
+
+@pytest.mark.parametrize("tied", [False, True])
+def test_decode_choice_over_ragged_rows(wb, tied):
+    """Decode rows of many lengths, some with no row to choose from (the
+    balanced split of the scoring over the SMs, with ranges that cross
+    rows); with tied keys (two distinct key vectors) thousands of equal
+    scores crowd the threshold's bin and the radix passes decide."""
+    g = torch.Generator().manual_seed(5 + tied)
+    B, T, H, C, N, top_k, window = 40, 1, 32, 128, 6000, 256, 128
+    q = torch.randn(B, T, H, C, generator=g).bfloat16()
+    e = torch.randn(B, N, 2 * C, generator=g).bfloat16()
+    if tied:
+        pair = torch.randn(2, C, generator=g)
+        e[..., :C] = pair[(torch.arange(N) % 5 == 0).long()][None].bfloat16()
+    positions = torch.randint(100, N + 200, (B, 1), generator=g)
+    qd, ed = q.cuda(), e.cuda()
+    _, chosen = wb.exact_attention(qd, ed[..., :C], ed[..., C:], positions.cuda(), C ** -0.5, top_k, window)
+    assert wb.device_status() == 0
+    k = _np(e[..., :C])
+    _, _, expected = oat.exact_attention(_np(q), k, _np(e[..., C:]), positions.numpy(), C ** -0.5, top_k, window)
+    pos_clipped = np.minimum(positions.numpy(), N - 1)
+    _assert_chosen_alike(_np(q), k, pos_clipped, C ** -0.5, chosen.cpu().numpy(), expected)

@@ -10,18 +10,19 @@
 // radix select per query reads them.
 //
 // score_kernel: S^T = K Q^T with the 128 keys of a tile as M and up to 256
-// (query, head) columns as N (K tiles by TMA, Q once by TMA), S^T
-// double-buffered in TMEM. Thread r of warps 0-3 owns key r: it reads its
+// (query, head) columns as N (K tiles by TMA, Q by TMA per query group),
+// S^T double-buffered in TMEM. Thread r of warps 0-3 owns key r: it reads its
 // row of S^T 32 columns at a time and takes the running maximum over each
 // query's H consecutive columns, writing one fp32 score per (query, key)
 // (coalesced: consecutive threads, consecutive keys). Key tiles of a query
 // group are split over gridDim.y; scores need no merge.
 //
 // topk_kernel: one CTA per query. Scores become order-preserving 32-bit
-// keys; four 8-bit MSB-first histogram passes find the top_k-th key
-// (the row is cached in shared memory when it fits); a block scan then
-// writes every row above it and, among rows equal to it, the lowest row
-// indices until top_k are chosen. Deterministic; ties resolve by row index.
+// keys (cached in shared memory when the row fits); a histogram over the
+// keys' range and a sort of the one bin that holds the top_k-th key find it
+// (radix passes when that bin is crowded); a block scan then writes every
+// row above it and, among rows equal to it, the lowest row indices until
+// top_k are chosen. Deterministic; ties resolve by row index.
 #pragma once
 
 #include <climits>
@@ -37,8 +38,11 @@ struct ScoreParams {
   int64_t ld;
   unsigned* status;
   int B, T, H, N, window, TQ, groups_per_row, chunk_tiles;
+  int balanced;              // 1: the live key tiles of all groups split evenly over the grid
   float scale;
 };
+
+constexpr int SCORE_BAL_GROUPS = 1024;  // most query groups the balanced split takes
 
 template <int NCOL, int STAGES>
 struct ScoreLayout {
@@ -52,10 +56,34 @@ struct ScoreLayout {
   static constexpr int OFF_BAR = OFF_LAST + 256 * 4;
   static constexpr int NBAR = 1 + 2 * STAGES + 4;
   static constexpr int OFF_MISC = OFF_BAR + NBAR * 8;
-  static constexpr int BYTES = OFF_MISC + 16 + 1024;
+  static constexpr int OFF_PRE = OFF_MISC + 32;
+  static constexpr int BYTES = OFF_PRE + (SCORE_BAL_GROUPS + 1) * 4 + 1024;
   static constexpr int TMEM_COLS = 2 * NCOL <= 32 ? 32 : 2 * NCOL <= 64 ? 64 : 2 * NCOL <= 128 ? 128 : 2 * NCOL <= 256 ? 256 : 512;
 };
 
+// Key tiles group g's queries read (rows 0 .. max over its queries of p - window).
+__device__ __forceinline__ int score_group_tiles(const ScoreParams& p, int g, int* last_out) {
+  const int b = g / p.groups_per_row;
+  const int t0 = (g - b * p.groups_per_row) * p.TQ;
+  const int TQg = min(p.TQ, p.T - t0);
+  int maxlast = -1;
+  for (int tq = 0; tq < TQg; ++tq) {
+    int64_t last = p.positions[static_cast<int64_t>(b) * p.T + t0 + tq] - p.window;
+    if (last > p.N - 1) last = p.N - 1;
+    if (last < -1) last = -1;
+    if (last_out) last_out[tq] = static_cast<int>(last);
+    maxlast = max(maxlast, static_cast<int>(last));
+  }
+  return maxlast >= 0 ? maxlast / 128 + 1 : 0;
+}
+
+// A CTA's work is one or more segments: key tiles [tile0, tile0 + ntiles) of
+// a query group. Grid (groups, splits): one segment, chunk_tiles of the
+// group's tiles. Balanced (decode-sized calls): the groups' live tiles laid
+// end to end and cut into gridDim.x equal ranges, so that rows of any
+// lengths keep every CTA equally busy; a range spans one or more groups.
+// Between segments the CTA drains (all roles meet at a barrier) and loads
+// the next group's queries.
 template <int NCOL, int STAGES>
 __global__ void __launch_bounds__(192, 1)
     score_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
@@ -75,36 +103,45 @@ __global__ void __launch_bounds__(192, 1)
   uint64_t* s_full = k_empty + STAGES;
   uint64_t* s_free = s_full + 2;
   uint32_t* s_tmem = reinterpret_cast<uint32_t*>(smem + L::OFF_MISC);
-  int* s_maxlast = reinterpret_cast<int*>(smem + L::OFF_MISC + 4);
+  int* s_seg = reinterpret_cast<int*>(smem + L::OFF_MISC + 4);  // group, tile0, ntiles of the segment
+  int* s_pre = reinterpret_cast<int*>(smem + L::OFF_PRE);       // balanced: live tiles before group g
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int group = blockIdx.x, split = blockIdx.y;
-  const int b = group / p.groups_per_row;
-  const int t0 = (group - b * p.groups_per_row) * p.TQ;
-  const int TQg = min(p.TQ, p.T - t0);
+  const int groups = p.B * p.groups_per_row;
 
-  if (threadIdx.x == 0) *s_maxlast = -1;
-  __syncthreads();
-  for (int tq = threadIdx.x; tq < TQg; tq += blockDim.x) {
-    const int64_t pos = p.positions[static_cast<int64_t>(b) * p.T + t0 + tq];
-    int64_t last = pos - p.window;
-    if (last > p.N - 1) last = p.N - 1;
-    if (last < -1) last = -1;
-    s_last[tq] = static_cast<int>(last);
-    atomicMax(s_maxlast, static_cast<int>(last));
+  // the CTA's range of work
+  int64_t range_lo = 0, range_hi = 0;
+  if (p.balanced) {
+    // live tiles per group, then an in-place prefix sum: thread t sums a
+    // contiguous run of groups, a warp scan and a pass over the six warps'
+    // totals give each run's offset
+    for (int g = threadIdx.x; g < groups; g += blockDim.x) s_pre[g + 1] = score_group_tiles(p, g, nullptr);
+    __syncthreads();
+    const int per = (groups + blockDim.x - 1) / blockDim.x;
+    const int g0 = 1 + threadIdx.x * per, g1 = min(groups + 1, g0 + per);
+    int run = 0;
+    for (int g = g0; g < g1; ++g) run += s_pre[g];
+    int incl = run;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int y = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += y;
+    }
+    if (lane == 31) s_lse[warp] = __int_as_float(incl);  // the warps' totals, before s_lse is used
+    __syncthreads();
+    int offset = incl - run;
+    for (int w = 0; w < warp; ++w) offset += __float_as_int(s_lse[w]);
+    for (int g = g0; g < g1; ++g) {
+      offset += s_pre[g];
+      s_pre[g] = offset;
+    }
+    if (threadIdx.x == 0) s_pre[0] = 0;
+    __syncthreads();
+    const int64_t total = s_pre[groups];
+    range_lo = total * blockIdx.x / gridDim.x;
+    range_hi = total * (blockIdx.x + 1) / gridDim.x;
+    if (range_lo >= range_hi) return;
   }
-  for (int c = threadIdx.x; c < NCOL; c += blockDim.x) {
-    const int tq = c / p.H, h = c - tq * p.H;
-    // padding columns get +inf: their scores are -inf and never win a maximum
-    s_lse[c] = tq < TQg ? p.lse[(static_cast<int64_t>(b) * p.T + t0 + tq) * p.H + h] : INFINITY;
-  }
-  __syncthreads();
-  const int maxlast = *s_maxlast;
-  const int tiles_total = maxlast >= 0 ? maxlast / BN + 1 : 0;
-  const int tile0 = split * p.chunk_tiles;
-  const int left = tiles_total - tile0;
-  const int ntiles = left <= 0 ? 0 : (left < p.chunk_tiles ? left : p.chunk_tiles);
-  if (ntiles == 0) return;
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
@@ -131,86 +168,166 @@ __global__ void __launch_bounds__(192, 1)
   tc_fence_after();
   const uint32_t tmem = *s_tmem;
 
-  if (warp == 5) {
-    if (lane == 0) {
-      const int qrow0 = (b * p.T + t0) * p.H;
-      mbar_expect_tx(q_full, L::Q_BYTES);
-      tma_load_2d(sQ, &tm_q, q_full, 0, qrow0);
-      tma_load_2d(sQ + NCOL * 128, &tm_q, q_full, 64, qrow0);
-      for (int j = 0; j < ntiles; ++j) {
-        const int st = j % STAGES;
-        if (j >= STAGES && !mbar_wait(k_empty + st, ((j / STAGES) & 1) ^ 1, p.status)) break;
-        const int n0 = (tile0 + j) * BN;
-        mbar_expect_tx(k_full + st, L::K_BYTES);
-        tma_load_3d(sK + st * L::K_BYTES, &tm_k, k_full + st, 0, n0, b);
-        tma_load_3d(sK + st * L::K_BYTES + BN * 128, &tm_k, k_full + st, 64, n0, b);
+  bool ok = true;
+  int jbase = 0;  // tiles of earlier segments: ring and TMEM phases run on across segments
+  int g_next = 0;
+  for (int seg = 0; ok; ++seg) {
+    // the segment: thread 0 finds it, every thread reads it
+    if (threadIdx.x == 0) {
+      int g = -1, tile0 = 0, nt = 0;
+      if (p.balanced) {
+        // groups that end before the range, or have no live tile, hold no segment
+        while (g_next < groups && (s_pre[g_next + 1] <= range_lo || s_pre[g_next + 1] == s_pre[g_next])) ++g_next;
+        if (g_next < groups && s_pre[g_next] < range_hi) {
+          g = g_next;
+          const int64_t a = max(range_lo, static_cast<int64_t>(s_pre[g]));
+          const int64_t e = min(range_hi, static_cast<int64_t>(s_pre[g + 1]));
+          tile0 = static_cast<int>(a - s_pre[g]);
+          nt = static_cast<int>(e - a);
+          ++g_next;
+        }
+      } else if (seg == 0) {
+        g = blockIdx.x;
+        const int tiles_total = score_group_tiles(p, g, nullptr);
+        tile0 = blockIdx.y * p.chunk_tiles;
+        const int left = tiles_total - tile0;
+        nt = left <= 0 ? 0 : min(left, p.chunk_tiles);
       }
+      s_seg[0] = nt > 0 ? g : -1;
+      s_seg[1] = tile0;
+      s_seg[2] = nt;
     }
-    __syncwarp();
-  } else if (warp == 4) {
-    if (lane == 0) {
-      constexpr uint32_t IDESC = idesc_bf16(128, NCOL, 0, 0);
-      const uint32_t q_addr = smem_u32(sQ), k_addr = smem_u32(sK);
-      bool ok = mbar_wait(q_full, 0, p.status);
-      for (int j = 0; ok && j < ntiles; ++j) {
-        const int st = j % STAGES;
-        if (!(ok = mbar_wait(k_full + st, (j / STAGES) & 1, p.status))) break;
-        if (j >= 2 && !(ok = mbar_wait(s_free + (j & 1), ((j >> 1) & 1) ^ 1, p.status))) break;
+    __syncthreads();
+    const int group = s_seg[0], tile0 = s_seg[1], ntiles = s_seg[2];
+    if (group < 0) break;
+    const int b = group / p.groups_per_row;
+    const int t0 = (group - b * p.groups_per_row) * p.TQ;
+    const int TQg = min(p.TQ, p.T - t0);
+    if (threadIdx.x == 0) score_group_tiles(p, group, s_last);
+    for (int c = threadIdx.x; c < NCOL; c += blockDim.x) {
+      const int tq = c / p.H, h = c - tq * p.H;
+      // padding columns get +inf: their scores are -inf and never win a maximum
+      s_lse[c] = tq < TQg ? p.lse[(static_cast<int64_t>(b) * p.T + t0 + tq) * p.H + h] : INFINITY;
+    }
+    __syncthreads();
+
+    if (warp == 5) {
+      if (lane == 0) {
+        const int qrow0 = (b * p.T + t0) * p.H;
+        mbar_expect_tx(q_full, L::Q_BYTES);
+        tma_load_2d(sQ, &tm_q, q_full, 0, qrow0);
+        tma_load_2d(sQ + NCOL * 128, &tm_q, q_full, 64, qrow0);
+        for (int jj = 0; jj < ntiles; ++jj) {
+          const int j = jbase + jj, st = j % STAGES;
+          if (j >= STAGES && !mbar_wait(k_empty + st, ((j / STAGES) & 1) ^ 1, p.status)) break;
+          const int n0 = (tile0 + jj) * BN;
+          mbar_expect_tx(k_full + st, L::K_BYTES);
+          tma_load_3d(sK + st * L::K_BYTES, &tm_k, k_full + st, 0, n0, b);
+          tma_load_3d(sK + st * L::K_BYTES + BN * 128, &tm_k, k_full + st, 64, n0, b);
+        }
+      }
+      __syncwarp();
+    } else if (warp == 4) {
+      if (lane == 0) {
+        constexpr uint32_t IDESC = idesc_bf16(128, NCOL, 0, 0);
+        const uint32_t q_addr = smem_u32(sQ), k_addr = smem_u32(sK);
+        bool mok = mbar_wait(q_full, seg & 1, p.status);
+        for (int jj = 0; mok && jj < ntiles; ++jj) {
+          const int j = jbase + jj, st = j % STAGES;
+          if (!(mok = mbar_wait(k_full + st, (j / STAGES) & 1, p.status))) break;
+          if (j >= 2 && !(mok = mbar_wait(s_free + (j & 1), ((j >> 1) & 1) ^ 1, p.status))) break;
+          tc_fence_after();
+#pragma unroll
+          for (int kk = 0; kk < C / 16; ++kk) {
+            mma_ss(tmem + (j & 1) * NCOL,
+                   sdesc_sw128(k_addr + st * L::K_BYTES + (kk >> 2) * (BN * 128) + (kk & 3) * 32, 16, 1024),
+                   sdesc_sw128(q_addr + (kk >> 2) * (NCOL * 128) + (kk & 3) * 32, 16, 1024), IDESC, kk > 0 ? 1u : 0u);
+          }
+          mma_commit(k_empty + st);
+          mma_commit(s_full + (j & 1));
+        }
+      }
+      __syncwarp();
+    } else {
+      const int r = threadIdx.x;
+      const uint32_t lane_addr = tmem + (static_cast<uint32_t>(warp * 32) << 16);
+      const int64_t rowbase = static_cast<int64_t>(b) * p.T + t0;
+      for (int jj = 0; jj < ntiles; ++jj) {
+        const int j = jbase + jj;
+        if (!__all_sync(0xffffffffu, mbar_wait(s_full + (j & 1), (j >> 1) & 1, p.status))) {
+          ok = false;
+          break;
+        }
         tc_fence_after();
+        const int n = (tile0 + jj) * BN + r;
+        if (TQg == 1 && NCOL <= 64) {
+          // one query (decode): the key's score is the maximum over all the
+          // columns (padding columns give -inf), a tree over independent terms
+          float w[NCOL];
+          if constexpr (NCOL == 16) {
+            uint32_t x[16];
+            tmem_ld16(lane_addr + (j & 1) * NCOL, x);
 #pragma unroll
-        for (int kk = 0; kk < C / 16; ++kk) {
-          mma_ss(tmem + (j & 1) * NCOL,
-                 sdesc_sw128(k_addr + st * L::K_BYTES + (kk >> 2) * (BN * 128) + (kk & 3) * 32, 16, 1024),
-                 sdesc_sw128(q_addr + (kk >> 2) * (NCOL * 128) + (kk & 3) * 32, 16, 1024), IDESC, kk > 0 ? 1u : 0u);
+            for (int c = 0; c < 16; ++c) w[c] = fmaf(__uint_as_float(x[c]), p.scale, -s_lse[c]);
+          } else {
+#pragma unroll
+            for (int c32 = 0; c32 < NCOL / 32; ++c32) {
+              uint32_t x[32];
+              tmem_ld32(lane_addr + (j & 1) * NCOL + c32 * 32, x);
+#pragma unroll
+              for (int c = 0; c < 32; ++c) w[c32 * 32 + c] = fmaf(__uint_as_float(x[c]), p.scale, -s_lse[c32 * 32 + c]);
+            }
+          }
+#pragma unroll
+          for (int width = NCOL / 2; width > 0; width >>= 1) {
+#pragma unroll
+            for (int c = 0; c < width; ++c) w[c] = fmaxf(w[c], w[c + width]);
+          }
+          tc_fence_before();
+          mbar_arrive(s_free + (j & 1));
+          if (n <= s_last[0]) p.scores[rowbase * p.ld + n] = w[0];
+          continue;
         }
-        mma_commit(k_empty + st);
-        mma_commit(s_full + (j & 1));
-      }
-    }
-    __syncwarp();
-  } else {
-    const int r = threadIdx.x;
-    const uint32_t lane_addr = tmem + (static_cast<uint32_t>(warp * 32) << 16);
-    const int64_t rowbase = static_cast<int64_t>(b) * p.T + t0;
-    for (int j = 0; j < ntiles; ++j) {
-      if (!__all_sync(0xffffffffu, mbar_wait(s_full + (j & 1), (j >> 1) & 1, p.status))) break;
-      tc_fence_after();
-      const int n = (tile0 + j) * BN + r;
-      int tq = 0, next = p.H;
-      float cur = -INFINITY;
+        int tq = 0, next = p.H;
+        float cur = -INFINITY;
 #pragma unroll 1
-      for (int c32 = 0; c32 < NCOL / 32 + (NCOL % 32 ? 1 : 0); ++c32) {
-        float v[32];
-        if constexpr (NCOL % 32 == 0) {
-          uint32_t x[32];
-          tmem_ld32(lane_addr + (j & 1) * NCOL + c32 * 32, x);
+        for (int c32 = 0; c32 < NCOL / 32 + (NCOL % 32 ? 1 : 0); ++c32) {
+          float v[32];
+          if constexpr (NCOL % 32 == 0) {
+            uint32_t x[32];
+            tmem_ld32(lane_addr + (j & 1) * NCOL + c32 * 32, x);
 #pragma unroll
-          for (int c = 0; c < 32; ++c) v[c] = __uint_as_float(x[c]);
-        } else {
-          uint32_t x[16];
-          tmem_ld16(lane_addr + (j & 1) * NCOL, x);
+            for (int c = 0; c < 32; ++c) v[c] = __uint_as_float(x[c]);
+          } else {
+            uint32_t x[16];
+            tmem_ld16(lane_addr + (j & 1) * NCOL, x);
 #pragma unroll
-          for (int c = 0; c < 16; ++c) v[c] = __uint_as_float(x[c]);
+            for (int c = 0; c < 16; ++c) v[c] = __uint_as_float(x[c]);
 #pragma unroll
-          for (int c = 16; c < 32; ++c) v[c] = -INFINITY;
-        }
+            for (int c = 16; c < 32; ++c) v[c] = -INFINITY;
+          }
 #pragma unroll
-        for (int c = 0; c < 32; ++c) {
-          const int gc = c32 * 32 + c;
-          if (gc < NCOL) {
-            cur = fmaxf(cur, fmaf(v[c], p.scale, -s_lse[gc]));
-            if (gc + 1 == next) {
-              if (tq < TQg && n <= s_last[tq]) p.scores[(rowbase + tq) * p.ld + n] = cur;
-              cur = -INFINITY;
-              ++tq;
-              next += p.H;
+          for (int c = 0; c < 32; ++c) {
+            const int gc = c32 * 32 + c;
+            if (gc < NCOL) {
+              cur = fmaxf(cur, fmaf(v[c], p.scale, -s_lse[gc]));
+              if (gc + 1 == next) {
+                if (tq < TQg && n <= s_last[tq]) p.scores[(rowbase + tq) * p.ld + n] = cur;
+                cur = -INFINITY;
+                ++tq;
+                next += p.H;
+              }
             }
           }
         }
+        tc_fence_before();
+        mbar_arrive(s_free + (j & 1));
       }
-      tc_fence_before();
-      mbar_arrive(s_free + (j & 1));
     }
+    jbase += ntiles;
+    // the segment is drained: its products were all read (or a wait failed)
+    ok = __syncthreads_and(ok);
+    tc_fence_after();
   }
   tc_fence_before();
   __syncthreads();
@@ -257,14 +374,48 @@ __device__ __forceinline__ int block_exclusive_scan(int v, int* s_warp, int* tot
   return before;
 }
 
+constexpr int SELECT_BINS = 2048;  // first-pass histogram bins
+constexpr int SELECT_CAND = 4096;  // keys of the threshold's bin kept in shared memory
+
+// Block-wide minimum and maximum of one key per thread.
+__device__ __forceinline__ void block_minmax(uint32_t& lo, uint32_t& hi, uint32_t* s_red) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    lo = min(lo, __shfl_xor_sync(0xffffffffu, lo, o));
+    hi = max(hi, __shfl_xor_sync(0xffffffffu, hi, o));
+  }
+  if (lane == 0) {
+    s_red[warp] = lo;
+    s_red[32 + warp] = hi;
+  }
+  __syncthreads();
+  lo = UINT_MAX;
+  hi = 0;
+  for (int w = 0; w < TOPK_THREADS / 32; ++w) {
+    lo = min(lo, s_red[w]);
+    hi = max(hi, s_red[32 + w]);
+  }
+  __syncthreads();
+}
+
 // One CTA per query: chosen[b, t, :K] from scores[b*T + t, 0 .. last].
+// The K-th largest key: a histogram of the keys over SELECT_BINS equal
+// ranges of [min key, max key] (a monotone map, so the bins are ordered)
+// finds the bin where the count from the top reaches K; the keys of that
+// bin, usually a few dozen, are gathered and sorted in shared memory. When
+// that bin holds more than SELECT_CAND keys, four 8-bit radix passes find
+// the key instead.
 __global__ void __launch_bounds__(TOPK_THREADS)
     topk_kernel(const float* __restrict__ scores, int64_t ld, const int64_t* __restrict__ positions,
                 int64_t* __restrict__ chosen, int T, int N, int K, int window, int cache_cap) {
-  extern __shared__ uint32_t s_keys[];  // cache_cap keys, then 256 histogram bins, then 32 scan slots
+  // dynamic shared memory: cache_cap keys, SELECT_BINS bins, SELECT_CAND candidates, 64 reduction slots
+  extern __shared__ uint32_t s_keys[];
   uint32_t* s_hist = s_keys + cache_cap;
-  int* s_warp = reinterpret_cast<int*>(s_hist + 256);
+  uint32_t* s_cand = s_hist + SELECT_BINS;
+  int* s_warp = reinterpret_cast<int*>(s_cand + SELECT_CAND);
   __shared__ uint32_t s_sel[2];
+  __shared__ int s_ncand;
   if (K <= 0) return;
   const int64_t row = blockIdx.x;
   const int64_t pos = positions[row];
@@ -278,75 +429,190 @@ __global__ void __launch_bounds__(TOPK_THREADS)
   }
   const float* src = scores + row * ld;
   const bool cached = count <= cache_cap;
-  if (cached)
-    for (int i = threadIdx.x; i < count; i += blockDim.x) s_keys[i] = order_key(src[i]);
-  uint32_t prefix = 0, mask = 0;
-  int remaining = K;  // how many of the top rows lie at or below the current prefix
-  for (int shift = 24; shift >= 0; shift -= 8) {
-    for (int i = threadIdx.x; i < 256; i += blockDim.x) s_hist[i] = 0;
-    __syncthreads();
+  auto key_at = [&](int i) { return cached ? s_keys[i] : order_key(src[i]); };
+  uint32_t lo = UINT_MAX, hi = 0;
+  // the row's keys (16-byte loads, four in flight per thread) into shared
+  // memory with their minimum and maximum
+  const bool vec = cached && (ld & 3) == 0 && (reinterpret_cast<uintptr_t>(scores) & 15) == 0;
+  const int n4 = vec ? count / 4 : 0;
+  for (int i4 = threadIdx.x; i4 < n4; i4 += 4 * TOPK_THREADS) {
+    float4 f[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u)
+      f[u] = i4 + u * TOPK_THREADS < n4 ? __ldg(reinterpret_cast<const float4*>(src) + i4 + u * TOPK_THREADS)
+                                       : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      if (i4 + u * TOPK_THREADS < n4) {
+        const uint4 k4 = make_uint4(order_key(f[u].x), order_key(f[u].y), order_key(f[u].z), order_key(f[u].w));
+        reinterpret_cast<uint4*>(s_keys)[i4 + u * TOPK_THREADS] = k4;
+        lo = min(lo, min(min(k4.x, k4.y), min(k4.z, k4.w)));
+        hi = max(hi, max(max(k4.x, k4.y), max(k4.z, k4.w)));
+      }
+    }
+  }
+  for (int i = 4 * n4 + threadIdx.x; i < count; i += blockDim.x) {
+    const uint32_t key = order_key(src[i]);
+    if (cached) s_keys[i] = key;
+    lo = min(lo, key);
+    hi = max(hi, key);
+  }
+  for (int i = threadIdx.x; i < SELECT_BINS; i += blockDim.x) s_hist[i] = 0;
+  if (threadIdx.x == 0) s_ncand = 0;
+  block_minmax(lo, hi, reinterpret_cast<uint32_t*>(s_warp));
+  // bin(key) = floor((key - lo) * SELECT_BINS / (hi - lo + 1)) in float: monotone in key
+  const float bscale = static_cast<float>(SELECT_BINS) / (static_cast<float>(hi - lo) + 1.f);
+  auto bin_of = [&](uint32_t key) {
+    return min(SELECT_BINS - 1, static_cast<int>(static_cast<float>(key - lo) * bscale));
+  };
+#pragma unroll 4
+  for (int i = threadIdx.x; i < count; i += blockDim.x) atomicAdd(&s_hist[bin_of(key_at(i))], 1u);
+  __syncthreads();
+  // the bin where the count from the top reaches K: thread t sums bins
+  // SELECT_BINS - 1 - (t * PER + e), e < PER, highest first
+  constexpr int PER = SELECT_BINS / TOPK_THREADS;
+  int mine = 0;
+#pragma unroll
+  for (int e = 0; e < PER; ++e) mine += s_hist[SELECT_BINS - 1 - (threadIdx.x * PER + e)];
+  int total;
+  const int before = block_exclusive_scan(mine, s_warp, &total);
+  if (before < K && before + mine >= K) {
+    int acc = before;
+    for (int e = 0; e < PER; ++e) {
+      const int bin = SELECT_BINS - 1 - (threadIdx.x * PER + e);
+      if (acc + static_cast<int>(s_hist[bin]) >= K) {
+        s_sel[0] = static_cast<uint32_t>(bin);
+        s_sel[1] = static_cast<uint32_t>(acc);  // keys in higher bins
+        break;
+      }
+      acc += s_hist[bin];
+    }
+  }
+  __syncthreads();
+  const int tbin = static_cast<int>(s_sel[0]);
+  const int above_bin = static_cast<int>(s_sel[1]);
+  const int nbin = static_cast<int>(s_hist[tbin]);
+  uint32_t thr;
+  int remaining;  // keys equal to thr that are taken
+  if (nbin <= SELECT_CAND) {
+#pragma unroll 4
     for (int i = threadIdx.x; i < count; i += blockDim.x) {
-      const uint32_t key = cached ? s_keys[i] : order_key(src[i]);
-      if ((key & mask) == prefix) atomicAdd(&s_hist[(key >> shift) & 255u], 1u);
+      const uint32_t key = key_at(i);
+      if (bin_of(key) == tbin) s_cand[atomicAdd(&s_ncand, 1)] = key;
     }
     __syncthreads();
-    if (threadIdx.x < 32) {  // the bin where the count from the top reaches `remaining`
-      const int lane = threadIdx.x;
-      uint32_t c[8];
-      int sum = 0;
-#pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        c[i] = s_hist[255 - (lane * 8 + i)];
-        sum += c[i];
+    int size = 2;
+    while (size < nbin) size <<= 1;
+    for (int e = nbin + threadIdx.x; e < size; e += blockDim.x) s_cand[e] = 0u;  // below every key
+    __syncthreads();
+    // bitonic sort, descending
+    for (int span = 2; span <= size; span <<= 1) {
+      for (int stride = span >> 1; stride > 0; stride >>= 1) {
+        for (int pr = threadIdx.x; pr < size / 2; pr += blockDim.x) {
+          const int a = 2 * stride * (pr / stride) + (pr % stride), b2 = a + stride;
+          const uint32_t ka = s_cand[a], kb = s_cand[b2];
+          if ((a & span) == 0 ? ka < kb : ka > kb) {
+            s_cand[a] = kb;
+            s_cand[b2] = ka;
+          }
+        }
+        __syncthreads();
       }
-      int incl = sum;  // inclusive scan over lanes, high bins first
-#pragma unroll
-      for (int o = 1; o < 32; o <<= 1) {
-        const int y = __shfl_up_sync(0xffffffffu, incl, o);
-        if (lane >= o) incl += y;
+    }
+    const int need = K - above_bin;  // 1 .. nbin keys of the bin are taken
+    thr = s_cand[need - 1];
+    int first = need - 1;  // the first position of thr in the sorted bin
+    while (first > 0 && s_cand[first - 1] == thr) --first;
+    remaining = need - first;
+    __syncthreads();
+  } else {  // a bin too full to gather: radix passes over all keys
+    uint32_t prefix = 0, mask = 0;
+    remaining = K;
+    for (int shift = 24; shift >= 0; shift -= 8) {
+      for (int i = threadIdx.x; i < 256; i += blockDim.x) s_hist[i] = 0;
+      __syncthreads();
+      for (int i = threadIdx.x; i < count; i += blockDim.x) {
+        const uint32_t key = key_at(i);
+        if ((key & mask) == prefix) atomicAdd(&s_hist[(key >> shift) & 255u], 1u);
       }
-      const int excl = incl - sum;
-      if (excl < remaining && incl >= remaining) {
-        int acc = excl;
+      __syncthreads();
+      if (threadIdx.x < 32) {  // the bin where the count from the top reaches `remaining`
+        const int lane = threadIdx.x;
+        uint32_t c[8];
+        int sum = 0;
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
-          if (acc + static_cast<int>(c[i]) >= remaining) {
-            s_sel[0] = 255 - (lane * 8 + i);
-            s_sel[1] = static_cast<uint32_t>(acc);
-            break;
+          c[i] = s_hist[255 - (lane * 8 + i)];
+          sum += c[i];
+        }
+        int incl = sum;  // inclusive scan over lanes, high bins first
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+          const int y = __shfl_up_sync(0xffffffffu, incl, o);
+          if (lane >= o) incl += y;
+        }
+        const int excl = incl - sum;
+        if (excl < remaining && incl >= remaining) {
+          int acc = excl;
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            if (acc + static_cast<int>(c[i]) >= remaining) {
+              s_sel[0] = 255 - (lane * 8 + i);
+              s_sel[1] = static_cast<uint32_t>(acc);
+              break;
+            }
+            acc += c[i];
           }
-          acc += c[i];
         }
       }
+      __syncthreads();
+      prefix |= s_sel[0] << shift;
+      mask |= 255u << shift;
+      remaining -= static_cast<int>(s_sel[1]);
+      __syncthreads();
     }
-    __syncthreads();
-    prefix |= s_sel[0] << shift;
-    mask |= 255u << shift;
-    remaining -= static_cast<int>(s_sel[1]);
-    __syncthreads();
+    thr = prefix;
   }
-  // prefix is the K-th largest key; `remaining` rows equal to it are taken
-  const uint32_t thr = prefix;
+  // every key above thr, and the `remaining` lowest-indexed keys equal to
+  // it, in row order: warp w takes rows [w * span, (w + 1) * span), 32 at a
+  // time (lane l reads row base + l, so shared memory serves a warp without
+  // bank conflicts); ballots rank the keys inside each step and the warps'
+  // counts place the warps
   const int above = K - remaining;
-  const int per = (count + TOPK_THREADS - 1) / TOPK_THREADS;
-  const int i0 = threadIdx.x * per, i1 = min(count, i0 + per);
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  constexpr int WARPS = TOPK_THREADS / 32;
+  const int span = (count + WARPS - 1) / WARPS;
+  const int w0 = min(count, warp * span), w1 = min(count, w0 + span);
   int gt = 0, eq = 0;
-  for (int i = i0; i < i1; ++i) {
-    const uint32_t key = cached ? s_keys[i] : order_key(src[i]);
-    gt += key > thr;
-    eq += key == thr;
+  for (int base = w0; base < w1; base += 32) {
+    const int i = base + lane;
+    const uint32_t key = i < w1 ? key_at(i) : 0u;
+    gt += __popc(__ballot_sync(0xffffffffu, i < w1 && key > thr));
+    eq += __popc(__ballot_sync(0xffffffffu, i < w1 && key == thr));
   }
-  int total;
-  int gt_off = block_exclusive_scan(gt, s_warp, &total);
-  int eq_off = block_exclusive_scan(eq, s_warp, &total);
-  for (int i = i0; i < i1; ++i) {
-    const uint32_t key = cached ? s_keys[i] : order_key(src[i]);
-    if (key > thr) {
-      out[gt_off++] = i;
-    } else if (key == thr) {
-      if (eq_off < remaining) out[above + eq_off] = i;
-      ++eq_off;
+  if (lane == 0) {
+    s_warp[warp] = gt;
+    s_warp[32 + warp] = eq;
+  }
+  __syncthreads();
+  int gt_off = 0, eq_off = 0;
+  for (int v = 0; v < warp; ++v) {
+    gt_off += s_warp[v];
+    eq_off += s_warp[32 + v];
+  }
+  const unsigned below = (1u << lane) - 1u;
+  for (int base = w0; base < w1; base += 32) {
+    const int i = base + lane;
+    const uint32_t key = i < w1 ? key_at(i) : 0u;
+    const bool is_gt = i < w1 && key > thr, is_eq = i < w1 && key == thr;
+    const unsigned bg = __ballot_sync(0xffffffffu, is_gt), be = __ballot_sync(0xffffffffu, is_eq);
+    if (is_gt) out[gt_off + __popc(bg & below)] = i;
+    if (is_eq) {
+      const int e = eq_off + __popc(be & below);
+      if (e < remaining) out[above + e] = i;
     }
+    gt_off += __popc(bg);
+    eq_off += __popc(be);
   }
 }
 

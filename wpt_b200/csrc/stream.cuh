@@ -273,6 +273,28 @@ __global__ void __launch_bounds__(STREAM_THREADS, 1)
       // issued, keeping two tiles in flight; before blocking on a free stage,
       // every issued tile is published first, since the consumer may need one
       // of them to free that stage.
+      // The rows of tile j + 1 are looked up (idx loads in flight) while
+      // tile j's copies are in flight.
+      auto lookup = [&](int j, int (&rw)[2]) {
+#pragma unroll
+        for (int half = 0; half < 2; ++half) {
+          const int64_t slot = (tile0 + j) * BN + lt + half * 64;
+          int64_t row = -1;
+          if (j < ntiles && slot < total) {
+            if (!gather) {
+              row = range_lo + slot;
+            } else if (slot < p.K) {
+              row = idx_row[slot];
+            } else {
+              row = pos_g - p.window + 1 + (slot - p.K);
+            }
+            if (row < 0 || row >= p.N) row = -1;
+          }
+          rw[half] = static_cast<int>(row);
+        }
+      };
+      int next_rows[2];
+      lookup(0, next_rows);
       bool ok = true;
       int published = 0;
       for (int j = 0; j < ntiles; ++j) {
@@ -291,22 +313,9 @@ __global__ void __launch_bounds__(STREAM_THREADS, 1)
         // a failed wait is carried to the barrier below, where the two loader
         // warps agree on it, and the stage's rows are left alone
         int* rows = s_row + st * BN;
-  #pragma unroll
-        for (int half = 0; half < 2 && ok; ++half) {
-          const int i = lt + half * 64;
-          const int64_t slot = (tile0 + j) * BN + i;
-          int64_t row = -1;
-          if (slot < total) {
-            if (!gather) {
-              row = range_lo + slot;
-            } else if (slot < p.K) {
-              row = idx_row[slot];
-            } else {
-              row = pos_g - p.window + 1 + (slot - p.K);
-            }
-            if (row < 0 || row >= p.N) row = -1;
-          }
-          rows[i] = static_cast<int>(row);
+        if (ok) {
+          rows[lt] = next_rows[0];
+          rows[lt + 64] = next_rows[1];
         }
         ok = named_barrier_and(2, STREAM_LOADERS, ok);
         if (!ok) break;
@@ -322,6 +331,7 @@ __global__ void __launch_bounds__(STREAM_THREADS, 1)
           cp_async_16(dv + off, has ? vb + static_cast<int64_t>(row) * p.vsn + ch * 8 : p.v, has);
         }
         cp_async_commit();
+        lookup(j + 1, next_rows);
         if (published == j - 1) {
           cp_async_wait<1>();
           fence_proxy_async();

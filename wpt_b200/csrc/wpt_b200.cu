@@ -219,7 +219,10 @@ int launch_score(const CUtensorMap& tq, const CUtensorMap& tk, const wpt::ScoreP
   static_assert(L::BYTES <= 232448, "score kernel shared memory exceeds 227 KB");
   auto kernel = wpt::score_kernel<NCOL, STAGES>;
   if (int rc = allow_smem(kernel, L::BYTES)) return rc;
-  kernel<<<dim3(groups, splits), 192, L::BYTES, stream>>>(tq, tk, p);
+  int sms = 148;
+  current_device(&sms);
+  const dim3 grid = p.balanced ? dim3(sms) : dim3(groups, splits);  // balanced: one CTA per SM
+  kernel<<<grid, 192, L::BYTES, stream>>>(tq, tk, p);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "score_kernel launch");
   return WPT_OK;
@@ -441,6 +444,9 @@ extern "C" int wpt_attn_topk(const void* q, const void* k, int64_t k_stride_b, i
   p.groups_per_row = (T + p.TQ - 1) / p.TQ;
   p.scale = scale;
   const int64_t groups = static_cast<int64_t>(B) * p.groups_per_row;
+  // one query per group (decode) and few groups: the groups' live key tiles
+  // split evenly over one CTA per SM, whatever the rows' lengths
+  p.balanced = T == 1 && p.TQ == 1 && groups <= wpt::SCORE_BAL_GROUPS ? 1 : 0;
   const int tiles = (N + 127) / 128;
   int64_t chunk = (static_cast<int64_t>(tiles) * groups + 4 * 148 - 1) / (4 * 148);
   if (chunk < 4) chunk = 4;
@@ -467,7 +473,7 @@ extern "C" int wpt_attn_topk(const void* q, const void* k, int64_t k_stride_b, i
   }
   if (rc) return rc;
   const int cap = N < 49152 ? N : 49152;
-  const int smem = (cap + 256 + 32) * 4;
+  const int smem = (cap + wpt::SELECT_BINS + wpt::SELECT_CAND + 64) * 4;
   if (int rc2 = allow_smem(wpt::topk_kernel, smem)) return rc2;
   wpt::topk_kernel<<<static_cast<unsigned>(static_cast<int64_t>(B) * T), wpt::TOPK_THREADS, smem, s>>>(
       scores, ld_scores, positions, chosen, T, N, K, window, cap);

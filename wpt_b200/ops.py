@@ -129,10 +129,16 @@ def stream_forward(q, k, v, positions, scale, window=0, floor=None, idx=None, si
         slots = min(N, window + TQ - 1) if window > 0 else N
     tiles = max(1, math.ceil(slots / 128))
     if chunk_tiles is None:
+        chunk_tiles = int(os.environ.get("WPT_B200_CHUNK", "0"))
+    if not chunk_tiles and gather:
+        # every query gathers exactly `tiles` tiles: its slots split so that
+        # the grid is about one CTA per SM
+        chunk_tiles = math.ceil(tiles / max(1, SM_COUNT // groups))
+    elif not chunk_tiles:
         # at least 16 key tiles per CTA (a CTA's start-up costs about as much
-        # as streaming a few tiles), more when that still gives two CTAs per SM
-        chunk_tiles = int(os.environ.get("WPT_B200_CHUNK", "0")) or max(
-            min(16, tiles), 16 * math.ceil(tiles * groups / (2 * SM_COUNT) / 16))
+        # as streaming a few tiles), more when that still gives two CTAs per
+        # SM for rows of the table's full length (most rows are shorter)
+        chunk_tiles = max(min(16, tiles), 16 * math.ceil(tiles * groups / (2 * SM_COUNT) / 16))
     chunk_tiles = max(1, min(int(chunk_tiles), tiles))
     splits = math.ceil(tiles / chunk_tiles)
     out = torch.empty_like(q)
