@@ -189,3 +189,27 @@ def test_partials_merged_by_the_caller_equal_the_whole_call(wb):
     ref_out, ref_lse, _ = oat.exact_attention(_np(q), _np(e[..., :C]), _np(e[..., C:]), positions.numpy(),
                                               C ** -0.5, 0, 0)
     _check(wb, out.reshape(1, 1, 32, C), lse.reshape(1, 1, 32), ref_out, ref_lse)
+
+
+def test_sparse_window_rows_outside_the_table(wb):
+    """Gather mode's window tiles come by TMA: windows that start before row
+    0 (early positions) or run past the table's end (a position beyond it)
+    read zeros there and mask those rows, as the reference's -1 rows are."""
+    B, T, H, N, K, W = 4, 1, 32, 1500, 256, 1024
+    g = torch.Generator().manual_seed(77)
+    C = 128
+    q = torch.randn(B, T, H, C, generator=g).bfloat16()
+    e = torch.randn(B, N, 2 * C, generator=g).bfloat16()
+    sink = torch.randn(H, generator=g) * 0.5
+    positions = torch.tensor([[5], [700], [1499], [1540]])
+    idx = torch.full((B, T, K), -1, dtype=torch.long)
+    for b in range(B):
+        far = int(positions[b, 0]) - W + 1
+        if far > 0:
+            pick = torch.randperm(far, generator=g)[:K]
+            idx[b, 0, :len(pick)] = pick
+    out = wb.sparse_attention(q.cuda(), e.cuda()[..., :C], e.cuda()[..., C:], sink.cuda(), idx.cuda(),
+                              positions.cuda(), C ** -0.5, W)
+    ref_out, _ = oat.sparse_attention(_np(q), _np(e[..., :C]), _np(e[..., C:]), sink.double().numpy(), idx.numpy(),
+                                      positions.numpy(), C ** -0.5, W)
+    _check(wb, out, None, ref_out, None)

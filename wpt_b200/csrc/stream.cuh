@@ -22,10 +22,11 @@
 // more than one split every CTA writes a partial result for the merge
 // kernel (merge.cuh).
 //
-// Loads: 2 loader warps copy each slot's 256-byte K and V rows with 16-byte
-// cp.async (coalesced: 16 lanes per row) into 128-byte-swizzled tiles, so
-// arbitrary row gathers cost the same as contiguous ones; they publish a
-// stage after cp.async.wait_group and a proxy fence. Warp 4 issues the MMAs.
+// Loads: range mode takes whole tiles by TMA. Gather mode: 2 loader warps
+// copy each slot's 256-byte K and V rows with 16-byte cp.async (coalesced:
+// 16 lanes per row) into 128-byte-swizzled tiles and publish a stage after
+// cp.async.wait_group and a proxy fence; a tile of the query's window rows
+// (one contiguous range) comes by TMA instead. Warp 4 issues the MMAs.
 // Warps 0-3 do the softmax: thread r owns slot r of a tile, holds its
 // NCOL scores, and the per-column maximum and sum over the 128 slots come
 // from a 31-shuffle transpose reduction per warp plus shared memory across
@@ -55,6 +56,7 @@ struct StreamParams {
   float* part_lse;             // (splits, B*T*H)
   unsigned* status;
   int B, T, H, N, K, window, TQ, groups_per_row, splits, chunk_tiles;
+  int window_tma;              // gather mode: tiles of window rows come by TMA (the maps are valid)
   float scale_log2;
 };
 
@@ -190,9 +192,15 @@ __global__ void __launch_bounds__(STREAM_THREADS, 1)
     total = s_range[1] >= s_range[0] ? static_cast<int64_t>(s_range[1]) - s_range[0] + 1 : 0;
   }
   const int64_t tiles_total = (total + BN - 1) / BN;
+  // range mode: chunk_tiles consecutive tiles per split; gather mode: tiles
+  // split, split + splits, ... (the window's contiguous tiles, loaded by TMA,
+  // and the gathered ones spread evenly over the splits)
   const int64_t tile0 = static_cast<int64_t>(split) * p.chunk_tiles;
   const int64_t left = tiles_total - tile0;
-  const int ntiles = static_cast<int>(left <= 0 ? 0 : (left < p.chunk_tiles ? left : p.chunk_tiles));
+  const int ntiles =
+      GATHER ? static_cast<int>(split < tiles_total ? (tiles_total - split + gridDim.y - 1) / gridDim.y : 0)
+             : static_cast<int>(left <= 0 ? 0 : (left < p.chunk_tiles ? left : p.chunk_tiles));
+  auto tile_of = [&](int j) -> int64_t { return GATHER ? split + static_cast<int64_t>(j) * gridDim.y : tile0 + j; };
 
   if (ntiles == 0) {  // nothing to read: an empty partial, or the sink alone
     if (static_cast<int>(threadIdx.x) < NCOL) {
@@ -278,7 +286,7 @@ __global__ void __launch_bounds__(STREAM_THREADS, 1)
       auto lookup = [&](int j, int (&rw)[2]) {
 #pragma unroll
         for (int half = 0; half < 2; ++half) {
-          const int64_t slot = (tile0 + j) * BN + lt + half * 64;
+          const int64_t slot = tile_of(j) * BN + lt + half * 64;
           int64_t row = -1;
           if (j < ntiles && slot < total) {
             if (!gather) {
@@ -320,15 +328,29 @@ __global__ void __launch_bounds__(STREAM_THREADS, 1)
         ok = named_barrier_and(2, STREAM_LOADERS, ok);
         if (!ok) break;
         const uint32_t dk = smem_u32(sK + st * L::KV_BYTES), dv = smem_u32(sV + st * L::KV_BYTES);
-  #pragma unroll 4
-        for (int it = 0; it < (BN * 16) / STREAM_LOADERS; ++it) {
-          const int flat = it * STREAM_LOADERS + lt;
-          const int r = flat >> 4, ch = flat & 15;
-          const int row = rows[r];
-          const bool has = row >= 0;
-          const uint32_t off = (ch >> 3) * (BN * 128) + sw128_offset(r, ch & 7);
-          cp_async_16(dk + off, has ? kb + static_cast<int64_t>(row) * p.ksn + ch * 8 : p.k, has);
-          cp_async_16(dv + off, has ? vb + static_cast<int64_t>(row) * p.vsn + ch * 8 : p.v, has);
+        const int64_t first = tile_of(j) * BN;
+        if (gather && p.window_tma && first >= p.K) {
+          // a tile of window rows is one contiguous range: whole tiles by TMA
+          // (rows outside the table read as zeros and are masked)
+          if (lt == 0) {
+            const int n0 = static_cast<int>(pos_g - p.window + 1 + (first - p.K));
+            mbar_expect_tx_only(full + st, 2 * L::KV_BYTES);
+            tma_load_3d(sK + st * L::KV_BYTES, &tm_k, full + st, 0, n0, b);
+            tma_load_3d(sK + st * L::KV_BYTES + BN * 128, &tm_k, full + st, 64, n0, b);
+            tma_load_3d(sV + st * L::KV_BYTES, &tm_v, full + st, 0, n0, b);
+            tma_load_3d(sV + st * L::KV_BYTES + BN * 128, &tm_v, full + st, 64, n0, b);
+          }
+        } else {
+#pragma unroll 4
+          for (int it = 0; it < (BN * 16) / STREAM_LOADERS; ++it) {
+            const int flat = it * STREAM_LOADERS + lt;
+            const int r = flat >> 4, ch = flat & 15;
+            const int row = rows[r];
+            const bool has = row >= 0;
+            const uint32_t off = (ch >> 3) * (BN * 128) + sw128_offset(r, ch & 7);
+            cp_async_16(dk + off, has ? kb + static_cast<int64_t>(row) * p.ksn + ch * 8 : p.k, has);
+            cp_async_16(dv + off, has ? vb + static_cast<int64_t>(row) * p.vsn + ch * 8 : p.v, has);
+          }
         }
         cp_async_commit();
         lookup(j + 1, next_rows);

@@ -396,12 +396,19 @@ extern "C" int wpt_attn_decode(const void* q, const void* k, const void* v, int6
   p.scale_log2 = scale * wpt::LOG2E;
   const int64_t groups = static_cast<int64_t>(B) * p.groups_per_row;
   if (groups >= (int64_t(1) << 31)) return fail(WPT_ERR_UNSUPPORTED, "too many query groups");
-  CUtensorMap tk, tv;  // range mode loads whole tiles by TMA; gather mode does not read the maps
+  // range mode loads whole tiles by TMA; gather mode loads its window's
+  // tiles by TMA when the tables allow tensor maps, else copies every row
+  CUtensorMap tk, tv;
   memset(&tk, 0, sizeof(tk));
   memset(&tv, 0, sizeof(tv));
-  if (!gather) {
+  const auto mappable = [&](const void* t, int64_t sb, int64_t sn) {
+    return aligned16(t) && sn % 8 == 0 && (B == 1 || sb % 8 == 0) && sn >= C;
+  };
+  p.window_tma = 0;
+  if (!gather || (mappable(k, k_stride_b, k_stride_n) && mappable(v, v_stride_b, v_stride_n) && window > 0)) {
     if (int rc = table_map(&tk, k, k_stride_b, k_stride_n, B, N, C)) return rc;
     if (int rc = table_map(&tv, v, v_stride_b, v_stride_n, B, N, C)) return rc;
+    p.window_tma = gather ? 1 : 0;
   }
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const int rc = gather ? launch_stream_g<true>(tk, tv, p, ncol, static_cast<int>(groups), s)
