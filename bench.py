@@ -398,6 +398,30 @@ def profile_case(args):
         q = (torch.randn(B, 1, 32, C, generator=g, device=device) * 0.5).bfloat16()
         pos = (L - 1).to(device)[:, None].contiguous()
         fn = lambda: ops.stream_forward(q, table[..., :C], table[..., C:], pos, C ** -0.5)  # noqa: E731
+    elif args.case == "select":  # config 3's first B rows: exact + top-1024 choice, then the sparse layer
+        L = config3_lengths()[:B]
+        g = torch.Generator(device=device).manual_seed(10)
+        table = (torch.randn(B, 32768, 2 * C, generator=g, device=device) * 0.5).bfloat16()
+        q = (torch.randn(B, 1, 32, C, generator=g, device=device) * 0.5).bfloat16()
+        sink = torch.randn(32, generator=g, device=device) * 0.5
+        pos = (L - 1).to(device)[:, None].contiguous()
+        k, v = table[..., :C], table[..., C:]
+
+        def fn():
+            _, chosen = wpt_b200.exact_attention(q, k, v, pos, C ** -0.5, 1024, 128)
+            wpt_b200.sparse_attention(q, k, v, sink, chosen, pos, C ** -0.5, 1024)
+    elif args.case == "accept":  # config 4's acceptance on B rows, stochastic then greedy
+        R, n, V = B, 16, 65536
+        ga = torch.Generator(device=device).manual_seed(4)
+        scores = torch.randn(R, n + 1, V, generator=ga, device=device) * 2.0
+        qprob = torch.softmax(torch.randn(R, n, V, generator=ga, device=device) * 2.0, -1)
+        drafted = torch.multinomial(qprob.reshape(-1, V), 1, generator=ga).view(R, n)
+        uniforms = torch.rand(R, n, generator=ga, device=device)
+        resample = torch.rand(R, generator=ga, device=device)
+
+        def fn():
+            wpt_b200.accept(scores, drafted, qprob, uniforms, resample, 1.0, None)
+            wpt_b200.accept(scores, drafted, qprob, uniforms, resample, 1.0, 1)
     else:
         raise SystemExit(f"unknown case {args.case}")
     for _ in range(args.warmup):
@@ -418,7 +442,8 @@ def main():
     parser.add_argument("--impl", default="b200", choices=["b200", "reference"])
     parser.add_argument("--no-secondary", action="store_true")
     parser.add_argument("--e2e-steps", type=int, default=10)
-    parser.add_argument("--case", default=None, help="profile one kernel: prefill, window or decode")
+    parser.add_argument("--case", default=None,
+                        help="profile one path: prefill, window, decode, select (A4 + A5) or accept")
     parser.add_argument("--case-batch", type=int, default=4)
     args = parser.parse_args()
     if args.case:
