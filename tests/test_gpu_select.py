@@ -152,3 +152,19 @@ def test_decode_choice_over_ragged_rows(wb, tied):
     _, _, expected = oat.exact_attention(_np(q), k, _np(e[..., C:]), positions.numpy(), C ** -0.5, top_k, window)
     pos_clipped = np.minimum(positions.numpy(), N - 1)
     _assert_chosen_alike(_np(q), k, pos_clipped, C ** -0.5, chosen.cpu().numpy(), expected)
+
+
+def test_decode_choice_over_rows_longer_than_the_key_cache(wb):
+    """Rows of more candidates than the select kernel caches in shared
+    memory: the passes read the scores from global memory."""
+    g = torch.Generator().manual_seed(11)
+    B, T, H, C, N, top_k, window = 2, 1, 32, 128, 60000, 1024, 128
+    q = torch.randn(B, T, H, C, generator=g).bfloat16()
+    e = torch.randn(B, N, 2 * C, generator=g).bfloat16()
+    positions = torch.tensor([[59999], [50000]])
+    qd, ed = q.cuda(), e.cuda()
+    _, chosen = wb.exact_attention(qd, ed[..., :C], ed[..., C:], positions.cuda(), C ** -0.5, top_k, window)
+    assert wb.device_status() == 0
+    k = _np(e[..., :C])
+    _, _, expected = oat.exact_attention(_np(q), k, _np(e[..., C:]), positions.numpy(), C ** -0.5, top_k, window)
+    _assert_chosen_alike(_np(q), k, positions.numpy(), C ** -0.5, chosen.cpu().numpy(), expected)

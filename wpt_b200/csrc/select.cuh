@@ -344,7 +344,7 @@ __device__ __forceinline__ uint32_t order_key(float x) {
   return (bits & 0x80000000u) ? ~bits : (bits | 0x80000000u);
 }
 
-constexpr int TOPK_THREADS = 512;
+constexpr int TOPK_THREADS = 1024;
 
 // Block-wide exclusive scan of one int per thread (TOPK_THREADS threads);
 // returns this thread's prefix and sets *total.
@@ -375,7 +375,7 @@ __device__ __forceinline__ int block_exclusive_scan(int v, int* s_warp, int* tot
 }
 
 constexpr int SELECT_BINS = 2048;  // first-pass histogram bins
-constexpr int SELECT_CAND = 4096;  // keys of the threshold's bin kept in shared memory
+constexpr int SELECT_CAND = 4096;  // (key, row) pairs of the threshold's bin kept in shared memory
 
 // Block-wide minimum and maximum of one key per thread.
 __device__ __forceinline__ void block_minmax(uint32_t& lo, uint32_t& hi, uint32_t* s_red) {
@@ -409,10 +409,11 @@ __device__ __forceinline__ void block_minmax(uint32_t& lo, uint32_t& hi, uint32_
 __global__ void __launch_bounds__(TOPK_THREADS)
     topk_kernel(const float* __restrict__ scores, int64_t ld, const int64_t* __restrict__ positions,
                 int64_t* __restrict__ chosen, int T, int N, int K, int window, int cache_cap) {
-  // dynamic shared memory: cache_cap keys, SELECT_BINS bins, SELECT_CAND candidates, 64 reduction slots
+  // dynamic shared memory: cache_cap keys, SELECT_BINS bins, SELECT_CAND
+  // 8-byte candidates (8-byte aligned), 64 reduction slots
   extern __shared__ uint32_t s_keys[];
   uint32_t* s_hist = s_keys + cache_cap;
-  uint32_t* s_cand = s_hist + SELECT_BINS;
+  uint64_t* s_cand = reinterpret_cast<uint64_t*>(s_hist + SELECT_BINS + (cache_cap & 1));
   int* s_warp = reinterpret_cast<int*>(s_cand + SELECT_CAND);
   __shared__ uint32_t s_sel[2];
   __shared__ int s_ncand;
@@ -492,26 +493,41 @@ __global__ void __launch_bounds__(TOPK_THREADS)
   const int tbin = static_cast<int>(s_sel[0]);
   const int above_bin = static_cast<int>(s_sel[1]);
   const int nbin = static_cast<int>(s_hist[tbin]);
+  // Rows are read in warp spans: warp w takes rows [w * span, (w + 1) * span),
+  // 32 at a time (lane l reads row base + l, so shared memory serves a warp
+  // without bank conflicts); ballots rank keys inside a step.
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  constexpr int WARPS = TOPK_THREADS / 32;
+  const int span = (count + WARPS - 1) / WARPS;
+  const int w0 = min(count, warp * span), w1 = min(count, w0 + span);
   uint32_t thr;
-  int remaining;  // keys equal to thr that are taken
+  int remaining;    // keys equal to thr that are taken
+  int gt = 0, eq = 0;  // this warp's keys above thr and equal to it
   if (nbin <= SELECT_CAND) {
+    // one pass: the threshold bin's (key, row) pairs into shared memory, and
+    // this warp's count of keys in higher bins
+    if (threadIdx.x < 64) s_warp[threadIdx.x] = 0;
+    int hi_w = 0;
 #pragma unroll 4
-    for (int i = threadIdx.x; i < count; i += blockDim.x) {
-      const uint32_t key = key_at(i);
-      if (bin_of(key) == tbin) s_cand[atomicAdd(&s_ncand, 1)] = key;
+    for (int base = w0; base < w1; base += 32) {
+      const int i = base + lane;
+      const uint32_t key = i < w1 ? key_at(i) : 0u;
+      const int bin = i < w1 ? bin_of(key) : -1;
+      hi_w += __popc(__ballot_sync(0xffffffffu, bin > tbin));
+      if (bin == tbin) s_cand[atomicAdd(&s_ncand, 1)] = (static_cast<uint64_t>(key) << 32) | static_cast<uint32_t>(i);
     }
     __syncthreads();
     int size = 2;
     while (size < nbin) size <<= 1;
-    for (int e = nbin + threadIdx.x; e < size; e += blockDim.x) s_cand[e] = 0u;  // below every key
+    for (int e = nbin + threadIdx.x; e < size; e += blockDim.x) s_cand[e] = 0ull;  // below every pair
     __syncthreads();
     // bitonic sort, descending
-    for (int span = 2; span <= size; span <<= 1) {
-      for (int stride = span >> 1; stride > 0; stride >>= 1) {
+    for (int sp = 2; sp <= size; sp <<= 1) {
+      for (int stride = sp >> 1; stride > 0; stride >>= 1) {
         for (int pr = threadIdx.x; pr < size / 2; pr += blockDim.x) {
           const int a = 2 * stride * (pr / stride) + (pr % stride), b2 = a + stride;
-          const uint32_t ka = s_cand[a], kb = s_cand[b2];
-          if ((a & span) == 0 ? ka < kb : ka > kb) {
+          const uint64_t ka = s_cand[a], kb = s_cand[b2];
+          if ((a & sp) == 0 ? ka < kb : ka > kb) {
             s_cand[a] = kb;
             s_cand[b2] = ka;
           }
@@ -520,10 +536,20 @@ __global__ void __launch_bounds__(TOPK_THREADS)
       }
     }
     const int need = K - above_bin;  // 1 .. nbin keys of the bin are taken
-    thr = s_cand[need - 1];
+    thr = static_cast<uint32_t>(s_cand[need - 1] >> 32);
     int first = need - 1;  // the first position of thr in the sorted bin
-    while (first > 0 && s_cand[first - 1] == thr) --first;
+    while (first > 0 && static_cast<uint32_t>(s_cand[first - 1] >> 32) == thr) --first;
     remaining = need - first;
+    // the bin's keys above thr and equal to it, counted into their rows' warps
+    for (int e = threadIdx.x; e < nbin; e += blockDim.x) {
+      const uint32_t key = static_cast<uint32_t>(s_cand[e] >> 32);
+      const int w = static_cast<int>(static_cast<uint32_t>(s_cand[e])) / span;
+      if (key > thr) atomicAdd(&s_warp[w], 1);
+      else if (key == thr) atomicAdd(&s_warp[32 + w], 1);
+    }
+    __syncthreads();
+    gt = hi_w + s_warp[warp];
+    eq = s_warp[32 + warp];
     __syncthreads();
   } else {  // a bin too full to gather: radix passes over all keys
     uint32_t prefix = 0, mask = 0;
@@ -537,7 +563,6 @@ __global__ void __launch_bounds__(TOPK_THREADS)
       }
       __syncthreads();
       if (threadIdx.x < 32) {  // the bin where the count from the top reaches `remaining`
-        const int lane = threadIdx.x;
         uint32_t c[8];
         int sum = 0;
 #pragma unroll
@@ -572,24 +597,17 @@ __global__ void __launch_bounds__(TOPK_THREADS)
       __syncthreads();
     }
     thr = prefix;
+#pragma unroll 4
+    for (int base = w0; base < w1; base += 32) {
+      const int i = base + lane;
+      const uint32_t key = i < w1 ? key_at(i) : 0u;
+      gt += __popc(__ballot_sync(0xffffffffu, i < w1 && key > thr));
+      eq += __popc(__ballot_sync(0xffffffffu, i < w1 && key == thr));
+    }
   }
   // every key above thr, and the `remaining` lowest-indexed keys equal to
-  // it, in row order: warp w takes rows [w * span, (w + 1) * span), 32 at a
-  // time (lane l reads row base + l, so shared memory serves a warp without
-  // bank conflicts); ballots rank the keys inside each step and the warps'
-  // counts place the warps
+  // it, in row order: the warps' counts place the warps
   const int above = K - remaining;
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  constexpr int WARPS = TOPK_THREADS / 32;
-  const int span = (count + WARPS - 1) / WARPS;
-  const int w0 = min(count, warp * span), w1 = min(count, w0 + span);
-  int gt = 0, eq = 0;
-  for (int base = w0; base < w1; base += 32) {
-    const int i = base + lane;
-    const uint32_t key = i < w1 ? key_at(i) : 0u;
-    gt += __popc(__ballot_sync(0xffffffffu, i < w1 && key > thr));
-    eq += __popc(__ballot_sync(0xffffffffu, i < w1 && key == thr));
-  }
   if (lane == 0) {
     s_warp[warp] = gt;
     s_warp[32 + warp] = eq;
@@ -601,6 +619,7 @@ __global__ void __launch_bounds__(TOPK_THREADS)
     eq_off += s_warp[32 + v];
   }
   const unsigned below = (1u << lane) - 1u;
+#pragma unroll 4
   for (int base = w0; base < w1; base += 32) {
     const int i = base + lane;
     const uint32_t key = i < w1 ? key_at(i) : 0u;

@@ -479,8 +479,8 @@ extern "C" int wpt_attn_topk(const void* q, const void* k, int64_t k_stride_b, i
     default: rc = launch_score<256>(tq, tk, p, static_cast<int>(groups), splits, s); break;
   }
   if (rc) return rc;
-  const int cap = N < 49152 ? N : 49152;
-  const int smem = (cap + wpt::SELECT_BINS + wpt::SELECT_CAND + 64) * 4;
+  const int cap = N < 47104 ? N : 47104;  // keys cached in shared memory (the rest of it: bins, candidates)
+  const int smem = (cap + 1 + wpt::SELECT_BINS + 2 * wpt::SELECT_CAND + 64) * 4;
   if (int rc2 = allow_smem(wpt::topk_kernel, smem)) return rc2;
   wpt::topk_kernel<<<static_cast<unsigned>(static_cast<int64_t>(B) * T), wpt::TOPK_THREADS, smem, s>>>(
       scores, ld_scores, positions, chosen, T, N, K, window, cap);
