@@ -22,6 +22,7 @@ __global__ void __launch_bounds__(256) merge_kernel(const float* __restrict__ pa
                                                     int64_t rows, int64_t split_stride, int H,
                                                     const float* __restrict__ sink, __nv_bfloat16* __restrict__ out,
                                                     float* __restrict__ lse_out) {
+  griddep_wait();  // the partials come from the kernel before (programmatic dependent launch)
   const int64_t row = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (row >= rows) return;
@@ -63,6 +64,7 @@ template <int C>
 __global__ void __launch_bounds__(MERGE_THREADS) merge_wide_kernel(
     const float* __restrict__ part_o, const float* __restrict__ part_lse, int splits, int64_t split_stride, int H,
     const float* __restrict__ sink, __nv_bfloat16* __restrict__ out, float* __restrict__ lse_out) {
+  griddep_wait();  // the partials come from the kernel before (programmatic dependent launch)
   constexpr int GROUPS = MERGE_THREADS / C;
   __shared__ float s_w[MERGE_MAX_SPLITS];
   __shared__ float s_red[MERGE_THREADS / 32 + 1];

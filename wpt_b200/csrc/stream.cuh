@@ -240,6 +240,7 @@ __global__ void __launch_bounds__(STREAM_THREADS, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *s_tmem;
+  griddep_launch();  // the merge that follows may start launching (it waits for this grid's results)
 
   if (warp >= 5) {
     // ---------------------------------------------------------- loaders

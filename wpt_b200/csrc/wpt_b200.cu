@@ -229,18 +229,32 @@ int launch_score(const CUtensorMap& tq, const CUtensorMap& tk, const wpt::ScoreP
 }
 
 template <int C>
+// pdl: the merge directly follows the attention kernel that wrote the
+// partials, and launches while that kernel finishes (programmatic dependent
+// launch; the merge waits for it on the device before reading).
 int launch_merge(const float* part_o, const float* part_lse, int splits, int64_t rows, int64_t split_stride, int H,
-                 const float* sink, void* out, float* lse, cudaStream_t stream) {
+                 const float* sink, void* out, float* lse, cudaStream_t stream, bool pdl = false) {
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  cfg.stream = stream;
+  cfg.dynamicSmemBytes = 0;
+  __nv_bfloat16* o = static_cast<__nv_bfloat16*>(out);
+  cudaError_t e;
   if (splits >= 16 && splits <= wpt::MERGE_MAX_SPLITS && rows <= 4096) {  // few rows, many splits: a CTA per row
-    wpt::merge_wide_kernel<C><<<static_cast<unsigned>(rows), wpt::MERGE_THREADS, 0, stream>>>(
-        part_o, part_lse, splits, split_stride, H, sink, static_cast<__nv_bfloat16*>(out), lse);
+    cfg.gridDim = dim3(static_cast<unsigned>(rows));
+    cfg.blockDim = dim3(wpt::MERGE_THREADS);
+    e = cudaLaunchKernelEx(&cfg, wpt::merge_wide_kernel<C>, part_o, part_lse, splits, split_stride, H, sink, o, lse);
   } else {
     const int warps = 8;
     const int64_t blocks = (rows + warps - 1) / warps;
-    wpt::merge_kernel<C><<<static_cast<unsigned>(blocks), warps * 32, 0, stream>>>(
-        part_o, part_lse, splits, rows, split_stride, H, sink, static_cast<__nv_bfloat16*>(out), lse);
+    cfg.gridDim = dim3(static_cast<unsigned>(blocks));
+    cfg.blockDim = dim3(warps * 32);
+    e = cudaLaunchKernelEx(&cfg, wpt::merge_kernel<C>, part_o, part_lse, splits, rows, split_stride, H, sink, o, lse);
   }
-  cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "merge_kernel launch");
   return WPT_OK;
 }
@@ -323,8 +337,8 @@ extern "C" int wpt_attn_prefill(const void* q, const void* k, const void* v, int
   if (rc) return rc;
   if (splits > 1) {
     const int64_t rows = static_cast<int64_t>(B) * T * H;
-    rc = C == 128 ? launch_merge<128>(part_o, part_lse, splits, rows, rows, H, sink, out, lse, s)
-                  : launch_merge<64>(part_o, part_lse, splits, rows, rows, H, sink, out, lse, s);
+    rc = C == 128 ? launch_merge<128>(part_o, part_lse, splits, rows, rows, H, sink, out, lse, s, true)
+                  : launch_merge<64>(part_o, part_lse, splits, rows, rows, H, sink, out, lse, s, true);
   }
   return rc;
 }
@@ -416,7 +430,7 @@ extern "C" int wpt_attn_decode(const void* q, const void* k, const void* v, int6
   if (rc) return rc;
   if (splits > 1 && !partials_only) {
     const int64_t rows = static_cast<int64_t>(B) * T * H;
-    return launch_merge<128>(part_o, part_lse, splits, rows, rows, H, sink, out, lse, s);
+    return launch_merge<128>(part_o, part_lse, splits, rows, rows, H, sink, out, lse, s, true);
   }
   return WPT_OK;
 }
