@@ -46,11 +46,19 @@ def _rows(x):
 
 
 def _splits_for(ctas, tiles):
-    """Split count that gives at least about two CTAs per SM when the grid
-    is small, never more splits than key tiles."""
+    """Split count for a grid of `ctas` work items over `tiles` key tiles
+    each: the persistent kernel runs the ctas * splits items in waves of
+    one per SM, so the estimate is waves x (tiles per item + about 2 tiles'
+    worth of per-item cost), plus half a tile per split for the merge; the
+    cheapest count up to 32 (never more than the tiles) wins."""
     if ctas >= SM_COUNT or tiles <= 1:
         return 1
-    return int(max(1, min(tiles, 32, math.ceil(2 * SM_COUNT / ctas))))
+    best, best_cost = 1, None
+    for s in range(1, min(tiles, 32) + 1):
+        cost = math.ceil(ctas * s / SM_COUNT) * (tiles / s + 2) + (0.5 * s if s > 1 else 0.0)
+        if best_cost is None or cost < best_cost:
+            best, best_cost = s, cost
+    return best
 
 
 def prefill_forward(q, k, v, positions, scale, window=0, floor=None, tree_bits=None, tree_base=None, sink=None,
