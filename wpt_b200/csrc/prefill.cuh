@@ -33,6 +33,11 @@
 // of O_A needs. Q pairs have QB buffers; K and V tiles stream through one
 // ring of NS stages, K one tile ahead: K(0), K(1), V(0), K(2), V(1), ...
 //
+// Output: a full query tile's rows go, as bf16, into the item's own Q
+// buffer (free once the item's last product is done) in the swizzled
+// layout of a TMA box, and one TMA store per 64 columns writes them out; the
+// loader reloads that buffer only after the store has read it (q_stored).
+//
 // Online softmax in base 2 with a lazy maximum: a row's running maximum is
 // only raised (and O rescaled) when a tile's maximum exceeds it by more
 // than 8, so P stays below 2^8 and O is rarely touched. The rescale is done
@@ -77,6 +82,7 @@ struct PrefillParams {
   float* part_lse;            // (splits, B*T*H)
   unsigned* status;
   int B, T, H, N, window, TQ, splits, items;
+  int tma_out;       // 1: full query tiles leave through shared memory and a TMA store (tm_o)
   float scale_log2;  // softmax scale * log2(e)
 };
 
@@ -92,8 +98,8 @@ struct PrefillLayout {
   static constexpr int OFF_KV = QB * Q_BYTES;
   static constexpr int OFF_BAR = OFF_KV + NS * KV_BYTES;
   // q_full[QB], q_empty[QB], kv_full[NS], kv_empty[NS], s_full[2], p_half[2],
-  // p_ready[2], o_final[2], o_free[2], item_full[IR], item_empty[IR]
-  static constexpr int NBAR = 2 * QB + 2 * NS + 10 + 2 * IR;
+  // p_ready[2], o_final[2], o_free[2], item_full[IR], item_empty[IR], q_stored[QB]
+  static constexpr int NBAR = 3 * QB + 2 * NS + 10 + 2 * IR;
   static constexpr int OFF_ITEM = OFF_BAR + NBAR * 8;  // IR x (first key tile, key tiles)
   static constexpr int OFF_MISC = OFF_ITEM + IR * 8;
   static constexpr int BYTES = OFF_MISC + 16 + 1024;  // + slack to align the base to 1024
@@ -316,7 +322,8 @@ __device__ __forceinline__ void prefill_issue_pv(uint32_t tmem, uint32_t kv_addr
 template <int C, int QB, int NS, int POLY8>
 __global__ void __launch_bounds__(PrefillLayout<C, QB, NS>::THREADS, 1)
     prefill_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
-                   const __grid_constant__ CUtensorMap tm_v, const PrefillParams p) {
+                   const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_o,
+                   const PrefillParams p) {
   using L = PrefillLayout<C, QB, NS>;
   constexpr int BM = L::BM, BN = L::BN, SUB = L::SUB, IR = L::IR;
   extern __shared__ uint8_t smem_raw[];
@@ -335,6 +342,7 @@ __global__ void __launch_bounds__(PrefillLayout<C, QB, NS>::THREADS, 1)
   uint64_t* o_free = o_final + 2;    // [warpgroup]: the epilogue has read O
   uint64_t* item_full = o_free + 2;
   uint64_t* item_empty = item_full + IR;
+  uint64_t* q_stored = item_empty + IR;  // [QB]: both warpgroups are done with the buffer as output staging
   int2* s_items = reinterpret_cast<int2*>(smem + L::OFF_ITEM);
   uint32_t* s_tmem = reinterpret_cast<uint32_t*>(smem + L::OFF_MISC);
 
@@ -360,6 +368,7 @@ __global__ void __launch_bounds__(PrefillLayout<C, QB, NS>::THREADS, 1)
       mbar_init(item_full + s, 1);
       mbar_init(item_empty + s, L::ITEM_READERS);
     }
+    for (int s = 0; s < QB; ++s) mbar_init(q_stored + s, 2);
     fence_mbar_init();
   }
   if (warp == L::MMA_WARP) {
@@ -418,7 +427,11 @@ __global__ void __launch_bounds__(PrefillLayout<C, QB, NS>::THREADS, 1)
                   tma_prefetch_l2_2d(&tm_q, s * 64, (nx.b * p.T + nx.t0 + w * p.TQ) * p.H);
             }
             const int qb = n % QB;
-            if (n >= QB) ok = mbar_wait(q_empty + qb, ((n / QB) & 1) ^ 1, p.status);
+            // the buffer's last item: its products have read Q, and its
+            // output (staged there) has left
+            if (n >= QB)
+              ok = mbar_wait(q_empty + qb, ((n / QB) & 1) ^ 1, p.status) &&
+                   mbar_wait(q_stored + qb, ((n / QB) & 1) ^ 1, p.status);
             if (ok) {
               mbar_expect_tx(q_full + qb, L::Q_BYTES);
               for (int w = 0; w < 2; ++w) {
@@ -616,7 +629,34 @@ __global__ void __launch_bounds__(PrefillLayout<C, QB, NS>::THREADS, 1)
       float denom = l;
       if (p.splits == 1 && p.sink != nullptr && valid) denom += fast_exp2(fmaf(p.sink[h], LOG2E, -msub));
       const float inv = denom > 0.f ? 1.f / denom : 0.f;
-      if (valid) {
+      // A full query tile's output goes through its own Q buffer (free once
+      // o_final says every product of the item is done): bf16 rows in the
+      // 128-byte-swizzled layout of the TMA box, then one TMA store per 64
+      // columns; the buffer is handed back to the loader (q_stored) once the
+      // store has read it. Other tiles store their rows directly.
+      const bool stage = p.tma_out && p.splits == 1 && p.TQ * p.H == BM && it.t0 + (w + 1) * p.TQ <= p.T;
+      uint8_t* tile = sQ + (n % QB) * L::Q_BYTES + w * L::QT_BYTES;
+      if (stage) {
+#pragma unroll
+        for (int v4 = 0; v4 < C / 8; ++v4) {
+          uint4 u;
+          u.x = pack_bf16(__uint_as_float(o[v4 * 8 + 0]) * inv, __uint_as_float(o[v4 * 8 + 1]) * inv);
+          u.y = pack_bf16(__uint_as_float(o[v4 * 8 + 2]) * inv, __uint_as_float(o[v4 * 8 + 3]) * inv);
+          u.z = pack_bf16(__uint_as_float(o[v4 * 8 + 4]) * inv, __uint_as_float(o[v4 * 8 + 5]) * inv);
+          u.w = pack_bf16(__uint_as_float(o[v4 * 8 + 6]) * inv, __uint_as_float(o[v4 * 8 + 7]) * inv);
+          *reinterpret_cast<uint4*>(tile + (v4 >> 3) * (BM * 128) + sw128_offset(row, v4 & 7)) = u;
+        }
+        p.lse[orow] = denom > 0.f ? (msub + log2f(denom)) * LN2 : -INFINITY;
+        fence_proxy_async();
+        named_barrier(1 + w, 128);
+        if (quad == 0 && lane == 0) {
+          const int row0 = static_cast<int>((static_cast<int64_t>(it.b) * p.T + it.t0 + w * p.TQ) * p.H);
+          for (int s = 0; s < SUB; ++s) tma_store_2d(&tm_o, tile + s * (BM * 128), s * 64, row0);
+          bulk_commit();
+          bulk_wait_read();
+          mbar_arrive(q_stored + n % QB);
+        }
+      } else if (valid) {
         if (p.splits == 1) {
           uint4* dst = reinterpret_cast<uint4*>(p.out + orow * C);
 #pragma unroll
@@ -639,9 +679,11 @@ __global__ void __launch_bounds__(PrefillLayout<C, QB, NS>::THREADS, 1)
           p.part_lse[prow] = l > 0.f ? (msub + log2f(l)) * LN2 : -INFINITY;
         }
       }
+      if (!stage && quad == 0 && lane == 0) mbar_arrive(q_stored + n % QB);
       g += nt;
       ++n;
     }
+    if (quad == 0 && lane == 0) bulk_wait_all();  // this warpgroup's output stores have landed
     tc_fence_before();
     __syncthreads();
   }

@@ -160,7 +160,7 @@ int prefill_poly8() {
 
 template <int C, int POLY8>
 int launch_prefill_p(const wpt::PrefillParams& p, const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
-                     cudaStream_t stream) {
+                     const CUtensorMap& to, cudaStream_t stream) {
   constexpr int QB = PrefillShape<C>::QB, NS = PrefillShape<C>::NS;
   using L = wpt::PrefillLayout<C, QB, NS>;
   static_assert(L::BYTES <= 232448, "prefill kernel shared memory exceeds 227 KB");
@@ -169,7 +169,7 @@ int launch_prefill_p(const wpt::PrefillParams& p, const CUtensorMap& tq, const C
   int sms = 148;
   current_device(&sms);
   const int grid = p.items < sms ? p.items : sms;  // persistent: one CTA per SM walks the items
-  kernel<<<grid, L::THREADS, L::BYTES, stream>>>(tq, tk, tv, p);
+  kernel<<<grid, L::THREADS, L::BYTES, stream>>>(tq, tk, tv, to, p);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "prefill_kernel launch");
   return WPT_OK;
@@ -177,13 +177,14 @@ int launch_prefill_p(const wpt::PrefillParams& p, const CUtensorMap& tq, const C
 
 template <int C>
 int launch_prefill(const wpt::PrefillParams& p, const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
+                   const CUtensorMap& to,
                    cudaStream_t stream) {
   switch (prefill_poly8()) {
-    case 0: return launch_prefill_p<C, 0>(p, tq, tk, tv, stream);
-    case 3: return launch_prefill_p<C, 3>(p, tq, tk, tv, stream);
-    case 4: return launch_prefill_p<C, 4>(p, tq, tk, tv, stream);
-    case 2: return launch_prefill_p<C, 2>(p, tq, tk, tv, stream);
-    default: return launch_prefill_p<C, 1>(p, tq, tk, tv, stream);
+    case 0: return launch_prefill_p<C, 0>(p, tq, tk, tv, to, stream);
+    case 3: return launch_prefill_p<C, 3>(p, tq, tk, tv, to, stream);
+    case 4: return launch_prefill_p<C, 4>(p, tq, tk, tv, to, stream);
+    case 2: return launch_prefill_p<C, 2>(p, tq, tk, tv, to, stream);
+    default: return launch_prefill_p<C, 1>(p, tq, tk, tv, to, stream);
   }
 }
 
@@ -298,12 +299,13 @@ extern "C" int wpt_attn_prefill(const void* q, const void* k, const void* v, int
   if (!aligned16(q) || !aligned16(out)) return fail(WPT_ERR_INVALID, "q and out must be 16-byte aligned");
   if (!(scale > 0.f)) return fail(WPT_ERR_INVALID, "scale must be positive");
 
-  CUtensorMap tq, tk, tv;
+  CUtensorMap tq, tk, tv, to;  // to: the output, same shape as q (full query tiles leave by TMA store)
   {
     cuuint64_t dims[2] = {static_cast<cuuint64_t>(C), static_cast<cuuint64_t>(B) * T * H};
     cuuint64_t strides[1] = {static_cast<cuuint64_t>(C) * 2};
     cuuint32_t box[2] = {64, 128};
     if (int rc = tensor_map(&tq, q, 2, dims, strides, box)) return rc;
+    if (int rc = tensor_map(&to, out, 2, dims, strides, box)) return rc;
   }
   if (int rc = table_map(&tk, k, k_stride_b, k_stride_n, B, N, C)) return rc;
   if (int rc = table_map(&tv, v, v_stride_b, v_stride_n, B, N, C)) return rc;
@@ -318,6 +320,7 @@ extern "C" int wpt_attn_prefill(const void* q, const void* k, const void* v, int
   p.lse = lse;
   p.part_o = part_o;
   p.part_lse = part_lse;
+  p.tma_out = splits > 1 ? 0 : 1;
   if (int rc = status_word(&p.status)) return rc;
   p.B = B;
   p.T = T;
@@ -333,7 +336,7 @@ extern "C" int wpt_attn_prefill(const void* q, const void* k, const void* v, int
   }
   p.scale_log2 = scale * wpt::LOG2E;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  int rc = C == 128 ? launch_prefill<128>(p, tq, tk, tv, s) : launch_prefill<64>(p, tq, tk, tv, s);
+  int rc = C == 128 ? launch_prefill<128>(p, tq, tk, tv, to, s) : launch_prefill<64>(p, tq, tk, tv, to, s);
   if (rc) return rc;
   if (splits > 1) {
     const int64_t rows = static_cast<int64_t>(B) * T * H;
