@@ -36,7 +36,7 @@ namespace wpt {
 
 constexpr int ACCEPT_THREADS = 1024;  // the top-k statistics kernel
 constexpr int STAT_THREADS = 256;     // the segment statistics kernel
-constexpr int STAT_SEG = 2048;        // entries of one statistics unit (one warp)
+constexpr int STAT_SEG = 8192;        // entries of one statistics unit (one warp)
 constexpr int DRAW_THREADS = 256;
 constexpr int DRAW_WARPS = DRAW_THREADS / 32;
 constexpr int DRAW_CHUNK = 256;       // entries of one float64 chunk sum
