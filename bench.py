@@ -8,18 +8,23 @@ attention TFLOP/s of algorithmic work (4*H*c per visible (query, key) pair).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
 
-With N > 1 it runs under torchrun, one rank per GPU; each rank takes its
-own batch of 8 rows (weak scaling, no collective on the data path) and the
-timed region is bracketed by barriers, its time the maximum over ranks.
-Secondary lines in the same JSON: decode attention GB/s (config 3, global
-and window-1024 rows; with N > 1 also the 262,144-token row split along its
-keys over the ranks with an NCCL combine), tree verification (config 4)
-and the acceptance step (config 4).
+With N > 1 it runs under torchrun, one rank per GPU, and scales strongly:
+the fixed batch of 8 rows is split over the ranks (8/4/2/1 rows each at
+N = 1/2/4/8), with no collective on the data path; the timed region is
+bracketed by barriers and its time is the maximum over ranks. A secondary
+line keeps the weak-scaling form (8 rows on every rank). Other secondary
+lines: decode attention GB/s (config 3, global and window-1024 rows, the
+64 rows balanced over the ranks by length; the 262,144-token row split
+along its keys over the ranks with one NCCL all-gather), tree verification
+(config 4) and the acceptance step (config 4).
 
---impl reference times the reference's CPU path: the CPU restatement of
-the reference's PyTorch attention (oracle/, pinned to the reference's own
-outputs by tests/test_oracle.py) in float32 with BLAS on the host cores,
-each step a bounded sample (one batch row of config 2, both passes).
+--impl reference times the reference's CPU path on the host cores: the
+reference's own PyTorch attention form (wpt_model.pytorch_kernels, from
+baseline/_ref when it is installed there, kind "reference"), else the CPU
+restatement of it (oracle/, pinned to the reference's outputs by
+tests/test_oracle.py; kind "port"). Each step is a bounded sample: 512
+consecutive queries of one config-2 batch row, both passes, the slices
+taken in turn so that 8 steps cover the row; its FLOPs are those queries'.
 """
 
 import argparse
@@ -139,6 +144,32 @@ def config3_lengths():
     return torch.randint(1024, 32769, (64,), generator=torch.Generator().manual_seed(0))
 
 
+def config3_inputs(device, rank=0):
+    """Config 3: 64 ragged rows, lengths U[1024, 32768] from seed 0, a
+    (64, 32768, 2c) entries table (rows past each length hold random values
+    that must not be read), one query of 32 heads per row, a sink."""
+    C, H = 128, 32
+    L = config3_lengths()
+    g = torch.Generator(device=device).manual_seed(10 + rank)
+    table = (torch.randn(64, 32768, 2 * C, generator=g, device=device) * 0.5).bfloat16()
+    q = (torch.randn(64, 1, H, C, generator=g, device=device) * 0.5).bfloat16()
+    sink = torch.randn(H, generator=g, device=device) * 0.5
+    pos = (L - 1).to(device)[:, None].contiguous()
+    return L, table, q, sink, pos
+
+
+def config4_inputs(device, rank=0):
+    """Config 4: B=32 rows of 8192 cached keys plus the 16 tree nodes' keys,
+    the nodes' queries (32 heads), the cache lengths and the draft tree."""
+    C, H, B4, L4, n4 = 128, 32, 32, 8192, 16
+    parents, depth = tree_parents()
+    g4 = torch.Generator(device=device).manual_seed(3 + rank)
+    t4 = (torch.randn(B4, L4 + n4, 2 * C, generator=g4, device=device) * 0.5).bfloat16()
+    q4 = (torch.randn(B4, n4, H, C, generator=g4, device=device) * 0.5).bfloat16()
+    cl = torch.full((B4,), L4, dtype=torch.int64, device=device)
+    return t4, q4, cl, parents, depth
+
+
 def tree_parents(n=16, seed=3):
     """§8(d) config 4's draft tree: node 0 the root at depth 1; node i's parent
     drawn uniformly among earlier nodes of depth < 4 with fewer than 2
@@ -201,107 +232,112 @@ def graph_timed(fn, steps, warmup):
     return s.elapsed_time(e) / steps
 
 
+def max_over_ranks(x, world, device, op=None):
+    """x on every rank -> its maximum over the ranks (its sum with op SUM)."""
+    if world == 1:
+        return x
+    t = torch.tensor([float(x)], dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=op or dist.ReduceOp.MAX)
+    return float(t)
+
+
+def bw_line(metric, nbytes, ms, gms, hbm, world):
+    line = {"metric": metric, "unit": "GB/s", "value": round(nbytes / ms / 1e6, 1),
+            "frac_of_hbm": round(nbytes / ms / 1e6 / (hbm * world), 3), "ms": round(ms, 4),
+            "algorithmic_bytes": nbytes}
+    if gms is not None:
+        line.update({"graph_value": round(nbytes / gms / 1e6, 1),
+                     "graph_frac_of_hbm": round(nbytes / gms / 1e6 / (hbm * world), 3), "graph_ms": round(gms, 4)})
+    return line
+
+
 def secondary(wb, ops, device, rank, world, hbm):
-    """Decode, verification and acceptance lines (each rank runs its own):
-    `ms` through the public call as written (host cost included when it
-    exceeds the device's), `graph_ms` the same calls replayed from a CUDA
-    graph."""
+    """Decode, verification and acceptance lines. With N > 1 every line
+    splits its fixed rows over the ranks (config-3 rows balanced by cached
+    length, config-4 rows in equal shares, the long row's keys in equal
+    shards) and reports the whole job's bytes or FLOPs over the slowest
+    rank's time. `ms` is through the public call as written (host cost
+    included when it exceeds the device's), `graph_ms` the same calls
+    replayed from a CUDA graph."""
+    from wpt_b200 import multi
     out = {}
     C, H = 128, 32
-    # config 3: 64 ragged decode rows
-    L = config3_lengths()
-    g = torch.Generator(device=device).manual_seed(10 + rank)
-    table = (torch.randn(64, 32768, 2 * C, generator=g, device=device) * 0.5).bfloat16()
-    q = (torch.randn(64, 1, H, C, generator=g, device=device) * 0.5).bfloat16()
-    sink = torch.randn(H, generator=g, device=device) * 0.5
-    pos = (L - 1).to(device)[:, None].contiguous()
+
+    def both(fn):
+        if world > 1:
+            dist.barrier()
+        ms = max_over_ranks(timed(fn, 20, 3), world, device)
+        if world > 1:
+            dist.barrier()
+        gms = max_over_ranks(graph_timed(fn, 20, 3), world, device)
+        return ms, gms
+
+    # config 3: 64 ragged decode rows, balanced over the ranks by length
+    L, table, q, sink, pos = config3_inputs(device, 0)
+    mine = multi.balanced_rows(L.tolist(), world)[rank] if world > 1 else list(range(64))
+    sel = torch.tensor(mine, device=device)
+    table, q, pos = table[sel].contiguous(), q[sel].contiguous(), pos[sel].contiguous()
+    R3 = len(mine)
     k, v = table[..., :C], table[..., C:]
-    empty = torch.empty(64, 1, 0, dtype=torch.int64, device=device)
+    empty = torch.empty(R3, 1, 0, dtype=torch.int64, device=device)
     f_g = lambda: wb.exact_attention(q, k, v, pos, C ** -0.5, 0, 128)  # noqa: E731
     f_w = lambda: wb.sparse_attention(q, k, v, sink, empty, pos, C ** -0.5, 1024)  # noqa: E731
-    ms_g, gms_g = timed(f_g, 20, 3), graph_timed(f_g, 20, 3)
-    ms_w, gms_w = timed(f_w, 20, 3), graph_timed(f_w, 20, 3)
+    ms_g, gms_g = both(f_g)
+    ms_w, gms_w = both(f_w)
     qo = 2 * 64 * H * C * 2
     bytes_g = int(L.sum()) * 2 * C * 2 + qo
     bytes_w = int(L.clamp(max=1024).sum()) * 2 * C * 2 + qo
-    out["decode_global"] = {"metric": "decode attention HBM GB/s (config 3, global rows)", "unit": "GB/s",
-                            "value": round(bytes_g / ms_g / 1e6, 1), "frac_of_hbm": round(bytes_g / ms_g / 1e6 / hbm, 3),
-                            "ms": round(ms_g, 4), "graph_value": round(bytes_g / gms_g / 1e6, 1),
-                            "graph_frac_of_hbm": round(bytes_g / gms_g / 1e6 / hbm, 3), "graph_ms": round(gms_g, 4),
-                            "algorithmic_bytes": bytes_g}
-    out["decode_window"] = {"metric": "decode attention HBM GB/s (config 3, window-1024 rows)", "unit": "GB/s",
-                            "value": round(bytes_w / ms_w / 1e6, 1), "frac_of_hbm": round(bytes_w / ms_w / 1e6 / hbm, 3),
-                            "ms": round(ms_w, 4), "graph_value": round(bytes_w / gms_w / 1e6, 1),
-                            "graph_frac_of_hbm": round(bytes_w / gms_w / 1e6 / hbm, 3), "graph_ms": round(gms_w, 4),
-                            "algorithmic_bytes": bytes_w}
+    out["decode_global"] = bw_line("decode attention HBM GB/s (config 3, global rows)", bytes_g, ms_g, gms_g, hbm,
+                                   world)
+    out["decode_window"] = bw_line("decode attention HBM GB/s (config 3, window-1024 rows)", bytes_w, ms_w, gms_w,
+                                   hbm, world)
     # A4 + A5 (the model's exact layer with its top-1024 selection, window 128; then the sparse layer
     # over those rows plus each query's last 1024 rows, with the sink)
     f_s = lambda: wb.exact_attention(q, k, v, pos, C ** -0.5, 1024, 128)  # noqa: E731
-    ms_s, gms_s = timed(f_s, 20, 3), graph_timed(f_s, 20, 3)
+    ms_s, gms_s = both(f_s)
     _, chosen = f_s()
     f_p = lambda: wb.sparse_attention(q, k, v, sink, chosen, pos, C ** -0.5, 1024)  # noqa: E731
-    ms_p, gms_p = timed(f_p, 20, 3), graph_timed(f_p, 20, 3)
+    ms_p, gms_p = both(f_p)
     bytes_s = bytes_g + int(L.sum()) * C * 2  # the attention's K and V, then K once more for the scores
     bytes_p = 64 * (1024 + 1024) * 2 * C * 2 + qo  # chosen + window rows, K and V, gathered
-    out["exact_top1024"] = {"metric": "exact attention + top-1024 row selection, HBM GB/s (config 3 rows)",
-                            "unit": "GB/s", "value": round(bytes_s / ms_s / 1e6, 1), "ms": round(ms_s, 4),
-                            "graph_value": round(bytes_s / gms_s / 1e6, 1),
-                            "graph_frac_of_hbm": round(bytes_s / gms_s / 1e6 / hbm, 3), "graph_ms": round(gms_s, 4),
-                            "algorithmic_bytes": bytes_s}
-    out["sparse_gather"] = {"metric": "sparse attention over 1024 chosen + 1024 window rows, GB/s (config 3)",
-                            "unit": "GB/s", "value": round(bytes_p / ms_p / 1e6, 1), "ms": round(ms_p, 4),
-                            "graph_value": round(bytes_p / gms_p / 1e6, 1),
-                            "graph_frac_of_hbm": round(bytes_p / gms_p / 1e6 / hbm, 3), "graph_ms": round(gms_p, 4),
-                            "algorithmic_bytes": bytes_p}
-    del table
+    out["exact_top1024"] = bw_line("exact attention + top-1024 row selection, HBM GB/s (config 3 rows)", bytes_s,
+                                   ms_s, gms_s, hbm, world)
+    out["sparse_gather"] = bw_line("sparse attention over 1024 chosen + 1024 window rows, GB/s (config 3)",
+                                   bytes_p, ms_p, gms_p, hbm, world)
+    del table, k, v, chosen
     # the 262,144-token row, split along its keys over the ranks
-    from wpt_b200 import multi
     N = 262144
     start, stop = multi.key_shard(N, world, rank)
-    gl = torch.Generator(device=device).manual_seed(20 + rank)
-    shard = (torch.randn(1, stop - start, 2 * C, generator=gl, device=device) * 0.5).bfloat16()
+    gl = torch.Generator(device=device).manual_seed(20)
+    full = (torch.randn(1, N, 2 * C, generator=gl, device=device) * 0.5).bfloat16()
+    shard = full[:, start:stop].contiguous()
+    del full
     ql = (torch.randn(1, 1, H, C, generator=torch.Generator(device=device).manual_seed(21), device=device) * 0.5
           ).bfloat16()
     pl = torch.full((1, 1), N - 1, dtype=torch.int64, device=device)
 
     def long_row():
         return multi.long_decode(ql, shard[..., :C], shard[..., C:], start, pl, C ** -0.5)
-    if world > 1:
-        dist.barrier()
-    ms_l = timed(long_row, 20, 3)
-    if world > 1:
-        t = torch.tensor([ms_l], device=device)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms_l = float(t)
-    bytes_l = N * 2 * C * 2
-    out["decode_long_row"] = {"metric": f"decode attention HBM GB/s (262,144-token row over {world} GPU(s))",
-                              "unit": "GB/s", "value": round(bytes_l / ms_l / 1e6, 1),
-                              "frac_of_hbm": round(bytes_l / ms_l / 1e6 / (hbm * world), 3), "ms": round(ms_l, 4)}
-    if world == 1:  # with more GPUs the call holds NCCL collectives: not captured
-        gms_l = graph_timed(long_row, 20, 3)
-        out["decode_long_row"].update({"graph_value": round(bytes_l / gms_l / 1e6, 1),
-                                       "graph_frac_of_hbm": round(bytes_l / gms_l / 1e6 / hbm, 3),
-                                       "graph_ms": round(gms_l, 4)})
+    long_row()  # the plan (split count, buffer) is made once, outside any capture
+    ms_l, gms_l = both(long_row)
+    out["decode_long_row"] = bw_line(f"decode attention HBM GB/s (262,144-token row over {world} GPU(s))",
+                                     N * 2 * C * 2, ms_l, gms_l, hbm, world)
     del shard
-    # config 4: tree verification
-    parents, depth = tree_parents()
-    B4, L4, n4 = 32, 8192, 16
-    g4 = torch.Generator(device=device).manual_seed(3 + rank)
-    t4 = (torch.randn(B4, L4 + n4, 2 * C, generator=g4, device=device) * 0.5).bfloat16()
-    q4 = (torch.randn(B4, n4, H, C, generator=g4, device=device) * 0.5).bfloat16()
-    cl = torch.full((B4,), L4, dtype=torch.int64, device=device)
-    bits = ops.tree_bits_from_parents(torch.tensor(parents)).to(device).expand(B4, n4).contiguous()
-    vpos = cl[:, None] + torch.arange(n4, device=device)
-    f_v = lambda: ops.prefill_forward(q4, t4[..., :C], t4[..., C:], vpos, C ** -0.5, tree_bits=bits,  # noqa: E731
-                                      tree_base=cl)
-    ms_v, gms_v = timed(f_v, 20, 3), graph_timed(f_v, 20, 3)
+    # config 4: tree verification, rows in equal shares
+    t4, q4, cl, parents, depth = config4_inputs(device, 0)
+    B4, L4 = t4.shape[0], t4.shape[1] - q4.shape[1]
+    part = multi.shard_rows(B4, world, rank)
+    t4, q4, cl = t4[part].contiguous(), q4[part].contiguous(), cl[part].contiguous()
+    par4 = torch.tensor(parents, device=device)
+    f_v = lambda: wb.tree_attention(q4, t4[..., :C], t4[..., C:], cl, par4, C ** -0.5)  # noqa: E731
+    ms_v, gms_v = both(f_v)
     flops_v = 4.0 * B4 * H * C * sum(L4 + d for d in depth)
     out["verify_tree"] = {"metric": "tree verification attention TFLOP/s (config 4)", "unit": "TFLOP/s",
                           "value": round(flops_v / ms_v / 1e9, 1), "ms": round(ms_v, 4),
                           "graph_value": round(flops_v / gms_v / 1e9, 1), "graph_ms": round(gms_v, 4),
                           "algorithmic_flops": flops_v}
     del t4
-    # config 4: acceptance step
+    # config 4: acceptance step, rows in equal shares
     R, n, V = 32, 16, 65536
     ga = torch.Generator(device=device).manual_seed(4)
     scores = torch.randn(R, n + 1, V, generator=ga, device=device) * 2.0
@@ -309,12 +345,16 @@ def secondary(wb, ops, device, rank, world, hbm):
     drafted = torch.multinomial(qprob.reshape(-1, V), 1, generator=ga).view(R, n)
     uniforms = torch.rand(R, n, generator=ga, device=device)
     resample = torch.rand(R, generator=ga, device=device)
+    part = multi.shard_rows(R, world, rank)
+    scores, qprob, drafted = scores[part].contiguous(), qprob[part].contiguous(), drafted[part].contiguous()
+    uniforms, resample = uniforms[part].contiguous(), resample[part].contiguous()
     bytes_a = R * (n + 1) * V * 4  # every target logit is read once (the softmax needs whole rows)
     for name, top_k, label in (("accept", None, "stochastic"), ("accept_greedy", 1, "greedy, argmax")):
         f_a = lambda: wb.accept(scores, drafted, qprob, uniforms, resample, 1.0, top_k)  # noqa: E731
-        ms_a, gms_a = timed(f_a, 20, 3), graph_timed(f_a, 20, 3)
+        ms_a, gms_a = both(f_a)
         _, accepted = f_a()
-        written = int(accepted.sum()) + R
+        written = int(max_over_ranks(int(accepted.sum()) + accepted.numel(), world, device, dist.ReduceOp.SUM
+                                     if world > 1 else None))
         out[name] = {"metric": f"speculative acceptance, written tokens/s (config 4, {label})", "unit": "tokens/s",
                      "value": round(written / ms_a * 1e3, 1), "ms": round(ms_a, 4),
                      "graph_value": round(written / gms_a * 1e3, 1), "graph_ms": round(gms_a, 4),
@@ -324,47 +364,107 @@ def secondary(wb, ops, device, rank, world, hbm):
 
 # ----------------------------------------------------------- CPU baseline
 
-def cpu_rows(seconds=10.0, max_rows=B2, dtype=np.float32):
-    """The CPU restatement on config-2 rows (both passes), until `seconds`
-    have passed (at least one row). Returns (TFLOP/s, rows, seconds, threads)."""
-    from oracle import attention as oat
-    causal, window = config2_flops(B=1)
-    g = torch.Generator().manual_seed(1)
-    done, flops, t0 = 0, 0.0, time.perf_counter()
-    while done < max_rows and (done == 0 or time.perf_counter() - t0 < seconds):
-        q = (torch.randn(1, T2, H2, C2, generator=g) * 0.5).bfloat16().float().numpy()
-        e = (torch.randn(1, T2, 2 * C2, generator=g) * 0.5).bfloat16().float().numpy()
-        sink = (torch.randn(H2, generator=torch.Generator().manual_seed(2)) * 0.5).numpy()
-        pos = np.arange(T2)[None]
-        oat.range_attention(q, e[..., :C2], e[..., C2:], pos, C2 ** -0.5, dtype=dtype)
-        oat.range_attention(q, e[..., :C2], e[..., C2:], pos, C2 ** -0.5, window=W2, sink=sink, dtype=dtype)
-        done += 1
-        flops += causal + window
+REF_DIR = os.path.join(ROOT, "baseline", "_ref")
+CPU_SLICE = 512  # queries per CPU-baseline step
+
+
+def reference_form():
+    """The reference's own PyTorch attention form (wpt_model.pytorch_kernels)
+    from baseline/_ref when it is installed there (baseline/install_ref.py),
+    else None."""
+    if not os.path.isdir(os.path.join(REF_DIR, "wpt_model")):
+        return None
+    if REF_DIR not in sys.path:
+        sys.path.insert(0, REF_DIR)
+    try:
+        from wpt_model import pytorch_kernels
+    except Exception:  # noqa: BLE001 - an unusable install is reported as the port instead
+        return None
+    return pytorch_kernels
+
+
+class CpuSample:
+    """The CPU baseline's unit of work: CPU_SLICE consecutive queries of one
+    config-2 batch row, the causal pass and the window-1024 pass with a sink,
+    through the reference's PyTorch form (kind "reference") or the oracle
+    port (kind "port"), on the host's cores. step() returns its FLOPs."""
+
+    def __init__(self):
+        g = torch.Generator().manual_seed(1)
+        self.q = (torch.randn(1, T2, H2, C2, generator=g) * 0.5).bfloat16()
+        self.e = (torch.randn(1, T2, 2 * C2, generator=g) * 0.5).bfloat16()
+        self.sink = torch.randn(H2, generator=torch.Generator().manual_seed(2)) * 0.5
+        self.form = reference_form()
+        self.kind = "reference" if self.form is not None else "port"
+        self.i = 0
+        if self.form is None:
+            self.qn = self.q.float().numpy()
+            self.en = self.e.float().numpy()
+
+    def step(self):
+        t0 = (self.i % (T2 // CPU_SLICE)) * CPU_SLICE
+        self.i += 1
+        part = slice(t0, t0 + CPU_SLICE)
+        if self.form is not None:
+            pos = torch.arange(t0, t0 + CPU_SLICE)[None]
+            q, k, v = self.q[:, part], self.e[..., :C2], self.e[..., C2:]
+            empty = torch.empty(1, CPU_SLICE, 0, dtype=torch.int64)
+            with torch.no_grad():
+                self.form.exact_attention(q, k, v, pos, C2 ** -0.5, 0, W2)
+                self.form.sparse_attention(q, k, v, self.sink, empty, pos, C2 ** -0.5, W2)
+        else:
+            from oracle import attention as oat
+            pos = np.arange(t0, t0 + CPU_SLICE)[None]
+            q, k, v = self.qn[:, part], self.en[..., :C2], self.en[..., C2:]
+            oat.range_attention(q, k, v, pos, C2 ** -0.5, dtype=np.float32)
+            oat.range_attention(q, k, v, pos, C2 ** -0.5, window=W2, sink=self.sink.numpy(), dtype=np.float32)
+        seen = sum(p + 1 for p in range(t0, t0 + CPU_SLICE)) + sum(min(p + 1, W2) for p in range(t0, t0 + CPU_SLICE))
+        return 4.0 * H2 * C2 * seen
+
+    def describe(self, steps):
+        what = ("the reference's own pytorch_kernels.exact_attention + sparse_attention (baseline/_ref), float32"
+                if self.form is not None else "the oracle port (oracle.attention.range_attention), float32 BLAS")
+        return (f"{steps} step(s) of {CPU_SLICE} consecutive queries of one config-2 batch row (B=1 sample of "
+                f"T={T2}, 16q/1kv, c=128), causal + window-1024/sink passes, {what}")
+
+
+def cpu_baseline(seconds=10.0):
+    """CpuSample steps until `seconds` have passed (at least one)."""
+    sample = CpuSample()
+    sample.step()  # warm-up (first-call costs)
+    steps, flops, t0 = 0, 0.0, time.perf_counter()
+    while steps == 0 or time.perf_counter() - t0 < seconds:
+        flops += sample.step()
+        steps += 1
     dt = time.perf_counter() - t0
-    return flops / dt / 1e12, done, dt
+    return {"value": round(flops / dt / 1e12, 5), "unit": "TFLOP/s", "cores": torch.get_num_threads(),
+            "kind": sample.kind, "sample": sample.describe(steps) + f", {dt:.1f} s"}
 
 
 def reference_arm(args, rank, world):
-    """--impl reference: the CPU restatement timed on the host cores."""
+    """--impl reference: the reference's CPU path timed on the host cores
+    (rank 0 only; other ranks exit without work)."""
     if rank != 0:
         return
-    causal, window = config2_flops(B=1)
+    sample = CpuSample()
     for _ in range(args.warmup):
-        cpu_rows(seconds=0.0, max_rows=1)
-    t0 = time.perf_counter()
+        sample.step()
+    flops, t0 = 0.0, time.perf_counter()
     for _ in range(args.steps):
-        cpu_rows(seconds=0.0, max_rows=1)
+        flops += sample.step()
     dt = time.perf_counter() - t0
-    value = (causal + window) * args.steps / dt / 1e12
-    cores = os.cpu_count()
-    line = {"impl": "reference", "metric": METRIC, "value": round(value, 4), "unit": "TFLOP/s", "n_gpus": args.gpus,
+    value = flops / dt / 1e12
+    cores = torch.get_num_threads()
+    line = {"impl": "reference", "metric": METRIC, "value": round(value, 5), "unit": "TFLOP/s", "n_gpus": args.gpus,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(dt / args.steps * 1e3, 2),
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-            "config": {"workload": "config 2 prefill (B=8, T=4096, 16q/1kv, c=128; causal + window 1024 + sink)",
-                       "global_batch": B2 * args.gpus, "seq_len": T2, "parallelism": "cpu"},
-            "cpu_baseline": {"value": round(value, 4), "unit": "TFLOP/s", "cores": cores, "kind": "port",
-                             "sample": "one batch row of config 2 per step (causal + window passes), float32 BLAS"},
-            "e2e": {"value": round(value, 4), "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (seeded N(0,1)*0.5, config 2 shapes)",
+            "config": {"workload": f"config 2 prefill, B=1 sample: {CPU_SLICE} queries of one batch row per step "
+                                   f"(T={T2}, 16q/1kv, c=128; causal + window 1024 + sink)",
+                       "global_batch": 1, "seq_len": T2, "parallelism": f"cpu, {cores} threads"},
+            "cpu_baseline": {"value": round(value, 5), "unit": "TFLOP/s", "cores": cores, "kind": sample.kind,
+                             "sample": sample.describe(args.steps)},
+            "e2e": {"value": round(value, 5), "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 
 
@@ -460,22 +560,41 @@ def main():
     if world > 1:
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=device)
     import wpt_b200
-    from wpt_b200 import build, ops
+    from wpt_b200 import build, multi, ops
     if rank == 0 or not os.path.exists(os.path.join(ROOT, "wpt_b200", "libwpt_b200.so")):
         build.build()
     if world > 1:
         dist.barrier()
     pk, pk_kind = peaks()
     torch.set_grad_enabled(False)
-    q, entries, positions, sink = config2_inputs(device, rank)
-    causal_flop, window_flop = config2_flops()
-    step_flop = causal_flop + window_flop
+    # strong scaling: the fixed batch of 8 rows, this rank's share of it
+    rows = multi.shard_rows(B2, world, rank)
+    q_all, e_all, p_all, sink = config2_inputs(device, 0)
+    q, entries, positions = q_all[rows].contiguous(), e_all[rows].contiguous(), p_all[rows].contiguous()
+    del q_all, e_all, p_all
+    Bm = q.shape[0]
+    causal_all, window_all = config2_flops()
+    causal_mine, _ = config2_flops(B=Bm)
+    step_flop = causal_all + window_all
+    C = C2
+    k, v = entries[..., :C], entries[..., C:]
+    empty = torch.empty(Bm, T2, 0, dtype=torch.int64, device=device)
+
+    def step(marks=None):
+        if marks is not None:
+            marks[0].record(stream)
+        causal, _ = wpt_b200.exact_attention(q, k, v, positions, C ** -0.5, 0, W2)  # the dominant kernel
+        if marks is not None:
+            marks[1].record(stream)
+        window = wpt_b200.sparse_attention(q, k, v, sink, empty, positions, C ** -0.5, W2)
+        return causal, window
+
+    stream = torch.cuda.current_stream()
     for _ in range(args.warmup):
-        prefill_step(wpt_b200, q, entries, positions, sink)
+        step()
     torch.cuda.synchronize()
     if wpt_b200.device_status() != 0:
         raise RuntimeError("kernel status error during warm-up")
-    stream = torch.cuda.current_stream()
     marks = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
     clocks = Clocks(local)
     if world > 1:
@@ -485,33 +604,41 @@ def main():
     launches0 = ops.LAUNCHES[0]
     start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     start.record(stream)
-    C = C2
-    k, v = entries[..., :C], entries[..., C:]
-    empty = torch.empty(B2, T2, 0, dtype=torch.int64, device=device)
     for i in range(args.steps):
-        marks[i][0].record(stream)
-        wpt_b200.exact_attention(q, k, v, positions, C ** -0.5, 0, W2)  # the dominant kernel: causal prefill
-        marks[i][1].record(stream)
-        wpt_b200.sparse_attention(q, k, v, sink, empty, positions, C ** -0.5, W2)
+        step(marks[i])
     stop.record(stream)
     torch.cuda.synchronize()
     launches = ops.LAUNCHES[0] - launches0
     if world > 1:
         dist.barrier()
     clock = clocks.stop()
-    ms = start.elapsed_time(stop)
+    ms = max_over_ranks(start.elapsed_time(stop), world, device)
     causal_ms = sum(a.elapsed_time(b) for a, b in marks) / args.steps
-    if world > 1:
-        t = torch.tensor([ms], device=device)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t)
+    launches = int(max_over_ranks(launches, world, device, dist.ReduceOp.SUM if world > 1 else None))
     ms_step = ms / args.steps
-    value = step_flop * world / (ms_step * 1e-3) / 1e12
-    achieved = causal_flop / (causal_ms * 1e-3) / 1e12
+    value = step_flop / (ms_step * 1e-3) / 1e12
+    achieved = causal_mine / (causal_ms * 1e-3) / 1e12
     status = wpt_b200.device_status()
 
+    # parity of the measured outputs (outside the timed region): this rank's
+    # first batch row, both passes, against the oracle (float32, host BLAS)
+    parity = None
+    if rank == 0:
+        from oracle import attention as oat
+        causal, window = step()
+        torch.cuda.synchronize()
+        q0, k0, v0 = (x[:1].float().cpu().numpy() for x in (q, k, v))
+        p0 = positions[:1].cpu().numpy()
+        rc, _ = oat.range_attention(q0, k0, v0, p0, C ** -0.5, dtype=np.float32)
+        rw, _ = oat.range_attention(q0, k0, v0, p0, C ** -0.5, window=W2, sink=sink.cpu().numpy(), dtype=np.float32)
+        parity = {"max_abs_causal": float(np.abs(causal[:1].float().cpu().numpy() - rc).max()),
+                  "max_abs_window": float(np.abs(window[:1].float().cpu().numpy() - rw).max()),
+                  "tolerance": 2e-2, "checked": "batch row 0 of the last step's outputs, all 4096 x 16 query "
+                                                "rows of both passes, against oracle.attention.range_attention"}
+        parity["ok"] = parity["max_abs_causal"] < 2e-2 and parity["max_abs_window"] < 2e-2
+
     # end to end through the public API: pinned host inputs in, outputs back,
-    # every step; the batch goes in chunks over three streams so that one
+    # every step; this rank's rows go in chunks over three streams so that one
     # chunk's copies in overlap another's kernels and a third's copies out
     q_h = q.cpu().pin_memory()
     e_h = entries.cpu().pin_memory()
@@ -519,10 +646,10 @@ def main():
     s_h = sink.cpu().pin_memory()
     o1_h = torch.empty(q.shape, dtype=q.dtype).pin_memory()
     o2_h = torch.empty(q.shape, dtype=q.dtype).pin_memory()
-    chunks = E2E_CHUNKS
-    rows = B2 // chunks
+    chunks = min(E2E_CHUNKS, Bm)
+    per = Bm // chunks
     lanes = [torch.cuda.Stream(device) for _ in range(3)]
-    slots = [(torch.empty_like(q[:rows]), torch.empty_like(entries[:rows]), torch.empty_like(positions[:rows]),
+    slots = [(torch.empty_like(q[:per]), torch.empty_like(entries[:per]), torch.empty_like(positions[:per]),
               torch.empty_like(sink)) for _ in lanes]
 
     def e2e_step():
@@ -530,7 +657,7 @@ def main():
         for c in range(chunks):
             lane = lanes[c % len(lanes)]
             q_d, e_d, p_d, s_d = slots[c % len(lanes)]
-            r = slice(c * rows, (c + 1) * rows)
+            r = slice(c * per, (c + 1) * per)
             lane.wait_stream(main)
             with torch.cuda.stream(lane):
                 q_d.copy_(q_h[r], non_blocking=True)
@@ -544,42 +671,53 @@ def main():
             main.wait_stream(lane)
     if world > 1:
         dist.barrier()
-    e2e_ms = timed(e2e_step, args.e2e_steps, 2, stream)
-    if world > 1:
-        t = torch.tensor([e2e_ms], device=device)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        e2e_ms = float(t)
-    h2d = q.numel() * 2 + entries.numel() * 2 + positions.numel() * 8 + chunks * sink.numel() * 4
-    d2h = 2 * q.numel() * 2
-    e2e_value = step_flop * world / (e2e_ms * 1e-3) / 1e12
+    e2e_ms = max_over_ranks(timed(e2e_step, args.e2e_steps, 2, stream), world, device)
+    h2d = B2 * T2 * H2 * C2 * 2 + B2 * T2 * 2 * C2 * 2 + B2 * T2 * 8 + world * chunks * H2 * 4
+    d2h = 2 * B2 * T2 * H2 * C2 * 2
+    e2e_value = step_flop / (e2e_ms * 1e-3) / 1e12
+    del q_h, e_h, o1_h, o2_h, slots
 
-    extra = {} if args.no_secondary else secondary(wpt_b200, ops, device, rank, world, pk["hbm_gbs"])
+    extra = {}
+    if not args.no_secondary:
+        if world > 1:  # the weak-scaling form: every rank its own batch of 8 rows
+            qw, ew, pw, _ = config2_inputs(device, rank)
+            kw, vw = ew[..., :C], ew[..., C:]
+            ew_empty = torch.empty(B2, T2, 0, dtype=torch.int64, device=device)
+
+            def weak_step():
+                wpt_b200.exact_attention(qw, kw, vw, pw, C ** -0.5, 0, W2)
+                wpt_b200.sparse_attention(qw, kw, vw, sink, ew_empty, pw, C ** -0.5, W2)
+            dist.barrier()
+            ms_w = max_over_ranks(timed(weak_step, args.steps, 2, stream), world, device)
+            extra["config2_weak"] = {"metric": METRIC + ", weak scaling: 8 rows on every rank", "unit": "TFLOP/s",
+                                     "value": round(step_flop * world / (ms_w * 1e-3) / 1e12, 2),
+                                     "ms_per_step": round(ms_w, 4), "global_batch": B2 * world}
+            del qw, ew, kw, vw
+        extra.update(secondary(wpt_b200, ops, device, rank, world, pk["hbm_gbs"]))
     status |= wpt_b200.device_status()
-    cpu = None
-    if rank == 0 and world == 1:
-        tf, rows, secs = cpu_rows(seconds=10.0)
-        cpu = {"value": round(tf, 4), "unit": "TFLOP/s", "cores": os.cpu_count(), "kind": "port",
-               "sample": f"{rows} batch row(s) of config 2 (causal + window passes), float32 BLAS, {secs:.1f} s"}
+    cpu = cpu_baseline(seconds=10.0) if rank == 0 and world == 1 else None
     if rank == 0:
-        peak = pk["bf16_tflops_sustained"]
+        peak = pk["bf16_tflops"]
         line = {
             "metric": METRIC, "value": round(value, 2), "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": round(ms_step, 4), "higher_is_better": True, "scaling": "weak",
+            "warmup": args.warmup, "ms_per_step": round(ms_step, 4), "higher_is_better": True, "scaling": "strong",
             "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded N(0,1)*0.5, config 2 shapes)",
-            "config": {"workload": "config 2 prefill: B=8 per GPU, T=4096, 16q/1kv heads, c=128; causal pass + "
-                                   "window-1024 pass with sink", "global_batch": B2 * world, "seq_len": T2,
-                       "parallelism": f"batch-sharded x{world} (weak)",
-                       "l2": "inputs larger than L2 (q 134 MB + kv 17 MB + outputs 268 MB per step)"},
+            "config": {"workload": "config 2 prefill: B=8, T=4096, 16q/1kv heads, c=128; causal pass + "
+                                   "window-1024 pass with sink", "global_batch": B2, "seq_len": T2,
+                       "parallelism": f"batch rows split over {world} GPU(s) ({Bm} on rank 0), strong scaling",
+                       "l2": "inputs larger than L2 (q 134 MB + kv 17 MB + outputs 268 MB per step at B=8)"},
             "e2e": {"value": round(e2e_value, 2), "unit": "TFLOP/s", "h2d_bytes_per_step": int(h2d),
                     "d2h_bytes_per_step": int(d2h), "ms_per_step": round(e2e_ms, 3)},
             "gpu_launches": int(launches),
             "roofline": {"bound": "tensor", "kernel": "prefill_kernel (causal pass)", "achieved": round(achieved, 2),
-                         "peak": peak, "peak_kind": f"bf16_tflops_sustained of {pk_kind}", "unit": "TFLOP/s",
+                         "peak": peak, "peak_kind": f"bf16_tflops (burst) of {pk_kind}: the timed region is "
+                                                    f"{ms:.0f} ms, not a seconds-long loop", "unit": "TFLOP/s",
                          "frac": round(achieved / peak, 4), "ms_per_launch": round(causal_ms, 4),
-                         "algorithmic_flops_per_launch": causal_flop,
-                         "traffic": profiled_traffic(),
+                         "algorithmic_flops_per_launch": causal_mine,
+                         "traffic": profiled_traffic() if Bm == B2 else None,
                          "traffic_source": "ncu dram__bytes_read+write of the causal pass at B=4, x2 for B=8 "
                                            "(profiles/prefill_kernel_config2.md)"},
+            "parity": parity,
             "clocks": clock,
             "status": status,
         }

@@ -132,12 +132,17 @@ int wpt_attn_topk(const void* q, const void* k, int64_t k_stride_b, int64_t k_st
  * synchronise the device, or a serving process that must not grow its
  * footprint mid-run.
  * Limit: splits * B * T * H * (C + 1) floats must fit in 2^21 (8 MiB);
- * larger calls return WPT_ERR_UNSUPPORTED and launch nothing. The first call
- * on a device looks up the array's device address (cudaGetSymbolAddress);
- * make that first call before any stream capture. Every call shares the
- * array: calls that overlap on the GPU (other streams, other threads) race
- * on it, so serialise them. Nothing in the array needs to start at zero:
- * each call writes every partial its merge reads.
+ * larger calls return WPT_ERR_UNSUPPORTED and launch nothing. out and lse
+ * are required (WPT_ERR_INVALID when NULL): the partials-only mode of
+ * wpt_attn_decode would leave its results in the private array, where the
+ * caller cannot read them. The first call on a device looks up the array's
+ * device address (cudaGetSymbolAddress); make that first call before any
+ * stream capture. That address (like the status word's) is cached for the
+ * life of the process: do not use the library across a cudaDeviceReset.
+ * Every call shares the array: calls that overlap on the GPU (other
+ * streams, other threads) race on it, so serialise them. Nothing in the
+ * array needs to start at zero: each call writes every partial its merge
+ * reads.
  */
 int wpt_attn_decode_noalloc(const void* q, const void* k, const void* v, int64_t k_stride_b, int64_t k_stride_n,
                             int64_t v_stride_b, int64_t v_stride_n, const int64_t* positions,
@@ -156,6 +161,20 @@ int wpt_attn_decode_noalloc(const void* q, const void* k, const void* v, int64_t
  */
 int wpt_attn_merge(const float* part_o, const float* part_lse, int splits, int64_t rows, int64_t split_stride,
                    int H, int C, const float* sink, void* out, float* lse, void* stream);
+
+/*
+ * The same merge over partials gathered from several places (the GPUs that
+ * each hold a share of a long row's keys): `groups` chunks of group_floats
+ * floats side by side at `parts`, chunk g holding `per` splits' output
+ * partials (per, rows, C) fp32 followed by their log-sums (per, rows) fp32
+ * (group_floats >= per * rows * (C + 1); pad it to keep chunks 16-byte
+ * aligned). One wpt_attn_decode call in partials-only mode writes such a
+ * chunk (part_o = the chunk, part_lse = the chunk + per * rows * C), so an
+ * in-place all-gather of the chunks is the only exchange a long row needs.
+ * No reference counterpart (the reference decodes on one GPU).
+ */
+int wpt_attn_merge_groups(const float* parts, int groups, int per, int64_t rows, int64_t group_floats, int H, int C,
+                          const float* sink, void* out, float* lse, void* stream);
 
 /*
  * The acceptance step of speculative decoding, WPT's rule
@@ -182,6 +201,18 @@ int wpt_attn_merge(const float* part_o, const float* part_lse, int splits, int64
 int wpt_accept(const float* scores, const int64_t* drafted, const float* q, const float* uniforms,
                const float* resample, const int64_t* lengths, void* scratch, int64_t* tokens, int64_t* accepted,
                int R, int n, int V, float temperature, int top_k, void* stream);
+
+/*
+ * Ancestor masks of draft trees, the tree_bits argument of wpt_attn_prefill:
+ * parents int64 (B, n), -1 for a root (a child of the last cache row) and
+ * parents[b][i] < i otherwise; bits uint64 (B, n), bit j of bits[b][i] set
+ * when node j is i or one of its ancestors. n <= 64. Computed on the device
+ * so that verification needs no host synchronisation. Generalises the
+ * chain of drafts that WPT verifies (packages/wpt-inference/src/
+ * wpt_inference/__init__.py:207, parents[i] = i - 1) to a tree, with
+ * dense_attention's visible-mask semantics (attention.py:74-82).
+ */
+int wpt_tree_bits(const int64_t* parents, int B, int n, uint64_t* bits, void* stream);
 
 /* Bytes of scratch wpt_accept needs for R rows of n drafts over V entries
  * (0 for a bad shape). */

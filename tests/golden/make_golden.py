@@ -1,9 +1,10 @@
 """Writes the golden fixtures under tests/golden/ by running the REFERENCE's
-own code (imported from the reference checkout named by --reference, default
-/root/reference) on seeded inputs. Run once, in a machine that has the
-reference; the fixtures are committed and the tests read only them:
+own code (imported from the reference checkout named by --reference or the
+WPT_REFERENCE environment variable) on seeded inputs. Run once, in a machine
+that has the reference; the fixtures are committed and the tests read only
+them:
 
-    python tests/golden/make_golden.py --reference /root/reference
+    python tests/golden/make_golden.py --reference <the reference repository>
 
 What each fixture pins (paths relative to the reference repository):
   exact_small.npz       pytorch_kernels.exact_attention (+ top-k choice, LSE
@@ -247,7 +248,8 @@ def accept_case(wi, name, R, n, V, temperature, top_k, seed):
 
 def main():
     parser = argparse.ArgumentParser()
-    parser.add_argument("--reference", default="/root/reference")
+    parser.add_argument("--reference", default=os.environ.get("WPT_REFERENCE"), required="WPT_REFERENCE" not in os.environ,
+                        help="the reference repository's root (or set WPT_REFERENCE)")
     args = parser.parse_args()
     torch.set_num_threads(max(1, os.cpu_count() or 1))
     at, pk, wi = _import_reference(args.reference)

@@ -62,16 +62,10 @@ def test_chosen_columns_follows_the_reference():
     assert wpt_b200.chosen_columns(1024, 128, 5000) == 1024
 
 
-def test_tree_bits_from_parents():
+def test_tree_of_more_than_64_nodes_is_refused_before_any_launch():
     from wpt_b200 import ops
-    bits = ops.tree_bits_from_parents(torch.tensor([-1, 0, 0, 1, 1, 2, 4]))
-    assert bits.tolist() == [0b1, 0b11, 0b101, 0b1011, 0b10011, 0b100101, 0b1010011]
-    chain = ops.tree_bits_from_parents(torch.arange(64) - 1)
-    assert chain[0].item() == 1 and chain[-1].item() == -1  # all 64 bits, as a signed int64
-    with pytest.raises(ValueError):
-        ops.tree_bits_from_parents(torch.tensor([-1, 2, 0]))
     with pytest.raises(NotImplementedError):
-        ops.tree_bits_from_parents(torch.arange(65) - 1)
+        ops.tree_bits(torch.arange(65) - 1, 1)  # refused on the host, before the device is touched
 
 
 def test_kernel_choice_by_shape():
@@ -90,6 +84,26 @@ def test_cpu_tensors_are_refused_not_computed():
     k = torch.zeros(1, 4, 128, dtype=torch.bfloat16)
     with pytest.raises(ValueError, match="CUDA device only"):
         wpt_b200.exact_attention(q, k, k, torch.arange(4), 0.1, 0, 2)
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.float16])
+def test_inputs_not_in_bfloat16_are_refused_not_rounded(dtype):
+    # the reference computes in its inputs' dtype; rounding float32 inputs to
+    # bf16 would return float32 tensors of bf16 accuracy, so they are refused
+    # with the error the reference's kernel tests skip on
+    import wpt_b200
+    q = torch.zeros(1, 4, 2, 128, dtype=dtype)
+    k = torch.zeros(1, 4, 128, dtype=dtype)
+    sink = torch.zeros(2)
+    empty = torch.zeros(1, 4, 0, dtype=torch.int64)
+    calls = [lambda: wpt_b200.exact_attention(q, k, k, torch.arange(4), 0.1, 0, 2),
+             lambda: wpt_b200.sparse_attention(q, k, k, sink, empty, torch.arange(4), 0.1, 2),
+             lambda: wpt_b200.window_attention(q, k, k, sink, torch.arange(4), 0.1, window=1),
+             lambda: wpt_b200.tree_attention(q, k, k, torch.tensor([0]), torch.arange(4) - 1, 0.1),
+             lambda: wpt_b200.forward_with_lse(q, k, k, torch.arange(4), 0.1)]
+    for call in calls:
+        with pytest.raises(NotImplementedError, match="bfloat16"):
+            call()
 
 
 def test_module_has_the_reference_contract():

@@ -213,3 +213,37 @@ def test_sparse_window_rows_outside_the_table(wb):
     ref_out, _ = oat.sparse_attention(_np(q), _np(e[..., :C]), _np(e[..., C:]), sink.double().numpy(), idx.numpy(),
                                       positions.numpy(), C ** -0.5, W)
     _check(wb, out, None, ref_out, None)
+
+
+@pytest.mark.parametrize("shards,with_sink", [(2, False), (3, True), (8, True)])
+def test_long_row_shards_packed_and_merged_equal_one_call(wb, shards, with_sink):
+    # the kernel path of the multi-GPU long row on one GPU: each shard's
+    # partials go into its own chunk of one buffer (as the in-place
+    # all-gather leaves them on every rank), then one grouped merge
+    from wpt_b200 import multi, ops
+    g = torch.Generator().manual_seed(40 + shards)
+    H, C, N = 32, 128, 20000
+    q = (torch.randn(1, 1, H, C, generator=g) * 0.5).bfloat16().cuda()
+    e = (torch.randn(1, N, 2 * C, generator=g) * 0.5).bfloat16().cuda()
+    sink = (torch.randn(H, generator=g) * 0.5).cuda() if with_sink else None
+    positions = torch.tensor([[N - 1]]).cuda()
+    longest = max(multi.key_shard(N, shards, r)[1] - multi.key_shard(N, shards, r)[0] for r in range(shards))
+    splits, _ = ops.partials_plan(q.shape, longest, q.device)
+    rows = H
+    group = (splits * rows * (C + 1) + 3) // 4 * 4
+    parts = torch.empty(shards, group, dtype=torch.float32, device="cuda")
+    for r in range(shards):
+        a, b = multi.key_shard(N, shards, r)
+        chunk = parts[r]
+        ops.stream_partials(q, e[:, a:b, :C], e[:, a:b, C:], positions - a, C ** -0.5, splits=splits,
+                            into=(chunk[:splits * rows * C].view(splits, rows, C),
+                                  chunk[splits * rows * C:splits * rows * (C + 1)].view(splits, rows)))
+    out, lse = ops.merge_groups(parts, splits, rows, H, C, sink)
+    whole, whole_lse = ops.stream_forward(q, e[..., :C], e[..., C:], positions, C ** -0.5, sink=sink)
+    assert wb.device_status() == 0
+    assert (out.float().reshape(whole.shape) - whole.float()).abs().max().item() < 1e-2
+    assert (lse.reshape(whole_lse.shape) - whole_lse).abs().max().item() < 1e-4
+    ref, ref_lse = oat.range_attention(_np(q.cpu()), _np(e[..., :C].cpu()), _np(e[..., C:].cpu()),
+                                       np.array([[N - 1]]), C ** -0.5,
+                                       sink=None if sink is None else sink.double().cpu().numpy())
+    _check(wb, out.reshape(whole.shape), lse.reshape(whole_lse.shape), ref, ref_lse)

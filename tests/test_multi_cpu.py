@@ -1,8 +1,11 @@
 """The multi-GPU partitioning logic on CPU gloo ranks (world size 2 and 3):
-row sharding, length-balanced decode rows, and the long-row key split whose
-partials are all-gathered and merged by log-sum-exp. The per-shard
-attention and the merge are the CPU oracle here (no GPU in this suite); on
-the GPU they are the key-stream and merge kernels, checked by the gpu tests."""
+row sharding, length-balanced decode rows, and the long-row key split. The
+long row runs long_decode's production branch (the plan's all-reduce, each
+rank's partials written into its chunk of the shared buffer, the in-place
+all-gather, the grouped merge) with the three GPU calls it makes
+(ops.partials_plan, ops.stream_partials, ops.merge_groups) replaced by CPU
+restatements, since this suite has no GPU; the kernels themselves are
+checked by the gpu tests."""
 
 import os
 import socket
@@ -41,47 +44,85 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def _oracle_partial(q, k, v, local, scale):
-    out, lse = oat.range_attention(q.numpy(), k.numpy(), v.numpy(), local.numpy(), scale)
-    return torch.from_numpy(out).float(), torch.from_numpy(lse).float()
+SPLITS = 3  # partials per rank in the CPU stand-ins
 
 
-def _oracle_merge(parts_o, parts_lse, H, sink):
-    out, lse = oat.merge_partials(parts_o.double().numpy(), parts_lse.double().numpy(),
-                                  np.ones(parts_lse.shape), None if sink is None else np.tile(sink.numpy(), parts_lse.shape[1] // H))
-    return torch.from_numpy(out).float(), torch.from_numpy(lse).float()
+def _cpu_partials_plan(q_shape, N, device, window=0):
+    return SPLITS, 1
 
 
-def _long_rank(rank, world, port, result):
+def _cpu_stream_partials(q, k, v, local, scale, window=0, into=None, splits=None):
+    """The key-stream kernel's partials-only mode restated on the CPU: the
+    shard's keys cut into `splits` equal chunks, each chunk's output
+    normalised by its own sum and that sum's log (-inf for no key)."""
+    B, T, H, C = q.shape
+    n = k.shape[1]
+    per = -(-n // splits)
+    part_o, part_lse = into
+    for s in range(splits):
+        a, b = s * per, min(n, (s + 1) * per)
+        if a >= b:
+            part_o[s] = 0.0
+            part_lse[s] = float("-inf")
+            continue
+        out, lse = oat.range_attention(q.numpy(), k[:, a:b].numpy(), v[:, a:b].numpy(), (local - a).numpy(), scale)
+        part_o[s] = torch.from_numpy(np.nan_to_num(out)).reshape(B * T * H, C)
+        part_lse[s] = torch.from_numpy(lse).reshape(B * T * H)
+    return part_o, part_lse
+
+
+def _cpu_merge_groups(parts, per, rows, H, C, sink=None):
+    """The grouped merge kernel restated: chunk g = per splits' outputs
+    (per, rows, C) then their log-sums (per, rows)."""
+    G = parts.shape[0]
+    o = parts[:, :per * rows * C].reshape(G * per, rows, C).double().numpy()
+    lse = parts[:, per * rows * C:per * rows * (C + 1)].reshape(G * per, rows).double().numpy()
+    out, total = oat.merge_partials(o, lse, np.ones(lse.shape),
+                                    None if sink is None else np.tile(sink.numpy(), rows // H))
+    return torch.from_numpy(out).float(), torch.from_numpy(total).float()
+
+
+def _long_rank(rank, world, port, result, with_sink):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     dist.init_process_group("gloo", rank=rank, world_size=world)
+    # the production branch of long_decode, with the three GPU calls it
+    # makes replaced by their CPU restatements (no GPU in this suite)
+    from wpt_b200 import ops
+    ops.partials_plan = _cpu_partials_plan
+    ops.stream_partials = _cpu_stream_partials
+    ops.merge_groups = _cpu_merge_groups
     try:
         g = torch.Generator().manual_seed(5)
         B, T, H, C, N = 1, 2, 4, 16, 1000
         q = torch.randn(B, T, H, C, generator=g, dtype=torch.float64)
         k = torch.randn(B, N, C, generator=g, dtype=torch.float64)
         v = torch.randn(B, N, C, generator=g, dtype=torch.float64)
+        sink = torch.randn(H, generator=g, dtype=torch.float64) if with_sink else None
         positions = torch.tensor([[700, 999]])
         start, stop = multi.key_shard(N, world, rank)
-        out, lse = multi.long_decode(q, k[:, start:stop], v[:, start:stop], start, positions, 0.25,
-                                     partial=_oracle_partial, merge=_oracle_merge)
+        for _ in range(2):  # the second call reuses the plan and its buffer
+            out, lse = multi.long_decode(q.float(), k[:, start:stop].float(), v[:, start:stop].float(), start,
+                                         positions, 0.25, sink=None if sink is None else sink.float())
         if rank == 0:
             result["out"], result["lse"] = out.numpy(), lse.numpy()
     finally:
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("world", [2, 3])
-def test_long_row_split_over_gloo_ranks_equals_whole(world):
+@pytest.mark.parametrize("world,with_sink", [(2, False), (3, True)])
+def test_long_row_split_over_gloo_ranks_equals_whole(world, with_sink):
     port = _free_port()
     manager = mp.get_context("spawn").Manager()
     result = manager.dict()
-    mp.start_processes(_long_rank, args=(world, port, result), nprocs=world, start_method="spawn", join=True)
+    mp.start_processes(_long_rank, args=(world, port, result, with_sink), nprocs=world, start_method="spawn",
+                       join=True)
     g = torch.Generator().manual_seed(5)
     B, T, H, C, N = 1, 2, 4, 16, 1000
     q = torch.randn(B, T, H, C, generator=g, dtype=torch.float64)
     k = torch.randn(B, N, C, generator=g, dtype=torch.float64)
     v = torch.randn(B, N, C, generator=g, dtype=torch.float64)
-    ref, ref_lse, _ = oat.exact_attention(q.numpy(), k.numpy(), v.numpy(), np.array([[700, 999]]), 0.25, 0, 0)
+    sink = torch.randn(H, generator=g, dtype=torch.float64).numpy() if with_sink else None
+    q, k, v = (x.float().double() for x in (q, k, v))
+    ref, ref_lse = oat.range_attention(q.numpy(), k.numpy(), v.numpy(), np.array([[700, 999]]), 0.25, sink=sink)
     assert np.abs(result["out"] - ref).max() < 1e-5
     assert np.abs(result["lse"] - ref_lse).max() < 1e-5

@@ -38,12 +38,20 @@ def chosen_columns(top_k, window, N):
     return max(0, min(top_k, N - window))
 
 
-def _compute(x):
-    return x if x.dtype == torch.bfloat16 else x.to(torch.bfloat16)
-
-
 def _positions(positions, B):
     return positions.to(torch.int64).expand(B, -1).contiguous()
+
+
+def _bf16_only(*tensors):
+    """The kernels compute in bfloat16, WPT's compute dtype under autocast
+    (layers.py:13-17). The reference computes in its inputs' dtype, so
+    float32 or float16 inputs are refused, not silently rounded; the
+    reference's kernel tests skip on NotImplementedError
+    (tests/test_kernels.py:149-154)."""
+    for t in tensors:
+        if t.dtype != torch.bfloat16:
+            raise NotImplementedError(f"wpt_b200 computes attention in bfloat16; got {t.dtype} "
+                                      "(cast q, k and v to bfloat16, as WPT's autocast does)")
 
 
 # ------------------------------------------------------------ exact attention
@@ -73,11 +81,13 @@ class _Exact(torch.autograd.Function):
 def exact_attention(q, k, v, positions, scale, top_k, window):
     """pytorch_kernels.exact_attention's result: (output (B, T, H, c) in q's
     dtype, chosen rows (B, T, K) int64, -1 padded)."""
+    _bf16_only(q, k, v)
     return _Exact.apply(q, k, v, positions, scale, top_k, window)
 
 
 def forward_with_lse(q, k, v, positions, scale, window=0, sink=None):
     """Forward only, with the log-sum-exp: (out bf16, lse fp32)."""
+    _bf16_only(q, k, v)
     return ops.attention_forward(q, k, v, _positions(positions, q.shape[0]), scale, window=window, sink=sink)
 
 
@@ -118,6 +128,7 @@ def sparse_attention(q, k, v, sink, idx, positions, scale, window):
     """pytorch_kernels.sparse_attention's result: the output (B, T, H, c), in
     q's dtype, over each query's rows idx (B, T, K) (-1 for none) and its
     last `window` rows, with sink (H,) in each head's denominator."""
+    _bf16_only(q, k, v)
     return _Sparse.apply(q, k, v, sink, idx, positions, scale, window)
 
 
@@ -129,6 +140,7 @@ def window_attention(q, k, v, sink, positions, scale, window=None):
     query t reads table rows t .. t + window - 1 that are not before the
     text, with the sink in each head's denominator. window defaults to
     WINDOW (128, attention.py:53)."""
+    _bf16_only(q, k, v)
     W = WINDOW if window is None else int(window)
     B, T, H, c = q.shape
     positions = _positions(positions, B)
@@ -147,10 +159,10 @@ def tree_attention(q, k, v, cache_len, parents, scale, sink=None):
     the rows before cache_len[b] and those of its ancestors and itself
     (parents (n,) or (B, n), -1 for a root). A chain (parents[i] = i - 1) is
     exact_attention at positions cache_len + i. Returns (out bf16, lse)."""
+    _bf16_only(q, k, v)
     B, n, H, c = q.shape
     cache_len = torch.as_tensor(cache_len, dtype=torch.int64, device=q.device).reshape(-1).expand(B).contiguous()
-    bits = ops.tree_bits_from_parents(parents).to(q.device)
-    bits = bits.expand(B, n).contiguous()
+    bits = ops.tree_bits(torch.as_tensor(parents, dtype=torch.int64, device=q.device), B)
     positions = cache_len[:, None] + torch.arange(n, device=q.device, dtype=torch.int64)
     return ops.prefill_forward(q, k, v, positions, scale, tree_bits=bits, tree_base=cache_len, sink=sink)
 

@@ -31,6 +31,8 @@ SIGNATURES = {
     "wpt_attn_decode_noalloc": [_P, _P, _P, _I64, _I64, _I64, _I64, _P, _P, _P, _I, _P, _P, _P, _I, _I, _I, _I,
                                 _I, _I, _I, _I, _F, _P],
     "wpt_attn_merge": [_P, _P, _I, _I64, _I64, _I, _I, _P, _P, _P, _P],
+    "wpt_tree_bits": [_P, _I, _I, _P, _P],
+    "wpt_attn_merge_groups": [_P, _I, _I, _I64, _I64, _I, _I, _P, _P, _P, _P],
 }
 
 RESTYPES = {"wpt_last_error": ctypes.c_char_p, "wpt_accept_scratch_bytes": ctypes.c_size_t}

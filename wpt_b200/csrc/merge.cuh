@@ -15,11 +15,29 @@
 
 namespace wpt {
 
+// Where split s's partials sit. Splits come in groups of `per` (one group
+// per GPU of a long row, gathered side by side): within a group, split
+// stride `stride` rows; group g's output partials start at g * group_o
+// floats and its log-sums at g * group_l floats. One group (per = splits)
+// is the plain (splits, rows) layout.
+struct SplitLayout {
+  int per;
+  int64_t stride, group_o, group_l;
+  __device__ __forceinline__ int64_t o(int s, int C) const {
+    const int g = s / per;
+    return g * group_o + (s - g * per) * stride * C;
+  }
+  __device__ __forceinline__ int64_t l(int s) const {
+    const int g = s / per;
+    return g * group_l + (s - g * per) * stride;
+  }
+};
+
 // One warp per row; lane j handles columns j, j + 32, ...
 template <int C>
 __global__ void __launch_bounds__(256) merge_kernel(const float* __restrict__ part_o,
                                                     const float* __restrict__ part_lse, int splits,
-                                                    int64_t rows, int64_t split_stride, int H,
+                                                    int64_t rows, SplitLayout lay, int H,
                                                     const float* __restrict__ sink, __nv_bfloat16* __restrict__ out,
                                                     float* __restrict__ lse_out) {
   griddep_wait();  // the partials come from the kernel before (programmatic dependent launch)
@@ -28,7 +46,7 @@ __global__ void __launch_bounds__(256) merge_kernel(const float* __restrict__ pa
   if (row >= rows) return;
   const int h = static_cast<int>(row % H);
   float m = -INFINITY;
-  for (int s = 0; s < splits; ++s) m = fmaxf(m, part_lse[s * split_stride + row]);
+  for (int s = 0; s < splits; ++s) m = fmaxf(m, part_lse[lay.l(s) + row]);
   const float sk = sink != nullptr ? sink[h] : -INFINITY;
   m = fmaxf(m, sk);
   float acc[C / 32];
@@ -37,11 +55,11 @@ __global__ void __launch_bounds__(256) merge_kernel(const float* __restrict__ pa
   float denom = 0.f;
   if (m != -INFINITY) {
     for (int s = 0; s < splits; ++s) {
-      const float ls = part_lse[s * split_stride + row];
+      const float ls = part_lse[lay.l(s) + row];
       if (ls == -INFINITY) continue;
       const float w = __expf(ls - m);
       denom += w;
-      const float* o = part_o + (s * split_stride + row) * C;
+      const float* o = part_o + lay.o(s, C) + row * C;
 #pragma unroll
       for (int i = 0; i < C / 32; ++i) acc[i] = fmaf(w, o[lane + 32 * i], acc[i]);
     }
@@ -62,11 +80,12 @@ __global__ void __launch_bounds__(256) merge_kernel(const float* __restrict__ pa
 constexpr int MERGE_THREADS = 512, MERGE_MAX_SPLITS = 2048;
 template <int C>
 __global__ void __launch_bounds__(MERGE_THREADS) merge_wide_kernel(
-    const float* __restrict__ part_o, const float* __restrict__ part_lse, int splits, int64_t split_stride, int H,
+    const float* __restrict__ part_o, const float* __restrict__ part_lse, int splits, SplitLayout lay, int H,
     const float* __restrict__ sink, __nv_bfloat16* __restrict__ out, float* __restrict__ lse_out) {
   griddep_wait();  // the partials come from the kernel before (programmatic dependent launch)
   constexpr int GROUPS = MERGE_THREADS / C;
   __shared__ float s_w[MERGE_MAX_SPLITS];
+  __shared__ int64_t s_off[MERGE_MAX_SPLITS];  // each split's output offset (floats) for this row
   __shared__ float s_red[MERGE_THREADS / 32 + 1];
   __shared__ float s_acc[GROUPS][C];
   const int64_t row = blockIdx.x;
@@ -74,7 +93,7 @@ __global__ void __launch_bounds__(MERGE_THREADS) merge_wide_kernel(
   const int h = static_cast<int>(row % H);
   // maximum of the log-sums (and the sink)
   float m = -INFINITY;
-  for (int s = t; s < splits; s += MERGE_THREADS) m = fmaxf(m, part_lse[s * split_stride + row]);
+  for (int s = t; s < splits; s += MERGE_THREADS) m = fmaxf(m, part_lse[lay.l(s) + row]);
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
   if (lane == 0) s_red[warp] = m;
@@ -87,9 +106,10 @@ __global__ void __launch_bounds__(MERGE_THREADS) merge_wide_kernel(
   // weights exp(lse_s - m) and their sum
   float d = 0.f;
   for (int s = t; s < splits; s += MERGE_THREADS) {
-    const float ls = part_lse[s * split_stride + row];
+    const float ls = part_lse[lay.l(s) + row];
     const float w = (m == -INFINITY || ls == -INFINITY) ? 0.f : __expf(ls - m);
     s_w[s] = w;
+    s_off[s] = lay.o(s, C);
     d += w;
   }
 #pragma unroll
@@ -103,10 +123,10 @@ __global__ void __launch_bounds__(MERGE_THREADS) merge_wide_kernel(
   int s = g;
   for (; s + 3 * GROUPS < splits; s += 4 * GROUPS) {
     const float w0 = s_w[s], w1 = s_w[s + GROUPS], w2 = s_w[s + 2 * GROUPS], w3 = s_w[s + 3 * GROUPS];
-    const float o0 = w0 != 0.f ? o[s * split_stride * C] : 0.f;
-    const float o1 = w1 != 0.f ? o[(s + GROUPS) * split_stride * C] : 0.f;
-    const float o2 = w2 != 0.f ? o[(s + 2 * GROUPS) * split_stride * C] : 0.f;
-    const float o3 = w3 != 0.f ? o[(s + 3 * GROUPS) * split_stride * C] : 0.f;
+    const float o0 = w0 != 0.f ? o[s_off[s]] : 0.f;
+    const float o1 = w1 != 0.f ? o[s_off[s + GROUPS]] : 0.f;
+    const float o2 = w2 != 0.f ? o[s_off[s + 2 * GROUPS]] : 0.f;
+    const float o3 = w3 != 0.f ? o[s_off[s + 3 * GROUPS]] : 0.f;
     acc0 = fmaf(w0, o0, acc0);
     acc1 = fmaf(w1, o1, acc1);
     acc2 = fmaf(w2, o2, acc2);
@@ -114,7 +134,7 @@ __global__ void __launch_bounds__(MERGE_THREADS) merge_wide_kernel(
   }
   for (; s < splits; s += GROUPS) {
     const float w = s_w[s];
-    if (w != 0.f) acc0 = fmaf(w, o[s * split_stride * C], acc0);
+    if (w != 0.f) acc0 = fmaf(w, o[s_off[s]], acc0);
   }
   s_acc[g][c] = (acc0 + acc1) + (acc2 + acc3);
   __syncthreads();

@@ -17,6 +17,7 @@
 #include "prefill.cuh"
 #include "select.cuh"
 #include "stream.cuh"
+#include "tree.cuh"
 
 namespace {
 
@@ -38,6 +39,13 @@ int cuda_fail(cudaError_t e, const char* what) {
 
 __device__ unsigned g_status_word;
 
+// One lock for every per-device cache of a device symbol's address (the
+// status word here, the no-alloc scratch below). The caches are filled once
+// per device and never refreshed: the library must not be used across a
+// cudaDeviceReset (or any teardown of the device's primary context), after
+// which the cached addresses would be stale.
+std::mutex g_symbol_lock;
+
 // The device address of the status word on the current device.
 int status_word(unsigned** out) {
   static unsigned* cached[64] = {};
@@ -45,6 +53,7 @@ int status_word(unsigned** out) {
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
   if (dev < 0 || dev >= 64) return fail(WPT_ERR_INVALID, "device %d out of range", dev);
+  std::lock_guard<std::mutex> guard(g_symbol_lock);
   if (cached[dev] == nullptr) {
     void* p = nullptr;
     e = cudaGetSymbolAddress(&p, g_status_word);
@@ -233,7 +242,7 @@ template <int C>
 // pdl: the merge directly follows the attention kernel that wrote the
 // partials, and launches while that kernel finishes (programmatic dependent
 // launch; the merge waits for it on the device before reading).
-int launch_merge(const float* part_o, const float* part_lse, int splits, int64_t rows, int64_t split_stride, int H,
+int launch_merge(const float* part_o, const float* part_lse, int splits, int64_t rows, wpt::SplitLayout lay, int H,
                  const float* sink, void* out, float* lse, cudaStream_t stream, bool pdl = false) {
   cudaLaunchConfig_t cfg = {};
   cudaLaunchAttribute attr[1];
@@ -248,16 +257,28 @@ int launch_merge(const float* part_o, const float* part_lse, int splits, int64_t
   if (splits >= 16 && splits <= wpt::MERGE_MAX_SPLITS && rows <= 4096) {  // few rows, many splits: a CTA per row
     cfg.gridDim = dim3(static_cast<unsigned>(rows));
     cfg.blockDim = dim3(wpt::MERGE_THREADS);
-    e = cudaLaunchKernelEx(&cfg, wpt::merge_wide_kernel<C>, part_o, part_lse, splits, split_stride, H, sink, o, lse);
+    e = cudaLaunchKernelEx(&cfg, wpt::merge_wide_kernel<C>, part_o, part_lse, splits, lay, H, sink, o, lse);
   } else {
     const int warps = 8;
     const int64_t blocks = (rows + warps - 1) / warps;
     cfg.gridDim = dim3(static_cast<unsigned>(blocks));
     cfg.blockDim = dim3(warps * 32);
-    e = cudaLaunchKernelEx(&cfg, wpt::merge_kernel<C>, part_o, part_lse, splits, rows, split_stride, H, sink, o, lse);
+    e = cudaLaunchKernelEx(&cfg, wpt::merge_kernel<C>, part_o, part_lse, splits, rows, lay, H, sink, o, lse);
   }
   if (e != cudaSuccess) return cuda_fail(e, "merge_kernel launch");
   return WPT_OK;
+}
+
+// The plain (splits, rows) layout at split stride `split_stride` rows.
+template <int C>
+int launch_merge(const float* part_o, const float* part_lse, int splits, int64_t rows, int64_t split_stride, int H,
+                 const float* sink, void* out, float* lse, cudaStream_t stream, bool pdl = false) {
+  wpt::SplitLayout lay;
+  lay.per = splits;
+  lay.stride = split_stride;
+  lay.group_o = 0;
+  lay.group_l = 0;
+  return launch_merge<C>(part_o, part_lse, splits, rows, lay, H, sink, out, lse, stream, pdl);
 }
 
 }  // namespace
@@ -356,6 +377,30 @@ extern "C" int wpt_attn_merge(const float* part_o, const float* part_lse, int sp
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   return C == 128 ? launch_merge<128>(part_o, part_lse, splits, rows, split_stride, H, sink, out, lse, s)
                   : launch_merge<64>(part_o, part_lse, splits, rows, split_stride, H, sink, out, lse, s);
+}
+
+extern "C" int wpt_attn_merge_groups(const float* parts, int groups, int per, int64_t rows, int64_t group_floats,
+                                     int H, int C, const float* sink, void* out, float* lse, void* stream) {
+  if (C != 64 && C != 128) return fail(WPT_ERR_UNSUPPORTED, "head width %d: the kernels take 64 or 128", C);
+  if (groups < 1 || per < 1 || rows < 0 || H < 1)
+    return fail(WPT_ERR_INVALID, "bad merge shape groups=%d per=%d rows=%lld", groups, per,
+                static_cast<long long>(rows));
+  if (static_cast<int64_t>(groups) * per > wpt::MERGE_MAX_SPLITS * 32)
+    return fail(WPT_ERR_UNSUPPORTED, "%d x %d splits: too many", groups, per);
+  if (group_floats < static_cast<int64_t>(per) * rows * (C + 1))
+    return fail(WPT_ERR_INVALID, "group_floats %lld < per * rows * (C + 1)", static_cast<long long>(group_floats));
+  if (!parts || !out || !lse) return fail(WPT_ERR_INVALID, "a required pointer is NULL");
+  if (rows == 0) return WPT_OK;
+  wpt::SplitLayout lay;
+  lay.per = per;
+  lay.stride = rows;
+  lay.group_o = group_floats;
+  lay.group_l = group_floats;
+  const float* part_lse = parts + static_cast<int64_t>(per) * rows * C;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int splits = groups * per;
+  return C == 128 ? launch_merge<128>(parts, part_lse, splits, rows, lay, H, sink, out, lse, s)
+                  : launch_merge<64>(parts, part_lse, splits, rows, lay, H, sink, out, lse, s);
 }
 
 extern "C" int wpt_attn_decode(const void* q, const void* k, const void* v, int64_t k_stride_b, int64_t k_stride_n,
@@ -506,6 +551,20 @@ extern "C" int wpt_attn_topk(const void* q, const void* k, int64_t k_stride_b, i
   return WPT_OK;
 }
 
+extern "C" int wpt_tree_bits(const int64_t* parents, int B, int n, uint64_t* bits, void* stream) {
+  if (B < 1 || n < 1) return fail(WPT_ERR_INVALID, "empty tree batch B=%d n=%d", B, n);
+  if (n > 64) return fail(WPT_ERR_UNSUPPORTED, "a tree of %d nodes: the kernels take up to 64", n);
+  if (!parents || !bits) return fail(WPT_ERR_INVALID, "a required pointer is NULL");
+  const int64_t total = static_cast<int64_t>(B) * n;
+  const int64_t blocks = (total + 255) / 256;
+  if (blocks >= (int64_t(1) << 31)) return fail(WPT_ERR_UNSUPPORTED, "too many tree rows");
+  wpt::tree_bits_kernel<<<static_cast<unsigned>(blocks), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      parents, B, n, bits);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "tree_bits_kernel launch");
+  return WPT_OK;
+}
+
 extern "C" int wpt_temperature_scale(const float* x, int64_t n, float temperature, float* out, void* stream) {
   if (n < 0 || (n > 0 && (!x || !out))) return fail(WPT_ERR_INVALID, "bad temperature_scale arguments");
   if (!(temperature > 0.f)) return fail(WPT_ERR_INVALID, "temperature must be positive");
@@ -626,13 +685,12 @@ static __device__ __align__(256) float g_noalloc_scratch[WPT_NOALLOC_SCRATCH_FLO
 namespace {
 
 int noalloc_scratch(float** out) {
-  static std::mutex lock;
   static float* cached[64] = {};
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
   if (dev < 0 || dev >= 64) return fail(WPT_ERR_INVALID, "device %d out of range", dev);
-  std::lock_guard<std::mutex> guard(lock);
+  std::lock_guard<std::mutex> guard(g_symbol_lock);
   if (cached[dev] == nullptr) {
     void* p = nullptr;
     e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
@@ -650,11 +708,23 @@ extern "C" int wpt_attn_decode_noalloc(const void* q, const void* k, const void*
                                        const int64_t* positions, const int64_t* floor_rows, const int64_t* idx,
                                        int K, const float* sink, void* out, float* lse, int splits, int chunk_tiles,
                                        int B, int T, int H, int C, int N, int window, float scale, void* stream) {
+  // The partials live in the library's private array, where the caller
+  // cannot read them: the partials-only mode of wpt_attn_decode
+  // (out == lse == NULL) would compute nothing the caller can see.
+  if (out == nullptr || lse == nullptr)
+    return fail(WPT_ERR_INVALID, "no-alloc decode: out and lse are required (its partials are not readable)");
+  if (C != 128) return fail(WPT_ERR_UNSUPPORTED, "head width %d: the key-stream kernel takes 128", C);
+  if (H < 1 || H > 64) return fail(WPT_ERR_UNSUPPORTED, "%d heads: the key-stream kernel takes 1 to 64", H);
+  if (B < 1 || T < 1) return fail(WPT_ERR_INVALID, "empty shape B=%d T=%d", B, T);
+  if (splits < 1) return fail(WPT_ERR_INVALID, "splits must be >= 1");
+  if (splits > 65535) return fail(WPT_ERR_UNSUPPORTED, "%d splits: at most 65535", splits);
+  const int64_t rows = static_cast<int64_t>(B) * T * H;
+  if (rows >= (int64_t(1) << 31)) return fail(WPT_ERR_UNSUPPORTED, "B*T*H = %lld rows is too many",
+                                              static_cast<long long>(rows));
   float* part_o = nullptr;
   float* part_lse = nullptr;
   if (splits > 1) {
-    if (B < 1 || T < 1 || H < 1 || C < 1) return fail(WPT_ERR_INVALID, "empty shape B=%d T=%d H=%d C=%d", B, T, H, C);
-    const int64_t rows = static_cast<int64_t>(B) * T * H;
+    // splits < 2^16 and rows < 2^31, so the product fits in 64 bits
     const int64_t need = static_cast<int64_t>(splits) * rows * (C + 1);
     if (need > static_cast<int64_t>(WPT_NOALLOC_SCRATCH_FLOATS))
       return fail(WPT_ERR_UNSUPPORTED,

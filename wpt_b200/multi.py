@@ -9,10 +9,11 @@ partitions fit this path:
     rank takes its own rows and no data crosses NVLink (shard_rows,
     balanced_rows, which balances decode rows by their cached lengths);
   * one long row (long-context decode): its keys are split into contiguous
-    shards, one per rank. Each rank computes the partial attention of the
-    query over its shard (output normalised by its own softmax sum, and that
-    sum's log), the ranks all-gather those partials over NCCL, and each
-    merges them by log-sum-exp (the merge kernel): H x (C + 1) floats per rank
+    shards, one per rank. Each rank's kernel computes split partials of the
+    query over its shard (output normalised by each split's softmax sum, and
+    that sum's log) into its chunk of a shared-layout buffer, one in-place
+    NCCL all-gather exchanges the chunks, and every rank merges all splits
+    by log-sum-exp (the merge kernel): splits x H x (C + 1) floats per rank
     and query, latency-bound.
 """
 
@@ -50,46 +51,53 @@ def key_shard(n_rows, world, rank):
     return s.start, s.stop
 
 
-def long_decode(q, k_shard, v_shard, shard_start, positions, scale, sink=None, group=None, partial=None,
-                merge=None):
+_PLANS = {}  # (shape, shard length, world, device, group) -> (splits, group floats, parts buffer)
+
+
+def _long_plan(q, n_local, world, rank, group):
+    """Splits per rank and the gathered buffer of one long-row shape: the
+    split count comes from the longest shard (one all-reduce, made once per
+    shape), so that every rank's chunk has one layout."""
+    B, T, H, C = q.shape
+    key = (tuple(q.shape), n_local, world, q.device, id(group))
+    plan = _PLANS.get(key)
+    if plan is None:
+        longest = torch.tensor([n_local], dtype=torch.int64, device=q.device)
+        dist.all_reduce(longest, op=dist.ReduceOp.MAX, group=group)
+        splits, _ = ops.partials_plan(q.shape, int(longest.item()), q.device)
+        rows = B * T * H
+        group_floats = (splits * rows * (C + 1) + 3) // 4 * 4  # chunks start 16-byte aligned
+        parts = torch.empty(world, group_floats, dtype=torch.float32, device=q.device)
+        plan = _PLANS[key] = (splits, group_floats, parts)
+    return plan
+
+
+def long_decode(q, k_shard, v_shard, shard_start, positions, scale, sink=None, group=None):
     """Attention of q (B, T, H, C) over a long row whose keys are split over
     the ranks of `group`: this rank holds rows [shard_start, shard_start + n)
     as k_shard, v_shard (B, n, C). positions (B, T) are positions in the whole
     row. Returns (out (B, T, H, C) bf16, lse (B, T, H)) on every rank.
 
-    partial(q, k, v, local_positions, scale) -> (out, lse) computes this rank's
-    share (default: the key-stream kernel); merge(parts_o, parts_lse, H,
-    sink) -> (out rows, lse rows) combines the gathered shares (default: the
-    merge kernel). Tests substitute CPU versions to check the partitioning
-    with gloo ranks."""
+    Each rank's key-stream kernel writes its split partials straight into
+    its own chunk of a gathered buffer (output partials then log-sums), one
+    in-place NCCL all-gather brings every rank's chunk to every rank, and one
+    merge kernel combines all the splits. The buffer is allocated once per
+    shape and reused, so the call (kernel, collective, merge) can be
+    captured in a CUDA graph; calls on one stream are ordered, calls that
+    overlap on several streams would share it. The first call of a shape
+    makes one all-reduce (the longest shard, for the split count)."""
     B, T, H, C = q.shape
     world = dist.get_world_size(group) if dist.is_initialized() else 1
     local = positions - shard_start  # rows of this shard the query sees: 0 .. local (none when negative)
-    if partial is None and merge is None:
-        if world == 1:  # the whole row is here: one kernel call
-            return ops.stream_forward(q, k_shard, v_shard, local, scale, sink=sink)
-        # the kernel's own split partials go straight into the collective and
-        # one merge combines every rank's splits (no local merge, no copies)
-        part_o, part_lse = ops.stream_partials(q, k_shard, v_shard, local, scale)
-        S = part_o.shape[0]
-        parts_o = torch.empty(world * S, B * T * H, C, dtype=torch.float32, device=q.device)
-        parts_s = torch.empty(world * S, B * T * H, dtype=torch.float32, device=q.device)
-        dist.all_gather_into_tensor(parts_o, part_o, group=group)
-        dist.all_gather_into_tensor(parts_s, part_lse, group=group)
-        merged, merged_lse = ops.merge_partials(parts_o, parts_s, H, sink)
-        return merged.reshape(B, T, H, C), merged_lse.reshape(B, T, H)
-    partial = partial or (lambda q_, k_, v_, p_, s_: ops.stream_forward(q_, k_, v_, p_, s_))
-    merge = merge or ops.merge_partials
-    out, lse = partial(q, k_shard, v_shard, local, scale)
-    o = out.float().reshape(1, B * T * H, C)
-    s = lse.float().reshape(1, B * T * H)
-    if world > 1:  # one collective: each rank's (output, log-sum) rows packed side by side
-        packed = torch.cat([o, s.unsqueeze(-1)], dim=-1).contiguous()
-        gathered = torch.empty(world, B * T * H, C + 1, dtype=torch.float32, device=o.device)
-        dist.all_gather_into_tensor(gathered, packed, group=group)
-        parts_o = gathered[..., :C].contiguous()
-        parts_s = gathered[..., C].contiguous()
-    else:
-        parts_o, parts_s = o, s
-    merged, merged_lse = merge(parts_o, parts_s, H, sink)
+    if world == 1:  # the whole row is here: one kernel call
+        return ops.stream_forward(q, k_shard, v_shard, local, scale, sink=sink)
+    rank = dist.get_rank(group)
+    splits, group_floats, parts = _long_plan(q, k_shard.shape[1], world, rank, group)
+    rows = B * T * H
+    mine = parts[rank]
+    part_o = mine[:splits * rows * C].view(splits, rows, C)
+    part_lse = mine[splits * rows * C:splits * rows * (C + 1)].view(splits, rows)
+    ops.stream_partials(q, k_shard, v_shard, local, scale, into=(part_o, part_lse), splits=splits)
+    dist.all_gather_into_tensor(parts.view(-1), mine, group=group)  # in place: every rank's chunk to every rank
+    merged, merged_lse = ops.merge_groups(parts, splits, rows, H, C, sink)
     return merged.reshape(B, T, H, C), merged_lse.reshape(B, T, H)

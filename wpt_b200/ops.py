@@ -16,7 +16,6 @@ import torch
 
 from . import _lib
 
-SM_COUNT = 148
 LAUNCHES = [0]  # kernels this module has launched (read by bench.py around its timed region)
 
 
@@ -26,8 +25,29 @@ def _need_cuda(*tensors):
             raise ValueError("wpt_b200 computes on a CUDA device only; got a tensor on " + str(t.device))
 
 
+_SMS = {}
+
+
+def sm_count(device):
+    """The streaming multiprocessors of `device`, asked of the runtime once."""
+    index = device.index if device.index is not None else torch.cuda.current_device()
+    n = _SMS.get(index)
+    if n is None:
+        n = _SMS[index] = torch.cuda.get_device_properties(index).multi_processor_count
+    return n
+
+
 def _bf16(x):
-    return x if x.dtype == torch.bfloat16 else x.to(torch.bfloat16)
+    """The kernels compute in bf16 (WPT's compute dtype under autocast,
+    packages/wpt-model/src/wpt_model/layers.py:13-17). Other dtypes are
+    refused rather than rounded: the reference computes in the inputs'
+    dtype, so silently rounding float32 inputs would return float32
+    tensors of bf16 accuracy. NotImplementedError is what the reference's
+    kernel tests skip on (tests/test_kernels.py:149-154)."""
+    if x.dtype != torch.bfloat16:
+        raise NotImplementedError(f"wpt_b200 computes attention in bfloat16; got {x.dtype} "
+                                  "(cast q, k and v to bfloat16, as WPT's autocast does)")
+    return x
 
 
 def _table(x):
@@ -45,17 +65,17 @@ def _rows(x):
     return x.to(torch.int64).contiguous()
 
 
-def _splits_for(ctas, tiles):
+def _splits_for(ctas, tiles, sms):
     """Split count for a grid of `ctas` work items over `tiles` key tiles
     each: the persistent kernel runs the ctas * splits items in waves of
     one per SM, so the estimate is waves x (tiles per item + about 2 tiles'
     worth of per-item cost), plus half a tile per split for the merge; the
     cheapest count up to 32 (never more than the tiles) wins."""
-    if ctas >= SM_COUNT or tiles <= 1:
+    if ctas >= sms or tiles <= 1:
         return 1
     best, best_cost = 1, None
     for s in range(1, min(tiles, 32) + 1):
-        cost = math.ceil(ctas * s / SM_COUNT) * (tiles / s + 2) + (0.5 * s if s > 1 else 0.0)
+        cost = math.ceil(ctas * s / sms) * (tiles / s + 2) + (0.5 * s if s > 1 else 0.0)
         if best_cost is None or cost < best_cost:
             best, best_cost = s, cost
     return best
@@ -84,7 +104,7 @@ def prefill_forward(q, k, v, positions, scale, window=0, floor=None, tree_bits=N
     TQ = max(1, 128 // H)
     if splits is None:
         tiles = window // 128 + 2 if window else (N + 127) // 128
-        splits = _splits_for(B * math.ceil(T / (2 * TQ)), tiles)  # one CTA item per pair of query tiles
+        splits = _splits_for(B * math.ceil(T / (2 * TQ)), tiles, sm_count(q.device))  # one item per tile pair
     part_o = part_lse = None
     if splits > 1:
         part_o = torch.empty(splits, B * T * H, C, dtype=torch.float32, device=q.device)
@@ -111,6 +131,35 @@ def uses_stream(T, H, C):
     return C == 128 and H <= 64 and T * H <= 64
 
 
+def _stream_plan(B, T, H, N, K, window, gather, sms, chunk_tiles=None):
+    """(chunk_tiles, splits) of a key-stream call: each query group's key
+    slots are cut into chunks of chunk_tiles key tiles, one CTA per chunk."""
+    _, TQ = _stream_shape(T, H, gather)
+    groups = B * math.ceil(T / TQ)
+    if gather:
+        slots = K + max(window, 0)
+    else:
+        slots = min(N, window + TQ - 1) if window > 0 else N
+    tiles = max(1, math.ceil(slots / 128))
+    if chunk_tiles is None:
+        chunk_tiles = int(os.environ.get("WPT_B200_CHUNK", "0"))
+    if not chunk_tiles and gather:
+        # every query gathers exactly `tiles` tiles: its slots split so that
+        # the grid is about one CTA per SM
+        chunk_tiles = math.ceil(tiles / max(1, sms // groups))
+    elif not chunk_tiles and window > 0:
+        # window rows are short (window / 128 + 1 tiles): split them so that
+        # the grid covers every SM, at least two tiles a CTA
+        chunk_tiles = max(2, math.ceil(tiles / max(1, math.ceil(sms / groups))))
+    elif not chunk_tiles:
+        # at least 16 key tiles per CTA (a CTA's start-up costs about as much
+        # as streaming a few tiles), more when that still gives two CTAs per
+        # SM for rows of the table's full length (most rows are shorter)
+        chunk_tiles = max(min(16, tiles), 16 * math.ceil(tiles * groups / (2 * sms) / 16))
+    chunk_tiles = max(1, min(int(chunk_tiles), tiles))
+    return chunk_tiles, math.ceil(tiles / chunk_tiles)
+
+
 def stream_forward(q, k, v, positions, scale, window=0, floor=None, idx=None, sink=None, chunk_tiles=None):
     """(out (B, T, H, C) bf16, lse (B, T, H) fp32) from the key-stream
     kernel. Range mode (idx None): as prefill_forward. Gather mode: each
@@ -129,26 +178,7 @@ def stream_forward(q, k, v, positions, scale, window=0, floor=None, idx=None, si
         K = idx.shape[-1]
     if sink is not None:
         sink = sink.float().contiguous()
-    _, TQ = _stream_shape(T, H, gather)
-    groups = B * math.ceil(T / TQ)
-    if gather:
-        slots = K + max(window, 0)
-    else:
-        slots = min(N, window + TQ - 1) if window > 0 else N
-    tiles = max(1, math.ceil(slots / 128))
-    if chunk_tiles is None:
-        chunk_tiles = int(os.environ.get("WPT_B200_CHUNK", "0"))
-    if not chunk_tiles and gather:
-        # every query gathers exactly `tiles` tiles: its slots split so that
-        # the grid is about one CTA per SM
-        chunk_tiles = math.ceil(tiles / max(1, SM_COUNT // groups))
-    elif not chunk_tiles:
-        # at least 16 key tiles per CTA (a CTA's start-up costs about as much
-        # as streaming a few tiles), more when that still gives two CTAs per
-        # SM for rows of the table's full length (most rows are shorter)
-        chunk_tiles = max(min(16, tiles), 16 * math.ceil(tiles * groups / (2 * SM_COUNT) / 16))
-    chunk_tiles = max(1, min(int(chunk_tiles), tiles))
-    splits = math.ceil(tiles / chunk_tiles)
+    chunk_tiles, splits = _stream_plan(B, T, H, N, K, window, gather, sm_count(q.device), chunk_tiles)
     out = torch.empty_like(q)
     lse = torch.empty(B, T, H, dtype=torch.float32, device=q.device)
     part_o = part_lse = None
@@ -164,33 +194,70 @@ def stream_forward(q, k, v, positions, scale, window=0, floor=None, idx=None, si
     return out, lse
 
 
-def stream_partials(q, k, v, positions, scale, window=0):
+def partials_plan(q_shape, N, device, window=0):
+    """(splits, chunk_tiles) the key-stream kernel uses for partials of a
+    (B, T, H, C) query block over N keys: at least two splits."""
+    B, T, H, C = q_shape
+    chunk_tiles, splits = _stream_plan(B, T, H, N, 0, window, False, sm_count(device), None)
+    if splits < 2:  # at least two partials, so that the caller always has partials to merge
+        chunk_tiles, splits = max(1, math.ceil(chunk_tiles / 2)), 2
+    return splits, chunk_tiles
+
+
+def stream_partials(q, k, v, positions, scale, window=0, into=None, splits=None):
     """The key-stream kernel's split partials without the merge: (part_o
     (S, B*T*H, C) fp32, each split's output normalised by its own sum;
     part_lse (S, B*T*H) fp32, the natural log of that sum, -inf for a split
-    with no visible row), S >= 2. For callers that merge them with partials
-    computed elsewhere (merge_partials), e.g. on the other GPUs of a long row."""
+    with no visible row), S >= 2 (partials_plan). For callers that merge
+    them with partials computed elsewhere (merge_partials, merge_groups),
+    e.g. on the other GPUs of a long row. into=(part_o, part_lse): write
+    there (contiguous fp32 of those shapes) instead of new tensors.
+    splits: this many partials (>= 2) instead of partials_plan's count, the
+    keys cut into that many equal chunks of whole tiles (splits with no key
+    give -inf log-sums): ranks whose shards differ in length then still
+    produce chunks of one layout."""
     _need_cuda(q, k, v, positions)
     q = _bf16(q).contiguous()
     k, v = _table(k), _table(v)
     B, T, H, C = q.shape
     N = k.shape[1]
     positions = _rows(positions)
-    _, TQ = _stream_shape(T, H, False)
-    groups = B * math.ceil(T / TQ)
-    slots = min(N, window + TQ - 1) if window > 0 else N
-    tiles = max(1, math.ceil(slots / 128))
-    chunk_tiles = max(min(16, tiles), 16 * math.ceil(tiles * groups / (2 * SM_COUNT) / 16))
-    chunk_tiles = max(1, min(chunk_tiles, tiles))
-    splits = max(2, math.ceil(tiles / chunk_tiles))
-    part_o = torch.empty(splits, B * T * H, C, dtype=torch.float32, device=q.device)
-    part_lse = torch.empty(splits, B * T * H, dtype=torch.float32, device=q.device)
+    if splits is None:
+        splits, chunk_tiles = partials_plan(q.shape, N, q.device, window)
+    else:
+        splits = max(2, int(splits))
+        slots = min(N, window + 63) if window > 0 else N
+        chunk_tiles = max(1, math.ceil(math.ceil(slots / 128) / splits))
+    if into is None:
+        part_o = torch.empty(splits, B * T * H, C, dtype=torch.float32, device=q.device)
+        part_lse = torch.empty(splits, B * T * H, dtype=torch.float32, device=q.device)
+    else:
+        part_o, part_lse = into
+        if (part_o.shape != (splits, B * T * H, C) or part_lse.shape != (splits, B * T * H)
+                or not part_o.is_contiguous() or not part_lse.is_contiguous()):
+            raise ValueError("stream_partials: `into` does not match partials_plan's shapes")
     _lib.check(_lib.lib().wpt_attn_decode(
         _lib.ptr(q), _lib.ptr(k), _lib.ptr(v), k.stride(0), k.stride(1), v.stride(0), v.stride(1),
         _lib.ptr(positions), None, None, 0, None, None, None, _lib.ptr(part_o), _lib.ptr(part_lse), splits,
         chunk_tiles, B, T, H, C, N, int(window), float(scale), _lib.stream(q.device)))
     LAUNCHES[0] += 1
     return part_o, part_lse
+
+
+def merge_groups(parts, per, rows, H, C, sink=None, out=None, lse=None):
+    """Merge of partials gathered side by side: parts (G, group_floats) fp32,
+    chunk g = `per` splits' output partials (per, rows, C) then their
+    log-sums (per, rows). Returns (out (rows, C) bf16, lse (rows,) fp32)."""
+    _need_cuda(parts, sink)
+    G, group_floats = parts.shape
+    if sink is not None:
+        sink = sink.float().contiguous()
+    out = torch.empty(rows, C, dtype=torch.bfloat16, device=parts.device) if out is None else out
+    lse = torch.empty(rows, dtype=torch.float32, device=parts.device) if lse is None else lse
+    _lib.check(_lib.lib().wpt_attn_merge_groups(_lib.ptr(parts), G, per, rows, group_floats, H, C, _lib.ptr(sink),
+                                                _lib.ptr(out), _lib.ptr(lse), _lib.stream(parts.device)))
+    LAUNCHES[0] += 1
+    return out, lse
 
 
 def attention_forward(q, k, v, positions, scale, window=0, floor=None, sink=None):
@@ -241,28 +308,22 @@ def merge_partials(part_o, part_lse, H, sink=None, out=None, lse=None):
     return out, lse
 
 
-def tree_bits_from_parents(parents):
-    """(n,) or (B, n) parent indices (-1 for a root, parents[i] < i) ->
-    int64 bit masks: bit j of node i is set when node j is i or one of its
-    ancestors. Computed on the host (the tree is tiny) and returned on the
-    parents' device."""
-    device = parents.device if torch.is_tensor(parents) else torch.device("cpu")
-    par = torch.as_tensor(parents, dtype=torch.int64).cpu()
-    flat = par.reshape(-1, par.shape[-1])
-    n = flat.shape[-1]
+def tree_bits(parents, B):
+    """(n,) or (B, n) int64 parent indices on the GPU (-1 for a root,
+    parents[i] < i) -> (B, n) int64 ancestor masks: bit j of node i is set
+    when node j is i or one of its ancestors. One small kernel on the
+    current stream: no host synchronisation, so verification can be
+    captured in a CUDA graph. A parent that is not before its child ends
+    that node's walk (the mask then holds the nodes met so far)."""
+    n = parents.shape[-1]
     if n > 64:
         raise NotImplementedError(f"a tree of {n} nodes: the kernels take up to 64")
-    bits = torch.zeros_like(flat)
-    for r in range(flat.shape[0]):
-        masks = []
-        for i in range(n):
-            p = int(flat[r, i])
-            if p >= i:
-                raise ValueError("parents must come before their children (parents[i] < i)")
-            m = (1 << i) | (masks[p] if p >= 0 else 0)
-            masks.append(m)
-            bits[r, i] = m - (1 << 64) if m >= (1 << 63) else m
-    return bits.reshape(par.shape).to(device)
+    _need_cuda(parents)
+    par = parents.to(torch.int64).expand(B, n).contiguous()
+    bits = torch.empty(B, n, dtype=torch.int64, device=par.device)
+    _lib.check(_lib.lib().wpt_tree_bits(_lib.ptr(par), B, n, _lib.ptr(bits), _lib.stream(par.device)))
+    LAUNCHES[0] += 1
+    return bits
 
 
 def accept(scores, drafted, q, uniforms, resample, temperature=1.0, top_k=None, lengths=None):
