@@ -7,6 +7,9 @@ them:
     python tests/golden/make_golden.py --reference <the reference repository>
 
 What each fixture pins (paths relative to the reference repository):
+  grads.npz             gradients from the reference's autograd: exact attention
+                        (pytorch_kernels.py:123-139), sparse attention with a
+                        sink (:189-210), window_attention (attention.py:85-107)
   exact_small.npz       pytorch_kernels.exact_attention (+ top-k choice, LSE
                         read from the autograd node's saved tensors),
                         packages/wpt-model/src/wpt_model/pytorch_kernels.py:98-146
@@ -91,6 +94,65 @@ def sparse_small(pk):
     out = pk.sparse_attention(q, k, v, sink, idx, positions, 0.3, 5)
     np.savez(os.path.join(HERE, "sparse_small.npz"), q=_np(q), k=_np(k), v=_np(v), sink=_np(sink), idx=_np(idx),
              positions=_np(positions), scale=0.3, window=5, out=_np(out), lse=_lse_of(out))
+
+
+def grads(at, pk):
+    """Gradients of the reference's autograd: exact attention (the backward
+    of pytorch_kernels.py:123-139) on a causal pass and a generation pass,
+    sparse attention with chosen rows, -1 padding and a sink
+    (:189-210), and window_attention (attention.py:85-107, plain autograd),
+    each with a seeded d_out."""
+    g = torch.Generator().manual_seed(11)
+    cases = {}
+    # exact, causal prefill with ragged positions in row 1
+    B, T, H, c, N = 2, 40, 4, 16, 40
+    q = torch.randn(B, T, H, c, generator=g).requires_grad_()
+    k = torch.randn(B, N, c, generator=g).requires_grad_()
+    v = torch.randn(B, N, c, generator=g).requires_grad_()
+    positions = torch.stack([torch.arange(T), torch.clamp(torch.arange(T) - 5, min=0)])
+    d_out = torch.randn(B, T, H, c, generator=g)
+    out, _ = pk.exact_attention(q, k, v, positions, 0.3, 0, 8)
+    lse = _lse_of(out)
+    out.backward(d_out)
+    cases["exact"] = dict(q=_np(q), k=_np(k), v=_np(v), positions=_np(positions), scale=0.3, d_out=_np(d_out),
+                          out=_np(out), lse=lse, dq=_np(q.grad), dk=_np(k.grad), dv=_np(v.grad))
+    # sparse: chosen rows (some -1) plus the last `window` rows, with a sink
+    B, T, H, c, N, W = 2, 24, 4, 16, 60, 6
+    q = torch.randn(B, T, H, c, generator=g).requires_grad_()
+    k = torch.randn(B, N, c, generator=g).requires_grad_()
+    v = torch.randn(B, N, c, generator=g).requires_grad_()
+    sink = (torch.randn(H, generator=g) * 0.5).requires_grad_()
+    positions = (N - T + torch.arange(T)).expand(B, T).contiguous()
+    idx = torch.stack([torch.stack([torch.randperm(int(p) - W + 1, generator=g)[:7] for p in row])
+                       for row in positions])
+    idx[:, ::4, -3:] = -1
+    d_out = torch.randn(B, T, H, c, generator=g)
+    out = pk.sparse_attention(q, k, v, sink, idx, positions, 0.25, W)
+    lse = _lse_of(out)
+    out.backward(d_out)
+    cases["sparse"] = dict(q=_np(q), k=_np(k), v=_np(v), sink=_np(sink), idx=_np(idx), positions=_np(positions),
+                           scale=0.25, window=W, d_out=_np(d_out), out=_np(out), lse=lse, dq=_np(q.grad),
+                           dk=_np(k.grad), dv=_np(v.grad), d_sink=_np(sink.grad))
+    # window_attention's tail layout, through plain autograd
+    W, B, T, H, c = 8, 2, 20, 3, 16
+    q = torch.randn(B, T, H, c, generator=g).requires_grad_()
+    k = torch.randn(B, W - 1 + T, c, generator=g).requires_grad_()
+    v = torch.randn(B, W - 1 + T, c, generator=g).requires_grad_()
+    sink = (torch.randn(H, generator=g) * 0.5).requires_grad_()
+    positions = torch.stack([3 + torch.arange(T), 40 + torch.arange(T)])
+    d_out = torch.randn(B, T, H, c, generator=g)
+    saved = at.WINDOW
+    at.WINDOW = W
+    try:
+        out = at.window_attention(q, k, v, sink, positions, 0.25)
+    finally:
+        at.WINDOW = saved
+    out.backward(d_out)
+    cases["window"] = dict(q=_np(q), k=_np(k), v=_np(v), sink=_np(sink), positions=_np(positions), scale=0.25,
+                           window=W, d_out=_np(d_out), out=_np(out), dq=_np(q.grad), dk=_np(k.grad),
+                           dv=_np(v.grad), d_sink=_np(sink.grad))
+    np.savez(os.path.join(HERE, "grads.npz"), **{f"{case}_{key}": value for case, d in cases.items()
+                                                 for key, value in d.items()})
 
 
 def window_small(at):
@@ -250,9 +312,15 @@ def main():
     parser = argparse.ArgumentParser()
     parser.add_argument("--reference", default=os.environ.get("WPT_REFERENCE"), required="WPT_REFERENCE" not in os.environ,
                         help="the reference repository's root (or set WPT_REFERENCE)")
+    parser.add_argument("--only", default=None, help="comma-separated fixtures to write (default: all)")
     args = parser.parse_args()
     torch.set_num_threads(max(1, os.cpu_count() or 1))
     at, pk, wi = _import_reference(args.reference)
+    if args.only:
+        for name in args.only.split(","):
+            {"grads": lambda: grads(at, pk)}[name]()
+        return
+    grads(at, pk)
     exact_small(pk)
     exact_generation(pk)
     sparse_small(pk)

@@ -147,3 +147,37 @@ def test_range_attention_equals_exact_and_sparse_window():
     out, lse = oat.range_attention(q, k, v, positions, 0.3, window=17, sink=sink)
     ref_out, ref_lse = oat.sparse_attention(q, k, v, sink, np.zeros((B, T, 0), np.int64), positions, 0.3, 17)
     assert np.abs(out - ref_out).max() < 1e-10 and np.abs(lse - ref_lse).max() < 1e-10
+
+
+def _grad_case(d, name):
+    return {key[len(name) + 1:]: d[key] for key in d.files if key.startswith(name + "_")}
+
+
+def test_exact_backward_matches_reference_autograd(gold):
+    from oracle import backward as ob
+    g = _grad_case(gold("grads.npz"), "exact")
+    dq, dk, dv = ob.exact_backward(g["q"], g["k"], g["v"], g["positions"], g["out"], g["lse"], g["d_out"],
+                                   float(g["scale"]))
+    for got, want in ((dq, g["dq"]), (dk, g["dk"]), (dv, g["dv"])):
+        assert np.abs(got - want).max() < 1e-4 * max(1.0, np.abs(want).max())
+
+
+def test_sparse_backward_matches_reference_autograd(gold):
+    from oracle import backward as ob
+    g = _grad_case(gold("grads.npz"), "sparse")
+    dq, dk, dv, ds = ob.sparse_backward(g["q"], g["k"], g["v"], g["sink"], g["idx"], g["positions"], g["out"],
+                                        g["lse"], g["d_out"], float(g["scale"]), int(g["window"]))
+    for got, want in ((dq, g["dq"]), (dk, g["dk"]), (dv, g["dv"]), (ds, g["d_sink"])):
+        assert np.abs(got - want).max() < 1e-4 * max(1.0, np.abs(want).max())
+
+
+def test_window_backward_matches_reference_autograd(gold):
+    from oracle import backward as ob
+    g = _grad_case(gold("grads.npz"), "window")
+    out, lse = oat.window_attention(g["q"], g["k"], g["v"], g["sink"], g["positions"], float(g["scale"]),
+                                    int(g["window"]))
+    assert np.abs(out - g["out"]).max() < 1e-5
+    dq, dk, dv, ds = ob.window_backward(g["q"], g["k"], g["v"], g["sink"], g["positions"], out, lse, g["d_out"],
+                                        float(g["scale"]), int(g["window"]))
+    for got, want in ((dq, g["dq"]), (dk, g["dk"]), (dv, g["dv"]), (ds, g["d_sink"])):
+        assert np.abs(got - want).max() < 1e-4 * max(1.0, np.abs(want).max())
