@@ -32,10 +32,14 @@ SIGNATURES = {
                                 _I, _I, _I, _I, _F, _P],
     "wpt_attn_merge": [_P, _P, _I, _I64, _I64, _I, _I, _P, _P, _P, _P],
     "wpt_tree_bits": [_P, _I, _I, _P, _P],
+    "wpt_attn_backward_scratch_bytes": [_I, _I, _I, _I, _I],
+    "wpt_attn_backward": [_P, _P, _P, _I64, _I64, _I64, _I64, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _I,
+                          _I, _I, _I, _I, _I, _I, _F, _P],
     "wpt_attn_merge_groups": [_P, _I, _I, _I64, _I64, _I, _I, _P, _P, _P, _P],
 }
 
-RESTYPES = {"wpt_last_error": ctypes.c_char_p, "wpt_accept_scratch_bytes": ctypes.c_size_t}
+RESTYPES = {"wpt_last_error": ctypes.c_char_p, "wpt_accept_scratch_bytes": ctypes.c_size_t,
+            "wpt_attn_backward_scratch_bytes": ctypes.c_size_t}
 
 _lib = None
 

@@ -1,0 +1,583 @@
+// Backward pass of MQA attention over contiguous key ranges (one key-value
+// head), tcgen05 + TMEM + TMA on sm_100a.
+//
+// Gradients of WPT's exact attention (packages/wpt-model/src/wpt_model/
+// pytorch_kernels.py:123-139) and of its window/sink form (the window rows
+// of :189-210; attention.py:85-107), from the forward pass's output and
+// log-sum-exp. For a query row (token t, head h) with weights p_n over the
+// rows lo_t..hi_t it reads:
+//     delta = sum_c dO[c] O[c]
+//     dS_n  = p_n (dO . v_n - delta)              (dz_n = scale * dS_n)
+//     dQ    = scale * sum_n dS_n k_n
+//     dK_n  = scale * sum_rows dS_n q,   dV_n = sum_rows p_n dO
+//     d_sink[h] = -sum_rows exp(sink_h - lse) delta
+// p_n = exp(z_n - lse) is recomputed from the saved log-sum-exp, as the
+// reference does; P and dS enter the tensor-core products as bf16.
+//
+// Three kernels (query tiles are the forward's: TQ = 128 / H tokens x H
+// heads = 128 rows of one batch row):
+//   bwd_prep_kernel  one CTA per query tile: delta and lse * log2(e) per
+//                    row (laid out per tile for one bulk copy), each token's
+//                    rows lo..hi, the tile's key range, and per-tile partial
+//                    sums of the sink's gradient (bwd_sink_kernel adds them
+//                    in a fixed order, so d_sink is deterministic).
+//   bwd_kv_kernel    one CTA per (key tile, batch row): the keys are the
+//                    MMA's M, so dK and dV accumulate in TMEM over every query
+//                    tile that sees the key tile, and each CTA writes its key
+//                    tile's gradients once (no atomics):
+//                      S^T  = K Q^T      A=K (smem),    B=Q (smem)
+//                      dP^T = V dO^T     A=V (smem),    B=dO (smem)
+//                      dV  += P^T dO     A=P^T (TMEM),  B=dO (smem, MN-major)
+//                      dK  += dS^T Q     A=dS^T (TMEM), B=Q (smem, MN-major)
+//   bwd_q_kernel     one CTA per query tile: the rows are the MMA's M and the
+//                    key tiles stream through a ring:
+//                      S = Q K^T, dP = dO V^T, dQ += dS K (A=dS in TMEM,
+//                      B=K MN-major)
+// Seven tile products per (query tile, key tile) pair against the five of a
+// single kernel that adds dQ by atomics: the dQ pass recomputes S and dP
+// instead, and every gradient is written exactly once.
+//
+// Warps (both main kernels): warps 0-7 compute P and dS, warp w reading TMEM
+// lane quadrant w % 4 and column half w / 4 (64 of the tile's 128 columns),
+// one thread per lane; warp 8 loads by TMA (one lane), warp 9 issues the
+// products (one elected lane). TMEM: S at column 0, dP at 128, the
+// accumulators at 256 (and 384). P and dS are written as bf16 pairs over
+// the first 64 columns of S and dP; a named barrier between the loads of a
+// tile's S and dP and those writes keeps one half's writes from landing on
+// the other half's unread columns.
+//
+// Every mbarrier wait is bounded (common.cuh); a wait that runs out sets
+// the status word and every role stops, the compute warps together (their
+// barrier ANDs the flag).
+#pragma once
+
+#include <climits>
+
+#include "common.cuh"
+#include "prefill.cuh"
+
+namespace wpt {
+
+constexpr int BWD_THREADS = 320;
+constexpr int BWD_LOAD_WARP = 8, BWD_MMA_WARP = 9, BWD_COMPUTE = 256;
+
+struct BwdParams {
+  const int64_t* positions;    // (B, T) each query's own row
+  const int64_t* floor_rows;   // (B, T) or null: the lowest row each query reads
+  const __nv_bfloat16* out;    // (B, T, H, C) the forward pass's output
+  const __nv_bfloat16* d_out;  // (B, T, H, C)
+  const float* lse;            // (B, T, H) natural log, sink included
+  const float* sink;           // (H,) or null
+  float* ld;                   // (B, qtiles, 2, 128) scratch: lse * log2(e), then delta, per tile row
+  int2* ranges;                // (B, qtiles) scratch: lowest and highest key row the tile reads
+  int2* bounds;                // (B, T) scratch: each token's rows lo..hi
+  float* sink_part;            // (B * qtiles, H) scratch: per-tile sums of exp(sink - lse) * delta
+  void* dq;                    // (B, T, H, C)
+  void* dk;                    // (B, N, C)
+  void* dv;                    // (B, N, C)
+  float* d_sink;               // (H,) or null
+  unsigned* status;
+  int B, T, H, N, window, TQ, qtiles, ktiles;
+  int f32_grads;  // 1: dq, dk, dv in fp32 (a gathered-rows pass adds to them after), 0: bf16
+  float scale, scale_log2;
+};
+
+// Rows lo..hi query t of batch row b reads (hi < lo: none): hi = min(p, N - 1),
+// lo = max(0, p - window + 1 when window > 0, floor).
+__device__ __forceinline__ int2 bwd_token_rows(const BwdParams& p, int b, int t) {
+  const int64_t pos = p.positions[static_cast<int64_t>(b) * p.T + t];
+  const int64_t top = pos < static_cast<int64_t>(p.N) - 1 ? pos : static_cast<int64_t>(p.N) - 1;
+  int64_t low = 0;
+  if (p.window > 0 && pos - p.window + 1 > low) low = pos - p.window + 1;
+  if (p.floor_rows) {
+    const int64_t f = p.floor_rows[static_cast<int64_t>(b) * p.T + t];
+    if (f > low) low = f;
+  }
+  return make_int2(low > INT_MAX ? INT_MAX : static_cast<int>(low), top < -1 ? -1 : static_cast<int>(top));
+}
+
+__device__ __forceinline__ float bf16_dot8(uint4 a, uint4 b) {
+  const __nv_bfloat162* x = reinterpret_cast<const __nv_bfloat162*>(&a);
+  const __nv_bfloat162* y = reinterpret_cast<const __nv_bfloat162*>(&b);
+  float s = 0.f;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 u = __bfloat1622float2(x[i]), v = __bfloat1622float2(y[i]);
+    s = fmaf(u.x, v.x, s);
+    s = fmaf(u.y, v.y, s);
+  }
+  return s;
+}
+
+// One CTA of 128 threads per (query tile j, batch row b); thread r owns tile
+// row r (token j * TQ + r / H, head r % H). C = 128.
+__global__ void __launch_bounds__(128) bwd_prep_kernel(const BwdParams p) {
+  const int j = blockIdx.x, b = blockIdx.y, r = threadIdx.x;
+  const int lane = r & 31, warp = r >> 5;
+  const int tq = r / p.H, h = r - tq * p.H;
+  const int t = j * p.TQ + tq;
+  const bool valid = tq < p.TQ && t < p.T;
+  __shared__ float s_sink[128];
+  __shared__ int s_lo[4], s_hi[4];
+  if (r < p.H) s_sink[r] = 0.f;
+  __syncthreads();
+  float lse2 = 0.f, delta = 0.f;
+  int lo = INT_MAX, hi = -1;
+  if (valid) {
+    const int64_t row = (static_cast<int64_t>(b) * p.T + t) * p.H + h;
+    const uint4* o = reinterpret_cast<const uint4*>(p.out + row * 128);
+    const uint4* g = reinterpret_cast<const uint4*>(p.d_out + row * 128);
+    float acc0 = 0.f, acc1 = 0.f;
+#pragma unroll
+    for (int i = 0; i < 16; i += 2) {
+      acc0 += bf16_dot8(o[i], g[i]);
+      acc1 += bf16_dot8(o[i + 1], g[i + 1]);
+    }
+    delta = acc0 + acc1;
+    const float l = p.lse[row];
+    lse2 = l * LOG2E;
+    // a row that reads nothing has lse = sink (or -inf without one) and out = 0
+    if (p.sink != nullptr && l != -INFINITY) atomicAdd(&s_sink[h], __expf(p.sink[h] - l) * delta);
+    const int2 bt = bwd_token_rows(p, b, t);
+    if (h == 0) p.bounds[static_cast<int64_t>(b) * p.T + t] = bt;
+    if (bt.y >= bt.x) {
+      lo = bt.x;
+      hi = bt.y;
+    }
+  }
+  float* ld = p.ld + (static_cast<int64_t>(b) * p.qtiles + j) * 256;
+  ld[r] = lse2;
+  ld[128 + r] = delta;
+  lo = __reduce_min_sync(0xffffffffu, lo);
+  hi = __reduce_max_sync(0xffffffffu, hi);
+  if (lane == 0) {
+    s_lo[warp] = lo;
+    s_hi[warp] = hi;
+  }
+  __syncthreads();
+  if (r == 0) {
+    int a = s_lo[0], z = s_hi[0];
+    for (int w = 1; w < 4; ++w) {
+      a = min(a, s_lo[w]);
+      z = max(z, s_hi[w]);
+    }
+    p.ranges[static_cast<int64_t>(b) * p.qtiles + j] = make_int2(a, z);
+  }
+  if (p.sink != nullptr && r < p.H)
+    p.sink_part[(static_cast<int64_t>(b) * p.qtiles + j) * p.H + r] = s_sink[r];
+}
+
+// d_sink[h] = -(sum over the tiles' partial sums), one CTA per head, a fixed
+// order of additions.
+__global__ void __launch_bounds__(256) bwd_sink_kernel(const float* __restrict__ part, int64_t tiles, int H,
+                                                       float* __restrict__ d_sink) {
+  const int h = blockIdx.x;
+  __shared__ float s_red[8];
+  float acc = 0.f;
+  for (int64_t i = threadIdx.x; i < tiles; i += 256) acc += part[i * H + h];
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+  if ((threadIdx.x & 31) == 0) s_red[threadIdx.x >> 5] = acc;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float total = 0.f;
+    for (int w = 0; w < 8; ++w) total += s_red[w];
+    d_sink[h] = -total;
+  }
+}
+
+// Whether query tile j of batch row b reads any key of the tile at n0.
+__device__ __forceinline__ bool bwd_tile_sees(const BwdParams& p, int b, int j, int n0) {
+  const int2 r = p.ranges[static_cast<int64_t>(b) * p.qtiles + j];
+  return r.y >= r.x && r.x <= n0 + 127 && r.y >= n0;
+}
+
+// 64 fp32 values of one thread (a TMEM row's half) to global memory at dst,
+// as bf16 (f32 == 0) or fp32, times mul.
+__device__ __forceinline__ void bwd_store64(void* dst, const uint32_t (&v)[64], float mul, int f32) {
+  if (f32) {
+    float4* d = reinterpret_cast<float4*>(dst);
+#pragma unroll
+    for (int i = 0; i < 16; ++i)
+      d[i] = make_float4(__uint_as_float(v[4 * i]) * mul, __uint_as_float(v[4 * i + 1]) * mul,
+                         __uint_as_float(v[4 * i + 2]) * mul, __uint_as_float(v[4 * i + 3]) * mul);
+  } else {
+    uint4* d = reinterpret_cast<uint4*>(dst);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      uint4 u;
+      u.x = pack_bf16(__uint_as_float(v[8 * i + 0]) * mul, __uint_as_float(v[8 * i + 1]) * mul);
+      u.y = pack_bf16(__uint_as_float(v[8 * i + 2]) * mul, __uint_as_float(v[8 * i + 3]) * mul);
+      u.z = pack_bf16(__uint_as_float(v[8 * i + 4]) * mul, __uint_as_float(v[8 * i + 5]) * mul);
+      u.w = pack_bf16(__uint_as_float(v[8 * i + 6]) * mul, __uint_as_float(v[8 * i + 7]) * mul);
+      d[i] = u;
+    }
+  }
+}
+
+struct BwdKvLayout {
+  static constexpr int TILE = 128 * 128 * 2;     // a 128 x 128 bf16 tile, two 64-column chunks
+  static constexpr int CHUNK = 128 * 128;        // bytes between the chunks
+  static constexpr int NSQ = 2;                  // query-tile stages
+  static constexpr int STAGE = 2 * TILE + 1024;  // Q, dO, then lse * log2(e) and delta (2 x 128 fp32)
+  static constexpr int OFF_K = 0, OFF_V = TILE, OFF_ST = 2 * TILE;
+  static constexpr int OFF_BAR = OFF_ST + NSQ * STAGE;
+  // kv_full, st_full[NSQ], st_empty[NSQ], s_full, p_ready, acc_done
+  static constexpr int NBAR = 4 + 2 * NSQ;
+  static constexpr int OFF_MISC = OFF_BAR + NBAR * 8;
+  static constexpr int BYTES = OFF_MISC + 16 + 1024;
+};
+
+__global__ void __launch_bounds__(BWD_THREADS, 1)
+    bwd_kv_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_do,
+                  const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v,
+                  const BwdParams p) {
+  using L = BwdKvLayout;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::OFF_BAR);
+  uint64_t* kv_full = bars;
+  uint64_t* st_full = kv_full + 1;
+  uint64_t* st_empty = st_full + L::NSQ;
+  uint64_t* s_full = st_empty + L::NSQ;
+  uint64_t* p_ready = s_full + 1;
+  uint64_t* acc_done = p_ready + 1;
+  uint32_t* s_tmem = reinterpret_cast<uint32_t*>(smem + L::OFF_MISC);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int b = blockIdx.y, n0 = blockIdx.x * 128;  // key tile 0 first: under a causal mask it is read most
+
+  if (threadIdx.x == 0) {
+    mbar_init(kv_full, 1);
+    for (int s = 0; s < L::NSQ; ++s) {
+      mbar_init(st_full + s, 1);
+      mbar_init(st_empty + s, 1);
+    }
+    mbar_init(s_full, 1);
+    mbar_init(p_ready, BWD_COMPUTE);
+    mbar_init(acc_done, 1);
+    fence_mbar_init();
+  }
+  if (warp == BWD_MMA_WARP) {
+    tmem_alloc(s_tmem, 512);
+    tmem_relinquish();
+  }
+  if (warp == BWD_LOAD_WARP && lane == 0) {
+    tma_prefetch(&tm_q);
+    tma_prefetch(&tm_do);
+    tma_prefetch(&tm_k);
+    tma_prefetch(&tm_v);
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *s_tmem;  // S^T at 0, dP^T at 128, dV at 256, dK at 384
+
+  if (warp == BWD_LOAD_WARP) {
+    // ------------------------------------------------------------ TMA loader
+    if (lane == 0) {
+      bool ok = true;
+      mbar_expect_tx(kv_full, 2 * L::TILE);
+      for (int s = 0; s < 2; ++s) {
+        tma_load_3d(smem + L::OFF_K + s * L::CHUNK, &tm_k, kv_full, s * 64, n0, b);
+        tma_load_3d(smem + L::OFF_V + s * L::CHUNK, &tm_v, kv_full, s * 64, n0, b);
+      }
+      int u = 0;
+      for (int j = 0; ok && j < p.qtiles; ++j) {
+        if (!bwd_tile_sees(p, b, j, n0)) continue;
+        const int st = u % L::NSQ;
+        if (u >= L::NSQ && !(ok = mbar_wait(st_empty + st, ((u / L::NSQ) & 1) ^ 1, p.status))) break;
+        uint8_t* stage = smem + L::OFF_ST + st * L::STAGE;
+        mbar_expect_tx(st_full + st, 2 * L::TILE + 1024);
+        const int row0 = (b * p.T + j * p.TQ) * p.H;
+        for (int s = 0; s < 2; ++s) {
+          tma_load_2d(stage + s * L::CHUNK, &tm_q, st_full + st, s * 64, row0);
+          tma_load_2d(stage + L::TILE + s * L::CHUNK, &tm_do, st_full + st, s * 64, row0);
+        }
+        bulk_load(stage + 2 * L::TILE, p.ld + (static_cast<int64_t>(b) * p.qtiles + j) * 256, 1024, st_full + st);
+        ++u;
+      }
+    }
+    tc_fence_before();
+    __syncthreads();
+  } else if (warp == BWD_MMA_WARP) {
+    // ------------------------------------------------------ tcgen05 issuer
+    auto wait = [&](uint64_t* bar, int parity) {
+      return __all_sync(0xffffffffu, mbar_wait(bar, parity, p.status));
+    };
+    const uint32_t base = smem_u32(smem);
+    const uint64_t dk = sdesc_sw128(base + L::OFF_K, 16, 1024), dv = sdesc_sw128(base + L::OFF_V, 16, 1024);
+    bool ok = wait(kv_full, 0);
+    int u = 0;
+    for (int j = 0; ok && j < p.qtiles; ++j) {
+      if (!bwd_tile_sees(p, b, j, n0)) continue;
+      const int st = u % L::NSQ;
+      const uint32_t stage = base + L::OFF_ST + st * L::STAGE;
+      if (!(ok = wait(st_full + st, (u / L::NSQ) & 1))) break;
+      tc_fence_after();
+      prefill_s_steps<7>(tmem, dk, sdesc_sw128(stage, 16, 1024), idesc_bf16(128, 128, 0, 0));  // S^T = K Q^T
+      prefill_s_steps<7>(tmem + 128, dv, sdesc_sw128(stage + L::TILE, 16, 1024),
+                         idesc_bf16(128, 128, 0, 0));  // dP^T = V dO^T
+      mma_commit_warp(s_full);
+      if (!(ok = wait(p_ready, u & 1))) break;
+      tc_fence_after();
+      // dV += P^T dO and dK += dS^T Q: A from TMEM, B MN-major (query rows are K)
+      prefill_pv_steps<7, 0>(tmem + 256, tmem, sdesc_sw128(stage + L::TILE, L::CHUNK, 1024),
+                             idesc_bf16(128, 128, 0, 1), u > 0 ? 1u : 0u);
+      prefill_pv_steps<7, 0>(tmem + 384, tmem + 128, sdesc_sw128(stage, L::CHUNK, 1024),
+                             idesc_bf16(128, 128, 0, 1), u > 0 ? 1u : 0u);
+      mma_commit_warp(st_empty + st);
+      ++u;
+    }
+    mma_commit_warp(acc_done);  // once every product above has completed
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  } else {
+    // ------------------------------------------- P and dS (warps 0-7)
+    const int quad = warp & 3, half = warp >> 2;
+    const int row = quad * 32 + lane, n = n0 + row;  // this thread's key
+    const uint32_t lane_addr = tmem + (static_cast<uint32_t>(quad * 32) << 16);
+    const float sl2 = p.scale_log2;
+    bool ok = true;
+    int u = 0;
+    for (int j = 0; ok && j < p.qtiles; ++j) {
+      if (!bwd_tile_sees(p, b, j, n0)) continue;
+      const int st = u % L::NSQ;
+      const float* lds = reinterpret_cast<const float*>(smem + L::OFF_ST + st * L::STAGE + 2 * L::TILE);
+      // the stage's copies (its lse and delta are read here) and the tile's
+      // S^T and dP^T; the stage is not refilled before this thread's
+      // p_ready arrival, so the parity names this use of it
+      ok = __all_sync(0xffffffffu, mbar_wait(st_full + st, (u / L::NSQ) & 1, p.status) &&
+                                       mbar_wait(s_full, u & 1, p.status));
+      tc_fence_after();
+      uint32_t s[64], d[64];
+      if (ok) {
+        tmem_ld64(lane_addr + half * 64, s);
+        tmem_ld64(lane_addr + 128 + half * 64, d);
+      }
+      // every thread's reads of S^T and dP^T land before any P or dS write
+      ok = named_barrier_and(1, BWD_COMPUTE, ok);
+      if (!ok) break;
+      // the columns (query rows) of this half that see key n: by token
+      uint64_t vis = 0;
+      const int c0 = half * 64;
+      for (int tq = c0 / p.H; tq < p.TQ && tq * p.H < c0 + 64; ++tq) {
+        const int t = j * p.TQ + tq;
+        if (t >= p.T) break;
+        const int2 bt = p.bounds[static_cast<int64_t>(b) * p.T + t];
+        if (n >= bt.x && n <= bt.y) {
+          const int a = max(tq * p.H, c0) - c0, z = min(tq * p.H + p.H, c0 + 64) - c0;  // columns a .. z - 1
+          const uint64_t hi_mask = z >= 64 ? ~0ull : ((1ull << z) - 1ull);
+          vis |= hi_mask & ~((1ull << a) - 1ull);
+        }
+      }
+      uint32_t pk[32], dsk[32];
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        const int c = c0 + 2 * i;
+        const float p0 = (vis >> (2 * i)) & 1ull ? fast_exp2(fmaf(__uint_as_float(s[2 * i]), sl2, -lds[c])) : 0.f;
+        const float p1 =
+            (vis >> (2 * i + 1)) & 1ull ? fast_exp2(fmaf(__uint_as_float(s[2 * i + 1]), sl2, -lds[c + 1])) : 0.f;
+        const float g0 = p0 * (__uint_as_float(d[2 * i]) - lds[128 + c]);
+        const float g1 = p1 * (__uint_as_float(d[2 * i + 1]) - lds[128 + c + 1]);
+        pk[i] = pack_bf16(p0, p1);
+        dsk[i] = pack_bf16(g0, g1);
+      }
+      tmem_st32(lane_addr + half * 32, pk);         // P^T over S^T's first 64 columns
+      tmem_st32(lane_addr + 128 + half * 32, dsk);  // dS^T over dP^T's first 64 columns
+      tmem_wait_st();
+      tc_fence_before();
+      mbar_arrive(p_ready);
+      ++u;
+    }
+    if (ok) ok = __all_sync(0xffffffffu, mbar_wait(acc_done, 0, p.status));
+    tc_fence_after();
+    uint32_t gv[64], gk[64];
+    if (ok && u > 0) {
+      tmem_ld64(lane_addr + 256 + half * 64, gv);
+      tmem_ld64(lane_addr + 384 + half * 64, gk);
+    } else {
+#pragma unroll
+      for (int i = 0; i < 64; ++i) gv[i] = gk[i] = 0u;
+    }
+    if (ok && n < p.N) {
+      const int64_t off = (static_cast<int64_t>(b) * p.N + n) * 128 + half * 64;
+      const int es = p.f32_grads ? 4 : 2;
+      bwd_store64(static_cast<uint8_t*>(p.dv) + off * es, gv, 1.f, p.f32_grads);
+      bwd_store64(static_cast<uint8_t*>(p.dk) + off * es, gk, p.scale, p.f32_grads);
+    }
+    tc_fence_before();
+    __syncthreads();
+  }
+}
+
+struct BwdQLayout {
+  static constexpr int TILE = 128 * 128 * 2, CHUNK = 128 * 128;
+  static constexpr int NS = 2;  // key-tile stages (K and V)
+  static constexpr int OFF_Q = 0, OFF_DO = TILE, OFF_LD = 2 * TILE;
+  static constexpr int OFF_KV = 2 * TILE + 1024;
+  static constexpr int STAGE = 2 * TILE;
+  static constexpr int OFF_BAR = OFF_KV + NS * STAGE;
+  // q_full, kv_full[NS], kv_empty[NS], s_full, ds_ready, acc_done
+  static constexpr int NBAR = 4 + 2 * NS;
+  static constexpr int OFF_MISC = OFF_BAR + NBAR * 8;
+  static constexpr int BYTES = OFF_MISC + 16 + 1024;
+};
+
+__global__ void __launch_bounds__(BWD_THREADS, 1)
+    bwd_q_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_do,
+                 const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v,
+                 const BwdParams p) {
+  using L = BwdQLayout;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::OFF_BAR);
+  uint64_t* q_full = bars;
+  uint64_t* kv_full = q_full + 1;
+  uint64_t* kv_empty = kv_full + L::NS;
+  uint64_t* s_full = kv_empty + L::NS;
+  uint64_t* ds_ready = s_full + 1;
+  uint64_t* acc_done = ds_ready + 1;
+  uint32_t* s_tmem = reinterpret_cast<uint32_t*>(smem + L::OFF_MISC);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int b = blockIdx.y, j = p.qtiles - 1 - static_cast<int>(blockIdx.x);  // later tiles read more keys: first
+  const int2 rg = p.ranges[static_cast<int64_t>(b) * p.qtiles + j];
+  const int kt0 = rg.y >= rg.x ? rg.x / 128 : 0;
+  const int nt = rg.y >= rg.x ? rg.y / 128 - kt0 + 1 : 0;
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int s = 0; s < L::NS; ++s) {
+      mbar_init(kv_full + s, 1);
+      mbar_init(kv_empty + s, 1);
+    }
+    mbar_init(s_full, 1);
+    mbar_init(ds_ready, BWD_COMPUTE);
+    mbar_init(acc_done, 1);
+    fence_mbar_init();
+  }
+  if (warp == BWD_MMA_WARP) {
+    tmem_alloc(s_tmem, 512);
+    tmem_relinquish();
+  }
+  if (warp == BWD_LOAD_WARP && lane == 0) {
+    tma_prefetch(&tm_q);
+    tma_prefetch(&tm_do);
+    tma_prefetch(&tm_k);
+    tma_prefetch(&tm_v);
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *s_tmem;  // S at 0, dP at 128, dQ at 256
+
+  if (warp == BWD_LOAD_WARP) {
+    if (lane == 0) {
+      bool ok = true;
+      const int row0 = (b * p.T + j * p.TQ) * p.H;
+      mbar_expect_tx(q_full, 2 * L::TILE + 1024);
+      for (int s = 0; s < 2; ++s) {
+        tma_load_2d(smem + L::OFF_Q + s * L::CHUNK, &tm_q, q_full, s * 64, row0);
+        tma_load_2d(smem + L::OFF_DO + s * L::CHUNK, &tm_do, q_full, s * 64, row0);
+      }
+      bulk_load(smem + L::OFF_LD, p.ld + (static_cast<int64_t>(b) * p.qtiles + j) * 256, 1024, q_full);
+      for (int i = 0; ok && i < nt; ++i) {
+        const int st = i % L::NS;
+        if (i >= L::NS && !(ok = mbar_wait(kv_empty + st, ((i / L::NS) & 1) ^ 1, p.status))) break;
+        uint8_t* stage = smem + L::OFF_KV + st * L::STAGE;
+        mbar_expect_tx(kv_full + st, 2 * L::TILE);
+        for (int s = 0; s < 2; ++s) {
+          tma_load_3d(stage + s * L::CHUNK, &tm_k, kv_full + st, s * 64, (kt0 + i) * 128, b);
+          tma_load_3d(stage + L::TILE + s * L::CHUNK, &tm_v, kv_full + st, s * 64, (kt0 + i) * 128, b);
+        }
+      }
+    }
+    tc_fence_before();
+    __syncthreads();
+  } else if (warp == BWD_MMA_WARP) {
+    auto wait = [&](uint64_t* bar, int parity) {
+      return __all_sync(0xffffffffu, mbar_wait(bar, parity, p.status));
+    };
+    const uint32_t base = smem_u32(smem);
+    const uint64_t dq = sdesc_sw128(base + L::OFF_Q, 16, 1024), ddo = sdesc_sw128(base + L::OFF_DO, 16, 1024);
+    bool ok = wait(q_full, 0);
+    for (int i = 0; ok && i < nt; ++i) {
+      const int st = i % L::NS;
+      const uint32_t stage = base + L::OFF_KV + st * L::STAGE;
+      if (!(ok = wait(kv_full + st, (i / L::NS) & 1))) break;
+      tc_fence_after();
+      prefill_s_steps<7>(tmem, dq, sdesc_sw128(stage, 16, 1024), idesc_bf16(128, 128, 0, 0));  // S = Q K^T
+      prefill_s_steps<7>(tmem + 128, ddo, sdesc_sw128(stage + L::TILE, 16, 1024),
+                         idesc_bf16(128, 128, 0, 0));  // dP = dO V^T
+      mma_commit_warp(s_full);
+      if (!(ok = wait(ds_ready, i & 1))) break;
+      tc_fence_after();
+      // dQ += dS K: A = dS (TMEM), B = K (keys are K, MN-major)
+      prefill_pv_steps<7, 0>(tmem + 256, tmem + 128, sdesc_sw128(stage, L::CHUNK, 1024), idesc_bf16(128, 128, 0, 1),
+                             i > 0 ? 1u : 0u);
+      mma_commit_warp(kv_empty + st);
+    }
+    mma_commit_warp(acc_done);
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  } else {
+    const int quad = warp & 3, half = warp >> 2;
+    const int row = quad * 32 + lane;  // this thread's query row
+    const int tq = row / p.H, h = row - tq * p.H;
+    const int t = j * p.TQ + tq;
+    const bool valid = tq < p.TQ && t < p.T;
+    const uint32_t lane_addr = tmem + (static_cast<uint32_t>(quad * 32) << 16);
+    const float sl2 = p.scale_log2;
+    int2 bt = make_int2(1, 0);
+    if (valid) bt = p.bounds[static_cast<int64_t>(b) * p.T + t];
+    bool ok = __all_sync(0xffffffffu, mbar_wait(q_full, 0, p.status));
+    const float* lds = reinterpret_cast<const float*>(smem + L::OFF_LD);
+    const float lse2 = lds[row], delta = lds[128 + row];
+    for (int i = 0; ok && i < nt; ++i) {
+      ok = __all_sync(0xffffffffu, mbar_wait(s_full, i & 1, p.status));
+      tc_fence_after();
+      uint32_t s[64], d[64];
+      if (ok) {
+        tmem_ld64(lane_addr + half * 64, s);
+        tmem_ld64(lane_addr + 128 + half * 64, d);
+      }
+      ok = named_barrier_and(1, BWD_COMPUTE, ok);
+      if (!ok) break;
+      const int nb = (kt0 + i) * 128 + half * 64;  // this half's first key
+      const int a = bt.x - nb, z = bt.y - nb;      // visible columns a .. z
+      uint32_t dsk[32];
+#pragma unroll
+      for (int k2 = 0; k2 < 32; ++k2) {
+        const int c = 2 * k2;
+        const bool v0 = c >= a && c <= z, v1 = c + 1 >= a && c + 1 <= z;
+        const float p0 = v0 ? fast_exp2(fmaf(__uint_as_float(s[c]), sl2, -lse2)) : 0.f;
+        const float p1 = v1 ? fast_exp2(fmaf(__uint_as_float(s[c + 1]), sl2, -lse2)) : 0.f;
+        dsk[k2] = pack_bf16(p0 * (__uint_as_float(d[c]) - delta), p1 * (__uint_as_float(d[c + 1]) - delta));
+      }
+      tmem_st32(lane_addr + 128 + half * 32, dsk);  // dS over dP's first 64 columns
+      tmem_wait_st();
+      tc_fence_before();
+      mbar_arrive(ds_ready);
+    }
+    if (ok) ok = __all_sync(0xffffffffu, mbar_wait(acc_done, 0, p.status));
+    tc_fence_after();
+    uint32_t g[64];
+    if (ok && nt > 0) {
+      tmem_ld64(lane_addr + 256 + half * 64, g);
+    } else {
+#pragma unroll
+      for (int i = 0; i < 64; ++i) g[i] = 0u;
+    }
+    if (ok && valid) {
+      const int64_t off = ((static_cast<int64_t>(b) * p.T + t) * p.H + h) * 128 + half * 64;
+      bwd_store64(static_cast<uint8_t*>(p.dq) + off * (p.f32_grads ? 4 : 2), g, p.scale, p.f32_grads);
+    }
+    tc_fence_before();
+    __syncthreads();
+  }
+}
+
+}  // namespace wpt

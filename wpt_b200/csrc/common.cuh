@@ -98,6 +98,16 @@ __device__ __forceinline__ void tma_prefetch_l2_2d(const CUtensorMap* map, int x
                : "memory");
 }
 
+// Untiled bulk copy of `bytes` (a multiple of 16, both addresses 16-byte
+// aligned) from global to shared memory, completing on an mbarrier's
+// transaction count.
+__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                   smem_u32(dst)),
+               "l"(src), "r"(bytes), "r"(smem_u32(bar))
+               : "memory");
+}
+
 // ------------------------------------------------------ cp.async (16 bytes)
 __device__ __forceinline__ void cp_async_16(uint32_t dst, const void* src, bool fill) {
   // fill == false writes zeros (src-size 0): rows a query may not read

@@ -12,6 +12,7 @@
 
 #include "../../include/wpt_attn.h"
 #include "accept.cuh"
+#include "backward.cuh"
 #include "common.cuh"
 #include "merge.cuh"
 #include "prefill.cuh"
@@ -365,6 +366,113 @@ extern "C" int wpt_attn_prefill(const void* q, const void* k, const void* v, int
                   : launch_merge<64>(part_o, part_lse, splits, rows, rows, H, sink, out, lse, s, true);
   }
   return rc;
+}
+
+// ---------------------------------------------------------------- backward
+namespace {
+
+struct BwdScratch {
+  int64_t ld, ranges, bounds, sink_part, total;  // byte offsets, each 256-aligned
+};
+
+BwdScratch bwd_scratch(int B, int T, int H) {
+  const int TQ = 128 / H;
+  const int64_t qtiles = (T + TQ - 1) / TQ;
+  auto up = [](int64_t x) { return (x + 255) / 256 * 256; };
+  BwdScratch s;
+  s.ld = 0;
+  s.ranges = s.ld + up(static_cast<int64_t>(B) * qtiles * 256 * 4);
+  s.bounds = s.ranges + up(static_cast<int64_t>(B) * qtiles * 8);
+  s.sink_part = s.bounds + up(static_cast<int64_t>(B) * T * 8);
+  s.total = s.sink_part + up(static_cast<int64_t>(B) * qtiles * H * 4);
+  return s;
+}
+
+}  // namespace
+
+extern "C" size_t wpt_attn_backward_scratch_bytes(int B, int T, int H, int C, int N) {
+  if (B < 1 || T < 1 || H < 1 || H > 128 || C != 128 || N < 1) return 0;
+  return static_cast<size_t>(bwd_scratch(B, T, H).total);
+}
+
+extern "C" int wpt_attn_backward(const void* q, const void* k, const void* v, int64_t k_stride_b, int64_t k_stride_n,
+                                 int64_t v_stride_b, int64_t v_stride_n, const int64_t* positions,
+                                 const int64_t* floor_rows, const float* sink, const void* out, const float* lse,
+                                 const void* d_out, void* dq, void* dk, void* dv, float* d_sink, void* scratch,
+                                 int f32_grads, int B, int T, int H, int C, int N, int window, float scale,
+                                 void* stream) {
+  if (C != 128) return fail(WPT_ERR_UNSUPPORTED, "head width %d: the backward kernels take 128", C);
+  if (H < 1 || H > 128) return fail(WPT_ERR_UNSUPPORTED, "%d heads: the kernels take 1 to 128", H);
+  if (B < 1 || T < 1 || N < 1) return fail(WPT_ERR_INVALID, "empty shape B=%d T=%d N=%d", B, T, N);
+  if (static_cast<int64_t>(B) * T * H + 256 >= (int64_t(1) << 31)) return fail(WPT_ERR_UNSUPPORTED, "B*T*H too large");
+  if (static_cast<int64_t>(B) * N * C >= (int64_t(1) << 40)) return fail(WPT_ERR_UNSUPPORTED, "B*N too large");
+  if (!q || !k || !v || !positions || !out || !lse || !d_out || !dq || !dk || !dv || !scratch)
+    return fail(WPT_ERR_INVALID, "a required pointer is NULL");
+  if (!aligned16(q) || !aligned16(out) || !aligned16(d_out) || !aligned16(dq) || !aligned16(dk) || !aligned16(dv) ||
+      !aligned16(scratch))
+    return fail(WPT_ERR_INVALID, "q, out, d_out, dq, dk, dv and scratch must be 16-byte aligned");
+  if (sink == nullptr && d_sink != nullptr) return fail(WPT_ERR_INVALID, "d_sink needs sink");
+  if (!(scale > 0.f)) return fail(WPT_ERR_INVALID, "scale must be positive");
+  CUtensorMap tq, tdo, tk, tv;
+  {
+    cuuint64_t dims[2] = {static_cast<cuuint64_t>(C), static_cast<cuuint64_t>(B) * T * H};
+    cuuint64_t strides[1] = {static_cast<cuuint64_t>(C) * 2};
+    cuuint32_t box[2] = {64, 128};
+    if (int rc = tensor_map(&tq, q, 2, dims, strides, box)) return rc;
+    if (int rc = tensor_map(&tdo, d_out, 2, dims, strides, box)) return rc;
+  }
+  if (int rc = table_map(&tk, k, k_stride_b, k_stride_n, B, N, C)) return rc;
+  if (int rc = table_map(&tv, v, v_stride_b, v_stride_n, B, N, C)) return rc;
+  const BwdScratch lay = bwd_scratch(B, T, H);
+  uint8_t* base = static_cast<uint8_t*>(scratch);
+  wpt::BwdParams p;
+  p.positions = positions;
+  p.floor_rows = floor_rows;
+  p.out = static_cast<const __nv_bfloat16*>(out);
+  p.d_out = static_cast<const __nv_bfloat16*>(d_out);
+  p.lse = lse;
+  p.sink = sink;
+  p.ld = reinterpret_cast<float*>(base + lay.ld);
+  p.ranges = reinterpret_cast<int2*>(base + lay.ranges);
+  p.bounds = reinterpret_cast<int2*>(base + lay.bounds);
+  p.sink_part = reinterpret_cast<float*>(base + lay.sink_part);
+  p.dq = dq;
+  p.dk = dk;
+  p.dv = dv;
+  p.d_sink = d_sink;
+  if (int rc = status_word(&p.status)) return rc;
+  p.B = B;
+  p.T = T;
+  p.H = H;
+  p.N = N;
+  p.window = window > 0 ? window : 0;
+  p.TQ = 128 / H;
+  p.qtiles = (T + p.TQ - 1) / p.TQ;
+  p.ktiles = (N + 127) / 128;
+  p.f32_grads = f32_grads ? 1 : 0;
+  p.scale = scale;
+  p.scale_log2 = scale * wpt::LOG2E;
+  if (p.qtiles > 65535 * 32 || B > 65535) return fail(WPT_ERR_UNSUPPORTED, "backward grid too large");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  wpt::bwd_prep_kernel<<<dim3(p.qtiles, B), 128, 0, st>>>(p);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "bwd_prep_kernel launch");
+  if (d_sink != nullptr) {
+    wpt::bwd_sink_kernel<<<H, 256, 0, st>>>(p.sink_part, static_cast<int64_t>(B) * p.qtiles, H, d_sink);
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return cuda_fail(e, "bwd_sink_kernel launch");
+  }
+  static_assert(wpt::BwdKvLayout::BYTES <= 232448, "backward key kernel shared memory exceeds 227 KB");
+  static_assert(wpt::BwdQLayout::BYTES <= 232448, "backward query kernel shared memory exceeds 227 KB");
+  if (int rc = allow_smem(wpt::bwd_kv_kernel, wpt::BwdKvLayout::BYTES)) return rc;
+  if (int rc = allow_smem(wpt::bwd_q_kernel, wpt::BwdQLayout::BYTES)) return rc;
+  wpt::bwd_kv_kernel<<<dim3(p.ktiles, B), wpt::BWD_THREADS, wpt::BwdKvLayout::BYTES, st>>>(tq, tdo, tk, tv, p);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "bwd_kv_kernel launch");
+  wpt::bwd_q_kernel<<<dim3(p.qtiles, B), wpt::BWD_THREADS, wpt::BwdQLayout::BYTES, st>>>(tq, tdo, tk, tv, p);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "bwd_q_kernel launch");
+  return WPT_OK;
 }
 
 extern "C" int wpt_attn_merge(const float* part_o, const float* part_lse, int splits, int64_t rows,
