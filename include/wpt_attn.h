@@ -163,6 +163,40 @@ int wpt_attn_merge(const float* part_o, const float* part_lse, int splits, int64
                    int H, int C, const float* sink, void* out, float* lse, void* stream);
 
 /*
+ * Gradients of the attention above (exact, window/sink, and sparse with
+ * chosen rows), on the tensor cores, from the forward pass's out (bf16) and
+ * lse. Replaces the backward passes of the reference's forms: the PyTorch
+ * form's _Exact.backward and _Sparse.backward (pytorch_kernels.py:123-139,
+ * 189-210) and the Triton form's _exact_backward_kernel and sparse backward
+ * kernels (triton_kernels.py:546-571, 719-908).
+ *   positions, floor_rows, window  the rows each query read, as in
+ *                wpt_attn_prefill (range part)
+ *   idx, K       idx (B, T, K) int64 chosen rows (-1 for none), read on top
+ *                of the range part (sparse_attention's rows: chosen, then the
+ *                last `window`); K = 0 / idx NULL for exact or window attention
+ *   sink         fp32 (H,) or NULL; d_sink fp32 (H,) or NULL receives its
+ *                gradient, -sum exp(sink - lse) delta (deterministic order)
+ *   d_out        bf16 (B, T, H, C) contiguous
+ *   dq           (B, T, H, C); dk, dv (B, N, C), contiguous; bf16, or fp32 when
+ *                f32_grads != 0 (required when K > 0: chosen rows are added
+ *                by fp32 atomics; wpt_f32_to_bf16 converts)
+ *   scratch      wpt_attn_backward_scratch_bytes(B, T, H, C, N) bytes, 16-byte aligned
+ * C must be 128, H at most 128 (64 with chosen rows).
+ */
+int wpt_attn_backward(const void* q, const void* k, const void* v, int64_t k_stride_b, int64_t k_stride_n,
+                      int64_t v_stride_b, int64_t v_stride_n, const int64_t* positions, const int64_t* floor_rows,
+                      const int64_t* idx, int K, const float* sink, const void* out, const float* lse,
+                      const void* d_out, void* dq, void* dk, void* dv, float* d_sink, void* scratch, int f32_grads,
+                      int B, int T, int H, int C, int N, int window, float scale, void* stream);
+
+/* Bytes of scratch wpt_attn_backward needs (0 for a shape it does not take). */
+size_t wpt_attn_backward_scratch_bytes(int B, int T, int H, int C, int N);
+
+/* y[i] = bf16(x[i]) (round to nearest even) for n fp32 values, n a multiple
+ * of 4, x 16-byte and y 8-byte aligned. */
+int wpt_f32_to_bf16(const float* x, int64_t n, void* y, void* stream);
+
+/*
  * The same merge over partials gathered from several places (the GPUs that
  * each hold a share of a long row's keys): `groups` chunks of group_floats
  * floats side by side at `parts`, chunk g holding `per` splits' output

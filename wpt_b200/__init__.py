@@ -19,9 +19,9 @@ makes WPT's exact and sparse layers run on these kernels. It exposes
 with the reference's argument meanings, dtypes, -1 conventions and errors.
 Forward passes run hand-written CUDA kernels (libwpt_b200.so, C ABI in
 include/wpt_attn.h); there is no CPU path and no other backend: a missing
-library or a CPU tensor raises. The backward passes evaluate the reference's
-own gradient formulas (pytorch_kernels.py:123-139,189-210) with torch on
-the GPU from the saved log-sum-exp.
+library or a CPU tensor raises. The backward passes (exact, sparse and
+window attention; pytorch_kernels.py:123-139,189-210) are hand-written
+tensor-core kernels too, from the saved output and log-sum-exp.
 """
 
 import torch
@@ -72,9 +72,8 @@ class _Exact(torch.autograd.Function):
 
     @staticmethod
     def backward(ctx, d_out, _d_chosen):
-        from .backward import exact_backward
         q, k, v, positions, out, lse = ctx.saved_tensors
-        dq, dk, dv = exact_backward(q, k, v, positions, out, lse, d_out, ctx.scale)
+        dq, dk, dv, _ = ops.attention_backward(q, k, v, positions, out, lse, d_out, ctx.scale)
         return dq, dk, dv, None, None, None, None
 
 
@@ -92,12 +91,6 @@ def forward_with_lse(q, k, v, positions, scale, window=0, sink=None):
 
 
 # ----------------------------------------------------------- sparse attention
-
-def _window_rows(positions, window, N):
-    """pytorch_kernels.py:149-153."""
-    rows = positions[..., None] - window + 1 + torch.arange(window, device=positions.device)
-    return rows.masked_fill((rows < 0) | (rows >= N), -1)
-
 
 class _Sparse(torch.autograd.Function):
     @staticmethod
@@ -117,11 +110,11 @@ class _Sparse(torch.autograd.Function):
 
     @staticmethod
     def backward(ctx, d_out):
-        from .backward import sparse_backward
         q, k, v, sink, idx, positions, out, lse = ctx.saved_tensors
-        rows = torch.cat([idx, _window_rows(positions, ctx.window, k.shape[1])], -1)
-        dq, dk, dv, d_sink = sparse_backward(q, k, v, sink, rows, out, lse, d_out, ctx.scale)
-        return dq, dk, dv, d_sink, None, None, None, None
+        # the window rows by the range kernels, the chosen rows by the gather kernel
+        dq, dk, dv, d_sink = ops.attention_backward(q, k, v, positions, out, lse, d_out, ctx.scale,
+                                                    window=ctx.window, sink=sink, idx=idx)
+        return dq, dk, dv, None if d_sink is None else d_sink.to(sink.dtype), None, None, None, None
 
 
 def sparse_attention(q, k, v, sink, idx, positions, scale, window):
@@ -134,12 +127,29 @@ def sparse_attention(q, k, v, sink, idx, positions, scale, window):
 
 # ----------------------------------------------------------- window attention
 
+class _Window(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, q, k, v, sink, rows, floor, scale, W):
+        out, lse = ops.attention_forward(q, k, v, rows, scale, window=W, floor=floor, sink=sink)
+        ctx.save_for_backward(q, k, v, sink, rows, floor, out, lse)
+        ctx.scale, ctx.window = scale, W
+        return out
+
+    @staticmethod
+    def backward(ctx, d_out):
+        q, k, v, sink, rows, floor, out, lse = ctx.saved_tensors
+        dq, dk, dv, d_sink = ops.attention_backward(q, k, v, rows, out, lse, d_out, ctx.scale, window=ctx.window,
+                                                    floor=floor, sink=sink)
+        return dq, dk, dv, None if d_sink is None else d_sink.to(sink.dtype), None, None, None, None
+
+
 def window_attention(q, k, v, sink, positions, scale, window=None):
     """attention.py:85-107: q (B, T, H, c) at positions (T,) or (B, T); k, v
     (B, window - 1 + T, c), the window - 1 rows before the pass then its own;
     query t reads table rows t .. t + window - 1 that are not before the
     text, with the sink in each head's denominator. window defaults to
-    WINDOW (128, attention.py:53)."""
+    WINDOW (128, attention.py:53). Differentiable in q, k, v and sink, as
+    the reference's (plain autograd there; the backward kernels here)."""
     _bf16_only(q, k, v)
     W = WINDOW if window is None else int(window)
     B, T, H, c = q.shape
@@ -147,8 +157,7 @@ def window_attention(q, k, v, sink, positions, scale, window=None):
     t = torch.arange(T, device=q.device, dtype=torch.int64)
     rows = (t + W - 1).expand(B, T).contiguous()  # each query's own row in the table
     floor = rows - positions  # the row of position 0: rows before it are before the text
-    out, _ = ops.attention_forward(q, k, v, rows, scale, window=W, floor=floor, sink=sink)
-    return out.to(q.dtype)
+    return _Window.apply(q, k, v, sink, rows, floor, scale, W)
 
 
 # ----------------------------------------------------------- tree attention

@@ -55,6 +55,7 @@
 
 #include "common.cuh"
 #include "prefill.cuh"
+#include "stream.cuh"
 
 namespace wpt {
 
@@ -577,6 +578,314 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
     }
     tc_fence_before();
     __syncthreads();
+  }
+}
+
+
+// ------------------------------------------------- gathered rows (sparse)
+//
+// The chosen-row share of sparse attention's gradients
+// (pytorch_kernels.py:189-210 over idx; the window rows are the range
+// kernels' share, added to the same fp32 gradients). One CTA per query
+// (b, t), its K chosen rows in tiles of 128 gathered rows, the rows as the
+// MMA's M and the query's heads (padded to NCOL = 16, 32 or 64) as N:
+//   S^T  = K_g Q^T        A=K_g (smem),          B=Q (smem)
+//   dP^T = V_g dO^T       A=V_g (smem),          B=dO (smem)
+//   dV_g = P^T dO         A=P^T (TMEM),          B=dO (smem, MN-major)
+//   dK_g = dS^T Q         A=dS^T (TMEM),         B=Q (smem, MN-major)
+//   dQ^T += K_g^T dS^T    A=K_g (smem, MN-major), B=dS^T (smem)
+// dV_g and dK_g rows are added into the fp32 gradients of the rows they
+// belong to (vector atomics: different queries choose the same rows); dQ^T
+// accumulates in TMEM over the tiles and is added to the query's fp32 dq
+// (which only this CTA touches) at the end.
+// Warps 0-3 (one TMEM lane quadrant each, thread = gathered row, or channel
+// at the end) compute P and dS; warp 4 allocates TMEM and issues; warps 5-6
+// gather the rows by 16-byte cp.async into the swizzled tiles.
+
+constexpr int GBWD_THREADS = 224, GBWD_LOADERS = 64;
+
+struct GatherBwdParams {
+  const __nv_bfloat16* q;      // (B, T, H, C)
+  const __nv_bfloat16* d_out;  // (B, T, H, C)
+  const __nv_bfloat16* k;      // table rows at k + b * ksb + n * ksn
+  const __nv_bfloat16* v;
+  int64_t ksb, ksn, vsb, vsn;
+  const int64_t* idx;          // (B, T, K), -1 for none
+  const float* ld;             // the prep kernel's per-tile lse * log2(e) and delta
+  float* dq;                   // (B, T, H, C) fp32, added to
+  float* dk;                   // (B, N, C) fp32, added to
+  float* dv;                   // (B, N, C) fp32, added to
+  unsigned* status;
+  int B, T, H, N, K, TQ, qtiles;
+  float scale, scale_log2;
+};
+
+template <int NCOL>
+struct GatherBwdLayout {
+  static constexpr int QT = NCOL * 128 * 2;     // Q or dO: NCOL rows x 128 columns, two chunks
+  static constexpr int TILE = 128 * 128 * 2;   // a gathered K or V tile
+  static constexpr int OFF_Q = 0, OFF_DO = QT, OFF_DS = 2 * QT;  // dS^T: NCOL rows x 128 gathered rows
+  static constexpr int OFF_KV = ((3 * QT + 1023) / 1024) * 1024;
+  static constexpr int STAGE = 2 * TILE;       // K_g then V_g
+  static constexpr int NS = 2;
+  static constexpr int OFF_ROWS = OFF_KV + NS * STAGE;  // int [NS][128]
+  static constexpr int OFF_LD = OFF_ROWS + NS * 128 * 4;  // lse2[64], delta[64]
+  static constexpr int OFF_BAR = OFF_LD + 128 * 4;
+  // q_full, full[NS], kv_empty[NS], s_full, p_ready, acc_ready, acc_free
+  static constexpr int NBAR = 5 + 2 * NS;
+  static constexpr int OFF_MISC = OFF_BAR + NBAR * 8;
+  static constexpr int BYTES = OFF_MISC + 16 + 1024;
+};
+
+template <int NCOL>
+__device__ __forceinline__ void gbwd_ld(uint32_t taddr, uint32_t (&r)[NCOL]) {
+  if constexpr (NCOL == 16) {
+    tmem_ld16(taddr, r);
+  } else if constexpr (NCOL == 32) {
+    tmem_ld32(taddr, r);
+  } else {
+    tmem_ld64(taddr, r);
+  }
+}
+
+template <int NW>
+__device__ __forceinline__ void gbwd_st(uint32_t taddr, const uint32_t (&r)[NW]) {
+  if constexpr (NW == 8) {
+    uint32_t x[16];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) x[i] = i < 8 ? r[i] : 0u;
+    tmem_st16(taddr, x);  // the upper 8 columns are not read (K = 16 heads)
+  } else if constexpr (NW == 16) {
+    tmem_st16(taddr, r);
+  } else {
+    tmem_st32(taddr, r);
+  }
+}
+
+template <int NCOL>
+__global__ void __launch_bounds__(GBWD_THREADS, 1) bwd_gather_kernel(const GatherBwdParams p) {
+  using L = GatherBwdLayout<NCOL>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  int* s_rows = reinterpret_cast<int*>(smem + L::OFF_ROWS);
+  float* s_l2 = reinterpret_cast<float*>(smem + L::OFF_LD);
+  float* s_dl = s_l2 + 64;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::OFF_BAR);
+  uint64_t* q_full = bars;
+  uint64_t* full = q_full + 1;
+  uint64_t* kv_empty = full + L::NS;
+  uint64_t* s_full = kv_empty + L::NS;
+  uint64_t* p_ready = s_full + 1;
+  uint64_t* acc_ready = p_ready + 1;
+  uint64_t* acc_free = acc_ready + 1;
+  uint32_t* s_tmem = reinterpret_cast<uint32_t*>(smem + L::OFF_MISC);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t bt = blockIdx.x;  // the query (b, t)
+  const int b = static_cast<int>(bt / p.T), t = static_cast<int>(bt - static_cast<int64_t>(b) * p.T);
+  const int ntiles = (p.K + 127) / 128;
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, GBWD_LOADERS);
+    for (int s = 0; s < L::NS; ++s) {
+      mbar_init(full + s, GBWD_LOADERS);
+      mbar_init(kv_empty + s, 1);
+    }
+    mbar_init(s_full, 1);
+    mbar_init(p_ready, 128);
+    mbar_init(acc_ready, 1);
+    mbar_init(acc_free, 128);
+    fence_mbar_init();
+  }
+  if (warp == 4) {
+    tmem_alloc(s_tmem, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *s_tmem;  // S^T 0, dP^T 64, dV_g 128, dK_g 256, dQ^T 384
+
+  if (warp >= 5) {
+    // --------------------------------------------------------- loaders
+    const int lt = threadIdx.x - 160;
+    const int64_t qrow = (static_cast<int64_t>(b) * p.T + t) * p.H;
+    for (int it = lt; it < NCOL * 16; it += GBWD_LOADERS) {
+      const int h = it >> 4, ch = it & 15;
+      const bool ok = h < p.H;
+      const int64_t off = (qrow + (ok ? h : 0)) * 128 + ch * 8;
+      const uint32_t dst = (ch >> 3) * (NCOL * 128) + sw128_offset(h, ch & 7);
+      cp_async_16(smem_u32(smem + L::OFF_Q + dst), p.q + off, ok);
+      cp_async_16(smem_u32(smem + L::OFF_DO + dst), p.d_out + off, ok);
+    }
+    if (lt < 64) {
+      const int j = t / p.TQ, r0 = (t - j * p.TQ) * p.H;
+      const float* ld = p.ld + (static_cast<int64_t>(b) * p.qtiles + j) * 256;
+      s_l2[lt] = lt < p.H ? ld[r0 + lt] : 0.f;
+      s_dl[lt] = lt < p.H ? ld[128 + r0 + lt] : 0.f;
+    }
+    cp_async_commit();
+    cp_async_wait<0>();
+    fence_proxy_async();
+    mbar_arrive(q_full);
+    const int64_t* idx = p.idx + bt * p.K;
+    const uint8_t* kb = reinterpret_cast<const uint8_t*>(p.k + static_cast<int64_t>(b) * p.ksb);
+    const uint8_t* vb = reinterpret_cast<const uint8_t*>(p.v + static_cast<int64_t>(b) * p.vsb);
+    bool ok = true;
+    for (int i = 0; ok && i < ntiles; ++i) {
+      const int st = i % L::NS;
+      if (i >= L::NS) ok = mbar_wait(kv_empty + st, ((i / L::NS) & 1) ^ 1, p.status);
+      ok = named_barrier_and(2, GBWD_LOADERS, ok);
+      if (!ok) break;
+      uint8_t* stage = smem + L::OFF_KV + st * L::STAGE;
+#pragma unroll
+      for (int hr = 0; hr < 2; ++hr) {  // this thread's two rows of the tile
+        const int r = lt + 64 * hr;
+        const int slot = i * 128 + r;
+        int64_t row = slot < p.K ? idx[slot] : -1;
+        if (row < 0 || row >= p.N) row = -1;
+        s_rows[st * 128 + r] = static_cast<int>(row);
+        const bool live = row >= 0;
+        const uint8_t* ks = kb + (live ? row : 0) * p.ksn * 2;
+        const uint8_t* vs = vb + (live ? row : 0) * p.vsn * 2;
+#pragma unroll
+        for (int ch = 0; ch < 16; ++ch) {
+          const uint32_t dst = (ch >> 3) * (128 * 128) + sw128_offset(r, ch & 7);
+          cp_async_16(smem_u32(stage + dst), ks + ch * 16, live);
+          cp_async_16(smem_u32(stage + L::TILE + dst), vs + ch * 16, live);
+        }
+      }
+      cp_async_commit();
+      cp_async_wait<0>();
+      fence_proxy_async();
+      mbar_arrive(full + st);
+    }
+    tc_fence_before();
+    __syncthreads();
+  } else if (warp == 4) {
+    // ------------------------------------------------------------ issuer
+    auto wait = [&](uint64_t* bar, int parity) {
+      return __all_sync(0xffffffffu, mbar_wait(bar, parity, p.status));
+    };
+    const uint32_t base = smem_u32(smem);
+    const uint64_t dq_k = sdesc_sw128(base + L::OFF_Q, 16, 1024), ddo_k = sdesc_sw128(base + L::OFF_DO, 16, 1024);
+    const uint64_t dq_mn = sdesc_sw128(base + L::OFF_Q, NCOL * 128, 1024);
+    const uint64_t ddo_mn = sdesc_sw128(base + L::OFF_DO, NCOL * 128, 1024);
+    const uint64_t dds = sdesc_sw128(base + L::OFF_DS, 16, 1024);
+    bool ok = wait(q_full, 0);
+    for (int i = 0; ok && i < ntiles; ++i) {
+      const int st = i % L::NS;
+      const uint32_t stage = base + L::OFF_KV + st * L::STAGE;
+      if (!(ok = wait(full + st, (i / L::NS) & 1))) break;
+      tc_fence_after();
+      stream_s_steps<NCOL, 7>(tmem, sdesc_sw128(stage, 16, 1024), dq_k, idesc_bf16(128, NCOL, 0, 0));
+      stream_s_steps<NCOL, 7>(tmem + 64, sdesc_sw128(stage + L::TILE, 16, 1024), ddo_k, idesc_bf16(128, NCOL, 0, 0));
+      mma_commit_warp(s_full);
+      if (!(ok = wait(p_ready, i & 1))) break;
+      if (i > 0 && !(ok = wait(acc_free, (i - 1) & 1))) break;
+      tc_fence_after();
+      prefill_pv_steps<NCOL / 16 - 1, 0>(tmem + 128, tmem, ddo_mn, idesc_bf16(128, 128, 0, 1), 0u);      // dV_g
+      prefill_pv_steps<NCOL / 16 - 1, 0>(tmem + 256, tmem + 64, dq_mn, idesc_bf16(128, 128, 0, 1), 0u);  // dK_g
+      stream_pv_steps<NCOL, 7>(tmem + 384, sdesc_sw128(stage, 128 * 128, 1024), dds, idesc_bf16(128, NCOL, 1, 0),
+                               i > 0 ? 1u : 0u);  // dQ^T += K_g^T dS^T
+      mma_commit_warp(acc_ready);
+      mma_commit_warp(kv_empty + st);
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  } else {
+    // -------------------------------------------- P and dS (warps 0-3)
+    const int r = warp * 32 + lane;  // this thread's gathered row in each tile
+    const uint32_t lane_addr = tmem + (static_cast<uint32_t>(warp * 32) << 16);
+    const float sl2 = p.scale_log2;
+    uint8_t* sds = smem + L::OFF_DS;
+    bool ok = __all_sync(0xffffffffu, mbar_wait(q_full, 0, p.status));
+    for (int i = 0; ok && i < ntiles; ++i) {
+      const int st = i % L::NS;
+      ok = __all_sync(0xffffffffu,
+                      mbar_wait(full + st, (i / L::NS) & 1, p.status) && mbar_wait(s_full, i & 1, p.status));
+      if (!ok) break;
+      tc_fence_after();
+      const int row = s_rows[st * 128 + r];
+      uint32_t s[NCOL], d[NCOL];
+      gbwd_ld<NCOL>(lane_addr, s);
+      gbwd_ld<NCOL>(lane_addr + 64, d);
+      uint32_t pk[NCOL / 2], dsk[NCOL / 2];
+#pragma unroll
+      for (int h2 = 0; h2 < NCOL / 2; ++h2) {
+        float pp[2], gg[2];
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          const int h = 2 * h2 + e;
+          const bool live = row >= 0 && h < p.H;
+          pp[e] = live ? fast_exp2(fmaf(__uint_as_float(s[h]), sl2, -s_l2[h])) : 0.f;
+          gg[e] = pp[e] * (__uint_as_float(d[h]) - s_dl[h]);
+        }
+        pk[h2] = pack_bf16(pp[0], pp[1]);
+        dsk[h2] = pack_bf16(gg[0], gg[1]);
+        // dS^T as the dQ product's B operand: head rows, gathered rows along K
+        const __nv_bfloat162 g2 = __floats2bfloat162_rn(gg[0], gg[1]);
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          const int h = 2 * h2 + e;
+          const uint32_t off = (r >> 6) * (NCOL * 128) + sw128_offset(h, (r & 63) >> 3) + (r & 7) * 2;
+          *reinterpret_cast<__nv_bfloat16*>(sds + off) = e == 0 ? g2.x : g2.y;
+        }
+      }
+      gbwd_st<NCOL / 2>(lane_addr, pk);        // P^T over S^T's columns
+      gbwd_st<NCOL / 2>(lane_addr + 64, dsk);  // dS^T over dP^T's columns
+      fence_proxy_async();
+      tmem_wait_st();
+      tc_fence_before();
+      mbar_arrive(p_ready);
+      ok = __all_sync(0xffffffffu, mbar_wait(acc_ready, i & 1, p.status));
+      if (!ok) break;
+      tc_fence_after();
+      // this row's shares of dV and dK, added into the gradients of table row `row`
+#pragma unroll
+      for (int c32 = 0; c32 < 4; ++c32) {
+        uint32_t gv[32], gk[32];
+        tmem_ld32(lane_addr + 128 + c32 * 32, gv);
+        tmem_ld32(lane_addr + 256 + c32 * 32, gk);
+        if (row >= 0) {
+          float* dvr = p.dv + (static_cast<int64_t>(b) * p.N + row) * 128 + c32 * 32;
+          float* dkr = p.dk + (static_cast<int64_t>(b) * p.N + row) * 128 + c32 * 32;
+#pragma unroll
+          for (int e = 0; e < 8; ++e) {
+            atomicAdd(reinterpret_cast<float4*>(dvr) + e,
+                      make_float4(__uint_as_float(gv[4 * e]), __uint_as_float(gv[4 * e + 1]),
+                                  __uint_as_float(gv[4 * e + 2]), __uint_as_float(gv[4 * e + 3])));
+            atomicAdd(reinterpret_cast<float4*>(dkr) + e,
+                      make_float4(__uint_as_float(gk[4 * e]) * p.scale, __uint_as_float(gk[4 * e + 1]) * p.scale,
+                                  __uint_as_float(gk[4 * e + 2]) * p.scale, __uint_as_float(gk[4 * e + 3]) * p.scale));
+          }
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(acc_free);
+    }
+    if (ok) {
+      // dQ^T: lane c of the four warps is channel c, NCOL head columns
+      tc_fence_after();
+      uint32_t g[NCOL];
+      gbwd_ld<NCOL>(lane_addr + 384, g);
+      const int c = r;
+      float* dq = p.dq + bt * p.H * 128 + c;
+      for (int h = 0; h < p.H; ++h) dq[h * 128] += __uint_as_float(g[h]) * p.scale;
+    }
+    tc_fence_before();
+    __syncthreads();
+  }
+}
+
+// fp32 gradients to bf16 (the sparse path accumulates in fp32).
+__global__ void __launch_bounds__(256) f32_to_bf16_kernel(const float4* __restrict__ x, int64_t n4,
+                                                          uint2* __restrict__ y) {
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n4;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const float4 v = x[i];
+    y[i] = make_uint2(pack_bf16(v.x, v.y), pack_bf16(v.z, v.w));
   }
 }
 

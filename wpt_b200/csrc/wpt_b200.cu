@@ -84,10 +84,29 @@ int encoder(EncodeTiled* out) {
 }
 
 // A bf16 tensor map with 128-byte swizzle and 64-element inner boxes.
+// Makes the current device's primary context current on this host thread.
+// Runtime calls bind it lazily, but the driver's tensor-map encoder needs it
+// bound already, and a thread that has made no runtime call on the device
+// yet (autograd's backward worker, for one) has none: cudaSetDevice binds it.
+// Once per thread and device.
+int bind_context() {
+  static thread_local int bound = -1;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  if (bound != dev) {
+    e = cudaSetDevice(dev);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaSetDevice");
+    bound = dev;
+  }
+  return WPT_OK;
+}
+
 int tensor_map(CUtensorMap* map, const void* base, int rank, const cuuint64_t* dims, const cuuint64_t* strides_bytes,
                const cuuint32_t* box) {
   EncodeTiled encode;
   if (int rc = encoder(&encode)) return rc;
+  if (int rc = bind_context()) return rc;
   cuuint32_t elem[3] = {1, 1, 1};
   CUresult r = encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, rank, const_cast<void*>(base), dims, strides_bytes,
                       box, elem, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
@@ -395,12 +414,28 @@ extern "C" size_t wpt_attn_backward_scratch_bytes(int B, int T, int H, int C, in
   return static_cast<size_t>(bwd_scratch(B, T, H).total);
 }
 
+template <int NCOL>
+int launch_gather_bwd(const wpt::GatherBwdParams& g, cudaStream_t st) {
+  using L = wpt::GatherBwdLayout<NCOL>;
+  static_assert(L::BYTES <= 232448, "gathered-rows backward shared memory exceeds 227 KB");
+  if (int rc = allow_smem(wpt::bwd_gather_kernel<NCOL>, L::BYTES)) return rc;
+  wpt::bwd_gather_kernel<NCOL><<<static_cast<unsigned>(static_cast<int64_t>(g.B) * g.T), wpt::GBWD_THREADS, L::BYTES,
+                                 st>>>(g);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "bwd_gather_kernel launch");
+  return WPT_OK;
+}
+
 extern "C" int wpt_attn_backward(const void* q, const void* k, const void* v, int64_t k_stride_b, int64_t k_stride_n,
                                  int64_t v_stride_b, int64_t v_stride_n, const int64_t* positions,
-                                 const int64_t* floor_rows, const float* sink, const void* out, const float* lse,
-                                 const void* d_out, void* dq, void* dk, void* dv, float* d_sink, void* scratch,
-                                 int f32_grads, int B, int T, int H, int C, int N, int window, float scale,
-                                 void* stream) {
+                                 const int64_t* floor_rows, const int64_t* idx, int K, const float* sink,
+                                 const void* out, const float* lse, const void* d_out, void* dq, void* dk, void* dv,
+                                 float* d_sink, void* scratch, int f32_grads, int B, int T, int H, int C, int N,
+                                 int window, float scale, void* stream) {
+  if (K < 0 || (K > 0 && idx == nullptr)) return fail(WPT_ERR_INVALID, "K=%d chosen rows need idx", K);
+  if (K > 0 && !f32_grads)
+    return fail(WPT_ERR_INVALID, "gradients over chosen rows accumulate in fp32: pass f32_grads = 1");
+  if (K > 0 && H > 64) return fail(WPT_ERR_UNSUPPORTED, "%d heads: the gathered-rows backward takes up to 64", H);
   if (C != 128) return fail(WPT_ERR_UNSUPPORTED, "head width %d: the backward kernels take 128", C);
   if (H < 1 || H > 128) return fail(WPT_ERR_UNSUPPORTED, "%d heads: the kernels take 1 to 128", H);
   if (B < 1 || T < 1 || N < 1) return fail(WPT_ERR_INVALID, "empty shape B=%d T=%d N=%d", B, T, N);
@@ -472,6 +507,51 @@ extern "C" int wpt_attn_backward(const void* q, const void* k, const void* v, in
   wpt::bwd_q_kernel<<<dim3(p.qtiles, B), wpt::BWD_THREADS, wpt::BwdQLayout::BYTES, st>>>(tq, tdo, tk, tv, p);
   e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "bwd_q_kernel launch");
+  if (K > 0) {  // the chosen rows' share, added to the fp32 gradients above
+    wpt::GatherBwdParams g;
+    g.q = static_cast<const __nv_bfloat16*>(q);
+    g.d_out = static_cast<const __nv_bfloat16*>(d_out);
+    g.k = static_cast<const __nv_bfloat16*>(k);
+    g.v = static_cast<const __nv_bfloat16*>(v);
+    g.ksb = k_stride_b;
+    g.ksn = k_stride_n;
+    g.vsb = v_stride_b;
+    g.vsn = v_stride_n;
+    g.idx = idx;
+    g.ld = p.ld;
+    g.dq = static_cast<float*>(dq);
+    g.dk = static_cast<float*>(dk);
+    g.dv = static_cast<float*>(dv);
+    g.status = p.status;
+    g.B = B;
+    g.T = T;
+    g.H = H;
+    g.N = N;
+    g.K = K;
+    g.TQ = p.TQ;
+    g.qtiles = p.qtiles;
+    g.scale = scale;
+    g.scale_log2 = p.scale_log2;
+    const int rc = H <= 16 ? launch_gather_bwd<16>(g, st) : H <= 32 ? launch_gather_bwd<32>(g, st)
+                                                                     : launch_gather_bwd<64>(g, st);
+    if (rc) return rc;
+  }
+  return WPT_OK;
+}
+
+extern "C" int wpt_f32_to_bf16(const float* x, int64_t n, void* y, void* stream) {
+  if (n < 0 || (n > 0 && (!x || !y))) return fail(WPT_ERR_INVALID, "bad f32_to_bf16 arguments");
+  if (n % 4 || !aligned16(x) || reinterpret_cast<uintptr_t>(y) % 8)
+    return fail(WPT_ERR_INVALID, "f32_to_bf16 takes a multiple of 4 values, x 16-byte and y 8-byte aligned");
+  if (n == 0) return WPT_OK;
+  int sms = 148;
+  current_device(&sms);
+  const int64_t want = (n / 4 + 255) / 256;
+  const int blocks = static_cast<int>(std::min<int64_t>(want, static_cast<int64_t>(sms) * 8));
+  wpt::f32_to_bf16_kernel<<<blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      reinterpret_cast<const float4*>(x), n / 4, static_cast<uint2*>(y));
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "f32_to_bf16_kernel launch");
   return WPT_OK;
 }
 

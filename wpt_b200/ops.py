@@ -308,25 +308,34 @@ def merge_partials(part_o, part_lse, H, sink=None, out=None, lse=None):
     return out, lse
 
 
-def attention_backward(q, k, v, positions, out, lse, d_out, scale, window=0, floor=None, sink=None, f32=False):
+def attention_backward(q, k, v, positions, out, lse, d_out, scale, window=0, floor=None, sink=None, idx=None,
+                       f32=False):
     """Gradients of range attention (each query reads rows max(0, p - window
-    + 1, floor) .. min(p, N - 1), sink (H,) in the denominators) from the
-    forward pass's out (bf16) and lse: (dq (B, T, H, C), dk, dv (B, N, C) in
-    bf16, or fp32 when f32; d_sink (H,) fp32 or None). Tensor-core kernels
-    (bwd_prep, bwd_kv, bwd_q) on the current stream."""
-    _need_cuda(q, k, v, positions, out, lse, d_out, floor, sink)
+    + 1, floor) .. min(p, N - 1)), plus its chosen rows idx (B, T, K) when
+    given (sparse attention), sink (H,) in the denominators, from the forward
+    pass's out (bf16) and lse: (dq (B, T, H, C), dk, dv (B, N, C) in bf16, or
+    fp32 when f32; d_sink (H,) fp32 or None). Tensor-core kernels (bwd_prep,
+    bwd_kv, bwd_q, and bwd_gather for chosen rows) on the current stream."""
+    _need_cuda(q, k, v, positions, out, lse, d_out, floor, sink, idx)
     q = _bf16(q).contiguous()
     k, v = _table(k), _table(v)
     B, T, H, C = q.shape
     N = k.shape[1]
     positions = _rows(positions)
     floor = None if floor is None else _rows(floor)
+    K = 0
+    if idx is not None and idx.shape[-1] > 0:
+        idx = _rows(idx)
+        K = idx.shape[-1]
+    else:
+        idx = None
     out = _bf16(out).contiguous()
     d_out = d_out.to(torch.bfloat16).contiguous()
     lse = lse.float().contiguous()
     if sink is not None:
         sink = sink.float().contiguous()
-    dtype = torch.float32 if f32 else torch.bfloat16
+    wide = f32 or K > 0  # chosen rows are added by fp32 atomics
+    dtype = torch.float32 if wide else torch.bfloat16
     dq = torch.empty(B, T, H, C, dtype=dtype, device=q.device)
     dk = torch.empty(B, N, C, dtype=dtype, device=q.device)
     dv = torch.empty(B, N, C, dtype=dtype, device=q.device)
@@ -338,11 +347,21 @@ def attention_backward(q, k, v, positions, out, lse, d_out, scale, window=0, flo
     scratch = torch.empty(nbytes, dtype=torch.uint8, device=q.device)
     _lib.check(_lib.lib().wpt_attn_backward(
         _lib.ptr(q), _lib.ptr(k), _lib.ptr(v), k.stride(0), k.stride(1), v.stride(0), v.stride(1),
-        _lib.ptr(positions), _lib.ptr(floor), _lib.ptr(sink), _lib.ptr(out), _lib.ptr(lse), _lib.ptr(d_out),
-        _lib.ptr(dq), _lib.ptr(dk), _lib.ptr(dv), _lib.ptr(d_sink), _lib.ptr(scratch), 1 if f32 else 0,
-        B, T, H, C, N, int(window), float(scale), _lib.stream(q.device)))
-    LAUNCHES[0] += 3 + (sink is not None)
+        _lib.ptr(positions), _lib.ptr(floor), _lib.ptr(idx), K, _lib.ptr(sink), _lib.ptr(out), _lib.ptr(lse),
+        _lib.ptr(d_out), _lib.ptr(dq), _lib.ptr(dk), _lib.ptr(dv), _lib.ptr(d_sink), _lib.ptr(scratch),
+        1 if wide else 0, B, T, H, C, N, int(window), float(scale), _lib.stream(q.device)))
+    LAUNCHES[0] += 3 + (sink is not None) + (K > 0)
+    if wide and not f32:
+        dq, dk, dv = (to_bf16(x) for x in (dq, dk, dv))
     return dq, dk, dv, d_sink
+
+
+def to_bf16(x):
+    """A contiguous fp32 tensor rounded to bf16 by the library's kernel."""
+    y = torch.empty(x.shape, dtype=torch.bfloat16, device=x.device)
+    _lib.check(_lib.lib().wpt_f32_to_bf16(_lib.ptr(x), x.numel(), _lib.ptr(y), _lib.stream(x.device)))
+    LAUNCHES[0] += 1
+    return y
 
 
 def tree_bits(parents, B):
