@@ -362,6 +362,99 @@ def secondary(wb, ops, device, rank, world, hbm):
     return out
 
 
+def backward_lines(ops, device, rank, world, pk):
+    """Config 2's backward passes (training through the same kernels): the
+    causal pass's gradients and the window-1024 pass's (with the sink's),
+    strong-scaled like the headline. Algorithmic FLOPs: 2.5 x the forward
+    pass's (five products per visible pair: S, dP, dQ, dK, dV; the kernels
+    run seven, recomputing S and dP for dQ instead of adding dQ by atomics)."""
+    from wpt_b200 import multi
+    rows = multi.shard_rows(B2, world, rank)
+    q_all, e_all, p_all, sink = config2_inputs(device, 0)
+    q, e, pos = q_all[rows].contiguous(), e_all[rows].contiguous(), p_all[rows].contiguous()
+    del q_all, e_all, p_all
+    d_out = torch.randn(q.shape, generator=torch.Generator(device=device).manual_seed(5), device=device).bfloat16()
+    k, v = e[..., :C2], e[..., C2:]
+    out_c, lse_c = ops.attention_forward(q, k, v, pos, C2 ** -0.5)
+    out_w, lse_w = ops.attention_forward(q, k, v, pos, C2 ** -0.5, window=W2, sink=sink)
+    f_c = lambda: ops.attention_backward(q, k, v, pos, out_c, lse_c, d_out, C2 ** -0.5)  # noqa: E731
+    f_w = lambda: ops.attention_backward(q, k, v, pos, out_w, lse_w, d_out, C2 ** -0.5, window=W2,  # noqa: E731
+                                         sink=sink)
+    causal, window = config2_flops()
+    out = {}
+    for name, fn, flop in (("backward_causal", f_c, causal), ("backward_window", f_w, window)):
+        if world > 1:
+            dist.barrier()
+        ms = max_over_ranks(timed(fn, 10, 3), world, device)
+        achieved = 2.5 * flop / (ms * 1e-3) / 1e12
+        out[name] = {"metric": f"prefill backward TFLOP/s (config 2, {name.split('_')[1]} pass; 2.5 x forward FLOPs)",
+                     "unit": "TFLOP/s", "value": round(achieved, 1), "ms": round(ms, 4),
+                     "frac_of_bf16_burst": round(achieved / (pk["bf16_tflops"] * world), 3),
+                     "algorithmic_flops": 2.5 * flop}
+    return out
+
+
+def triton_bar(device):
+    """The reference's own GPU form, unmodified (wpt_model.triton_kernels from
+    baseline/_ref, Triton compiling for this GPU), timed on the same inputs as
+    this library's lines: config 2's two prefill passes and the causal pass's
+    backward, config 3's global and window decode. Also whether the
+    reference's TileLang form builds here. The first call of each shape
+    includes Triton's compilation and autotuning; the timed calls follow it."""
+    if reference_form() is None:
+        return {"unavailable": "the reference is not installed in baseline/_ref (baseline/install_ref.py)"}
+    try:
+        from wpt_model import triton_kernels as tk
+    except Exception as error:  # noqa: BLE001 - reported, not raised
+        return {"unavailable": f"wpt_model.triton_kernels does not import: {type(error).__name__}: {error}"}
+    out = {"form": "wpt_model.triton_kernels (reference, unmodified)"}
+    try:
+        q, e, pos, sink = config2_inputs(device, 0)
+        k, v = e[..., :C2], e[..., C2:]
+        empty = torch.empty(B2, T2, 0, dtype=torch.int64, device=device)
+        causal, window = config2_flops()
+        f_c = lambda: tk.exact_attention(q, k, v, pos, C2 ** -0.5, 0, W2)  # noqa: E731
+        f_w = lambda: tk.sparse_attention(q, k, v, sink, empty, pos, C2 ** -0.5, W2)  # noqa: E731
+        t0 = time.perf_counter()
+        f_c()
+        f_w()
+        torch.cuda.synchronize()
+        out["first_calls_s"] = round(time.perf_counter() - t0, 1)
+        ms_c, ms_w = timed(f_c, 5, 2), timed(f_w, 3, 1)
+        out["config2_causal"] = {"unit": "TFLOP/s", "value": round(causal / ms_c / 1e9, 1), "ms": round(ms_c, 4)}
+        out["config2_window"] = {"unit": "TFLOP/s", "value": round(window / ms_w / 1e9, 1), "ms": round(ms_w, 4)}
+        qg = q.detach().clone().requires_grad_()
+        kg, vg = k.detach().clone().requires_grad_(), v.detach().clone().requires_grad_()
+        d_out = torch.randn(q.shape, generator=torch.Generator(device=device).manual_seed(5), device=device).bfloat16()
+        with torch.enable_grad():
+            o, _ = tk.exact_attention(qg, kg, vg, pos, C2 ** -0.5, 0, W2)
+            f_b = lambda: torch.autograd.grad(o, (qg, kg, vg), d_out, retain_graph=True)  # noqa: E731
+            ms_b = timed(f_b, 3, 1)
+        out["config2_causal_backward"] = {"unit": "TFLOP/s", "value": round(2.5 * causal / ms_b / 1e9, 1),
+                                          "ms": round(ms_b, 4)}
+        del q, e, qg, kg, vg, o
+        L, table, q3, sink3, pos3 = config3_inputs(device, 0)
+        k3, v3 = table[..., :C2], table[..., C2:]
+        empty3 = torch.empty(64, 1, 0, dtype=torch.int64, device=device)
+        f_g = lambda: tk.exact_attention(q3, k3, v3, pos3, C2 ** -0.5, 0, 128)  # noqa: E731
+        f_s = lambda: tk.sparse_attention(q3, k3, v3, sink3, empty3, pos3, C2 ** -0.5, 1024)  # noqa: E731
+        qo = 2 * 64 * 32 * C2 * 2
+        for name, fn, nbytes in (("config3_decode_global", f_g, int(L.sum()) * 2 * C2 * 2 + qo),
+                                 ("config3_decode_window", f_s, int(L.clamp(max=1024).sum()) * 2 * C2 * 2 + qo)):
+            fn()
+            ms = timed(fn, 10, 2)
+            out[name] = {"unit": "GB/s", "value": round(nbytes / ms / 1e6, 1), "ms": round(ms, 4)}
+        del table
+    except Exception as error:  # noqa: BLE001 - reported, not raised
+        out["error"] = f"{type(error).__name__}: {str(error)[:300]}"
+    try:
+        from wpt_model import tilelang_kernels  # noqa: F401
+        out["tilelang"] = "imports"
+    except Exception as error:  # noqa: BLE001
+        out["tilelang"] = f"does not import: {type(error).__name__}: {str(error)[:200]}"
+    return out
+
+
 # ----------------------------------------------------------- CPU baseline
 
 REF_DIR = os.path.join(ROOT, "baseline", "_ref")
@@ -522,6 +615,16 @@ def profile_case(args):
         def fn():
             wpt_b200.accept(scores, drafted, qprob, uniforms, resample, 1.0, None)
             wpt_b200.accept(scores, drafted, qprob, uniforms, resample, 1.0, 1)
+    elif args.case == "backward":  # config 2's causal backward on B rows
+        q, entries, positions, sink = config2_inputs(device, 0)
+        q, entries, positions = q[:B].contiguous(), entries[:B].contiguous(), positions[:B].contiguous()
+        d_out = torch.randn(q.shape, generator=torch.Generator(device=device).manual_seed(5), device=device).bfloat16()
+        k, v = entries[..., :C], entries[..., C:]
+        out, lse = ops.attention_forward(q, k, v, positions, C ** -0.5)
+        fn = lambda: ops.attention_backward(q, k, v, positions, out, lse, d_out, C ** -0.5)  # noqa: E731
+    elif args.case == "bars":  # the reference's Triton form on this GPU (no timing of this library)
+        print(json.dumps({"case": "bars", "triton_bar": triton_bar(device)}), flush=True)
+        return
     else:
         raise SystemExit(f"unknown case {args.case}")
     for _ in range(args.warmup):
@@ -694,6 +797,9 @@ def main():
                                      "ms_per_step": round(ms_w, 4), "global_batch": B2 * world}
             del qw, ew, kw, vw
         extra.update(secondary(wpt_b200, ops, device, rank, world, pk["hbm_gbs"]))
+        extra.update(backward_lines(ops, device, rank, world, pk))
+        if world == 1:  # the reference's own GPU form on this GPU, same inputs
+            extra["reference_triton"] = triton_bar(device)
     status |= wpt_b200.device_status()
     cpu = cpu_baseline(seconds=10.0) if rank == 0 and world == 1 else None
     if rank == 0:

@@ -1,0 +1,86 @@
+"""The multi-GPU long row on real GPUs: one process per GPU over NCCL, each
+holding a contiguous shard of a long row's keys; multi.long_decode's
+production branch (partials into the shared-layout buffer, one in-place
+all-gather, the grouped merge) must equal one GPU's call over the whole row
+and the CPU oracle, on every rank, twice in a row (the plan's buffer is
+reused). Skipped with fewer than two GPUs; the same logic runs on gloo
+ranks on CPU in tests/test_multi_cpu.py."""
+
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+pytestmark = pytest.mark.gpu
+
+C, H = 128, 32
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _inputs(N, seed):
+    g = torch.Generator().manual_seed(seed)
+    q = (torch.randn(1, 1, H, C, generator=g) * 0.5).bfloat16()
+    e = (torch.randn(1, N, 2 * C, generator=g) * 0.5).bfloat16()
+    sink = torch.randn(H, generator=g) * 0.5
+    return q, e, sink
+
+
+def _rank(rank, world, port, N, result):
+    import datetime
+
+    import torch.distributed as dist
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    torch.cuda.set_device(rank)
+    device = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
+                            device_id=device)
+    try:
+        import wpt_b200
+        from wpt_b200 import multi
+        for seed in (1, 2):
+            q, e, sink = _inputs(N, seed)
+            start, stop = multi.key_shard(N, world, rank)
+            shard = e[:, start:stop].to(device)
+            pos = torch.tensor([[N - 1 - 7 * seed]], device=device)
+            out, lse = multi.long_decode(q.to(device), shard[..., :C], shard[..., C:], start, pos, C ** -0.5,
+                                         sink=sink.to(device))
+            torch.cuda.synchronize()
+            result[(rank, seed)] = (out.float().cpu().numpy(), lse.cpu().numpy(), wpt_b200.device_status())
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_long_row_over_nccl_ranks_equals_one_gpu_and_oracle():
+    import wpt_b200
+    from oracle import attention as oat
+    from wpt_b200 import build
+    build.build()
+    world, N = min(4, torch.cuda.device_count()), 50000
+    manager = mp.get_context("spawn").Manager()
+    result = manager.dict()
+    mp.start_processes(_rank, args=(world, _free_port(), N, result), nprocs=world, start_method="spawn", join=True)
+    for seed in (1, 2):
+        q, e, sink = _inputs(N, seed)
+        pos = torch.tensor([[N - 1 - 7 * seed]])
+        whole, whole_lse = wpt_b200.forward_with_lse(q.cuda(), e.cuda()[..., :C], e.cuda()[..., C:], pos.cuda(),
+                                                     C ** -0.5, sink=sink.cuda())
+        ref, ref_lse = oat.range_attention(q.float().numpy(), e[..., :C].float().numpy(),
+                                           e[..., C:].float().numpy(), pos.numpy(), C ** -0.5,
+                                           sink=sink.double().numpy())
+        for rank in range(world):
+            out, lse, status = result[(rank, seed)]
+            assert status == 0
+            assert np.abs(out - whole.float().cpu().numpy()).max() < 1e-2
+            assert np.abs(lse - whole_lse.cpu().numpy()).max() < 1e-4
+            assert np.abs(out - ref).max() < 2e-2
+            assert np.abs(lse - ref_lse).max() < 1e-3

@@ -147,10 +147,6 @@ def _stream_plan(B, T, H, N, K, window, gather, sms, chunk_tiles=None):
         # every query gathers exactly `tiles` tiles: its slots split so that
         # the grid is about one CTA per SM
         chunk_tiles = math.ceil(tiles / max(1, sms // groups))
-    elif not chunk_tiles and window > 0:
-        # window rows are short (window / 128 + 1 tiles): split them so that
-        # the grid covers every SM, at least two tiles a CTA
-        chunk_tiles = max(2, math.ceil(tiles / max(1, math.ceil(sms / groups))))
     elif not chunk_tiles:
         # at least 16 key tiles per CTA (a CTA's start-up costs about as much
         # as streaming a few tiles), more when that still gives two CTAs per
