@@ -188,6 +188,35 @@ def accept(scores, drafted, q, uniforms, resample, temperature=1.0, top_k=None, 
     return ops.accept(scores, drafted, q, uniforms, resample, temperature, top_k, lengths)
 
 
-__all__ = ["accept", "NAME", "WINDOW", "chosen_columns", "exact_attention", "sparse_attention", "window_attention",
+# ------------------------------------------------------------- installation
+
+def install(kernels, attention=None, device=None, check=True):
+    """Makes this module the attention form of the WPT process that imported
+    `kernels` (wpt_model.kernels, kernels.py:62-112) and, given `attention`
+    (wpt_model.attention), its window layers' window_attention too
+    (attention.py:85, which WPT calls directly rather than through a form).
+
+    check: first runs the reference's own install check on this module,
+    kernels._try (kernels.py:115-144: both operations forward and backward
+    on a small input on `device`), which raises if the kernels cannot work.
+    The window wrapper reads attention.WINDOW at each call and casts q, k and
+    v to the compute dtype (autocast's bf16), as kernels.exact_attention
+    does for the form's operations (kernels.py:160-171)."""
+    import sys
+    me = sys.modules[__name__]
+    if check:
+        kernels._try(me, device if device is not None else torch.device("cuda", torch.cuda.current_device()))
+    kernels._kernels, kernels._form = me, "b200"
+    if attention is not None:
+        def window(q, k, v, sink, positions, scale):
+            dtype = kernels.compute_dtype(q)
+            with torch.autocast(q.device.type, enabled=False):
+                return window_attention(q.to(dtype), k.to(dtype), v.to(dtype), sink.float(), positions, scale,
+                                        window=attention.WINDOW)
+        attention.window_attention = window
+    return me
+
+
+__all__ = ["install", "accept", "NAME", "WINDOW", "chosen_columns", "exact_attention", "sparse_attention", "window_attention",
            "tree_attention",
            "forward_with_lse", "device_status", "LibraryMissing"]
