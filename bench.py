@@ -18,6 +18,11 @@ lines: decode attention GB/s (config 3, global and window-1024 rows, the
 along its keys over the ranks with one NCCL all-gather), tree verification
 (config 4) and the acceptance step (config 4).
 
+--case config5 runs BASELINE config 5 end to end (the reference's own WPT
+model, 64 rows, 2048-token prompts, 256 generated tokens) once with the
+reference's Triton form and once with this library installed: about seven
+minutes, so it is not part of the default run.
+
 --impl reference times the reference's CPU path on the host cores: the
 reference's own PyTorch attention form (wpt_model.pytorch_kernels, from
 baseline/_ref when it is installed there, kind "reference"), else the CPU
@@ -455,6 +460,82 @@ def triton_bar(device):
     return out
 
 
+CONFIG5 = dict(vocab_size=65536, block_size=2048, window_layers=4, sparse_groups=3, sparse_layers=4, d_model=2048,
+               attention_heads=16, attention_head_dim=128, n_experts=32, top_k=4, expert_width=1024,
+               latent_width=1024, shared_width=2048, engram_layers=[2], engram_order=3, engram_heads=8,
+               engram_dim=16, engram_table_size=50021, residual_groups=48)
+
+
+def config5_line(device, rows=64, prompt=2048, steps=256):
+    """end-to-end greedy decode of a random-init WPT
+    (the reference's own model code from baseline/_ref) with 24 layers (4
+    window, exact, 4 window, then 3 x (exact + 4 sparse)), d_model 2048, 16
+    query heads of 128, vocab 65536, window 1024, bf16 autocast: `rows`
+    prompts of `prompt` random ids (seed 5) read by one WPT.extend, then
+    `steps` tokens generated one extend at a time. Run once with the
+    reference's own GPU form (Triton) and once with this library installed;
+    tokens/s of each. The routed experts and the rest of the model are the
+    reference's PyTorch code in both runs. Agreement: the share of rows
+    whose first generated token (argmax after the prompt) is the same in
+    both runs (a random model's scores differ where bf16 rounding sends a
+    token to other experts, so the scores themselves are not compared)."""
+    if reference_form() is None:
+        return {"unavailable": "the reference is not installed in baseline/_ref (baseline/install_ref.py)"}
+    import wpt_b200
+    try:
+        from wpt_model import WPT, ModelConfig, attention, kernels
+    except Exception as error:  # noqa: BLE001 - reported, not raised
+        return {"unavailable": f"wpt_model does not import: {type(error).__name__}: {error}"}
+    saved = (attention.WINDOW, attention.window_attention, kernels._kernels, kernels._form)
+    attention.WINDOW = 1024
+    out = {"metric": "end-to-end decode tokens/s (config 5: 24-layer WPT, 64 rows, 2048-token prompt, 256 new)",
+           "model": "random-init WPT, " + ", ".join(f"{k}={v}" for k, v in CONFIG5.items() if k in
+                                                   ("d_model", "attention_heads", "n_experts", "vocab_size"))}
+    try:
+        torch.manual_seed(0)
+        with torch.device(device):
+            model = WPT(ModelConfig(**CONFIG5)).eval()
+        ids = torch.randint(CONFIG5["vocab_size"], (rows, prompt), generator=torch.Generator().manual_seed(5))
+        ids = ids.to(device)
+
+        def run():
+            cache = model.new_cache(rows)
+            torch.cuda.synchronize()
+            t0 = time.perf_counter()
+            scores, _ = model.extend(ids, cache)
+            first = scores[:, -1].argmax(-1, keepdim=True)
+            torch.cuda.synchronize()
+            t1 = time.perf_counter()
+            nxt = first
+            for _ in range(steps):
+                scores, _ = model.extend(nxt, cache)
+                nxt = scores[:, -1].argmax(-1, keepdim=True)
+            torch.cuda.synchronize()
+            t2 = time.perf_counter()
+            del cache
+            return {"prefill_s": round(t1 - t0, 3), "decode_s": round(t2 - t1, 3),
+                    "prefill_tokens_per_s": round(rows * prompt / (t1 - t0), 1),
+                    "decode_tokens_per_s": round(rows * steps / (t2 - t1), 1),
+                    "tokens_per_s": round(rows * (prompt + steps) / (t2 - t0), 1)}, first
+        kernels._kernels, kernels._form = kernels._decide(device, "triton"), "triton"
+        run()  # warm-up: Triton's compilation and autotuning at these shapes
+        ref, ref_first = run()
+        wpt_b200.install(kernels, attention)
+        run()  # the same warm-up for this form
+        ours, first = run()
+        out.update({"reference_triton": ref, "b200": ours, "unit": "tokens/s",
+                    "value": ours["tokens_per_s"], "vs_reference_triton": round(ours["tokens_per_s"] /
+                                                                                ref["tokens_per_s"], 3),
+                    "first_token_agreement": round((first == ref_first).float().mean().item(), 4)})
+        del model
+    except Exception as error:  # noqa: BLE001 - reported, not raised
+        out["error"] = f"{type(error).__name__}: {str(error)[:300]}"
+    finally:
+        attention.WINDOW, attention.window_attention, kernels._kernels, kernels._form = saved
+    torch.cuda.empty_cache()
+    return out
+
+
 # ----------------------------------------------------------- CPU baseline
 
 REF_DIR = os.path.join(ROOT, "baseline", "_ref")
@@ -624,6 +705,9 @@ def profile_case(args):
         fn = lambda: ops.attention_backward(q, k, v, positions, out, lse, d_out, C ** -0.5)  # noqa: E731
     elif args.case == "bars":  # the reference's Triton form on this GPU (no timing of this library)
         print(json.dumps({"case": "bars", "triton_bar": triton_bar(device)}), flush=True)
+        return
+    elif args.case == "config5":  # the end-to-end decode, both forms
+        print(json.dumps({"case": "config5", "config5": config5_line(device)}), flush=True)
         return
     else:
         raise SystemExit(f"unknown case {args.case}")
