@@ -189,6 +189,19 @@ int wpt_attn_backward(const void* q, const void* k, const void* v, int64_t k_str
                       const void* d_out, void* dq, void* dk, void* dv, float* d_sink, void* scratch, int f32_grads,
                       int B, int T, int H, int C, int N, int window, float scale, void* stream);
 
+/*
+ * Failure-detection test hook (no counterpart in the reference; tests only).
+ * From the next wpt_attn_backward call on, the query-tile kernel's loader
+ * does not issue the copy of key tile `skip_key_tile` of each of its CTAs
+ * (-1: off), and that kernel's mbarrier waits give up after wait_ns
+ * nanoseconds (0: the default, 2 s). A wait that gives up sets bit 0 of the
+ * status word (wpt_status), every role of the CTA stops, the loader lets
+ * the copies it did issue land, TMEM is freed and the kernel returns: the
+ * context stays usable, and the gradients of that call are not written.
+ * Nothing is ever in flight for the skipped tile, so nothing lands late.
+ */
+int wpt_debug_backward_fault(int skip_key_tile, unsigned long long wait_ns);
+
 /* Bytes of scratch wpt_attn_backward needs (0 for a shape it does not take). */
 size_t wpt_attn_backward_scratch_bytes(int B, int T, int H, int C, int N);
 

@@ -200,3 +200,31 @@ def test_reference_try_both_sequence_forward_and_backward(wb):
     _close_grad(v.grad, ev + sv, "dv")
     assert np.abs(sink.grad.cpu().numpy() - ss).max() <= 1e-2 * max(1.0, np.abs(ss).max())
     assert q.grad.dtype == torch.bfloat16 and sink.grad.dtype == torch.float32
+
+
+def test_a_wait_that_runs_out_reports_and_leaves_the_context_usable(wb):
+    # failure detection without a fault: the query-tile kernel's loader does
+    # not issue key tile 0's copy (nothing is in flight for it) and its waits
+    # give up after 1 ms; the call returns, status bit 0 is set, and after a
+    # reset the next call (hook off) is correct
+    from wpt_b200 import _lib, ops
+    B, T, H = 1, 16, 16
+    q, e, d_out = _case(B, T, H, T, seed=3)
+    k, v = e[..., :C], e[..., C:]
+    positions = torch.arange(T).expand(B, T).contiguous().cuda()
+    out, lse = ops.attention_forward(q, k, v, positions, C ** -0.5)
+    assert wb.device_status() == 0
+    _lib.check(_lib.lib().wpt_debug_backward_fault(0, 1_000_000))
+    try:
+        ops.attention_backward(q, k, v, positions, out, lse, d_out, C ** -0.5)
+        assert wb.device_status(reset=True) & 1  # a bounded wait ran out, and the status says so
+    finally:
+        _lib.check(_lib.lib().wpt_debug_backward_fault(-1, 0))
+    assert wb.device_status() == 0
+    dq, dk, dv, _ = ops.attention_backward(q, k, v, positions, out, lse, d_out, C ** -0.5)
+    assert wb.device_status() == 0
+    rq, rk, rv = ob.exact_backward(_np(q), _np(k), _np(v), positions.cpu().numpy(), _np(out), _np(lse), _np(d_out),
+                                   C ** -0.5)
+    _close_grad(dq, rq, "dq")
+    _close_grad(dk, rk, "dk")
+    _close_grad(dv, rv, "dv")

@@ -42,6 +42,13 @@ def _positions(positions, B):
     return positions.to(torch.int64).expand(B, -1).contiguous()
 
 
+def _needs_grad(*tensors):
+    """Whether autograd would record this call (grad mode on and an input
+    that requires a gradient): when not, the forward runs without the
+    autograd Function's bookkeeping, a few microseconds a call."""
+    return torch.is_grad_enabled() and any(t is not None and t.requires_grad for t in tensors)
+
+
 def _bf16_only(*tensors):
     """The kernels compute in bfloat16, WPT's compute dtype under autocast
     (layers.py:13-17). The reference computes in its inputs' dtype, so
@@ -56,15 +63,18 @@ def _bf16_only(*tensors):
 
 # ------------------------------------------------------------ exact attention
 
+def _exact_forward(q, k, v, positions, scale, top_k, window):
+    B, T, H, c = q.shape
+    positions = _positions(positions, B)
+    out, lse = ops.attention_forward(q, k, v, positions, scale)
+    chosen = ops.select_rows(q, k, positions, lse, scale, chosen_columns(top_k, window, k.shape[1]), window)
+    return out, chosen, positions, lse
+
+
 class _Exact(torch.autograd.Function):
     @staticmethod
     def forward(ctx, q, k, v, positions, scale, top_k, window):
-        B, T, H, c = q.shape
-        N = k.shape[1]
-        positions = _positions(positions, B)
-        out, lse = ops.attention_forward(q, k, v, positions, scale)
-        K = chosen_columns(top_k, window, N)
-        chosen = ops.select_rows(q, k, positions, lse, scale, K, window)
+        out, chosen, positions, lse = _exact_forward(q, k, v, positions, scale, top_k, window)
         ctx.save_for_backward(q, k, v, positions, out, lse)
         ctx.scale = scale
         ctx.mark_non_differentiable(chosen)
@@ -81,6 +91,8 @@ def exact_attention(q, k, v, positions, scale, top_k, window):
     """pytorch_kernels.exact_attention's result: (output (B, T, H, c) in q's
     dtype, chosen rows (B, T, K) int64, -1 padded)."""
     _bf16_only(q, k, v)
+    if not _needs_grad(q, k, v):
+        return _exact_forward(q, k, v, positions, scale, top_k, window)[:2]
     return _Exact.apply(q, k, v, positions, scale, top_k, window)
 
 
@@ -92,18 +104,23 @@ def forward_with_lse(q, k, v, positions, scale, window=0, sink=None):
 
 # ----------------------------------------------------------- sparse attention
 
+def _sparse_forward(q, k, v, sink, idx, positions, scale, window):
+    B, T, H, c = q.shape
+    positions = _positions(positions, B)
+    if idx.shape[-1] == 0:
+        out, lse = ops.attention_forward(q, k, v, positions, scale, window=window, sink=sink)
+    elif ops.uses_stream(1, H, c):
+        out, lse = ops.stream_forward(q, k, v, positions, scale, window=window, idx=idx, sink=sink)
+    else:
+        raise NotImplementedError(f"sparse attention with {H} heads of width {c}: the gather kernel takes "
+                                  "head width 128 and up to 64 heads")
+    return out, positions, lse
+
+
 class _Sparse(torch.autograd.Function):
     @staticmethod
     def forward(ctx, q, k, v, sink, idx, positions, scale, window):
-        B, T, H, c = q.shape
-        positions = _positions(positions, B)
-        if idx.shape[-1] == 0:
-            out, lse = ops.attention_forward(q, k, v, positions, scale, window=window, sink=sink)
-        elif ops.uses_stream(1, H, c):
-            out, lse = ops.stream_forward(q, k, v, positions, scale, window=window, idx=idx, sink=sink)
-        else:
-            raise NotImplementedError(f"sparse attention with {H} heads of width {c}: the gather kernel takes "
-                                      "head width 128 and up to 64 heads")
+        out, positions, lse = _sparse_forward(q, k, v, sink, idx, positions, scale, window)
         ctx.save_for_backward(q, k, v, sink, idx, positions, out, lse)
         ctx.scale, ctx.window = scale, window
         return out.to(q.dtype)
@@ -122,6 +139,8 @@ def sparse_attention(q, k, v, sink, idx, positions, scale, window):
     q's dtype, over each query's rows idx (B, T, K) (-1 for none) and its
     last `window` rows, with sink (H,) in each head's denominator."""
     _bf16_only(q, k, v)
+    if not _needs_grad(q, k, v, sink):
+        return _sparse_forward(q, k, v, sink, idx, positions, scale, window)[0]
     return _Sparse.apply(q, k, v, sink, idx, positions, scale, window)
 
 
@@ -157,6 +176,8 @@ def window_attention(q, k, v, sink, positions, scale, window=None):
     t = torch.arange(T, device=q.device, dtype=torch.int64)
     rows = (t + W - 1).expand(B, T).contiguous()  # each query's own row in the table
     floor = rows - positions  # the row of position 0: rows before it are before the text
+    if not _needs_grad(q, k, v, sink):
+        return ops.attention_forward(q, k, v, rows, scale, window=W, floor=floor, sink=sink)[0]
     return _Window.apply(q, k, v, sink, rows, floor, scale, W)
 
 

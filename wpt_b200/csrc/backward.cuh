@@ -81,6 +81,11 @@ struct BwdParams {
   int B, T, H, N, window, TQ, qtiles, ktiles;
   int f32_grads;  // 1: dq, dk, dv in fp32 (a gathered-rows pass adds to them after), 0: bf16
   float scale, scale_log2;
+  // the query-tile kernel's wait limit, and (a failure-detection test hook,
+  // -1 when off) a key tile whose copy its loader does not issue, so that
+  // the waits for it run out while nothing is in flight
+  unsigned long long wait_ns;
+  int skip_key_tile;
 };
 
 // Rows lo..hi query t of batch row b reads (hi < lo: none): hi = min(p, N - 1),
@@ -193,6 +198,38 @@ __device__ __forceinline__ bool bwd_tile_sees(const BwdParams& p, int b, int j, 
   return r.y >= r.x && r.x <= n0 + 127 && r.y >= n0;
 }
 
+// The first query tile at or after j that reads a key of the tile at n0
+// (qtiles when none). Warp-collective: the lanes test 32 tiles with one load
+// each and a ballot keeps the answer (base, mask) for the next calls, so a
+// key tile that most query tiles skip costs a load per 32 tiles, not one
+// per tile.
+struct BwdTileScan {
+  int base = -64;
+  uint32_t mask = 0;
+  __device__ __forceinline__ int next(const BwdParams& p, int b, int n0, int j) {
+    const int lane = threadIdx.x & 31;
+    while (j < p.qtiles) {
+      if (j >= base + 32) {
+        base = j & ~31;
+        const int jj = base + lane;
+        mask = __ballot_sync(0xffffffffu, jj < p.qtiles && bwd_tile_sees(p, b, jj, n0));
+      }
+      const uint32_t m = mask & (0xffffffffu << (j - base));
+      if (m) return base + __ffs(m) - 1;
+      j = base + 32;
+    }
+    return p.qtiles;
+  }
+};
+
+// Work order of the key-tile kernel: key tile 0 of every batch row first
+// (under a causal mask it is read by the most query tiles), then tile 1, ...
+__device__ __forceinline__ void bwd_kv_place(const BwdParams& p, int& b, int& n0) {
+  const int idx = static_cast<int>(blockIdx.x);
+  b = idx % p.B;
+  n0 = (idx / p.B) * 128;
+}
+
 // 64 fp32 values of one thread (a TMEM row's half) to global memory at dst,
 // as bf16 (f32 == 0) or fp32, times mul.
 __device__ __forceinline__ void bwd_store64(void* dst, const uint32_t (&v)[64], float mul, int f32) {
@@ -223,8 +260,8 @@ struct BwdKvLayout {
   static constexpr int STAGE = 2 * TILE + 1024;  // Q, dO, then lse * log2(e) and delta (2 x 128 fp32)
   static constexpr int OFF_K = 0, OFF_V = TILE, OFF_ST = 2 * TILE;
   static constexpr int OFF_BAR = OFF_ST + NSQ * STAGE;
-  // kv_full, st_full[NSQ], st_empty[NSQ], s_full, p_ready, acc_done
-  static constexpr int NBAR = 4 + 2 * NSQ;
+  // kv_full, st_full[NSQ], st_empty[NSQ], s_full[2], p_ready[2], acc_done
+  static constexpr int NBAR = 6 + 2 * NSQ;
   static constexpr int OFF_MISC = OFF_BAR + NBAR * 8;
   static constexpr int BYTES = OFF_MISC + 16 + 1024;
 };
@@ -240,12 +277,13 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
   uint64_t* kv_full = bars;
   uint64_t* st_full = kv_full + 1;
   uint64_t* st_empty = st_full + L::NSQ;
-  uint64_t* s_full = st_empty + L::NSQ;
-  uint64_t* p_ready = s_full + 1;
-  uint64_t* acc_done = p_ready + 1;
+  uint64_t* s_full = st_empty + L::NSQ;  // [half]: S^T and dP^T of the tile's half are in TMEM
+  uint64_t* p_ready = s_full + 2;        // [half]: its P^T and dS^T are
+  uint64_t* acc_done = p_ready + 2;
   uint32_t* s_tmem = reinterpret_cast<uint32_t*>(smem + L::OFF_MISC);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int b = blockIdx.y, n0 = blockIdx.x * 128;  // key tile 0 first: under a causal mask it is read most
+  int b, n0;
+  bwd_kv_place(p, b, n0);
 
   if (threadIdx.x == 0) {
     mbar_init(kv_full, 1);
@@ -253,8 +291,10 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
       mbar_init(st_full + s, 1);
       mbar_init(st_empty + s, 1);
     }
-    mbar_init(s_full, 1);
-    mbar_init(p_ready, BWD_COMPUTE);
+    for (int g = 0; g < 2; ++g) {
+      mbar_init(s_full + g, 1);
+      mbar_init(p_ready + g, BWD_COMPUTE / 2);
+    }
     mbar_init(acc_done, 1);
     fence_mbar_init();
   }
@@ -275,94 +315,110 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
 
   if (warp == BWD_LOAD_WARP) {
     // ------------------------------------------------------------ TMA loader
+    // the whole warp scans the query tiles; lane 0 issues the copies
+    bool ok = true;
     if (lane == 0) {
-      bool ok = true;
       mbar_expect_tx(kv_full, 2 * L::TILE);
       for (int s = 0; s < 2; ++s) {
         tma_load_3d(smem + L::OFF_K + s * L::CHUNK, &tm_k, kv_full, s * 64, n0, b);
         tma_load_3d(smem + L::OFF_V + s * L::CHUNK, &tm_v, kv_full, s * 64, n0, b);
       }
-      int u = 0;
-      for (int j = 0; ok && j < p.qtiles; ++j) {
-        if (!bwd_tile_sees(p, b, j, n0)) continue;
-        const int st = u % L::NSQ;
-        if (u >= L::NSQ && !(ok = mbar_wait(st_empty + st, ((u / L::NSQ) & 1) ^ 1, p.status))) break;
-        uint8_t* stage = smem + L::OFF_ST + st * L::STAGE;
-        mbar_expect_tx(st_full + st, 2 * L::TILE + 1024);
-        const int row0 = (b * p.T + j * p.TQ) * p.H;
-        for (int s = 0; s < 2; ++s) {
-          tma_load_2d(stage + s * L::CHUNK, &tm_q, st_full + st, s * 64, row0);
-          tma_load_2d(stage + L::TILE + s * L::CHUNK, &tm_do, st_full + st, s * 64, row0);
+    }
+    BwdTileScan scan;
+    int u = 0;
+    for (int j = scan.next(p, b, n0, 0); ok && j < p.qtiles; j = scan.next(p, b, n0, j + 1), ++u) {
+      const int st = u % L::NSQ;
+      if (lane == 0) {
+        if (u >= L::NSQ) ok = mbar_wait(st_empty + st, ((u / L::NSQ) & 1) ^ 1, p.status);
+        if (ok) {
+          uint8_t* stage = smem + L::OFF_ST + st * L::STAGE;
+          mbar_expect_tx(st_full + st, 2 * L::TILE + 1024);
+          const int row0 = (b * p.T + j * p.TQ) * p.H;
+          for (int s = 0; s < 2; ++s) {
+            tma_load_2d(stage + s * L::CHUNK, &tm_q, st_full + st, s * 64, row0);
+            tma_load_2d(stage + L::TILE + s * L::CHUNK, &tm_do, st_full + st, s * 64, row0);
+          }
+          bulk_load(stage + 2 * L::TILE, p.ld + (static_cast<int64_t>(b) * p.qtiles + j) * 256, 1024,
+                    st_full + st);
         }
-        bulk_load(stage + 2 * L::TILE, p.ld + (static_cast<int64_t>(b) * p.qtiles + j) * 256, 1024, st_full + st);
-        ++u;
       }
+      ok = __shfl_sync(0xffffffffu, ok, 0);
     }
     tc_fence_before();
     __syncthreads();
   } else if (warp == BWD_MMA_WARP) {
     // ------------------------------------------------------ tcgen05 issuer
+    // A query tile's rows come in two halves of 64 (g = 0, 1), one per
+    // compute warpgroup. Order: S_0 dP_0 S_1 dP_1 of tile u, then per tile
+    // dV/dK of half 0, S_0 dP_0 of tile u + 1, dV/dK of half 1, S_1 dP_1 of
+    // tile u + 1: each warpgroup's P and dS are computed while the tensor
+    // pipe runs the other half's products. tcgen05 products run in issue
+    // order, so S_g of the next tile overwrites P_g only after dV has read it.
     auto wait = [&](uint64_t* bar, int parity) {
       return __all_sync(0xffffffffu, mbar_wait(bar, parity, p.status));
     };
     const uint32_t base = smem_u32(smem);
     const uint64_t dk = sdesc_sw128(base + L::OFF_K, 16, 1024), dv = sdesc_sw128(base + L::OFF_V, 16, 1024);
+    auto issue_s = [&](int uu, int g) {  // S^T_g = K Q_g^T and dP^T_g = V dO_g^T (N = 64 query rows)
+      const uint32_t stage = base + L::OFF_ST + (uu % L::NSQ) * L::STAGE + g * 64 * 128;
+      prefill_s_steps<7>(tmem + 64 * g, dk, sdesc_sw128(stage, 16, 1024), idesc_bf16(128, 64, 0, 0));
+      prefill_s_steps<7>(tmem + 128 + 64 * g, dv, sdesc_sw128(stage + L::TILE, 16, 1024), idesc_bf16(128, 64, 0, 0));
+      mma_commit_warp(s_full + g);
+    };
+    auto issue_acc = [&](int uu, int g, uint32_t acc0) {  // dV += P_g^T dO_g, dK += dS_g^T Q_g (K = 64 rows)
+      const uint32_t stage = base + L::OFF_ST + (uu % L::NSQ) * L::STAGE + g * 64 * 128;
+      prefill_pv_steps<3, 0>(tmem + 256, tmem + 64 * g, sdesc_sw128(stage + L::TILE, L::CHUNK, 1024),
+                             idesc_bf16(128, 128, 0, 1), acc0);
+      prefill_pv_steps<3, 0>(tmem + 384, tmem + 128 + 64 * g, sdesc_sw128(stage, L::CHUNK, 1024),
+                             idesc_bf16(128, 128, 0, 1), acc0);
+    };
     bool ok = wait(kv_full, 0);
-    int u = 0;
-    for (int j = 0; ok && j < p.qtiles; ++j) {
-      if (!bwd_tile_sees(p, b, j, n0)) continue;
-      const int st = u % L::NSQ;
-      const uint32_t stage = base + L::OFF_ST + st * L::STAGE;
-      if (!(ok = wait(st_full + st, (u / L::NSQ) & 1))) break;
+    BwdTileScan scan;
+    int j = scan.next(p, b, n0, 0);
+    if (ok && j < p.qtiles && (ok = wait(st_full, 0))) {
       tc_fence_after();
-      prefill_s_steps<7>(tmem, dk, sdesc_sw128(stage, 16, 1024), idesc_bf16(128, 128, 0, 0));  // S^T = K Q^T
-      prefill_s_steps<7>(tmem + 128, dv, sdesc_sw128(stage + L::TILE, 16, 1024),
-                         idesc_bf16(128, 128, 0, 0));  // dP^T = V dO^T
-      mma_commit_warp(s_full);
+      issue_s(0, 0);
+      issue_s(0, 1);
+    }
+    for (int u = 0; ok && j < p.qtiles; ++u) {
+      const int jn = scan.next(p, b, n0, j + 1);
       if (!(ok = wait(p_ready, u & 1))) break;
       tc_fence_after();
-      // dV += P^T dO and dK += dS^T Q: A from TMEM, B MN-major (query rows are K)
-      prefill_pv_steps<7, 0>(tmem + 256, tmem, sdesc_sw128(stage + L::TILE, L::CHUNK, 1024),
-                             idesc_bf16(128, 128, 0, 1), u > 0 ? 1u : 0u);
-      prefill_pv_steps<7, 0>(tmem + 384, tmem + 128, sdesc_sw128(stage, L::CHUNK, 1024),
-                             idesc_bf16(128, 128, 0, 1), u > 0 ? 1u : 0u);
-      mma_commit_warp(st_empty + st);
-      ++u;
+      issue_acc(u, 0, u > 0 ? 1u : 0u);
+      if (jn < p.qtiles) {
+        if (!(ok = wait(st_full + (u + 1) % L::NSQ, ((u + 1) / L::NSQ) & 1))) break;
+        tc_fence_after();
+        issue_s(u + 1, 0);
+      }
+      if (!(ok = wait(p_ready + 1, u & 1))) break;
+      tc_fence_after();
+      issue_acc(u, 1, 1u);
+      mma_commit_warp(st_empty + u % L::NSQ);
+      if (jn < p.qtiles) issue_s(u + 1, 1);
+      j = jn;
     }
     mma_commit_warp(acc_done);  // once every product above has completed
+    wait(acc_done, 0);  // so that no product or commit is in flight at the dealloc (bounded)
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
     tmem_dealloc(tmem, 512);
   } else {
-    // ------------------------------------------- P and dS (warps 0-7)
-    const int quad = warp & 3, half = warp >> 2;
+    // ----------------------- P and dS: warpgroup g owns the tiles' half g
+    const int quad = warp & 3, g = warp >> 2;
     const int row = quad * 32 + lane, n = n0 + row;  // this thread's key
     const uint32_t lane_addr = tmem + (static_cast<uint32_t>(quad * 32) << 16);
-    const float sl2 = p.scale_log2;
+    const uint64_t sl2 = f2_pack(p.scale_log2, p.scale_log2);
     bool ok = true;
+    BwdTileScan scan;
     int u = 0;
-    for (int j = 0; ok && j < p.qtiles; ++j) {
-      if (!bwd_tile_sees(p, b, j, n0)) continue;
+    for (int j = scan.next(p, b, n0, 0); ok && j < p.qtiles; j = scan.next(p, b, n0, j + 1), ++u) {
       const int st = u % L::NSQ;
       const float* lds = reinterpret_cast<const float*>(smem + L::OFF_ST + st * L::STAGE + 2 * L::TILE);
-      // the stage's copies (its lse and delta are read here) and the tile's
-      // S^T and dP^T; the stage is not refilled before this thread's
-      // p_ready arrival, so the parity names this use of it
-      ok = __all_sync(0xffffffffu, mbar_wait(st_full + st, (u / L::NSQ) & 1, p.status) &&
-                                       mbar_wait(s_full, u & 1, p.status));
-      tc_fence_after();
-      uint32_t s[64], d[64];
-      if (ok) {
-        tmem_ld64(lane_addr + half * 64, s);
-        tmem_ld64(lane_addr + 128 + half * 64, d);
-      }
-      // every thread's reads of S^T and dP^T land before any P or dS write
-      ok = named_barrier_and(1, BWD_COMPUTE, ok);
-      if (!ok) break;
-      // the columns (query rows) of this half that see key n: by token
+      // the columns (query rows 64 g + c) that see key n, by token (global
+      // loads issued before the waits below, so their latency hides)
       uint64_t vis = 0;
-      const int c0 = half * 64;
+      const int c0 = 64 * g;
       for (int tq = c0 / p.H; tq < p.TQ && tq * p.H < c0 + 64; ++tq) {
         const int t = j * p.TQ + tq;
         if (t >= p.T) break;
@@ -373,37 +429,61 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
           vis |= hi_mask & ~((1ull << a) - 1ull);
         }
       }
-      uint32_t pk[32], dsk[32];
+      // the stage's copies (its lse and delta are read here) and the half's
+      // S^T and dP^T; the stage is not refilled before this thread's
+      // p_ready arrival, so the parity names this use of it
+      ok = __all_sync(0xffffffffu, mbar_wait(st_full + st, (u / L::NSQ) & 1, p.status) &&
+                                       mbar_wait(s_full + g, u & 1, p.status));
+      if (!ok) break;
+      tc_fence_after();
 #pragma unroll
-      for (int i = 0; i < 32; ++i) {
-        const int c = c0 + 2 * i;
-        const float p0 = (vis >> (2 * i)) & 1ull ? fast_exp2(fmaf(__uint_as_float(s[2 * i]), sl2, -lds[c])) : 0.f;
-        const float p1 =
-            (vis >> (2 * i + 1)) & 1ull ? fast_exp2(fmaf(__uint_as_float(s[2 * i + 1]), sl2, -lds[c + 1])) : 0.f;
-        const float g0 = p0 * (__uint_as_float(d[2 * i]) - lds[128 + c]);
-        const float g1 = p1 * (__uint_as_float(d[2 * i + 1]) - lds[128 + c + 1]);
-        pk[i] = pack_bf16(p0, p1);
-        dsk[i] = pack_bf16(g0, g1);
+      for (int ch = 0; ch < 2; ++ch) {  // 32 columns at a time; a thread's writes only land on columns it has read
+        uint32_t s[32], d[32];
+        tmem_ld32(lane_addr + 64 * g + 32 * ch, s);
+        tmem_ld32(lane_addr + 128 + 64 * g + 32 * ch, d);
+        uint32_t pk[16], dsk[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          const int c = c0 + 32 * ch + 2 * i;
+          const uint64_t z = f2_fma(f2_pack(__uint_as_float(s[2 * i]), __uint_as_float(s[2 * i + 1])), sl2,
+                                    f2_pack(-lds[c], -lds[c + 1]));
+          float z0, z1, e0, e1;
+          f2_unpack(z, z0, z1);
+          if ((i & 3) == 3) {  // a quarter of the exponentials on the FMA pipe, the rest on the exp unit
+            exp2_poly_pair(z0, z1, e0, e1);
+          } else {
+            e0 = fast_exp2(z0);
+            e1 = fast_exp2(z1);
+          }
+          const int bit = 32 * ch + 2 * i;
+          e0 = (vis >> bit) & 1ull ? e0 : 0.f;
+          e1 = (vis >> (bit + 1)) & 1ull ? e1 : 0.f;
+          const uint64_t gd = f2_add(f2_pack(__uint_as_float(d[2 * i]), __uint_as_float(d[2 * i + 1])),
+                                     f2_pack(-lds[128 + c], -lds[128 + c + 1]));
+          float g0, g1;
+          f2_unpack(gd, g0, g1);
+          pk[i] = pack_bf16(e0, e1);
+          dsk[i] = pack_bf16(e0 * g0, e1 * g1);
+        }
+        tmem_st16(lane_addr + 64 * g + 16 * ch, pk);         // P^T_g over S^T_g's first 32 columns
+        tmem_st16(lane_addr + 128 + 64 * g + 16 * ch, dsk);  // dS^T_g over dP^T_g's
       }
-      tmem_st32(lane_addr + half * 32, pk);         // P^T over S^T's first 64 columns
-      tmem_st32(lane_addr + 128 + half * 32, dsk);  // dS^T over dP^T's first 64 columns
       tmem_wait_st();
       tc_fence_before();
-      mbar_arrive(p_ready);
-      ++u;
+      mbar_arrive(p_ready + g);
     }
     if (ok) ok = __all_sync(0xffffffffu, mbar_wait(acc_done, 0, p.status));
     tc_fence_after();
     uint32_t gv[64], gk[64];
     if (ok && u > 0) {
-      tmem_ld64(lane_addr + 256 + half * 64, gv);
-      tmem_ld64(lane_addr + 384 + half * 64, gk);
+      tmem_ld64(lane_addr + 256 + 64 * g, gv);
+      tmem_ld64(lane_addr + 384 + 64 * g, gk);
     } else {
 #pragma unroll
       for (int i = 0; i < 64; ++i) gv[i] = gk[i] = 0u;
     }
     if (ok && n < p.N) {
-      const int64_t off = (static_cast<int64_t>(b) * p.N + n) * 128 + half * 64;
+      const int64_t off = (static_cast<int64_t>(b) * p.N + n) * 128 + 64 * g;
       const int es = p.f32_grads ? 4 : 2;
       bwd_store64(static_cast<uint8_t*>(p.dv) + off * es, gv, 1.f, p.f32_grads);
       bwd_store64(static_cast<uint8_t*>(p.dk) + off * es, gk, p.scale, p.f32_grads);
@@ -420,8 +500,8 @@ struct BwdQLayout {
   static constexpr int OFF_KV = 2 * TILE + 1024;
   static constexpr int STAGE = 2 * TILE;
   static constexpr int OFF_BAR = OFF_KV + NS * STAGE;
-  // q_full, kv_full[NS], kv_empty[NS], s_full, ds_ready, acc_done
-  static constexpr int NBAR = 4 + 2 * NS;
+  // q_full, kv_full[NS], kv_empty[NS], s_full[2], ds_ready[2], acc_done
+  static constexpr int NBAR = 6 + 2 * NS;
   static constexpr int OFF_MISC = OFF_BAR + NBAR * 8;
   static constexpr int BYTES = OFF_MISC + 16 + 1024;
 };
@@ -437,12 +517,13 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
   uint64_t* q_full = bars;
   uint64_t* kv_full = q_full + 1;
   uint64_t* kv_empty = kv_full + L::NS;
-  uint64_t* s_full = kv_empty + L::NS;
-  uint64_t* ds_ready = s_full + 1;
-  uint64_t* acc_done = ds_ready + 1;
+  uint64_t* s_full = kv_empty + L::NS;  // [half]: S and dP of the key tile's half are in TMEM
+  uint64_t* ds_ready = s_full + 2;      // [half]: its dS is
+  uint64_t* acc_done = ds_ready + 2;
   uint32_t* s_tmem = reinterpret_cast<uint32_t*>(smem + L::OFF_MISC);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int b = blockIdx.y, j = p.qtiles - 1 - static_cast<int>(blockIdx.x);  // later tiles read more keys: first
+  // later query tiles read more keys: the last tile of every batch row first
+  const int b = static_cast<int>(blockIdx.x) % p.B, j = p.qtiles - 1 - static_cast<int>(blockIdx.x) / p.B;
   const int2 rg = p.ranges[static_cast<int64_t>(b) * p.qtiles + j];
   const int kt0 = rg.y >= rg.x ? rg.x / 128 : 0;
   const int nt = rg.y >= rg.x ? rg.y / 128 - kt0 + 1 : 0;
@@ -453,8 +534,10 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
       mbar_init(kv_full + s, 1);
       mbar_init(kv_empty + s, 1);
     }
-    mbar_init(s_full, 1);
-    mbar_init(ds_ready, BWD_COMPUTE);
+    for (int g = 0; g < 2; ++g) {
+      mbar_init(s_full + g, 1);
+      mbar_init(ds_ready + g, BWD_COMPUTE / 2);
+    }
     mbar_init(acc_done, 1);
     fence_mbar_init();
   }
@@ -483,49 +566,80 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
         tma_load_2d(smem + L::OFF_DO + s * L::CHUNK, &tm_do, q_full, s * 64, row0);
       }
       bulk_load(smem + L::OFF_LD, p.ld + (static_cast<int64_t>(b) * p.qtiles + j) * 256, 1024, q_full);
+      int last[L::NS];  // the last use of each stage whose copies were issued (-1: none)
+      for (int st = 0; st < L::NS; ++st) last[st] = -1;
       for (int i = 0; ok && i < nt; ++i) {
         const int st = i % L::NS;
-        if (i >= L::NS && !(ok = mbar_wait(kv_empty + st, ((i / L::NS) & 1) ^ 1, p.status))) break;
+        if (i >= L::NS && !(ok = mbar_wait_ns(kv_empty + st, ((i / L::NS) & 1) ^ 1, p.status, p.wait_ns))) break;
+        if (i == p.skip_key_tile) continue;  // test hook: this tile's copy is never issued
         uint8_t* stage = smem + L::OFF_KV + st * L::STAGE;
         mbar_expect_tx(kv_full + st, 2 * L::TILE);
         for (int s = 0; s < 2; ++s) {
           tma_load_3d(stage + s * L::CHUNK, &tm_k, kv_full + st, s * 64, (kt0 + i) * 128, b);
           tma_load_3d(stage + L::TILE + s * L::CHUNK, &tm_v, kv_full + st, s * 64, (kt0 + i) * 128, b);
         }
+        last[st] = i;
+      }
+      if (!ok) {
+        // a wait ran out: the copies issued here land before the CTA leaves
+        // (each stage's last issued use, and the query tile's), bounded too
+        mbar_wait_ns(q_full, 0, p.status, p.wait_ns);
+        for (int st = 0; st < L::NS; ++st)
+          if (last[st] >= 0) mbar_wait_ns(kv_full + st, (last[st] / L::NS) & 1, p.status, p.wait_ns);
       }
     }
     tc_fence_before();
     __syncthreads();
   } else if (warp == BWD_MMA_WARP) {
+    // the key tile's two halves of 64 keys (g = 0, 1), one per compute
+    // warpgroup, in the key-tile kernel's order: dQ += dS_0 K_0, the next
+    // tile's S_0 dP_0, dQ += dS_1 K_1, the next tile's S_1 dP_1
     auto wait = [&](uint64_t* bar, int parity) {
-      return __all_sync(0xffffffffu, mbar_wait(bar, parity, p.status));
+      return __all_sync(0xffffffffu, mbar_wait_ns(bar, parity, p.status, p.wait_ns));
     };
     const uint32_t base = smem_u32(smem);
     const uint64_t dq = sdesc_sw128(base + L::OFF_Q, 16, 1024), ddo = sdesc_sw128(base + L::OFF_DO, 16, 1024);
+    auto issue_s = [&](int i, int g) {  // S_g = Q K_g^T, dP_g = dO V_g^T (N = 64 keys)
+      const uint32_t stage = base + L::OFF_KV + (i % L::NS) * L::STAGE + g * 64 * 128;
+      prefill_s_steps<7>(tmem + 64 * g, dq, sdesc_sw128(stage, 16, 1024), idesc_bf16(128, 64, 0, 0));
+      prefill_s_steps<7>(tmem + 128 + 64 * g, ddo, sdesc_sw128(stage + L::TILE, 16, 1024), idesc_bf16(128, 64, 0, 0));
+      mma_commit_warp(s_full + g);
+    };
+    auto issue_dq = [&](int i, int g, uint32_t acc0) {  // dQ += dS_g K_g (K = 64 keys, K_g MN-major)
+      const uint32_t stage = base + L::OFF_KV + (i % L::NS) * L::STAGE + g * 64 * 128;
+      prefill_pv_steps<3, 0>(tmem + 256, tmem + 128 + 64 * g, sdesc_sw128(stage, L::CHUNK, 1024),
+                             idesc_bf16(128, 128, 0, 1), acc0);
+    };
     bool ok = wait(q_full, 0);
-    for (int i = 0; ok && i < nt; ++i) {
-      const int st = i % L::NS;
-      const uint32_t stage = base + L::OFF_KV + st * L::STAGE;
-      if (!(ok = wait(kv_full + st, (i / L::NS) & 1))) break;
+    if (ok && nt > 0 && (ok = wait(kv_full, 0))) {
       tc_fence_after();
-      prefill_s_steps<7>(tmem, dq, sdesc_sw128(stage, 16, 1024), idesc_bf16(128, 128, 0, 0));  // S = Q K^T
-      prefill_s_steps<7>(tmem + 128, ddo, sdesc_sw128(stage + L::TILE, 16, 1024),
-                         idesc_bf16(128, 128, 0, 0));  // dP = dO V^T
-      mma_commit_warp(s_full);
+      issue_s(0, 0);
+      issue_s(0, 1);
+    }
+    for (int i = 0; ok && i < nt; ++i) {
       if (!(ok = wait(ds_ready, i & 1))) break;
       tc_fence_after();
-      // dQ += dS K: A = dS (TMEM), B = K (keys are K, MN-major)
-      prefill_pv_steps<7, 0>(tmem + 256, tmem + 128, sdesc_sw128(stage, L::CHUNK, 1024), idesc_bf16(128, 128, 0, 1),
-                             i > 0 ? 1u : 0u);
-      mma_commit_warp(kv_empty + st);
+      issue_dq(i, 0, i > 0 ? 1u : 0u);
+      if (i + 1 < nt) {
+        if (!(ok = wait(kv_full + (i + 1) % L::NS, ((i + 1) / L::NS) & 1))) break;
+        tc_fence_after();
+        issue_s(i + 1, 0);
+      }
+      if (!(ok = wait(ds_ready + 1, i & 1))) break;
+      tc_fence_after();
+      issue_dq(i, 1, 1u);
+      mma_commit_warp(kv_empty + i % L::NS);
+      if (i + 1 < nt) issue_s(i + 1, 1);
     }
     mma_commit_warp(acc_done);
+    wait(acc_done, 0);  // so that no product or commit is in flight at the dealloc (bounded)
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
     tmem_dealloc(tmem, 512);
   } else {
-    const int quad = warp & 3, half = warp >> 2;
+    // ------------------------- dS: warpgroup g owns the key tiles' half g
+    const int quad = warp & 3, g = warp >> 2;
     const int row = quad * 32 + lane;  // this thread's query row
     const int tq = row / p.H, h = row - tq * p.H;
     const int t = j * p.TQ + tq;
@@ -534,53 +648,64 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
     const float sl2 = p.scale_log2;
     int2 bt = make_int2(1, 0);
     if (valid) bt = p.bounds[static_cast<int64_t>(b) * p.T + t];
-    bool ok = __all_sync(0xffffffffu, mbar_wait(q_full, 0, p.status));
+    bool ok = __all_sync(0xffffffffu, mbar_wait_ns(q_full, 0, p.status, p.wait_ns));
     const float* lds = reinterpret_cast<const float*>(smem + L::OFF_LD);
     const float lse2 = lds[row], delta = lds[128 + row];
+    const uint64_t sl2p = f2_pack(sl2, sl2), nl = f2_pack(-lse2, -lse2), nd = f2_pack(-delta, -delta);
     for (int i = 0; ok && i < nt; ++i) {
-      ok = __all_sync(0xffffffffu, mbar_wait(s_full, i & 1, p.status));
-      tc_fence_after();
-      uint32_t s[64], d[64];
-      if (ok) {
-        tmem_ld64(lane_addr + half * 64, s);
-        tmem_ld64(lane_addr + 128 + half * 64, d);
-      }
-      ok = named_barrier_and(1, BWD_COMPUTE, ok);
+      ok = __all_sync(0xffffffffu, mbar_wait_ns(s_full + g, i & 1, p.status, p.wait_ns));
       if (!ok) break;
-      const int nb = (kt0 + i) * 128 + half * 64;  // this half's first key
-      const int a = bt.x - nb, z = bt.y - nb;      // visible columns a .. z
-      uint32_t dsk[32];
+      tc_fence_after();
 #pragma unroll
-      for (int k2 = 0; k2 < 32; ++k2) {
-        const int c = 2 * k2;
-        const bool v0 = c >= a && c <= z, v1 = c + 1 >= a && c + 1 <= z;
-        const float p0 = v0 ? fast_exp2(fmaf(__uint_as_float(s[c]), sl2, -lse2)) : 0.f;
-        const float p1 = v1 ? fast_exp2(fmaf(__uint_as_float(s[c + 1]), sl2, -lse2)) : 0.f;
-        dsk[k2] = pack_bf16(p0 * (__uint_as_float(d[c]) - delta), p1 * (__uint_as_float(d[c + 1]) - delta));
+      for (int ch = 0; ch < 2; ++ch) {  // 32 keys at a time; a thread's writes only land on columns it has read
+        const int nb = (kt0 + i) * 128 + 64 * g + 32 * ch;  // these columns' first key
+        const int a = bt.x - nb, z = bt.y - nb;            // visible columns a .. z
+        uint32_t s[32], d[32];
+        tmem_ld32(lane_addr + 64 * g + 32 * ch, s);
+        tmem_ld32(lane_addr + 128 + 64 * g + 32 * ch, d);
+        uint32_t dsk[16];
+#pragma unroll
+        for (int k2 = 0; k2 < 16; ++k2) {
+          const int c = 2 * k2;
+          const uint64_t zz = f2_fma(f2_pack(__uint_as_float(s[c]), __uint_as_float(s[c + 1])), sl2p, nl);
+          float z0, z1, e0, e1;
+          f2_unpack(zz, z0, z1);
+          if ((k2 & 3) == 3) {  // a quarter of the exponentials on the FMA pipe
+            exp2_poly_pair(z0, z1, e0, e1);
+          } else {
+            e0 = fast_exp2(z0);
+            e1 = fast_exp2(z1);
+          }
+          e0 = c >= a && c <= z ? e0 : 0.f;
+          e1 = c + 1 >= a && c + 1 <= z ? e1 : 0.f;
+          const uint64_t gd = f2_add(f2_pack(__uint_as_float(d[c]), __uint_as_float(d[c + 1])), nd);
+          float g0, g1;
+          f2_unpack(gd, g0, g1);
+          dsk[k2] = pack_bf16(e0 * g0, e1 * g1);
+        }
+        tmem_st16(lane_addr + 128 + 64 * g + 16 * ch, dsk);  // dS_g over dP_g's first 32 columns
       }
-      tmem_st32(lane_addr + 128 + half * 32, dsk);  // dS over dP's first 64 columns
       tmem_wait_st();
       tc_fence_before();
-      mbar_arrive(ds_ready);
+      mbar_arrive(ds_ready + g);
     }
-    if (ok) ok = __all_sync(0xffffffffu, mbar_wait(acc_done, 0, p.status));
+    if (ok) ok = __all_sync(0xffffffffu, mbar_wait_ns(acc_done, 0, p.status, p.wait_ns));
     tc_fence_after();
-    uint32_t g[64];
+    uint32_t gq[64];
     if (ok && nt > 0) {
-      tmem_ld64(lane_addr + 256 + half * 64, g);
+      tmem_ld64(lane_addr + 256 + 64 * g, gq);
     } else {
 #pragma unroll
-      for (int i = 0; i < 64; ++i) g[i] = 0u;
+      for (int i = 0; i < 64; ++i) gq[i] = 0u;
     }
     if (ok && valid) {
-      const int64_t off = ((static_cast<int64_t>(b) * p.T + t) * p.H + h) * 128 + half * 64;
-      bwd_store64(static_cast<uint8_t*>(p.dq) + off * (p.f32_grads ? 4 : 2), g, p.scale, p.f32_grads);
+      const int64_t off = ((static_cast<int64_t>(b) * p.T + t) * p.H + h) * 128 + 64 * g;
+      bwd_store64(static_cast<uint8_t*>(p.dq) + off * (p.f32_grads ? 4 : 2), gq, p.scale, p.f32_grads);
     }
     tc_fence_before();
     __syncthreads();
   }
 }
-
 
 // ------------------------------------------------- gathered rows (sparse)
 //

@@ -59,17 +59,22 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 // Waits for the phase of `parity` to complete; false (and a status bit)
-// when it has not within WAIT_LIMIT_NS.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, unsigned* status) {
+// when it has not within limit_ns.
+__device__ __forceinline__ bool mbar_wait_ns(uint64_t* bar, uint32_t parity, unsigned* status,
+                                             unsigned long long limit_ns) {
   if (mbar_try_wait(bar, parity)) return true;
   const unsigned long long start = global_ns();
   for (uint32_t i = 1;; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
-    if ((i & 63u) == 0 && global_ns() - start > WAIT_LIMIT_NS) {
+    if ((i & 63u) == 0 && global_ns() - start > limit_ns) {
       atomicOr(status, STATUS_WAIT_TIMEOUT);
       return false;
     }
   }
+}
+// The same with the default limit, WAIT_LIMIT_NS.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, unsigned* status) {
+  return mbar_wait_ns(bar, parity, status, WAIT_LIMIT_NS);
 }
 
 // -------------------------------------------------------------------- TMA

@@ -1,6 +1,7 @@
 // The one translation unit of libwpt_b200.so: the kernels (headers beside
 // this file) and the extern "C" launchers declared in include/wpt_attn.h.
 #include <algorithm>
+#include <atomic>
 #include <cstdarg>
 #include <cstdio>
 #include <cstdlib>
@@ -102,8 +103,51 @@ int bind_context() {
   return WPT_OK;
 }
 
+// A tensor map depends only on its base address, shape, strides and box, so
+// each host thread keeps its last few encodings and a repeated call (a
+// decode loop over the same tables) skips the driver's encoder.
+struct MapKey {
+  const void* base;
+  int rank, dev;
+  cuuint64_t dims[3], strides[2];
+  cuuint32_t box[3];
+};
+
+int tensor_map_encode(CUtensorMap* map, const void* base, int rank, const cuuint64_t* dims,
+                      const cuuint64_t* strides_bytes, const cuuint32_t* box);
+int current_device(int* sms = nullptr);
+
 int tensor_map(CUtensorMap* map, const void* base, int rank, const cuuint64_t* dims, const cuuint64_t* strides_bytes,
                const cuuint32_t* box) {
+  constexpr int SLOTS = 16;
+  static thread_local MapKey keys[SLOTS];
+  static thread_local CUtensorMap maps[SLOTS];
+  static thread_local int used = 0, next = 0;
+  MapKey key;
+  memset(&key, 0, sizeof(key));
+  key.base = base;
+  key.rank = rank;
+  key.dev = current_device();
+  for (int i = 0; i < rank; ++i) {
+    key.dims[i] = dims[i];
+    key.box[i] = box[i];
+    if (i + 1 < rank) key.strides[i] = strides_bytes[i];
+  }
+  for (int i = 0; i < used; ++i)
+    if (memcmp(&keys[i], &key, sizeof(key)) == 0) {
+      *map = maps[i];
+      return WPT_OK;
+    }
+  if (int rc = tensor_map_encode(map, base, rank, dims, strides_bytes, box)) return rc;
+  keys[next] = key;
+  maps[next] = *map;
+  next = (next + 1) % SLOTS;
+  if (used < SLOTS) ++used;
+  return WPT_OK;
+}
+
+int tensor_map_encode(CUtensorMap* map, const void* base, int rank, const cuuint64_t* dims,
+                      const cuuint64_t* strides_bytes, const cuuint32_t* box) {
   EncodeTiled encode;
   if (int rc = encoder(&encode)) return rc;
   if (int rc = bind_context()) return rc;
@@ -132,7 +176,7 @@ int table_map(CUtensorMap* map, const void* base, int64_t stride_b, int64_t stri
 
 // The current device (and its SM count), asked of the runtime once per
 // thread and device change rather than on every launch.
-int current_device(int* sms = nullptr) {
+int current_device(int* sms) {
   static thread_local int cached_sms[64] = {};
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) dev = 0;
@@ -409,6 +453,17 @@ BwdScratch bwd_scratch(int B, int T, int H) {
 
 }  // namespace
 
+// The failure-detection test hook of wpt_debug_backward_fault.
+std::atomic<int> g_bwd_skip_key_tile{-1};
+std::atomic<unsigned long long> g_bwd_wait_ns{0};
+
+extern "C" int wpt_debug_backward_fault(int skip_key_tile, unsigned long long wait_ns) {
+  if (skip_key_tile < -1) return fail(WPT_ERR_INVALID, "skip_key_tile must be -1 (off) or a key tile index");
+  g_bwd_skip_key_tile.store(skip_key_tile);
+  g_bwd_wait_ns.store(wait_ns);
+  return WPT_OK;
+}
+
 extern "C" size_t wpt_attn_backward_scratch_bytes(int B, int T, int H, int C, int N) {
   if (B < 1 || T < 1 || H < 1 || H > 128 || C != 128 || N < 1) return 0;
   return static_cast<size_t>(bwd_scratch(B, T, H).total);
@@ -487,7 +542,12 @@ extern "C" int wpt_attn_backward(const void* q, const void* k, const void* v, in
   p.f32_grads = f32_grads ? 1 : 0;
   p.scale = scale;
   p.scale_log2 = scale * wpt::LOG2E;
-  if (p.qtiles > 65535 * 32 || B > 65535) return fail(WPT_ERR_UNSUPPORTED, "backward grid too large");
+  p.skip_key_tile = g_bwd_skip_key_tile.load();
+  p.wait_ns = g_bwd_wait_ns.load();
+  if (p.wait_ns == 0) p.wait_ns = wpt::WAIT_LIMIT_NS;
+  if (static_cast<int64_t>(p.qtiles) * B >= (int64_t(1) << 31) ||
+      static_cast<int64_t>(p.ktiles) * B >= (int64_t(1) << 31) || B > 65535)
+    return fail(WPT_ERR_UNSUPPORTED, "backward grid too large");
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   wpt::bwd_prep_kernel<<<dim3(p.qtiles, B), 128, 0, st>>>(p);
   cudaError_t e = cudaGetLastError();
@@ -501,10 +561,12 @@ extern "C" int wpt_attn_backward(const void* q, const void* k, const void* v, in
   static_assert(wpt::BwdQLayout::BYTES <= 232448, "backward query kernel shared memory exceeds 227 KB");
   if (int rc = allow_smem(wpt::bwd_kv_kernel, wpt::BwdKvLayout::BYTES)) return rc;
   if (int rc = allow_smem(wpt::bwd_q_kernel, wpt::BwdQLayout::BYTES)) return rc;
-  wpt::bwd_kv_kernel<<<dim3(p.ktiles, B), wpt::BWD_THREADS, wpt::BwdKvLayout::BYTES, st>>>(tq, tdo, tk, tv, p);
+  wpt::bwd_kv_kernel<<<static_cast<unsigned>(p.ktiles * B), wpt::BWD_THREADS, wpt::BwdKvLayout::BYTES, st>>>(
+      tq, tdo, tk, tv, p);
   e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "bwd_kv_kernel launch");
-  wpt::bwd_q_kernel<<<dim3(p.qtiles, B), wpt::BWD_THREADS, wpt::BwdQLayout::BYTES, st>>>(tq, tdo, tk, tv, p);
+  wpt::bwd_q_kernel<<<static_cast<unsigned>(p.qtiles * B), wpt::BWD_THREADS, wpt::BwdQLayout::BYTES, st>>>(
+      tq, tdo, tk, tv, p);
   e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "bwd_q_kernel launch");
   if (K > 0) {  // the chosen rows' share, added to the fp32 gradients above

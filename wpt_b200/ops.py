@@ -17,6 +17,8 @@ import torch
 from . import _lib
 
 LAUNCHES = [0]  # kernels this module has launched (read by bench.py around its timed region)
+# key tiles per key-stream CTA when set (WPT_B200_CHUNK, read once): overrides the split heuristic
+CHUNK_TILES = int(os.environ.get("WPT_B200_CHUNK", "0"))
 
 
 def _need_cuda(*tensors):
@@ -142,7 +144,7 @@ def _stream_plan(B, T, H, N, K, window, gather, sms, chunk_tiles=None):
         slots = min(N, window + TQ - 1) if window > 0 else N
     tiles = max(1, math.ceil(slots / 128))
     if chunk_tiles is None:
-        chunk_tiles = int(os.environ.get("WPT_B200_CHUNK", "0"))
+        chunk_tiles = CHUNK_TILES
     if not chunk_tiles and gather:
         # every query gathers exactly `tiles` tiles: its slots split so that
         # the grid is about one CTA per SM
@@ -152,6 +154,9 @@ def _stream_plan(B, T, H, N, K, window, gather, sms, chunk_tiles=None):
         # as streaming a few tiles), more when that still gives two CTAs per
         # SM for rows of the table's full length (most rows are shorter)
         chunk_tiles = max(min(16, tiles), 16 * math.ceil(tiles * groups / (2 * sms) / 16))
+        if tiles >= 64 and math.ceil(tiles / chunk_tiles) * groups < sms:
+            # a few long rows (a long-context decode): about one CTA per SM
+            chunk_tiles = max(2, math.ceil(tiles * groups / sms))
     chunk_tiles = max(1, min(int(chunk_tiles), tiles))
     return chunk_tiles, math.ceil(tiles / chunk_tiles)
 
@@ -172,7 +177,7 @@ def stream_forward(q, k, v, positions, scale, window=0, floor=None, idx=None, si
     if gather:
         idx = _rows(idx)
         K = idx.shape[-1]
-    if sink is not None:
+    if sink is not None and (sink.dtype != torch.float32 or not sink.is_contiguous()):
         sink = sink.float().contiguous()
     chunk_tiles, splits = _stream_plan(B, T, H, N, K, window, gather, sm_count(q.device), chunk_tiles)
     out = torch.empty_like(q)
