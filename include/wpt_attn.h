@@ -251,15 +251,19 @@ int wpt_accept(const float* scores, const int64_t* drafted, const float* q, cons
 
 /*
  * Ancestor masks of draft trees, the tree_bits argument of wpt_attn_prefill:
- * parents int64 (B, n), -1 for a root (a child of the last cache row) and
+ * parents int64 (B, n) at row stride parents_stride_b (0: one (n,) tree for
+ * every row), -1 for a root (a child of the last cache row) and
  * parents[b][i] < i otherwise; bits uint64 (B, n), bit j of bits[b][i] set
- * when node j is i or one of its ancestors. n <= 64. Computed on the device
- * so that verification needs no host synchronisation. Generalises the
- * chain of drafts that WPT verifies (packages/wpt-inference/src/
- * wpt_inference/__init__.py:207, parents[i] = i - 1) to a tree, with
- * dense_attention's visible-mask semantics (attention.py:74-82).
+ * when node j is i or one of its ancestors. n <= 64. With positions (B, n)
+ * int64 not NULL, also positions[b][i] = base[b] + i (node i's table row).
+ * Computed on the device so that verification needs no host
+ * synchronisation. Generalises the chain of drafts that WPT verifies
+ * (packages/wpt-inference/src/wpt_inference/__init__.py:207, parents[i] =
+ * i - 1) to a tree, with dense_attention's visible-mask semantics
+ * (attention.py:74-82).
  */
-int wpt_tree_bits(const int64_t* parents, int B, int n, uint64_t* bits, void* stream);
+int wpt_tree_bits(const int64_t* parents, int64_t parents_stride_b, int B, int n, uint64_t* bits,
+                  const int64_t* base, int64_t* positions, void* stream);
 
 /* Bytes of scratch wpt_accept needs for R rows of n drafts over V entries
  * (0 for a bad shape). */

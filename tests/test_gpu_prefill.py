@@ -126,16 +126,18 @@ def test_tree_verification_matches_oracle(wb):
 def test_tree_bits_on_the_device_match_the_ancestor_masks(wb):
     from wpt_b200 import ops
     parents = torch.tensor([[-1, 0, 0, 1, 1, 2, 4], [-1, 0, 1, 2, 3, 4, 5]])
-    bits = ops.tree_bits(parents.cuda(), 2).cpu()
+    bits, pos = ops.tree_bits(parents.cuda(), 2, torch.tensor([10, 500]).cuda())
+    bits = bits.cpu()
+    assert pos.cpu().tolist() == [[10 + i for i in range(7)], [500 + i for i in range(7)]]
     assert bits[0].tolist() == [0b1, 0b11, 0b101, 0b1011, 0b10011, 0b100101, 0b1010011]
     assert bits[1].tolist() == [(1 << (i + 1)) - 1 for i in range(7)]
-    chain = ops.tree_bits(torch.arange(64).cuda() - 1, 3).cpu()
+    chain = ops.tree_bits(torch.arange(64).cuda() - 1, 3)[0].cpu()
     assert chain.shape == (3, 64) and chain[0, 0].item() == 1 and chain[2, -1].item() == -1  # all 64 bits
     masks = oat.ancestors_mask(np.array([-1, 0, 0, 1, 1, 2, 4]))
     want = [(masks[i] * (1 << np.arange(7))).sum() for i in range(7)]
     assert bits[0].tolist() == [int(w) for w in want]
     # a parent that is not before its child ends that node's walk (no fault, no endless loop)
-    bad = ops.tree_bits(torch.tensor([-1, 2, 0]).cuda(), 1).cpu()
+    bad = ops.tree_bits(torch.tensor([-1, 2, 0]).cuda(), 1)[0].cpu()
     assert bad.tolist() == [[0b1, 0b10, 0b101]]
     assert wb.device_status() == 0
 

@@ -192,8 +192,7 @@ def tree_attention(q, k, v, cache_len, parents, scale, sink=None):
     _bf16_only(q, k, v)
     B, n, H, c = q.shape
     cache_len = torch.as_tensor(cache_len, dtype=torch.int64, device=q.device).reshape(-1).expand(B).contiguous()
-    bits = ops.tree_bits(torch.as_tensor(parents, dtype=torch.int64, device=q.device), B)
-    positions = cache_len[:, None] + torch.arange(n, device=q.device, dtype=torch.int64)
+    bits, positions = ops.tree_bits(torch.as_tensor(parents, dtype=torch.int64, device=q.device), B, cache_len)
     return ops.prefill_forward(q, k, v, positions, scale, tree_bits=bits, tree_base=cache_len, sink=sink)
 
 

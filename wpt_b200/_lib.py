@@ -31,7 +31,7 @@ SIGNATURES = {
     "wpt_attn_decode_noalloc": [_P, _P, _P, _I64, _I64, _I64, _I64, _P, _P, _P, _I, _P, _P, _P, _I, _I, _I, _I,
                                 _I, _I, _I, _I, _F, _P],
     "wpt_attn_merge": [_P, _P, _I, _I64, _I64, _I, _I, _P, _P, _P, _P],
-    "wpt_tree_bits": [_P, _I, _I, _P, _P],
+    "wpt_tree_bits": [_P, _I64, _I, _I, _P, _P, _P, _P],
     "wpt_attn_backward_scratch_bytes": [_I, _I, _I, _I, _I],
     "wpt_attn_backward": [_P, _P, _P, _I64, _I64, _I64, _I64, _P, _P, _P, _I, _P, _P, _P, _P, _P, _P, _P, _P,
                           _P, _I, _I, _I, _I, _I, _I, _I, _F, _P],

@@ -86,6 +86,12 @@ struct BwdParams {
   // the waits for it run out while nothing is in flight
   unsigned long long wait_ns;
   int skip_key_tile;
+  // the key-tile kernel's work split: each key tile's query tiles in
+  // kv_parts equal ranges of tile indices, one CTA each; with more than one
+  // part each CTA writes fp32 partial dK, dV (kv_part, (parts, B, N, 256):
+  // dK then dV) and bwd_kv_reduce_kernel adds them in part order
+  int kv_parts;
+  float* kv_part;
 };
 
 // Rows lo..hi query t of batch row b reads (hi < lo: none): hi = min(p, N - 1),
@@ -198,38 +204,6 @@ __device__ __forceinline__ bool bwd_tile_sees(const BwdParams& p, int b, int j, 
   return r.y >= r.x && r.x <= n0 + 127 && r.y >= n0;
 }
 
-// The first query tile at or after j that reads a key of the tile at n0
-// (qtiles when none). Warp-collective: the lanes test 32 tiles with one load
-// each and a ballot keeps the answer (base, mask) for the next calls, so a
-// key tile that most query tiles skip costs a load per 32 tiles, not one
-// per tile.
-struct BwdTileScan {
-  int base = -64;
-  uint32_t mask = 0;
-  __device__ __forceinline__ int next(const BwdParams& p, int b, int n0, int j) {
-    const int lane = threadIdx.x & 31;
-    while (j < p.qtiles) {
-      if (j >= base + 32) {
-        base = j & ~31;
-        const int jj = base + lane;
-        mask = __ballot_sync(0xffffffffu, jj < p.qtiles && bwd_tile_sees(p, b, jj, n0));
-      }
-      const uint32_t m = mask & (0xffffffffu << (j - base));
-      if (m) return base + __ffs(m) - 1;
-      j = base + 32;
-    }
-    return p.qtiles;
-  }
-};
-
-// Work order of the key-tile kernel: key tile 0 of every batch row first
-// (under a causal mask it is read by the most query tiles), then tile 1, ...
-__device__ __forceinline__ void bwd_kv_place(const BwdParams& p, int& b, int& n0) {
-  const int idx = static_cast<int>(blockIdx.x);
-  b = idx % p.B;
-  n0 = (idx / p.B) * 128;
-}
-
 // 64 fp32 values of one thread (a TMEM row's half) to global memory at dst,
 // as bf16 (f32 == 0) or fp32, times mul.
 __device__ __forceinline__ void bwd_store64(void* dst, const uint32_t (&v)[64], float mul, int f32) {
@@ -249,6 +223,93 @@ __device__ __forceinline__ void bwd_store64(void* dst, const uint32_t (&v)[64], 
       u.z = pack_bf16(__uint_as_float(v[8 * i + 4]) * mul, __uint_as_float(v[8 * i + 5]) * mul);
       u.w = pack_bf16(__uint_as_float(v[8 * i + 6]) * mul, __uint_as_float(v[8 * i + 7]) * mul);
       d[i] = u;
+    }
+  }
+}
+
+// The first query tile at or after j that reads a key of the tile at n0
+// (qtiles when none). Warp-collective: the lanes test 32 tiles with one load
+// each and a ballot keeps the answer (base, mask) for the next calls, so a
+// key tile that most query tiles skip costs a load per 32 tiles, not one
+// per tile.
+struct BwdTileScan {
+  int base = -64;
+  uint32_t mask = 0;
+  // the first query tile in [j, end) that reads the key tile at n0, or end
+  __device__ __forceinline__ int next(const BwdParams& p, int b, int n0, int j, int end) {
+    const int lane = threadIdx.x & 31;
+    while (j < end) {
+      if (j >= base + 32) {
+        base = j & ~31;
+        const int jj = base + lane;
+        mask = __ballot_sync(0xffffffffu, jj < end && bwd_tile_sees(p, b, jj, n0));
+      }
+      const uint32_t m = mask & (0xffffffffu << (j - base));
+      if (m) return min(end, base + __ffs(m) - 1);
+      j = base + 32;
+    }
+    return end;
+  }
+};
+
+// Work of one key-tile CTA: key tile n0 / 128 of batch row b, its query
+// tiles [jbeg, jend), part `part` of kv_parts. Order: key tile 0 (under a
+// causal mask the most read) of every part and batch row first, then tile 1, ...
+struct BwdKvUnit {
+  int b, n0, part, jbeg, jend;
+};
+__device__ __forceinline__ BwdKvUnit bwd_kv_place(const BwdParams& p) {
+  const int idx = static_cast<int>(blockIdx.x);
+  BwdKvUnit w;
+  const int per_tile = p.kv_parts * p.B;
+  w.n0 = (idx / per_tile) * 128;
+  const int rem = idx - (idx / per_tile) * per_tile;
+  w.part = rem / p.B;
+  w.b = rem - w.part * p.B;
+  w.jbeg = static_cast<int>(static_cast<int64_t>(w.part) * p.qtiles / p.kv_parts);
+  w.jend = static_cast<int>(static_cast<int64_t>(w.part + 1) * p.qtiles / p.kv_parts);
+  return w;
+}
+
+// Where a key-tile CTA's dK and dV rows go: the gradients themselves (one
+// part) or the unit's fp32 partials.
+__device__ __forceinline__ void bwd_kv_store(const BwdParams& p, const BwdKvUnit& w, int n, int g,
+                                             const uint32_t (&gv)[64], const uint32_t (&gk)[64]) {
+  if (p.kv_parts > 1) {
+    float* row = p.kv_part + ((static_cast<int64_t>(w.part) * p.B + w.b) * p.N + n) * 256 + 64 * g;
+    bwd_store64(row, gk, p.scale, 1);
+    bwd_store64(row + 128, gv, 1.f, 1);
+  } else {
+    const int64_t off = (static_cast<int64_t>(w.b) * p.N + n) * 128 + 64 * g;
+    const int es = p.f32_grads ? 4 : 2;
+    bwd_store64(static_cast<uint8_t*>(p.dv) + off * es, gv, 1.f, p.f32_grads);
+    bwd_store64(static_cast<uint8_t*>(p.dk) + off * es, gk, p.scale, p.f32_grads);
+  }
+}
+
+// dK, dV = the sum of the key-tile CTAs' fp32 partials, in part order
+// (deterministic), to bf16 or fp32. One thread per 4 values.
+__global__ void __launch_bounds__(256) bwd_kv_reduce_kernel(const float* __restrict__ part, int parts, int64_t rows,
+                                                            void* dk, void* dv, int f32) {
+  const int64_t n4 = rows * 64;  // 256 floats a row, 4 a thread
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n4;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    float4 acc = reinterpret_cast<const float4*>(part)[i];
+    for (int q = 1; q < parts; ++q) {
+      const float4 x = reinterpret_cast<const float4*>(part + q * rows * 256)[i];
+      acc.x += x.x;
+      acc.y += x.y;
+      acc.z += x.z;
+      acc.w += x.w;
+    }
+    const int64_t row = i / 64, c4 = i - row * 64;  // dK columns 0..127 (c4 < 32), then dV
+    const int64_t o = row * 128 + (c4 & 31) * 4;
+    void* dst = c4 < 32 ? dk : dv;
+    if (f32) {
+      *reinterpret_cast<float4*>(static_cast<float*>(dst) + o) = acc;
+    } else {
+      *reinterpret_cast<uint2*>(static_cast<__nv_bfloat16*>(dst) + o) =
+          make_uint2(pack_bf16(acc.x, acc.y), pack_bf16(acc.z, acc.w));
     }
   }
 }
@@ -282,8 +343,21 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
   uint64_t* acc_done = p_ready + 2;
   uint32_t* s_tmem = reinterpret_cast<uint32_t*>(smem + L::OFF_MISC);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  int b, n0;
-  bwd_kv_place(p, b, n0);
+  const BwdKvUnit w = bwd_kv_place(p);
+  const int b = w.b, n0 = w.n0, jbeg = w.jbeg, jend = w.jend;
+  {
+    // a unit no query tile of its range reads: zero gradients, no TMEM,
+    // no loads (every warp's scan gives the same answer)
+    BwdTileScan pre;
+    if (pre.next(p, b, n0, jbeg, jend) >= jend) {
+      const uint32_t zero[64] = {};
+      for (int r = threadIdx.x; r < 2 * 128; r += blockDim.x) {
+        const int n = n0 + (r >> 1);
+        if (n < p.N) bwd_kv_store(p, w, n, r & 1, zero, zero);
+      }
+      return;
+    }
+  }
 
   if (threadIdx.x == 0) {
     mbar_init(kv_full, 1);
@@ -326,7 +400,7 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
     }
     BwdTileScan scan;
     int u = 0;
-    for (int j = scan.next(p, b, n0, 0); ok && j < p.qtiles; j = scan.next(p, b, n0, j + 1), ++u) {
+    for (int j = scan.next(p, b, n0, jbeg, jend); ok && j < jend; j = scan.next(p, b, n0, j + 1, jend), ++u) {
       const int st = u % L::NSQ;
       if (lane == 0) {
         if (u >= L::NSQ) ok = mbar_wait(st_empty + st, ((u / L::NSQ) & 1) ^ 1, p.status);
@@ -374,18 +448,18 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
     };
     bool ok = wait(kv_full, 0);
     BwdTileScan scan;
-    int j = scan.next(p, b, n0, 0);
-    if (ok && j < p.qtiles && (ok = wait(st_full, 0))) {
+    int j = scan.next(p, b, n0, jbeg, jend);
+    if (ok && j < jend && (ok = wait(st_full, 0))) {
       tc_fence_after();
       issue_s(0, 0);
       issue_s(0, 1);
     }
-    for (int u = 0; ok && j < p.qtiles; ++u) {
-      const int jn = scan.next(p, b, n0, j + 1);
+    for (int u = 0; ok && j < jend; ++u) {
+      const int jn = scan.next(p, b, n0, j + 1, jend);
       if (!(ok = wait(p_ready, u & 1))) break;
       tc_fence_after();
       issue_acc(u, 0, u > 0 ? 1u : 0u);
-      if (jn < p.qtiles) {
+      if (jn < jend) {
         if (!(ok = wait(st_full + (u + 1) % L::NSQ, ((u + 1) / L::NSQ) & 1))) break;
         tc_fence_after();
         issue_s(u + 1, 0);
@@ -394,7 +468,7 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
       tc_fence_after();
       issue_acc(u, 1, 1u);
       mma_commit_warp(st_empty + u % L::NSQ);
-      if (jn < p.qtiles) issue_s(u + 1, 1);
+      if (jn < jend) issue_s(u + 1, 1);
       j = jn;
     }
     mma_commit_warp(acc_done);  // once every product above has completed
@@ -412,7 +486,7 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
     bool ok = true;
     BwdTileScan scan;
     int u = 0;
-    for (int j = scan.next(p, b, n0, 0); ok && j < p.qtiles; j = scan.next(p, b, n0, j + 1), ++u) {
+    for (int j = scan.next(p, b, n0, jbeg, jend); ok && j < jend; j = scan.next(p, b, n0, j + 1, jend), ++u) {
       const int st = u % L::NSQ;
       const float* lds = reinterpret_cast<const float*>(smem + L::OFF_ST + st * L::STAGE + 2 * L::TILE);
       // the columns (query rows 64 g + c) that see key n, by token (global
@@ -439,8 +513,7 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
 #pragma unroll
       for (int ch = 0; ch < 2; ++ch) {  // 32 columns at a time; a thread's writes only land on columns it has read
         uint32_t s[32], d[32];
-        tmem_ld32(lane_addr + 64 * g + 32 * ch, s);
-        tmem_ld32(lane_addr + 128 + 64 * g + 32 * ch, d);
+        tmem_ld32x2(lane_addr + 64 * g + 32 * ch, lane_addr + 128 + 64 * g + 32 * ch, s, d);
         uint32_t pk[16], dsk[16];
 #pragma unroll
         for (int i = 0; i < 16; ++i) {
@@ -482,12 +555,7 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
 #pragma unroll
       for (int i = 0; i < 64; ++i) gv[i] = gk[i] = 0u;
     }
-    if (ok && n < p.N) {
-      const int64_t off = (static_cast<int64_t>(b) * p.N + n) * 128 + 64 * g;
-      const int es = p.f32_grads ? 4 : 2;
-      bwd_store64(static_cast<uint8_t*>(p.dv) + off * es, gv, 1.f, p.f32_grads);
-      bwd_store64(static_cast<uint8_t*>(p.dk) + off * es, gk, p.scale, p.f32_grads);
-    }
+    if (ok && n < p.N) bwd_kv_store(p, w, n, g, gv, gk);
     tc_fence_before();
     __syncthreads();
   }
@@ -661,8 +729,7 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
         const int nb = (kt0 + i) * 128 + 64 * g + 32 * ch;  // these columns' first key
         const int a = bt.x - nb, z = bt.y - nb;            // visible columns a .. z
         uint32_t s[32], d[32];
-        tmem_ld32(lane_addr + 64 * g + 32 * ch, s);
-        tmem_ld32(lane_addr + 128 + 64 * g + 32 * ch, d);
+        tmem_ld32x2(lane_addr + 64 * g + 32 * ch, lane_addr + 128 + 64 * g + 32 * ch, s, d);
         uint32_t dsk[16];
 #pragma unroll
         for (int k2 = 0; k2 < 16; ++k2) {

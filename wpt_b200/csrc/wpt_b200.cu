@@ -435,19 +435,33 @@ extern "C" int wpt_attn_prefill(const void* q, const void* k, const void* v, int
 namespace {
 
 struct BwdScratch {
-  int64_t ld, ranges, bounds, sink_part, total;  // byte offsets, each 256-aligned
+  int64_t ld, ranges, bounds, sink_part, kv_part, total;  // byte offsets, each 256-aligned
+  int kv_parts;
 };
 
-BwdScratch bwd_scratch(int B, int T, int H) {
+// Parts per key tile of the key-tile kernel: enough CTAs for about two per
+// SM, since under a causal mask key tile 0 is read by every query tile and
+// the last one by a few, and the most-read tile sets the kernel's length.
+int bwd_kv_parts(int B, int N) {
+  int sms = 148;
+  current_device(&sms);
+  const int64_t units = static_cast<int64_t>(B) * ((N + 127) / 128);
+  const int64_t want = (2 * static_cast<int64_t>(sms) + units - 1) / units;
+  return static_cast<int>(want < 1 ? 1 : want > 8 ? 8 : want);
+}
+
+BwdScratch bwd_scratch(int B, int T, int H, int N) {
   const int TQ = 128 / H;
   const int64_t qtiles = (T + TQ - 1) / TQ;
   auto up = [](int64_t x) { return (x + 255) / 256 * 256; };
   BwdScratch s;
+  s.kv_parts = bwd_kv_parts(B, N);
   s.ld = 0;
   s.ranges = s.ld + up(static_cast<int64_t>(B) * qtiles * 256 * 4);
   s.bounds = s.ranges + up(static_cast<int64_t>(B) * qtiles * 8);
   s.sink_part = s.bounds + up(static_cast<int64_t>(B) * T * 8);
-  s.total = s.sink_part + up(static_cast<int64_t>(B) * qtiles * H * 4);
+  s.kv_part = s.sink_part + up(static_cast<int64_t>(B) * qtiles * H * 4);
+  s.total = s.kv_part + (s.kv_parts > 1 ? up(static_cast<int64_t>(s.kv_parts) * B * N * 256 * 4) : 0);
   return s;
 }
 
@@ -466,7 +480,7 @@ extern "C" int wpt_debug_backward_fault(int skip_key_tile, unsigned long long wa
 
 extern "C" size_t wpt_attn_backward_scratch_bytes(int B, int T, int H, int C, int N) {
   if (B < 1 || T < 1 || H < 1 || H > 128 || C != 128 || N < 1) return 0;
-  return static_cast<size_t>(bwd_scratch(B, T, H).total);
+  return static_cast<size_t>(bwd_scratch(B, T, H, N).total);
 }
 
 template <int NCOL>
@@ -513,7 +527,7 @@ extern "C" int wpt_attn_backward(const void* q, const void* k, const void* v, in
   }
   if (int rc = table_map(&tk, k, k_stride_b, k_stride_n, B, N, C)) return rc;
   if (int rc = table_map(&tv, v, v_stride_b, v_stride_n, B, N, C)) return rc;
-  const BwdScratch lay = bwd_scratch(B, T, H);
+  const BwdScratch lay = bwd_scratch(B, T, H, N);
   uint8_t* base = static_cast<uint8_t*>(scratch);
   wpt::BwdParams p;
   p.positions = positions;
@@ -542,11 +556,13 @@ extern "C" int wpt_attn_backward(const void* q, const void* k, const void* v, in
   p.f32_grads = f32_grads ? 1 : 0;
   p.scale = scale;
   p.scale_log2 = scale * wpt::LOG2E;
+  p.kv_parts = lay.kv_parts;
+  p.kv_part = reinterpret_cast<float*>(base + lay.kv_part);
   p.skip_key_tile = g_bwd_skip_key_tile.load();
   p.wait_ns = g_bwd_wait_ns.load();
   if (p.wait_ns == 0) p.wait_ns = wpt::WAIT_LIMIT_NS;
   if (static_cast<int64_t>(p.qtiles) * B >= (int64_t(1) << 31) ||
-      static_cast<int64_t>(p.ktiles) * B >= (int64_t(1) << 31) || B > 65535)
+      static_cast<int64_t>(p.ktiles) * B * p.kv_parts >= (int64_t(1) << 31) || B > 65535)
     return fail(WPT_ERR_UNSUPPORTED, "backward grid too large");
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   wpt::bwd_prep_kernel<<<dim3(p.qtiles, B), 128, 0, st>>>(p);
@@ -561,10 +577,20 @@ extern "C" int wpt_attn_backward(const void* q, const void* k, const void* v, in
   static_assert(wpt::BwdQLayout::BYTES <= 232448, "backward query kernel shared memory exceeds 227 KB");
   if (int rc = allow_smem(wpt::bwd_kv_kernel, wpt::BwdKvLayout::BYTES)) return rc;
   if (int rc = allow_smem(wpt::bwd_q_kernel, wpt::BwdQLayout::BYTES)) return rc;
-  wpt::bwd_kv_kernel<<<static_cast<unsigned>(p.ktiles * B), wpt::BWD_THREADS, wpt::BwdKvLayout::BYTES, st>>>(
-      tq, tdo, tk, tv, p);
+  wpt::bwd_kv_kernel<<<static_cast<unsigned>(static_cast<int64_t>(p.ktiles) * B * p.kv_parts), wpt::BWD_THREADS,
+                       wpt::BwdKvLayout::BYTES, st>>>(tq, tdo, tk, tv, p);
   e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "bwd_kv_kernel launch");
+  if (p.kv_parts > 1) {
+    int sms = 148;
+    current_device(&sms);
+    const int64_t n4 = static_cast<int64_t>(B) * N * 64;
+    const int blocks = static_cast<int>(std::min<int64_t>((n4 + 255) / 256, static_cast<int64_t>(sms) * 8));
+    wpt::bwd_kv_reduce_kernel<<<blocks, 256, 0, st>>>(p.kv_part, p.kv_parts, static_cast<int64_t>(B) * N, dk, dv,
+                                                      p.f32_grads);
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return cuda_fail(e, "bwd_kv_reduce_kernel launch");
+  }
   wpt::bwd_q_kernel<<<static_cast<unsigned>(p.qtiles * B), wpt::BWD_THREADS, wpt::BwdQLayout::BYTES, st>>>(
       tq, tdo, tk, tv, p);
   e = cudaGetLastError();
@@ -801,15 +827,18 @@ extern "C" int wpt_attn_topk(const void* q, const void* k, int64_t k_stride_b, i
   return WPT_OK;
 }
 
-extern "C" int wpt_tree_bits(const int64_t* parents, int B, int n, uint64_t* bits, void* stream) {
+extern "C" int wpt_tree_bits(const int64_t* parents, int64_t parents_stride_b, int B, int n, uint64_t* bits,
+                             const int64_t* base, int64_t* positions, void* stream) {
   if (B < 1 || n < 1) return fail(WPT_ERR_INVALID, "empty tree batch B=%d n=%d", B, n);
   if (n > 64) return fail(WPT_ERR_UNSUPPORTED, "a tree of %d nodes: the kernels take up to 64", n);
-  if (!parents || !bits) return fail(WPT_ERR_INVALID, "a required pointer is NULL");
+  if (!parents || !bits || (positions && !base)) return fail(WPT_ERR_INVALID, "a required pointer is NULL");
+  if (parents_stride_b != 0 && parents_stride_b < n)
+    return fail(WPT_ERR_INVALID, "parents_stride_b must be 0 (one tree for every row) or at least n");
   const int64_t total = static_cast<int64_t>(B) * n;
   const int64_t blocks = (total + 255) / 256;
   if (blocks >= (int64_t(1) << 31)) return fail(WPT_ERR_UNSUPPORTED, "too many tree rows");
   wpt::tree_bits_kernel<<<static_cast<unsigned>(blocks), 256, 0, static_cast<cudaStream_t>(stream)>>>(
-      parents, B, n, bits);
+      parents, parents_stride_b, B, n, bits, base, positions);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "tree_bits_kernel launch");
   return WPT_OK;

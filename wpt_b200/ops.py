@@ -154,8 +154,9 @@ def _stream_plan(B, T, H, N, K, window, gather, sms, chunk_tiles=None):
         # as streaming a few tiles), more when that still gives two CTAs per
         # SM for rows of the table's full length (most rows are shorter)
         chunk_tiles = max(min(16, tiles), 16 * math.ceil(tiles * groups / (2 * sms) / 16))
-        if tiles >= 64 and math.ceil(tiles / chunk_tiles) * groups < sms:
-            # a few long rows (a long-context decode): about one CTA per SM
+        if tiles >= 64 and 2 * math.ceil(tiles / chunk_tiles) * groups < sms:
+            # a few long rows (a shard of a long-context decode) that would
+            # leave most SMs idle: about one CTA per SM
             chunk_tiles = max(2, math.ceil(tiles * groups / sms))
     chunk_tiles = max(1, min(int(chunk_tiles), tiles))
     return chunk_tiles, math.ceil(tiles / chunk_tiles)
@@ -365,22 +366,28 @@ def to_bf16(x):
     return y
 
 
-def tree_bits(parents, B):
+def tree_bits(parents, B, base=None):
     """(n,) or (B, n) int64 parent indices on the GPU (-1 for a root,
-    parents[i] < i) -> (B, n) int64 ancestor masks: bit j of node i is set
-    when node j is i or one of its ancestors. One small kernel on the
-    current stream: no host synchronisation, so verification can be
-    captured in a CUDA graph. A parent that is not before its child ends
-    that node's walk (the mask then holds the nodes met so far)."""
+    parents[i] < i) -> ((B, n) int64 ancestor masks: bit j of node i is set
+    when node j is i or one of its ancestors; (B, n) positions base[b] + i
+    when base (B,) is given, else None). One small kernel on the current
+    stream: no host synchronisation, so verification can be captured in a
+    CUDA graph. A parent that is not before its child ends that node's walk
+    (the mask then holds the nodes met so far)."""
     n = parents.shape[-1]
     if n > 64:
         raise NotImplementedError(f"a tree of {n} nodes: the kernels take up to 64")
-    _need_cuda(parents)
-    par = parents.to(torch.int64).expand(B, n).contiguous()
+    _need_cuda(parents, base)
+    par = _rows(parents)
+    stride = 0 if par.dim() == 1 else n
+    if stride and par.shape != (B, n):
+        par = par.expand(B, n).contiguous()
     bits = torch.empty(B, n, dtype=torch.int64, device=par.device)
-    _lib.check(_lib.lib().wpt_tree_bits(_lib.ptr(par), B, n, _lib.ptr(bits), _lib.stream(par.device)))
+    positions = None if base is None else torch.empty(B, n, dtype=torch.int64, device=par.device)
+    _lib.check(_lib.lib().wpt_tree_bits(_lib.ptr(par), stride, B, n, _lib.ptr(bits), _lib.ptr(base),
+                                        _lib.ptr(positions), _lib.stream(par.device)))
     LAUNCHES[0] += 1
-    return bits
+    return bits, positions
 
 
 def accept(scores, drafted, q, uniforms, resample, temperature=1.0, top_k=None, lengths=None):
