@@ -265,6 +265,21 @@ int wpt_accept(const float* scores, const int64_t* drafted, const float* q, cons
 int wpt_tree_bits(const int64_t* parents, int64_t parents_stride_b, int B, int n, uint64_t* bits,
                   const int64_t* base, int64_t* positions, void* stream);
 
+/*
+ * The generation cache's entries write (packages/wpt-model/src/wpt_model/
+ * cache.py:110-128, Reading.everything's index put): row b's new entries
+ * src[b, j] for j < counts[b] go to dst[b, first[b] + j]; entries past a
+ * row's count are padding and are not written. One launch, no host
+ * synchronisation (the reference reads the table's size and the written
+ * rows back to the host first). Strides are in BYTES; rows of row_bytes
+ * (a multiple of 16, any dtype), 16-byte aligned bases and strides. A
+ * destination row at or past `capacity` is not written and sets the status
+ * word's shape bit (bit 1).
+ */
+int wpt_cache_append(const void* src, int64_t src_stride_b, int64_t src_stride_n, void* dst, int64_t dst_stride_b,
+                     int64_t dst_stride_n, const int64_t* first, const int64_t* counts, int B, int n, int row_bytes,
+                     int64_t capacity, void* stream);
+
 /* Bytes of scratch wpt_accept needs for R rows of n drafts over V entries
  * (0 for a bad shape). */
 size_t wpt_accept_scratch_bytes(int R, int n, int V);

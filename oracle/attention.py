@@ -13,6 +13,8 @@ the lines it follows (paths relative to the reference repository):
     sparse_attention  pytorch_kernels.py:149-153,171-187,213-217
     window_attention  packages/wpt-model/src/wpt_model/attention.py:85-107
     dense_attention   attention.py:74-82 (used for the tree-masked verification)
+    drafter_attention packages/wpt-model/src/wpt_model/drafter.py:141-151,
+                      its visible mask :189-195
 
 Differences from the reference that are deliberate and harmless:
   * arithmetic is float64 by default (the reference computes in float32);
@@ -245,3 +247,38 @@ def merge_partials(o, m, l, sink=None):
         total = np.logaddexp(total, sink)
     w = np.exp(lse_s - total[None])
     return np.sum(w[..., None] * np.asarray(o, np.float64), axis=0), total
+
+
+def dense_attention(q, k, v, sink, visible, scale, dtype=np.float64):
+    """attention.py:74-82: q (..., Q, H, c) over k, v (..., K, c), each query
+    reading the keys visible (..., Q, K) shows it, sink (H,) in each head's
+    denominator. Returns (out (..., Q, H, c), lse (..., Q, H))."""
+    q, k, v = (np.asarray(x, dtype) for x in (q, k, v))
+    z = np.einsum("...qhc,...kc->...qhk", q, k) * dtype(scale)
+    z = np.where(np.asarray(visible, bool)[..., :, None, :], z, NEG_INF)
+    l = np.logaddexp(_logsumexp(z), np.asarray(sink, dtype))
+    return np.einsum("...qhk,...kc->...qhc", np.exp(z - l[..., None]), v), l
+
+
+def drafter_visible(lengths, count, window):
+    """drafter.py:189-195: (R, count, count + window) bool over the table
+    [block; context]: every place reads the whole block, and context entry j
+    (position lengths - window + j) when it is not before the text and within
+    `window` tokens of the place (position lengths + i)."""
+    lengths = np.asarray(lengths, np.int64)
+    positions = lengths[:, None] + np.arange(count)[None]
+    context_positions = lengths[:, None] - window + np.arange(window)[None]
+    seen = (context_positions[:, None, :] >= 0) & (context_positions[:, None, :] > positions[..., None] - window)
+    return np.concatenate([np.ones((len(lengths), count, count), bool), seen], -1)
+
+
+def drafter_attention(q, block, context, sink, lengths, scale, dtype=np.float64):
+    """The drafter backbone's attention (drafter.py:141-151): q (R, count, H,
+    c), block (R, count, 2c) and context (R, window, 2c) entries (keys then
+    values), table [block; context] read through drafter_visible. Returns
+    (out, lse)."""
+    block, context = np.asarray(block, dtype), np.asarray(context, dtype)
+    c = block.shape[-1] // 2
+    table = np.concatenate([block, context], 1)
+    visible = drafter_visible(lengths, block.shape[1], context.shape[1])
+    return dense_attention(q, table[..., :c], table[..., c:], sink, visible, scale, dtype)

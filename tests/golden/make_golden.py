@@ -7,6 +7,8 @@ them:
     python tests/golden/make_golden.py --reference <the reference repository>
 
 What each fixture pins (paths relative to the reference repository):
+  cache_append.npz      the generation cache's entries table after ragged reads,
+                        through the reference's Rows/Reading (cache.py:54-134)
   grads.npz             gradients from the reference's autograd: exact attention
                         (pytorch_kernels.py:123-139), sparse attention with a
                         sink (:189-210), window_attention (attention.py:85-107)
@@ -153,6 +155,34 @@ def grads(at, pk):
                            dv=_np(v.grad), d_sink=_np(sink.grad))
     np.savez(os.path.join(HERE, "grads.npz"), **{f"{case}_{key}": value for case, d in cases.items()
                                                  for key, value in d.items()})
+
+
+def cache_append(root):
+    """The generation cache's entries of an exact layer through the
+    reference's own Rows/Reading (cache.py:54-134, Reading.everything
+    :110-128): a prompt of ragged counts, then two extends that grow the
+    table and write each row at its own length."""
+    from wpt_model.cache import Rows
+    from wpt_model.carry import Entries
+
+    class Layer:  # a module that passes on one entries table, as ExactAttention does
+        def passes_on(self):
+            return {"entries": Entries()}
+
+    g = torch.Generator().manual_seed(21)
+    B, width = 3, 16
+    layer, rows = Layer(), Rows(B, torch.device("cpu"))
+    steps = {}
+    for step, counts in enumerate(([5, 2, 7], [1, 4, 0], [9, 1, 3])):
+        counts = torch.tensor(counts)
+        n = int(counts.max())
+        new = torch.randn(B, n, width, generator=g)
+        reading = rows.reading(counts, undoable=False)
+        table = reading.everything(layer, "entries", new)
+        reading.finish()
+        steps.update({f"new{step}": _np(new).copy(), f"counts{step}": _np(counts).copy(),
+                      f"table{step}": _np(table).copy()})  # copies: later reads write the held table in place
+    np.savez(os.path.join(HERE, "cache_append.npz"), **steps)
 
 
 def window_small(at):
@@ -318,9 +348,10 @@ def main():
     at, pk, wi = _import_reference(args.reference)
     if args.only:
         for name in args.only.split(","):
-            {"grads": lambda: grads(at, pk)}[name]()
+            {"grads": lambda: grads(at, pk), "cache_append": lambda: cache_append(args.reference)}[name]()
         return
     grads(at, pk)
+    cache_append(args.reference)
     exact_small(pk)
     exact_generation(pk)
     sparse_small(pk)

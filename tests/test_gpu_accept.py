@@ -144,3 +144,21 @@ def test_temperature_scaling_is_ieee_division(wb, temperature):
     assert not differ.any(), (x[normal][differ][:8], got[normal][differ][:8], ref[normal][differ][:8])
     ulps = np.abs(got[~normal].view(np.int32).astype(np.int64) - ref[~normal].view(np.int32).astype(np.int64))
     assert ulps.max(initial=0) <= 1
+
+
+@pytest.mark.parametrize("V,temperature,top_k", [(65536, 1.0, None), (1000, 0.8, 40), (65536, 1.0, 1), (777, 1.3, None)])
+def test_sampling_without_drafts_matches_the_oracle(wb, V, temperature, top_k):
+    # the writer's plain sampling step (wpt_inference/__init__.py:173-182):
+    # the acceptance rule with no drafts draws every row's token from p_0
+    g = torch.Generator().manual_seed(V + (top_k or 0))
+    R = 16
+    scores = torch.randn(R, V, generator=g) * 2
+    resample = torch.rand(R, generator=g)
+    got = wb.sample(scores.cuda(), resample.cuda(), temperature, top_k)
+    assert wb.device_status() == 0
+    tokens, accepted = oa.accept(scores[:, None].numpy(), np.zeros((R, 0), np.int64), np.zeros((R, 0, V), np.float32),
+                                 np.zeros((R, 0), np.float32), resample.numpy(), temperature, top_k)
+    assert (accepted == 0).all()
+    assert np.array_equal(got.cpu().numpy(), tokens[:, 0])
+    if top_k == 1:
+        assert np.array_equal(got.cpu().numpy(), scores.argmax(-1).numpy())

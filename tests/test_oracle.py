@@ -181,3 +181,42 @@ def test_window_backward_matches_reference_autograd(gold):
                                         float(g["scale"]), int(g["window"]))
     for got, want in ((dq, g["dq"]), (dk, g["dk"]), (dv, g["dv"]), (ds, g["d_sink"])):
         assert np.abs(got - want).max() < 1e-4 * max(1.0, np.abs(want).max())
+
+
+def test_dense_attention_restatement_matches_the_tree_golden(gold):
+    # the tree golden was made by the reference's own dense_attention
+    # (attention.py:74-82) with a visible mask of the cache rows and each
+    # node's ancestors; the generic restatement gives the same outputs
+    d = gold("tree.npz")
+    q, k, v, sink = d["q"], d["k"], d["v"], d["sink"]
+    B, n = q.shape[:2]
+    parents = np.broadcast_to(d["parents"], (B, n))
+    for b in range(B):
+        L = int(np.broadcast_to(np.asarray(d["cache_len"]).reshape(-1), (B,))[b])
+        visible = np.concatenate([np.ones((n, L), bool), oat.ancestors_mask(parents[b])], 1)
+        out, _ = oat.dense_attention(q[b], k[b, :L + n], v[b, :L + n], sink, visible, float(d["scale"]))
+        assert np.abs(out - d["out_tree"][b]).max() < 1e-5
+
+
+def test_drafter_visible_mask_follows_the_reference_formula():
+    # place i reads the whole block, and context entry j when j > i (within
+    # the window) and its position is not before the text (j >= window - L)
+    vis = oat.drafter_visible([3, 200], 4, 8)
+    assert vis.shape == (2, 4, 12)
+    assert vis[:, :, :4].all()
+    for r, L in enumerate([3, 200]):
+        for i in range(4):
+            for j in range(8):
+                assert vis[r, i, 4 + j] == (j > i and j >= 8 - L)
+
+
+def test_cache_append_restatement_matches_the_reference_rows(gold):
+    from oracle import cache as oc
+    d = gold("cache_append.npz")
+    held, lengths = None, np.zeros(3, np.int64)
+    for step in range(3):
+        counts = d[f"counts{step}"]
+        held, table = oc.cache_append(held, d[f"new{step}"], lengths, counts)
+        assert table.shape == d[f"table{step}"].shape
+        assert np.array_equal(table, d[f"table{step}"])
+        lengths = lengths + counts

@@ -13,6 +13,7 @@ makes WPT's exact and sparse layers run on these kernels. It exposes
     exact_attention(q, k, v, positions, scale, top_k, window) -> (out, chosen)
     sparse_attention(q, k, v, sink, idx, positions, scale, window) -> out
     window_attention(q, k, v, sink, positions, scale)   (attention.py:85-107)
+    drafter_attention(q, block, context, sink, lengths, scale)   (drafter.py:141-151)
     tree_attention(q, k, v, cache_len, parents, scale, sink=None) -> (out, lse)
     accept(scores, drafted, q, uniforms, resample, temperature, top_k)
 
@@ -146,7 +147,11 @@ def sparse_attention(q, k, v, sink, idx, positions, scale, window):
 
 # ----------------------------------------------------------- window attention
 
-class _Window(torch.autograd.Function):
+class _Range(torch.autograd.Function):
+    """Attention of each query over the contiguous table rows max(0, p -
+    window + 1, floor) .. min(p, N - 1), p its entry of `rows`, with the
+    sink; backward by the library's kernels."""
+
     @staticmethod
     def forward(ctx, q, k, v, sink, rows, floor, scale, W):
         out, lse = ops.attention_forward(q, k, v, rows, scale, window=W, floor=floor, sink=sink)
@@ -160,6 +165,12 @@ class _Window(torch.autograd.Function):
         dq, dk, dv, d_sink = ops.attention_backward(q, k, v, rows, out, lse, d_out, ctx.scale, window=ctx.window,
                                                     floor=floor, sink=sink)
         return dq, dk, dv, None if d_sink is None else d_sink.to(sink.dtype), None, None, None, None
+
+
+def _range_attention(q, k, v, sink, rows, floor, scale, W):
+    if not _needs_grad(q, k, v, sink):
+        return ops.attention_forward(q, k, v, rows, scale, window=W, floor=floor, sink=sink)[0]
+    return _Range.apply(q, k, v, sink, rows, floor, scale, W)
 
 
 def window_attention(q, k, v, sink, positions, scale, window=None):
@@ -176,9 +187,33 @@ def window_attention(q, k, v, sink, positions, scale, window=None):
     t = torch.arange(T, device=q.device, dtype=torch.int64)
     rows = (t + W - 1).expand(B, T).contiguous()  # each query's own row in the table
     floor = rows - positions  # the row of position 0: rows before it are before the text
-    if not _needs_grad(q, k, v, sink):
-        return ops.attention_forward(q, k, v, rows, scale, window=W, floor=floor, sink=sink)[0]
-    return _Window.apply(q, k, v, sink, rows, floor, scale, W)
+    return _range_attention(q, k, v, sink, rows, floor, scale, W)
+
+
+# ---------------------------------------------------------- drafter attention
+
+def drafter_attention(q, block, context, sink, lengths, scale):
+    """The drafter backbone's attention (packages/wpt-model/src/wpt_model/
+    drafter.py:141-151): q (R, count, H, c) for the count places
+    of R blocks at positions lengths[r] + i; block (R, count, 2c) the places'
+    entries and context (R, W, 2c) the injected context's, at positions
+    lengths[r] - W + j (keys then values in each). Place i reads the whole
+    block (both directions) and the context entries within W tokens of it
+    that are not before the text (the visible mask of drafter.py:189-195),
+    with the sink in each head's denominator. Returns (R, count, H, c).
+
+    With the table ordered [context; block], place i's rows are one
+    contiguous range, max(i + 1, W - lengths[r]) .. W + count - 1, so the
+    range kernels compute it (forward and backward)."""
+    _bf16_only(q, block, context)
+    R, count, H, c = q.shape
+    W = context.shape[1]
+    table = torch.cat([context, block], 1)
+    lengths = torch.as_tensor(lengths, dtype=torch.int64, device=q.device).reshape(R, 1)
+    i = torch.arange(count, device=q.device, dtype=torch.int64)
+    rows = torch.full((R, count), W + count - 1, dtype=torch.int64, device=q.device)
+    floor = torch.maximum(i[None] + 1, W - lengths).contiguous()
+    return _range_attention(q, table[..., :c], table[..., c:], sink, rows, floor, scale, 0)
 
 
 # ----------------------------------------------------------- tree attention
@@ -206,6 +241,35 @@ def accept(scores, drafted, q, uniforms, resample, temperature=1.0, top_k=None, 
     last token's draw (inverse CDF). Returns (tokens (R, n + 1), -1 padded;
     accepted (R,))."""
     return ops.accept(scores, drafted, q, uniforms, resample, temperature, top_k, lengths)
+
+
+def sample(scores, resample, temperature=1.0, top_k=None):
+    """The writer's sampling step without drafts (wpt_inference/__init__.py:
+    173-182: softmax of the top_k-masked scores / temperature, then a draw;
+    SURVEY F3's sampling, the output head's product left to the caller):
+    scores (R, V) fp32 logits, resample (R,) the draws, each turned into a
+    token by inverse CDF (the first index whose float64 running sum of the
+    probabilities exceeds resample[i] times their total). top_k 1 is argmax.
+    Returns (R,) int64 tokens. The acceptance kernels with no drafts."""
+    R, V = scores.shape
+    empty = scores.new_empty(R, 0, V)
+    tokens, _ = ops.accept(scores[:, None], torch.empty(R, 0, dtype=torch.int64, device=scores.device), empty,
+                           scores.new_empty(R, 0), resample, temperature, top_k)
+    return tokens[:, 0]
+
+
+# ------------------------------------------------------------ cache append
+
+def cache_append(held, new, first, counts, need=None):
+    """The generation cache's entries write (packages/wpt-model/src/
+    wpt_model/cache.py:110-128, Reading.everything): row b's new
+    entries new[b, :counts[b]] are written after its first[b] earlier ones,
+    the table growing as the reference's does. Returns (held, held[:, :need]).
+    Given need (max_b(first[b] + counts[b]), which a caller keeping its own
+    count of each row's tokens knows), the call is one kernel with no host
+    synchronisation, where the reference reads the size and the written
+    rows back to the host on every exact layer of every step."""
+    return ops.cache_append(held, new, first, counts, need)
 
 
 # ------------------------------------------------------------- installation
@@ -237,6 +301,6 @@ def install(kernels, attention=None, device=None, check=True):
     return me
 
 
-__all__ = ["install", "accept", "NAME", "WINDOW", "chosen_columns", "exact_attention", "sparse_attention", "window_attention",
+__all__ = ["install", "drafter_attention", "cache_append", "sample", "accept", "NAME", "WINDOW", "chosen_columns", "exact_attention", "sparse_attention", "window_attention",
            "tree_attention",
            "forward_with_lse", "device_status", "LibraryMissing"]

@@ -37,6 +37,7 @@ SIGNATURES = {
                           _P, _I, _I, _I, _I, _I, _I, _I, _F, _P],
     "wpt_f32_to_bf16": [_P, _I64, _P, _P],
     "wpt_debug_backward_fault": [_I, ctypes.c_ulonglong],
+    "wpt_cache_append": [_P, _I64, _I64, _P, _I64, _I64, _P, _P, _I, _I, _I, _I64, _P],
     "wpt_attn_merge_groups": [_P, _I, _I, _I64, _I64, _I, _I, _P, _P, _P, _P],
 }
 

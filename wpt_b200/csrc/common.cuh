@@ -412,6 +412,20 @@ __device__ __forceinline__ bool named_barrier_and(int id, int count, bool flag) 
   return out != 0;
 }
 
+// Named barrier over `count` threads that also ORs a flag across them.
+__device__ __forceinline__ bool named_barrier_or(int id, int count, bool flag) {
+  uint32_t out;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.u32 p, %1, 0;\n\t"
+      "barrier.red.or.pred q, %2, %3, p;\n\t"
+      "selp.u32 %0, 1, 0, q;\n\t}\n"
+      : "=r"(out)
+      : "r"(flag ? 1u : 0u), "r"(id), "r"(count)
+      : "memory");
+  return out != 0;
+}
+
 // Named barrier over `count` threads (a multiple of 32) of this CTA.
 __device__ __forceinline__ void named_barrier(int id, int count) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");

@@ -419,6 +419,9 @@ __global__ void __launch_bounds__(STREAM_THREADS, 1)
       qlo_r[tq] = tq < TQg ? s_qlo[tq] : 1;
       qhi_r[tq] = tq < TQg ? s_qhi[tq] : 0;
     }
+    float mreg[NCOL];  // the columns' running maxima, as s_m holds them
+#pragma unroll
+    for (int c = 0; c < NCOL; ++c) mreg[c] = -INFINITY;
     bool ok = true;
     for (int j = 0; j < ntiles; ++j) {
       const int st = j % STAGES;
@@ -461,47 +464,60 @@ __global__ void __launch_bounds__(STREAM_THREADS, 1)
       }
 #pragma unroll
       for (int c = 0; c < NCOL; ++c) s[c] = ((vis >> c) & 1ull) ? s[c] * sl2 : -INFINITY;
-      // per-column maximum over the tile's 128 slots
+      // Lazy maximum: a column's running maximum (mreg, the copy of s_m) is
+      // raised only when a score exceeds it by more than 8 (base 2), so most
+      // tiles need no reduction over their 128 slots: one barrier ORs "some
+      // score of mine exceeds its column's maximum + 8" (or "my wait failed")
+      // and only then do the maxima, the rescale and the agreement on `ok`
+      // run, as below.
+      bool raise = false;
 #pragma unroll
-      for (int c32 = 0; c32 < (NCOL + 31) / 32; ++c32) {
-        float tmp[32];
+      for (int c = 0; c < NCOL; ++c) raise |= s[c] > mreg[c] + 8.f;
+      float areg[NCOL];
 #pragma unroll
-        for (int c = 0; c < 32; ++c) tmp[c] = (c32 * 32 + c < NCOL) ? s[(c32 * 32 + c) % NCOL] : -INFINITY;
-        const float m = transpose_reduce32(tmp, MaxOp());
-        if (c32 * 32 + lane < NCOL) s_red[warp * 64 + c32 * 32 + lane] = m;
-      }
-      ok = named_barrier_and(1, 128, ok);
-      if (!ok) break;
-      if (r < NCOL) {
-        const float tmax = fmaxf(fmaxf(s_red[r], s_red[64 + r]), fmaxf(s_red[128 + r], s_red[192 + r]));
-        const float mo = s_m[r];
-        float a = 1.f;
-        if (tmax > mo + 8.f) {
-          a = fast_exp2(mo - tmax);
-          s_m[r] = tmax;
-        }
-        s_alpha[r] = a;
-      }
-      named_barrier(1, 128);
-      float mreg[NCOL], areg[NCOL];
-#pragma unroll
-      for (int c4 = 0; c4 < NCOL / 4; ++c4) {
-        const float4 m4 = reinterpret_cast<const float4*>(s_m)[c4];
-        const float4 a4 = reinterpret_cast<const float4*>(s_alpha)[c4];
-        mreg[4 * c4] = m4.x;
-        mreg[4 * c4 + 1] = m4.y;
-        mreg[4 * c4 + 2] = m4.z;
-        mreg[4 * c4 + 3] = m4.w;
-        areg[4 * c4] = a4.x;
-        areg[4 * c4 + 1] = a4.y;
-        areg[4 * c4 + 2] = a4.z;
-        areg[4 * c4 + 3] = a4.w;
-      }
+      for (int c = 0; c < NCOL; ++c) areg[c] = 1.f;
       bool any = false;
+      if (named_barrier_or(1, 128, raise || !ok)) {
+        // per-column maximum over the tile's 128 slots
 #pragma unroll
-      for (int c = 0; c < NCOL; ++c) {
-        lp[c] *= areg[c];
-        any |= areg[c] != 1.f;
+        for (int c32 = 0; c32 < (NCOL + 31) / 32; ++c32) {
+          float tmp[32];
+#pragma unroll
+          for (int c = 0; c < 32; ++c) tmp[c] = (c32 * 32 + c < NCOL) ? s[(c32 * 32 + c) % NCOL] : -INFINITY;
+          const float m = transpose_reduce32(tmp, MaxOp());
+          if (c32 * 32 + lane < NCOL) s_red[warp * 64 + c32 * 32 + lane] = m;
+        }
+        ok = named_barrier_and(1, 128, ok);
+        if (!ok) break;
+        if (r < NCOL) {
+          const float tmax = fmaxf(fmaxf(s_red[r], s_red[64 + r]), fmaxf(s_red[128 + r], s_red[192 + r]));
+          const float mo = s_m[r];
+          float a = 1.f;
+          if (tmax > mo + 8.f) {
+            a = fast_exp2(mo - tmax);
+            s_m[r] = tmax;
+          }
+          s_alpha[r] = a;
+        }
+        named_barrier(1, 128);
+#pragma unroll
+        for (int c4 = 0; c4 < NCOL / 4; ++c4) {
+          const float4 m4 = reinterpret_cast<const float4*>(s_m)[c4];
+          const float4 a4 = reinterpret_cast<const float4*>(s_alpha)[c4];
+          mreg[4 * c4] = m4.x;
+          mreg[4 * c4 + 1] = m4.y;
+          mreg[4 * c4 + 2] = m4.z;
+          mreg[4 * c4 + 3] = m4.w;
+          areg[4 * c4] = a4.x;
+          areg[4 * c4 + 1] = a4.y;
+          areg[4 * c4 + 2] = a4.z;
+          areg[4 * c4 + 3] = a4.w;
+        }
+#pragma unroll
+        for (int c = 0; c < NCOL; ++c) {
+          lp[c] *= areg[c];
+          any |= areg[c] != 1.f;
+        }
       }
       if (any && j > 0) {  // every thread read the same alphas: uniform
         // (a failed wait skips the rescale; the next tile's barrier stops every warp)

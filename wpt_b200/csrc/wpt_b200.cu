@@ -14,6 +14,7 @@
 #include "../../include/wpt_attn.h"
 #include "accept.cuh"
 #include "backward.cuh"
+#include "cache.cuh"
 #include "common.cuh"
 #include "merge.cuh"
 #include "prefill.cuh"
@@ -841,6 +842,28 @@ extern "C" int wpt_tree_bits(const int64_t* parents, int64_t parents_stride_b, i
       parents, parents_stride_b, B, n, bits, base, positions);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "tree_bits_kernel launch");
+  return WPT_OK;
+}
+
+extern "C" int wpt_cache_append(const void* src, int64_t src_stride_b, int64_t src_stride_n, void* dst,
+                                int64_t dst_stride_b, int64_t dst_stride_n, const int64_t* first,
+                                const int64_t* counts, int B, int n, int row_bytes, int64_t capacity, void* stream) {
+  if (B < 0 || n < 0 || row_bytes < 0 || capacity < 0) return fail(WPT_ERR_INVALID, "bad cache_append shape");
+  if (B == 0 || n == 0 || row_bytes == 0) return WPT_OK;
+  if (!src || !dst || !first || !counts) return fail(WPT_ERR_INVALID, "a required pointer is NULL");
+  if (row_bytes % 16 || src_stride_b % 16 || src_stride_n % 16 || dst_stride_b % 16 || dst_stride_n % 16 ||
+      !aligned16(src) || !aligned16(dst))
+    return fail(WPT_ERR_INVALID, "cache_append copies 16-byte units: rows, strides and bases must be 16-byte multiples");
+  unsigned* status = nullptr;
+  if (int rc = status_word(&status)) return rc;
+  const int64_t warps = static_cast<int64_t>(B) * n;
+  const int64_t blocks = (warps + 7) / 8;
+  if (blocks >= (int64_t(1) << 31)) return fail(WPT_ERR_UNSUPPORTED, "too many rows to append");
+  wpt::cache_append_kernel<<<static_cast<unsigned>(blocks), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const uint8_t*>(src), src_stride_b, src_stride_n, static_cast<uint8_t*>(dst), dst_stride_b,
+      dst_stride_n, first, counts, B, n, row_bytes, capacity, status);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "cache_append_kernel launch");
   return WPT_OK;
 }
 

@@ -154,10 +154,6 @@ def _stream_plan(B, T, H, N, K, window, gather, sms, chunk_tiles=None):
         # as streaming a few tiles), more when that still gives two CTAs per
         # SM for rows of the table's full length (most rows are shorter)
         chunk_tiles = max(min(16, tiles), 16 * math.ceil(tiles * groups / (2 * sms) / 16))
-        if tiles >= 64 and 2 * math.ceil(tiles / chunk_tiles) * groups < sms:
-            # a few long rows (a shard of a long-context decode) that would
-            # leave most SMs idle: about one CTA per SM
-            chunk_tiles = max(2, math.ceil(tiles * groups / sms))
     chunk_tiles = max(1, min(int(chunk_tiles), tiles))
     return chunk_tiles, math.ceil(tiles / chunk_tiles)
 
@@ -364,6 +360,39 @@ def to_bf16(x):
     _lib.check(_lib.lib().wpt_f32_to_bf16(_lib.ptr(x), x.numel(), _lib.ptr(y), _lib.stream(x.device)))
     LAUNCHES[0] += 1
     return y
+
+
+def cache_append(held, new, first, counts, need=None):
+    """The generation cache's entries write (cache.py:110-128): row b's new
+    entries new[b, :counts[b]] go to rows first[b] .. of the held table
+    (B, capacity, ...), grown to max(need, 2 * capacity) rows (zeros) when
+    `need` rows do not fit, as the reference grows it. Returns (held, the
+    first `need` rows of it). need = max_b(first[b] + counts[b]) is what the
+    reference reads back to the host; a caller that knows it (its own count
+    of each row's tokens) passes it, and the call then launches one kernel
+    and synchronises nothing."""
+    _need_cuda(new, first, counts)
+    B, n = new.shape[:2]
+    first, counts = _rows(first), _rows(counts)
+    if need is None:
+        need = int((first + counts).max()) if B else 0  # the reference's own host read
+    if held is None:
+        held = new.new_zeros((B, 0) + tuple(new.shape[2:]))
+    cap = held.shape[1]
+    if need > cap:
+        held = torch.cat([held, held.new_zeros((B, max(need, 2 * cap) - cap) + tuple(held.shape[2:]))], 1)
+    held = held.to(new.dtype)
+    if B and n:
+        es = new.element_size()
+        row_bytes = es * math.prod(new.shape[2:])
+        if new.stride(-1) != 1 or (new.dim() > 3 and not new[0, 0].is_contiguous()):
+            new = new.contiguous()
+        _lib.check(_lib.lib().wpt_cache_append(
+            _lib.ptr(new), new.stride(0) * es, new.stride(1) * es, _lib.ptr(held), held.stride(0) * es,
+            held.stride(1) * es, _lib.ptr(first), _lib.ptr(counts), B, n, row_bytes, held.shape[1],
+            _lib.stream(new.device)))
+        LAUNCHES[0] += 1
+    return held, held[:, :need]
 
 
 def tree_bits(parents, B, base=None):
