@@ -27,6 +27,9 @@ What each fixture pins (paths relative to the reference repository):
                         rows; a strided subset of row 0's queries is stored
   tree.npz              attention.dense_attention with an ancestor mask
                         (attention.py:74-82), and exact_attention for a chain
+  drafter.npz           the drafter backbone's attention: Drafter.backbone's
+                        visible mask and dense_attention call (drafter.py:141-151,
+                        179-204) on a tiny random model
   accept_*.npz          wpt_inference.Writer._speculate (__init__.py:196-233)
                         with a fake model and drafter, torch.rand and
                         torch.multinomial replaced by explicit draws
@@ -183,6 +186,49 @@ def cache_append(root):
         steps.update({f"new{step}": _np(new).copy(), f"counts{step}": _np(counts).copy(),
                       f"table{step}": _np(table).copy()})  # copies: later reads write the held table in place
     np.savez(os.path.join(HERE, "cache_append.npz"), **steps)
+
+
+def drafter():
+    """The drafter backbone's attention through the reference's own
+    Drafter.backbone (drafter.py:179-204: the visible mask of :189-195, each
+    layer's DrafterLayer.attend of :141-151) on a tiny random model on the
+    CPU: what its dense_attention receives (queries, the [block; context]
+    table's keys and values, sink, visible mask, scale) and returns, for the
+    first layer call. Contexts partly before the text included."""
+    from types import SimpleNamespace
+
+    import torch.nn as nn
+    from wpt_model import drafter as dr
+    from wpt_model.config import ModelConfig
+
+    torch.manual_seed(31)
+    config = ModelConfig(vocab_size=64, block_size=16, window_layers=1, sparse_groups=1, sparse_layers=1,
+                         d_model=32, attention_heads=4, attention_head_dim=64, n_experts=4, top_k=2,
+                         expert_width=16, latent_width=16, shared_width=32, engram_layers=(), engram_order=2,
+                         engram_heads=1, engram_dim=8, engram_table_size=97, residual_groups=2)
+    drafter = dr.Drafter(config, dr.DrafterConfig(features=(1,), layers=1, block=4, markov_rank=4)).eval()
+    model = SimpleNamespace(embedding=nn.Embedding(config.vocab_size, config.d_model),
+                            head=nn.Linear(config.d_model, config.vocab_size, bias=False))
+    calls = []
+    inner = dr.dense_attention
+
+    def recording(q, k, v, sink, visible, scale):
+        out = inner(q, k, v, sink, visible, scale)
+        calls.append({"q": _np(q).copy(), "k": _np(k).copy(), "v": _np(v).copy(), "sink": _np(sink).copy(),
+                      "visible": _np(visible).copy(), "scale": np.float64(scale), "out": _np(out).copy()})
+        return out
+
+    lengths = torch.tensor([3, 50, 127, 128, 500])
+    R, count = len(lengths), 4
+    context = torch.randn(R, dr.WINDOW, config.d_model)
+    anchors = torch.randint(0, config.vocab_size, (R,))
+    dr.dense_attention = recording
+    try:
+        with torch.no_grad():
+            drafter.backbone(model, context, lengths, anchors, count)
+    finally:
+        dr.dense_attention = inner
+    np.savez(os.path.join(HERE, "drafter.npz"), lengths=_np(lengths), window=np.int64(dr.WINDOW), **calls[0])
 
 
 def window_small(at):
@@ -348,10 +394,12 @@ def main():
     at, pk, wi = _import_reference(args.reference)
     if args.only:
         for name in args.only.split(","):
-            {"grads": lambda: grads(at, pk), "cache_append": lambda: cache_append(args.reference)}[name]()
+            {"grads": lambda: grads(at, pk), "cache_append": lambda: cache_append(args.reference),
+             "drafter": drafter}[name]()
         return
     grads(at, pk)
     cache_append(args.reference)
+    drafter()
     exact_small(pk)
     exact_generation(pk)
     sparse_small(pk)

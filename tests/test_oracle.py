@@ -210,6 +210,19 @@ def test_drafter_visible_mask_follows_the_reference_formula():
                 assert vis[r, i, 4 + j] == (j > i and j >= 8 - L)
 
 
+def test_drafter_attention_restatement_matches_the_reference_backbone(gold):
+    # drafter.npz: the reference's own Drafter.backbone, its first layer's
+    # dense_attention call recorded (mask, table, output)
+    d = gold("drafter.npz")
+    lengths, W = d["lengths"], int(d["window"])
+    count = d["q"].shape[1]
+    assert np.array_equal(oat.drafter_visible(lengths, count, W), d["visible"])
+    block = np.concatenate([d["k"][:, :count], d["v"][:, :count]], -1)
+    context = np.concatenate([d["k"][:, count:], d["v"][:, count:]], -1)
+    out, _ = oat.drafter_attention(d["q"], block, context, d["sink"], lengths, float(d["scale"]))
+    assert np.abs(out - d["out"]).max() < 1e-5
+
+
 def test_cache_append_restatement_matches_the_reference_rows(gold):
     from oracle import cache as oc
     d = gold("cache_append.npz")
