@@ -684,6 +684,11 @@ def profile_case(args):
         def fn():
             _, chosen = wpt_b200.exact_attention(q, k, v, pos, C ** -0.5, 1024, 128)
             wpt_b200.sparse_attention(q, k, v, sink, chosen, pos, C ** -0.5, 1024)
+    elif args.case == "verify":  # config 4's tree verification on B rows (16 nodes over 8192 cached keys)
+        t4, q4, cl, parents, _ = config4_inputs(device, 0)
+        t4, q4, cl = t4[:B].contiguous(), q4[:B].contiguous(), cl[:B].contiguous()
+        par4 = torch.tensor(parents, device=device)
+        fn = lambda: wpt_b200.tree_attention(q4, t4[..., :C], t4[..., C:], cl, par4, C ** -0.5)  # noqa: E731
     elif args.case == "accept":  # config 4's acceptance on B rows, stochastic then greedy
         R, n, V = B, 16, 65536
         ga = torch.Generator(device=device).manual_seed(4)
@@ -730,7 +735,8 @@ def main():
     parser.add_argument("--no-secondary", action="store_true")
     parser.add_argument("--e2e-steps", type=int, default=10)
     parser.add_argument("--case", default=None,
-                        help="profile one path: prefill, window, decode, select (A4 + A5) or accept")
+                        help="profile one path: prefill, window, decode, select (A4 + A5), verify, accept, "
+                             "backward; bars (the Triton form) or config5 (end-to-end decode)")
     parser.add_argument("--case-batch", type=int, default=4)
     args = parser.parse_args()
     if args.case:

@@ -92,7 +92,12 @@ int wpt_attn_prefill(const void* q, const void* k, const void* v, int64_t k_stri
  *                chunk_tiles * 128 and chunk s goes to split s; rows past
  *                splits * chunk_tiles * 128 are not read, so splits must
  *                cover the longest row. splits > 1 needs part_o
- *                (splits, B*T*H, C) and part_lse (splits, B*T*H) fp32 scratch.
+ *                (splits, B*T*H, C) and part_lse (splits, B*T*H) fp32 scratch,
+ *                or both NULL with 2 to 8 splits: cluster mode, where each
+ *                group's splits run as one thread-block cluster and combine
+ *                in shared memory (no scratch, no second kernel). Cluster
+ *                mode suits grids of one wave (groups * splits at most the
+ *                SM count): a cluster holds its SMs until its last split ends.
  *   out == lse == NULL with splits > 1: the call stops at the partials
  *                (each split's output normalised by its own sum, and the
  *                natural log of that sum; no sink), for a caller that merges
@@ -208,6 +213,16 @@ size_t wpt_attn_backward_scratch_bytes(int B, int T, int H, int C, int N);
 /* y[i] = bf16(x[i]) (round to nearest even) for n fp32 values, n a multiple
  * of 4, x 16-byte and y 8-byte aligned. */
 int wpt_f32_to_bf16(const float* x, int64_t n, void* y, void* stream);
+
+/*
+ * The same merge without a sink, its result kept as a partial: out_o
+ * (rows, C) fp32, the splits' output normalised by their common sum, and
+ * out_lse (rows,) its natural log. Several GPUs that each hold a share of a
+ * long row's keys merge their own splits this way, so that one small
+ * partial per GPU is all they exchange.
+ */
+int wpt_attn_merge_partial(const float* part_o, const float* part_lse, int splits, int64_t rows, int64_t split_stride,
+                           int C, float* out_o, float* out_lse, void* stream);
 
 /*
  * The same merge over partials gathered from several places (the GPUs that

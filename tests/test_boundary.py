@@ -76,6 +76,20 @@ def test_kernel_choice_by_shape():
     assert ops._stream_shape(1, 32, False) == (32, 1)
     assert ops._stream_shape(3, 12, False) == (64, 5)
     assert ops._stream_shape(7, 12, True) == (16, 1)
+    # key-stream plans (chunk tiles, splits, cluster) at the benchmarked decode shapes on 148 SMs
+    assert ops._stream_plan_for(64, 1, 32, 32768, 0, 1024, False, 148, None) == (4, 2, True)   # window rows
+    assert ops._stream_plan_for(64, 1, 32, 32768, 0, 0, False, 148, None) == (64, 4, False)    # two waves: merge
+    assert ops._stream_plan_for(64, 1, 32, 32768, 1024, 1024, True, 148, None) == (8, 2, True)  # sparse gather
+    assert ops._stream_plan_for(1, 1, 32, 262144, 0, 0, False, 148, None)[2] is False
+
+
+def test_cluster_mode_takes_at_most_8_splits(library):
+    # part_o == part_lse == NULL selects the in-cluster merge, which holds at most 8 splits
+    from wpt_b200 import _lib
+    lib = _lib.lib()
+    rc = lib.wpt_attn_decode(None, None, None, 0, 0, 0, 0, None, None, None, 0, None, None, None, None, None, 9, 1,
+                             1, 1, 32, 128, 1024, 0, 1.0, None)
+    assert rc == _lib.ERR_INVALID and b"at most 8" in lib.wpt_last_error()
 
 
 def test_cpu_tensors_are_refused_not_computed():

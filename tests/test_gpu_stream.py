@@ -61,7 +61,7 @@ def test_decode_matches_oracle(wb, B, T, H, N):
     _check(wb, out, lse, ref_out, ref_lse)
 
 
-@pytest.mark.parametrize("chunk", [1, 3, 100])
+@pytest.mark.parametrize("chunk", [1, 3, 4, 16, 100])  # 32, 11 splits merged by a kernel; 8, 2 in a cluster; 1
 def test_decode_split_chunks_agree(wb, chunk):
     from wpt_b200 import ops
     q, e, positions = _decode_case(4, 1, 32, 4000, seed=chunk)
@@ -218,8 +218,9 @@ def test_sparse_window_rows_outside_the_table(wb):
 @pytest.mark.parametrize("shards,with_sink", [(2, False), (3, True), (8, True)])
 def test_long_row_shards_packed_and_merged_equal_one_call(wb, shards, with_sink):
     # the kernel path of the multi-GPU long row on one GPU: each shard's
-    # partials go into its own chunk of one buffer (as the in-place
-    # all-gather leaves them on every rank), then one grouped merge
+    # split partials, merged into one partial in its own chunk of one buffer
+    # (as the in-place all-gather leaves them on every rank), then one
+    # grouped merge of the chunks with the sink
     from wpt_b200 import multi, ops
     g = torch.Generator().manual_seed(40 + shards)
     H, C, N = 32, 128, 20000
@@ -227,18 +228,15 @@ def test_long_row_shards_packed_and_merged_equal_one_call(wb, shards, with_sink)
     e = (torch.randn(1, N, 2 * C, generator=g) * 0.5).bfloat16().cuda()
     sink = (torch.randn(H, generator=g) * 0.5).cuda() if with_sink else None
     positions = torch.tensor([[N - 1]]).cuda()
-    longest = max(multi.key_shard(N, shards, r)[1] - multi.key_shard(N, shards, r)[0] for r in range(shards))
-    splits, _ = ops.partials_plan(q.shape, longest, q.device)
     rows = H
-    group = (splits * rows * (C + 1) + 3) // 4 * 4
-    parts = torch.empty(shards, group, dtype=torch.float32, device="cuda")
+    chunk = (rows * (C + 1) + 3) // 4 * 4
+    parts = torch.empty(shards, chunk, dtype=torch.float32, device="cuda")
     for r in range(shards):
         a, b = multi.key_shard(N, shards, r)
-        chunk = parts[r]
-        ops.stream_partials(q, e[:, a:b, :C], e[:, a:b, C:], positions - a, C ** -0.5, splits=splits,
-                            into=(chunk[:splits * rows * C].view(splits, rows, C),
-                                  chunk[splits * rows * C:splits * rows * (C + 1)].view(splits, rows)))
-    out, lse = ops.merge_groups(parts, splits, rows, H, C, sink)
+        part_o, part_lse = ops.stream_partials(q, e[:, a:b, :C], e[:, a:b, C:], positions - a, C ** -0.5)
+        ops.merge_partial(part_o, part_lse, out_o=parts[r, :rows * C].view(rows, C),
+                          out_lse=parts[r, rows * C:rows * (C + 1)])
+    out, lse = ops.merge_groups(parts, 1, rows, H, C, sink)
     whole, whole_lse = ops.stream_forward(q, e[..., :C], e[..., C:], positions, C ** -0.5, sink=sink)
     assert wb.device_status() == 0
     assert (out.float().reshape(whole.shape) - whole.float()).abs().max().item() < 1e-2

@@ -1,11 +1,11 @@
 """The multi-GPU partitioning logic on CPU gloo ranks (world size 2 and 3):
 row sharding, length-balanced decode rows, and the long-row key split. The
-long row runs long_decode's production branch (the plan's all-reduce, each
-rank's partials written into its chunk of the shared buffer, the in-place
-all-gather, the grouped merge) with the three GPU calls it makes
-(ops.partials_plan, ops.stream_partials, ops.merge_groups) replaced by CPU
-restatements, since this suite has no GPU; the kernels themselves are
-checked by the gpu tests."""
+long row runs long_decode's production branch (each rank's split partials,
+their merge into one partial in the rank's chunk of the shared buffer, the
+in-place all-gather, the grouped merge) with the GPU calls it makes
+(ops.partials_plan, ops.stream_partials, ops.merge_partial,
+ops.merge_groups) replaced by CPU restatements, since this suite has no
+GPU; the kernels themselves are checked by the gpu tests."""
 
 import os
 import socket
@@ -71,6 +71,15 @@ def _cpu_stream_partials(q, k, v, local, scale, window=0, into=None, splits=None
     return part_o, part_lse
 
 
+def _cpu_merge_partial(part_o, part_lse, out_o=None, out_lse=None):
+    """The merge kernel's partial mode restated: the splits' normalised
+    output and log-sum together, no sink."""
+    o, total = oat.merge_partials(part_o.double().numpy(), part_lse.double().numpy(), np.ones(part_lse.shape))
+    out_o.copy_(torch.from_numpy(np.nan_to_num(o)).float())
+    out_lse.copy_(torch.from_numpy(total).float())
+    return out_o, out_lse
+
+
 def _cpu_merge_groups(parts, per, rows, H, C, sink=None):
     """The grouped merge kernel restated: chunk g = per splits' outputs
     (per, rows, C) then their log-sums (per, rows)."""
@@ -90,6 +99,7 @@ def _long_rank(rank, world, port, result, with_sink):
     from wpt_b200 import ops
     ops.partials_plan = _cpu_partials_plan
     ops.stream_partials = _cpu_stream_partials
+    ops.merge_partial = _cpu_merge_partial
     ops.merge_groups = _cpu_merge_groups
     try:
         g = torch.Generator().manual_seed(5)

@@ -40,6 +40,10 @@ def chosen_columns(top_k, window, N):
 
 
 def _positions(positions, B):
+    """positions (T,) or (B, T) -> (B, T) int64, contiguous (kernels.py:155-157)."""
+    if positions.dtype == torch.int64 and positions.dim() == 2 and positions.shape[0] == B and \
+            positions.is_contiguous():
+        return positions
     return positions.to(torch.int64).expand(B, -1).contiguous()
 
 

@@ -39,6 +39,7 @@ SIGNATURES = {
     "wpt_debug_backward_fault": [_I, ctypes.c_ulonglong],
     "wpt_cache_append": [_P, _I64, _I64, _P, _I64, _I64, _P, _P, _I, _I, _I, _I64, _P],
     "wpt_attn_merge_groups": [_P, _I, _I, _I64, _I64, _I, _I, _P, _P, _P, _P],
+    "wpt_attn_merge_partial": [_P, _P, _I, _I64, _I64, _I, _P, _P, _P],
 }
 
 RESTYPES = {"wpt_last_error": ctypes.c_char_p, "wpt_accept_scratch_bytes": ctypes.c_size_t,

@@ -6,7 +6,10 @@
 //     lse = log(sum_s exp(lse_s) + exp(sink_h))      (sink optional)
 //     out = sum_s exp(lse_s - lse) o_s
 // the same combination pytorch_kernels.py:183-184 makes over one block
-// (logaddexp with the sink, weights exp(z - lse)). Used by the split-KV
+// (logaddexp with the sink, weights exp(z - lse)). With out_f32 given, the
+// output stays fp32 and, with no sink, the result is itself a partial (the
+// normalised output of the splits together, and its log-sum) that a later
+// merge can combine with others. Used by the split-KV
 // paths of both attention kernels and by the multi-GPU long-sequence decode,
 // whose splits live on different GPUs.
 #pragma once
@@ -39,7 +42,7 @@ __global__ void __launch_bounds__(256) merge_kernel(const float* __restrict__ pa
                                                     const float* __restrict__ part_lse, int splits,
                                                     int64_t rows, SplitLayout lay, int H,
                                                     const float* __restrict__ sink, __nv_bfloat16* __restrict__ out,
-                                                    float* __restrict__ lse_out) {
+                                                    float* __restrict__ lse_out, float* __restrict__ out_f32) {
   griddep_wait();  // the partials come from the kernel before (programmatic dependent launch)
   const int64_t row = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
@@ -66,8 +69,13 @@ __global__ void __launch_bounds__(256) merge_kernel(const float* __restrict__ pa
     if (sink != nullptr) denom += __expf(sk - m);
   }
   const float inv = denom > 0.f ? 1.f / denom : 0.f;
+  if (out_f32 != nullptr) {  // a partial of its own (normalised output, fp32) for a later merge
 #pragma unroll
-  for (int i = 0; i < C / 32; ++i) out[row * C + lane + 32 * i] = __float2bfloat16_rn(acc[i] * inv);
+    for (int i = 0; i < C / 32; ++i) out_f32[row * C + lane + 32 * i] = acc[i] * inv;
+  } else {
+#pragma unroll
+    for (int i = 0; i < C / 32; ++i) out[row * C + lane + 32 * i] = __float2bfloat16_rn(acc[i] * inv);
+  }
   if (lane == 0) lse_out[row] = denom > 0.f ? m + __logf(denom) : -INFINITY;
 }
 
@@ -81,7 +89,8 @@ constexpr int MERGE_THREADS = 512, MERGE_MAX_SPLITS = 2048;
 template <int C>
 __global__ void __launch_bounds__(MERGE_THREADS) merge_wide_kernel(
     const float* __restrict__ part_o, const float* __restrict__ part_lse, int splits, SplitLayout lay, int H,
-    const float* __restrict__ sink, __nv_bfloat16* __restrict__ out, float* __restrict__ lse_out) {
+    const float* __restrict__ sink, __nv_bfloat16* __restrict__ out, float* __restrict__ lse_out,
+    float* __restrict__ out_f32) {
   griddep_wait();  // the partials come from the kernel before (programmatic dependent launch)
   constexpr int GROUPS = MERGE_THREADS / C;
   __shared__ float s_w[MERGE_MAX_SPLITS];
@@ -146,7 +155,11 @@ __global__ void __launch_bounds__(MERGE_THREADS) merge_wide_kernel(
 #pragma unroll
     for (int k = 0; k < GROUPS; ++k) a += s_acc[k][t];
     const float inv = denom > 0.f ? 1.f / denom : 0.f;
-    out[row * C + t] = __float2bfloat16_rn(a * inv);
+    if (out_f32 != nullptr) {
+      out_f32[row * C + t] = a * inv;
+    } else {
+      out[row * C + t] = __float2bfloat16_rn(a * inv);
+    }
     if (t == 0) lse_out[row] = denom > 0.f ? m + __logf(denom) : -INFINITY;
   }
 }

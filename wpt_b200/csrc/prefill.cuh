@@ -108,7 +108,8 @@ struct PrefillLayout {
   static constexpr int MMA_WARP = 8, LOAD_WARP = 9;
   // registers per thread after setmaxnreg: 168 at launch (65536 / 384), then
   // 128 x 56 + 256 x 224 = 384 x 168, the block's whole allocation
-  static constexpr int REGS_CONTROL = 56, REGS_SOFTMAX = 224;
+  static constexpr int REGS_LAUNCH = 168, REGS_CONTROL = 56, REGS_SOFTMAX = 224;
+  static_assert(128 * REGS_CONTROL + 256 * REGS_SOFTMAX == THREADS * REGS_LAUNCH, "register split");
   static constexpr int ITEM_READERS = 9;  // the issuer warp and the 8 softmax warps
 };
 

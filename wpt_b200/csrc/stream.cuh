@@ -20,13 +20,21 @@
 // row outside the table, is masked (pytorch_kernels.py:149-153,182).
 // Slots are split into chunks of chunk_tiles x 128 over gridDim.y; with
 // more than one split every CTA writes a partial result for the merge
-// kernel (merge.cuh).
+// kernel (merge.cuh), or, in cluster mode (at most 8 splits, the grid one
+// wave), the splits of a query group form one thread-block cluster: each
+// CTA leaves its unnormalised output and its columns' maximum and sum in
+// its own shared memory, and after a cluster barrier CTA k combines columns
+// k, k + splits, ... from all of them (distributed shared memory loads) and
+// writes the final output, so neither partials in HBM nor a second launch.
 //
 // Loads: range mode takes whole tiles by TMA. Gather mode: 2 loader warps
 // copy each slot's 256-byte K and V rows with 16-byte cp.async (coalesced:
 // 16 lanes per row) into 128-byte-swizzled tiles and publish a stage after
 // cp.async.wait_group and a proxy fence; a tile of the query's window rows
-// (one contiguous range) comes by TMA instead. Warp 4 issues the MMAs.
+// (one contiguous range) comes by TMA instead. Q's copy is in flight
+// together with the first tiles' (range mode: the first STAGES tiles' TMA
+// loads are issued before it; gather mode: tile 0's copies follow it in
+// the next cp.async group). Warp 4 issues the MMAs.
 // Warps 0-3 do the softmax: thread r owns slot r of a tile, holds its
 // NCOL scores, and the per-column maximum and sum over the 128 slots come
 // from a 31-shuffle transpose reduction per warp plus shared memory across
@@ -57,6 +65,7 @@ struct StreamParams {
   unsigned* status;
   int B, T, H, N, K, window, TQ, groups_per_row, splits, chunk_tiles;
   int window_tma;              // gather mode: tiles of window rows come by TMA (the maps are valid)
+  int cluster;                 // > 1: the splits of a group are one cluster and merge in shared memory
   float scale_log2;
 };
 
@@ -118,6 +127,61 @@ __device__ __forceinline__ void stream_pv_steps(uint32_t d, uint64_t dv, uint64_
   constexpr uint32_t off_v = (KK * 16 * 128) >> 4;
   constexpr uint32_t off_p = ((KK >> 2) * (NCOL * 128) + (KK & 3) * 32) >> 4;
   mma_ss_off_warp<off_v, off_p>(d, dv, dp, idesc, KK > 0 ? 1u : acc0);
+}
+
+// Cluster mode's combine, run by every thread of every CTA of the cluster
+// (one query group's splits). Each CTA has left, for its columns, the lazy
+// maximum (s_m, base 2), the sum of exponentials (s_l; 0 when the split saw
+// no visible key or failed) and the unnormalised output (s_o, column-major
+// with 128 floats per column). CTA k writes columns k, k + S, ...: the
+// output row sum_i w_i o_i / L and its log-sum, w_i = 2^(m_i - M) and
+// L = sum_i w_i l_i plus the sink's exp(sink - M), M the largest maximum.
+__device__ __forceinline__ void stream_cluster_merge(const StreamParams& p, const float* s_m, const float* s_l,
+                                                     const float* s_o, int64_t row0, int ncols) {
+  constexpr int C = 128;
+  cluster_sync();
+  const int S = p.cluster;
+  const int rank = static_cast<int>(cluster_rank());
+  const int mine = ncols > rank ? (ncols - rank + S - 1) / S : 0;  // columns rank, rank + S, ...
+  const uint32_t am = smem_u32(s_m), al = smem_u32(s_l), ao = smem_u32(s_o);
+  for (int item = threadIdx.x; item < mine * (C / 4); item += blockDim.x) {
+    const int c = rank + (item / (C / 4)) * S, quad = item % (C / 4);
+    float mi[8], li[8];
+    float M = -INFINITY;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      mi[i] = -INFINITY;
+      li[i] = 0.f;
+      if (i < S) {
+        mi[i] = dsmem_ld(dsmem_map(am + c * 4, i));
+        li[i] = dsmem_ld(dsmem_map(al + c * 4, i));
+        if (li[i] > 0.f) M = fmaxf(M, mi[i]);
+      }
+    }
+    const float msub = M == -INFINITY ? 0.f : M;
+    float L = 0.f;
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      if (i < S && li[i] > 0.f) {
+        const float w = fast_exp2(mi[i] - msub);
+        const float4 o = dsmem_ld4(dsmem_map(ao + (c * C + quad * 4) * 4, i));
+        L = fmaf(w, li[i], L);
+        acc.x = fmaf(w, o.x, acc.x);
+        acc.y = fmaf(w, o.y, acc.y);
+        acc.z = fmaf(w, o.z, acc.z);
+        acc.w = fmaf(w, o.w, acc.w);
+      }
+    }
+    if (p.sink != nullptr) L += fast_exp2(fmaf(p.sink[c % p.H], LOG2E, -msub));
+    const float inv = L > 0.f ? 1.f / L : 0.f;
+    uint2 packed;
+    packed.x = pack_bf16(acc.x * inv, acc.y * inv);
+    packed.y = pack_bf16(acc.z * inv, acc.w * inv);
+    *reinterpret_cast<uint2*>(p.out + (row0 + c) * C + quad * 4) = packed;
+    if (quad == 0) p.lse[row0 + c] = L > 0.f ? (msub + log2f(L)) * LN2 : -INFINITY;
+  }
+  cluster_sync();  // no CTA leaves while another still reads its shared memory
 }
 
 template <int NCOL, int STAGES, bool GATHER>
@@ -200,9 +264,36 @@ __global__ void __launch_bounds__(STREAM_THREADS, 1)
   const int ntiles =
       GATHER ? static_cast<int>(split < tiles_total ? (tiles_total - split + gridDim.y - 1) / gridDim.y : 0)
              : static_cast<int>(left <= 0 ? 0 : (left < p.chunk_tiles ? left : p.chunk_tiles));
-  auto tile_of = [&](int j) -> int64_t { return GATHER ? split + static_cast<int64_t>(j) * gridDim.y : tile0 + j; };
+  // Gather mode takes its tiles alternately from the gathered slots (16-byte
+  // copies, bounded by the requests an SM's L1 keeps in flight) and the
+  // window's (TMA), so that both kinds of load are in flight together.
+  const int64_t gathered_tiles = (static_cast<int64_t>(p.K) + BN - 1) / BN;  // tiles with a slot below K
+  const int kg = GATHER ? static_cast<int>(gathered_tiles > split ? (gathered_tiles - split + gridDim.y - 1) / gridDim.y
+                                                                  : 0)
+                        : 0;
+  const int kg_mine = kg < ntiles ? kg : ntiles;
+  const int pairs = kg_mine < ntiles - kg_mine ? kg_mine : ntiles - kg_mine;
+  auto tile_of = [&](int j) -> int64_t {
+    if constexpr (!GATHER) {
+      return tile0 + j;
+    } else {
+      int k;
+      if (j < 2 * pairs) {
+        k = (j & 1) ? kg_mine + (j >> 1) : (j >> 1);
+      } else {
+        k = kg_mine > pairs ? j - pairs : j;  // the longer kind's remaining tiles, in order
+      }
+      return split + static_cast<int64_t>(k) * gridDim.y;
+    }
+  };
 
   if (ntiles == 0) {  // nothing to read: an empty partial, or the sink alone
+    if (p.cluster > 1) {  // an empty share of the cluster's combine (s_m holds -inf)
+      if (threadIdx.x < 64) s_l[threadIdx.x] = 0.f;
+      stream_cluster_merge(p, s_m, s_l, reinterpret_cast<const float*>(sP),
+                           (static_cast<int64_t>(b) * p.T + t0) * p.H, TQg * p.H);
+      return;
+    }
     if (static_cast<int>(threadIdx.x) < NCOL) {
       const int col = threadIdx.x, tq = col / p.H, h = col - tq * p.H;
       if (tq < TQg) {
@@ -247,6 +338,19 @@ __global__ void __launch_bounds__(STREAM_THREADS, 1)
     const int lt = threadIdx.x - 160;
     const __nv_bfloat16* kb = p.k + static_cast<int64_t>(b) * p.ksb;
     const __nv_bfloat16* vb = p.v + static_cast<int64_t>(b) * p.vsb;
+    // range mode: whole 128-row tiles by TMA, one thread, completion by bytes
+    auto issue_tile = [&](int j) {
+      const int st = j % STAGES;
+      const int n0 = range_lo + static_cast<int>((tile0 + j) * BN);
+      mbar_expect_tx(full + st, 2 * L::KV_BYTES);
+      tma_load_3d(sK + st * L::KV_BYTES, &tm_k, full + st, 0, n0, b);
+      tma_load_3d(sK + st * L::KV_BYTES + BN * 128, &tm_k, full + st, 64, n0, b);
+      tma_load_3d(sV + st * L::KV_BYTES, &tm_v, full + st, 0, n0, b);
+      tma_load_3d(sV + st * L::KV_BYTES + BN * 128, &tm_v, full + st, 64, n0, b);
+    };
+    if (!GATHER && lt == 0) {  // the first stages need no free slot: in flight together with Q's copy
+      for (int j = 0; j < ntiles && j < STAGES; ++j) issue_tile(j);
+    }
     // Q: NCOL rows (query x head), zeros for padding columns
     for (int it = lt; it < NCOL * 16; it += STREAM_LOADERS) {
       const int col = it >> 4, ch = it & 15;
@@ -256,21 +360,14 @@ __global__ void __launch_bounds__(STREAM_THREADS, 1)
       cp_async_16(smem_u32(sQ + (ch >> 3) * (NCOL * 128) + sw128_offset(col, ch & 7)), ok ? src : p.q, ok);
     }
     cp_async_commit();
-    cp_async_wait<0>();
-    fence_proxy_async();
-    mbar_arrive(q_full);
     if constexpr (!GATHER) {
-      // range mode: whole 128-row tiles by TMA, one thread, completion by bytes
+      cp_async_wait<0>();
+      fence_proxy_async();
+      mbar_arrive(q_full);
       if (lt == 0) {
-        for (int j = 0; j < ntiles; ++j) {
-          const int st = j % STAGES;
-          if (j >= STAGES && !mbar_wait(kv_empty + st, ((j / STAGES) & 1) ^ 1, p.status)) break;
-          const int n0 = range_lo + static_cast<int>((tile0 + j) * BN);
-          mbar_expect_tx(full + st, 2 * L::KV_BYTES);
-          tma_load_3d(sK + st * L::KV_BYTES, &tm_k, full + st, 0, n0, b);
-          tma_load_3d(sK + st * L::KV_BYTES + BN * 128, &tm_k, full + st, 64, n0, b);
-          tma_load_3d(sV + st * L::KV_BYTES, &tm_v, full + st, 0, n0, b);
-          tma_load_3d(sV + st * L::KV_BYTES + BN * 128, &tm_v, full + st, 64, n0, b);
+        for (int j = STAGES; j < ntiles; ++j) {
+          if (!mbar_wait(kv_empty + j % STAGES, ((j / STAGES) & 1) ^ 1, p.status)) break;
+          issue_tile(j);
         }
       }
       __syncwarp();
@@ -355,6 +452,11 @@ __global__ void __launch_bounds__(STREAM_THREADS, 1)
         }
         cp_async_commit();
         lookup(j + 1, next_rows);
+        if (j == 0) {  // Q's copies, the group before tile 0's, were in flight with it
+          cp_async_wait<1>();
+          fence_proxy_async();
+          mbar_arrive(q_full);
+        }
         if (published == j - 1) {
           cp_async_wait<1>();
           fence_proxy_async();
@@ -577,7 +679,9 @@ __global__ void __launch_bounds__(STREAM_THREADS, 1)
     if (r < ncols) {
       const float l = (s_red[r] + s_red[64 + r]) + (s_red[128 + r] + s_red[192 + r]);
       const float m = s_m[r], msub = m == -INFINITY ? 0.f : m;
-      if (p.splits == 1) {
+      if (p.cluster > 1) {
+        s_l[r] = ok ? l : 0.f;  // combined across the cluster below
+      } else if (p.splits == 1) {
         float denom = l;
         if (p.sink != nullptr) denom += fast_exp2(fmaf(p.sink[r % p.H], LOG2E, -msub));
         s_l[r] = denom > 0.f ? 1.f / denom : 0.f;
@@ -605,7 +709,13 @@ __global__ void __launch_bounds__(STREAM_THREADS, 1)
         }
       }
       // thread r holds element r of the head width for every column (query, head)
-      if (p.splits == 1) {
+      if (p.cluster > 1) {
+        // unnormalised, into the P buffers (2 x NCOL x 128 bf16 = NCOL x 128
+        // floats; the last P V product, which read them, has completed)
+        float* dst = reinterpret_cast<float*>(sP) + r;
+#pragma unroll
+        for (int c = 0; c < NCOL; ++c) dst[c * C] = o[c];
+      } else if (p.splits == 1) {
         __nv_bfloat16* dst = p.out + row0 * C + r;
 #pragma unroll
         for (int c = 0; c < NCOL; ++c)
@@ -624,6 +734,9 @@ __global__ void __launch_bounds__(STREAM_THREADS, 1)
     tc_fence_after();
     tmem_dealloc(tmem, L::TMEM_COLS);
   }
+  if (p.cluster > 1)
+    stream_cluster_merge(p, s_m, s_l, reinterpret_cast<const float*>(sP), (static_cast<int64_t>(b) * p.T + t0) * p.H,
+                         TQg * p.H);
 }
 
 }  // namespace wpt

@@ -240,6 +240,19 @@ int launch_prefill_p(const wpt::PrefillParams& p, const CUtensorMap& tq, const C
   static_assert(L::BYTES <= 232448, "prefill kernel shared memory exceeds 227 KB");
   auto kernel = wpt::prefill_kernel<C, QB, NS, POLY8>;
   if (int rc = allow_smem(kernel, L::BYTES)) return rc;
+  // setmaxnreg redistributes the registers the block was launched with: a
+  // kernel built with fewer than REGS_LAUNCH would leave the softmax
+  // warpgroups' increase waiting forever, so it is refused here instead
+  static int regs = -1;
+  if (regs < 0) {
+    cudaFuncAttributes fa;
+    cudaError_t e = cudaFuncGetAttributes(&fa, kernel);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncGetAttributes(prefill_kernel)");
+    regs = fa.numRegs;
+  }
+  if (regs != L::REGS_LAUNCH)
+    return fail(WPT_ERR_CUDA, "prefill_kernel built with %d registers a thread, its register split needs %d", regs,
+                L::REGS_LAUNCH);
   int sms = 148;
   current_device(&sms);
   const int grid = p.items < sms ? p.items : sms;  // persistent: one CTA per SM walks the items
@@ -269,9 +282,19 @@ int launch_stream_n(const CUtensorMap& tk, const CUtensorMap& tv, const wpt::Str
   static_assert(L::BYTES <= 232448, "key-stream kernel shared memory exceeds 227 KB");
   auto kernel = wpt::stream_kernel<NCOL, STAGES, GATHER>;
   if (int rc = allow_smem(kernel, L::BYTES)) return rc;
-  dim3 grid(groups, p.splits);
-  kernel<<<grid, wpt::STREAM_THREADS, L::BYTES, stream>>>(tk, tv, p);
-  cudaError_t e = cudaGetLastError();
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;  // cluster mode: one group's splits per cluster
+  attr[0].val.clusterDim.x = 1;
+  attr[0].val.clusterDim.y = p.cluster > 1 ? p.cluster : 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = p.cluster > 1 ? 1 : 0;
+  cfg.gridDim = dim3(groups, p.splits);
+  cfg.blockDim = dim3(wpt::STREAM_THREADS);
+  cfg.dynamicSmemBytes = L::BYTES;
+  cfg.stream = stream;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, tk, tv, p);
   if (e != cudaSuccess) return cuda_fail(e, "stream_kernel launch");
   return WPT_OK;
 }
@@ -308,7 +331,8 @@ template <int C>
 // partials, and launches while that kernel finishes (programmatic dependent
 // launch; the merge waits for it on the device before reading).
 int launch_merge(const float* part_o, const float* part_lse, int splits, int64_t rows, wpt::SplitLayout lay, int H,
-                 const float* sink, void* out, float* lse, cudaStream_t stream, bool pdl = false) {
+                 const float* sink, void* out, float* lse, cudaStream_t stream, bool pdl = false,
+                 float* out_f32 = nullptr) {
   cudaLaunchConfig_t cfg = {};
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -322,13 +346,14 @@ int launch_merge(const float* part_o, const float* part_lse, int splits, int64_t
   if (splits >= 16 && splits <= wpt::MERGE_MAX_SPLITS && rows <= 4096) {  // few rows, many splits: a CTA per row
     cfg.gridDim = dim3(static_cast<unsigned>(rows));
     cfg.blockDim = dim3(wpt::MERGE_THREADS);
-    e = cudaLaunchKernelEx(&cfg, wpt::merge_wide_kernel<C>, part_o, part_lse, splits, lay, H, sink, o, lse);
+    e = cudaLaunchKernelEx(&cfg, wpt::merge_wide_kernel<C>, part_o, part_lse, splits, lay, H, sink, o, lse, out_f32);
   } else {
     const int warps = 8;
     const int64_t blocks = (rows + warps - 1) / warps;
     cfg.gridDim = dim3(static_cast<unsigned>(blocks));
     cfg.blockDim = dim3(warps * 32);
-    e = cudaLaunchKernelEx(&cfg, wpt::merge_kernel<C>, part_o, part_lse, splits, rows, lay, H, sink, o, lse);
+    e = cudaLaunchKernelEx(&cfg, wpt::merge_kernel<C>, part_o, part_lse, splits, rows, lay, H, sink, o, lse,
+                           out_f32);
   }
   if (e != cudaSuccess) return cuda_fail(e, "merge_kernel launch");
   return WPT_OK;
@@ -656,6 +681,23 @@ extern "C" int wpt_attn_merge(const float* part_o, const float* part_lse, int sp
                   : launch_merge<64>(part_o, part_lse, splits, rows, split_stride, H, sink, out, lse, s);
 }
 
+extern "C" int wpt_attn_merge_partial(const float* part_o, const float* part_lse, int splits, int64_t rows,
+                                      int64_t split_stride, int C, float* out_o, float* out_lse, void* stream) {
+  if (C != 64 && C != 128) return fail(WPT_ERR_UNSUPPORTED, "head width %d: the kernels take 64 or 128", C);
+  if (splits < 1 || rows < 0 || split_stride < rows)
+    return fail(WPT_ERR_INVALID, "bad merge shape splits=%d rows=%lld", splits, static_cast<long long>(rows));
+  if (!part_o || !part_lse || !out_o || !out_lse) return fail(WPT_ERR_INVALID, "a required pointer is NULL");
+  if (rows == 0) return WPT_OK;
+  wpt::SplitLayout lay;
+  lay.per = splits;
+  lay.stride = split_stride;
+  lay.group_o = 0;
+  lay.group_l = 0;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  return C == 128 ? launch_merge<128>(part_o, part_lse, splits, rows, lay, 1, nullptr, nullptr, out_lse, s, false, out_o)
+                  : launch_merge<64>(part_o, part_lse, splits, rows, lay, 1, nullptr, nullptr, out_lse, s, false, out_o);
+}
+
 extern "C" int wpt_attn_merge_groups(const float* parts, int groups, int per, int64_t rows, int64_t group_floats,
                                      int H, int C, const float* sink, void* out, float* lse, void* stream) {
   if (C != 64 && C != 128) return fail(WPT_ERR_UNSUPPORTED, "head width %d: the kernels take 64 or 128", C);
@@ -691,11 +733,15 @@ extern "C" int wpt_attn_decode(const void* q, const void* k, const void* v, int6
   if (static_cast<int64_t>(B) * T * H >= (int64_t(1) << 31)) return fail(WPT_ERR_UNSUPPORTED, "B*T*H too large");
   if (splits < 1 || chunk_tiles < 1) return fail(WPT_ERR_INVALID, "splits and chunk_tiles must be >= 1");
   if (splits > 65535) return fail(WPT_ERR_UNSUPPORTED, "%d splits: at most 65535", splits);
-  if (splits > 1 && (part_o == nullptr || part_lse == nullptr))
-    return fail(WPT_ERR_INVALID, "splits > 1 needs part_o and part_lse scratch");
+  // part_o and part_lse both NULL with 2..8 splits: cluster mode (the splits
+  // of a group merge in shared memory; no scratch, no merge launch)
+  const bool cluster = splits > 1 && part_o == nullptr && part_lse == nullptr;
+  if (cluster && splits > 8) return fail(WPT_ERR_INVALID, "%d splits without scratch: at most 8", splits);
+  if (splits > 1 && !cluster && (part_o == nullptr || part_lse == nullptr))
+    return fail(WPT_ERR_INVALID, "splits > 1 needs both part_o and part_lse scratch (or neither, for 2 to 8)");
   if (idx != nullptr && K < 0) return fail(WPT_ERR_INVALID, "K must be >= 0");
   // out and lse both NULL with splits > 1: partials only, merged by the caller
-  const bool partials_only = splits > 1 && out == nullptr && lse == nullptr;
+  const bool partials_only = splits > 1 && !cluster && out == nullptr && lse == nullptr;
   if (!q || !k || !v || !positions || ((!out || !lse) && !partials_only))
     return fail(WPT_ERR_INVALID, "a required pointer is NULL");
   if (!aligned16(q) || !aligned16(k) || !aligned16(v)) return fail(WPT_ERR_INVALID, "q, k, v must be 16-byte aligned");
@@ -717,7 +763,7 @@ extern "C" int wpt_attn_decode(const void* q, const void* k, const void* v, int6
   p.floor_rows = gather ? nullptr : floor_rows;
   p.idx = idx;
   p.K = gather ? K : 0;
-  p.sink = splits > 1 ? nullptr : sink;
+  p.sink = splits > 1 && !cluster ? nullptr : sink;
   p.out = static_cast<__nv_bfloat16*>(out);
   p.lse = lse;
   p.part_o = part_o;
@@ -732,6 +778,7 @@ extern "C" int wpt_attn_decode(const void* q, const void* k, const void* v, int6
   p.groups_per_row = (T + p.TQ - 1) / p.TQ;
   p.splits = splits;
   p.chunk_tiles = chunk_tiles;
+  p.cluster = cluster ? splits : 0;
   p.scale_log2 = scale * wpt::LOG2E;
   const int64_t groups = static_cast<int64_t>(B) * p.groups_per_row;
   if (groups >= (int64_t(1) << 31)) return fail(WPT_ERR_UNSUPPORTED, "too many query groups");
@@ -753,7 +800,7 @@ extern "C" int wpt_attn_decode(const void* q, const void* k, const void* v, int6
   const int rc = gather ? launch_stream_g<true>(tk, tv, p, ncol, static_cast<int>(groups), s)
                         : launch_stream_g<false>(tk, tv, p, ncol, static_cast<int>(groups), s);
   if (rc) return rc;
-  if (splits > 1 && !partials_only) {
+  if (splits > 1 && !partials_only && !cluster) {
     const int64_t rows = static_cast<int64_t>(B) * T * H;
     return launch_merge<128>(part_o, part_lse, splits, rows, rows, H, sink, out, lse, s, true);
   }

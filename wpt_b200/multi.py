@@ -11,10 +11,10 @@ partitions fit this path:
   * one long row (long-context decode): its keys are split into contiguous
     shards, one per rank. Each rank's kernel computes split partials of the
     query over its shard (output normalised by each split's softmax sum, and
-    that sum's log) into its chunk of a shared-layout buffer, one in-place
-    NCCL all-gather exchanges the chunks, and every rank merges all splits
-    by log-sum-exp (the merge kernel): splits x H x (C + 1) floats per rank
-    and query, latency-bound.
+    that sum's log), merges them into one partial in its chunk of a shared
+    buffer, one in-place NCCL all-gather exchanges the chunks, and every
+    rank merges the ranks' partials by log-sum-exp (the merge kernel): H x
+    (C + 1) floats per rank and query, latency-bound.
 """
 
 import torch
@@ -51,24 +51,25 @@ def key_shard(n_rows, world, rank):
     return s.start, s.stop
 
 
-_PLANS = {}  # (shape, shard length, world, device, group) -> (splits, group floats, parts buffer)
+_PLANS = {}  # (shape, shard length, world, device, group) -> the long row's buffers on this rank
 
 
-def _long_plan(q, n_local, world, rank, group):
-    """Splits per rank and the gathered buffer of one long-row shape: the
-    split count comes from the longest shard (one all-reduce, made once per
-    shape), so that every rank's chunk has one layout."""
+def _long_plan(q, n_local, world, group):
+    """The buffers of one long-row shape on this rank, allocated once: this
+    rank's split partials (its kernel's splits for its own shard) and the
+    exchanged buffer (world, chunk), chunk = one partial (rows, C) and its
+    log-sums (rows), padded to 16 bytes."""
     B, T, H, C = q.shape
     key = (tuple(q.shape), n_local, world, q.device, id(group))
     plan = _PLANS.get(key)
     if plan is None:
-        longest = torch.tensor([n_local], dtype=torch.int64, device=q.device)
-        dist.all_reduce(longest, op=dist.ReduceOp.MAX, group=group)
-        splits, _ = ops.partials_plan(q.shape, int(longest.item()), q.device)
         rows = B * T * H
-        group_floats = (splits * rows * (C + 1) + 3) // 4 * 4  # chunks start 16-byte aligned
-        parts = torch.empty(world, group_floats, dtype=torch.float32, device=q.device)
-        plan = _PLANS[key] = (splits, group_floats, parts)
+        splits, _ = ops.partials_plan(q.shape, n_local, q.device)
+        part_o = torch.empty(splits, rows, C, dtype=torch.float32, device=q.device)
+        part_lse = torch.empty(splits, rows, dtype=torch.float32, device=q.device)
+        chunk = (rows * (C + 1) + 3) // 4 * 4
+        parts = torch.empty(world, chunk, dtype=torch.float32, device=q.device)
+        plan = _PLANS[key] = (splits, part_o, part_lse, parts)
     return plan
 
 
@@ -78,26 +79,27 @@ def long_decode(q, k_shard, v_shard, shard_start, positions, scale, sink=None, g
     as k_shard, v_shard (B, n, C). positions (B, T) are positions in the whole
     row. Returns (out (B, T, H, C) bf16, lse (B, T, H)) on every rank.
 
-    Each rank's key-stream kernel writes its split partials straight into
-    its own chunk of a gathered buffer (output partials then log-sums), one
-    in-place NCCL all-gather brings every rank's chunk to every rank, and one
-    merge kernel combines all the splits. The buffer is allocated once per
-    shape and reused, so the call (kernel, collective, merge) can be
-    captured in a CUDA graph; calls on one stream are ordered, calls that
-    overlap on several streams would share it. The first call of a shape
-    makes one all-reduce (the longest shard, for the split count)."""
+    Each rank's key-stream kernel computes split partials of its shard, a
+    merge kernel combines them into one partial (normalised output and
+    log-sum, fp32) written straight into this rank's chunk of the exchanged
+    buffer, one in-place NCCL all-gather brings every rank's chunk to every
+    rank (rows x (C + 1) floats each, whatever the split counts), and one
+    merge kernel combines the ranks' partials with the sink. Buffers are
+    allocated once per shape and reused, and nothing synchronises the host,
+    so the call (kernels and collective) can be captured in a CUDA graph;
+    calls on one stream are ordered, calls that overlap on several streams
+    would share the buffers."""
     B, T, H, C = q.shape
     world = dist.get_world_size(group) if dist.is_initialized() else 1
     local = positions - shard_start  # rows of this shard the query sees: 0 .. local (none when negative)
     if world == 1:  # the whole row is here: one kernel call
         return ops.stream_forward(q, k_shard, v_shard, local, scale, sink=sink)
     rank = dist.get_rank(group)
-    splits, group_floats, parts = _long_plan(q, k_shard.shape[1], world, rank, group)
+    splits, part_o, part_lse, parts = _long_plan(q, k_shard.shape[1], world, group)
     rows = B * T * H
-    mine = parts[rank]
-    part_o = mine[:splits * rows * C].view(splits, rows, C)
-    part_lse = mine[splits * rows * C:splits * rows * (C + 1)].view(splits, rows)
     ops.stream_partials(q, k_shard, v_shard, local, scale, into=(part_o, part_lse), splits=splits)
+    mine = parts[rank]
+    ops.merge_partial(part_o, part_lse, out_o=mine[:rows * C].view(rows, C), out_lse=mine[rows * C:rows * (C + 1)])
     dist.all_gather_into_tensor(parts.view(-1), mine, group=group)  # in place: every rank's chunk to every rank
-    merged, merged_lse = ops.merge_groups(parts, splits, rows, H, C, sink)
+    merged, merged_lse = ops.merge_groups(parts, 1, rows, H, C, sink)
     return merged.reshape(B, T, H, C), merged_lse.reshape(B, T, H)

@@ -56,8 +56,8 @@ def _table(x):
     """A (B, N, C) table whose last dimension is contiguous, strides in
     multiples of 8 elements (16 bytes), at a 16-byte aligned address."""
     x = _bf16(x)
-    ok = (x.stride(-1) == 1 and x.stride(1) % 8 == 0 and (x.shape[0] == 1 or x.stride(0) % 8 == 0)
-          and x.data_ptr() % 16 == 0)
+    sb, sn, sc = x.stride()
+    ok = sc == 1 and sn % 8 == 0 and (sb % 8 == 0 or x.shape[0] == 1) and x.data_ptr() % 16 == 0
     return x if ok else x.contiguous()
 
 
@@ -133,9 +133,26 @@ def uses_stream(T, H, C):
     return C == 128 and H <= 64 and T * H <= 64
 
 
+_PLAN_CACHE = {}
+
+
 def _stream_plan(B, T, H, N, K, window, gather, sms, chunk_tiles=None):
-    """(chunk_tiles, splits) of a key-stream call: each query group's key
-    slots are cut into chunks of chunk_tiles key tiles, one CTA per chunk."""
+    """(chunk_tiles, splits, cluster) of a key-stream call: each query
+    group's key slots are cut into chunks of chunk_tiles key tiles, one CTA
+    per chunk; cluster: the splits of a group combine in shared memory as one
+    thread-block cluster (2 to 8 splits on a grid of one wave) instead of
+    through partials and a merge kernel. Remembered per shape (a decode loop
+    asks the same question every step)."""
+    key = (B, T, H, N, K, window, gather, sms, chunk_tiles)
+    plan = _PLAN_CACHE.get(key)
+    if plan is None:
+        if len(_PLAN_CACHE) > 4096:
+            _PLAN_CACHE.clear()
+        plan = _PLAN_CACHE[key] = _stream_plan_for(B, T, H, N, K, window, gather, sms, chunk_tiles)
+    return plan
+
+
+def _stream_plan_for(B, T, H, N, K, window, gather, sms, chunk_tiles):
     _, TQ = _stream_shape(T, H, gather)
     groups = B * math.ceil(T / TQ)
     if gather:
@@ -145,6 +162,7 @@ def _stream_plan(B, T, H, N, K, window, gather, sms, chunk_tiles=None):
     tiles = max(1, math.ceil(slots / 128))
     if chunk_tiles is None:
         chunk_tiles = CHUNK_TILES
+    auto = not chunk_tiles
     if not chunk_tiles and gather:
         # every query gathers exactly `tiles` tiles: its slots split so that
         # the grid is about one CTA per SM
@@ -154,8 +172,19 @@ def _stream_plan(B, T, H, N, K, window, gather, sms, chunk_tiles=None):
         # as streaming a few tiles), more when that still gives two CTAs per
         # SM for rows of the table's full length (most rows are shorter)
         chunk_tiles = max(min(16, tiles), 16 * math.ceil(tiles * groups / (2 * sms) / 16))
+        if tiles >= 64 and 2 * math.ceil(tiles / chunk_tiles) * groups < sms:
+            # a few long rows (a GPU's shard of a long-context decode) that
+            # would leave most SMs idle: about one CTA per SM
+            chunk_tiles = max(2, math.ceil(tiles * groups / sms))
     chunk_tiles = max(1, min(int(chunk_tiles), tiles))
-    return chunk_tiles, math.ceil(tiles / chunk_tiles)
+    splits = math.ceil(tiles / chunk_tiles)
+    if auto and splits == 1 and tiles >= 2 and 2 * groups <= sms:
+        # short rows (window rows) on fewer CTAs than SMs: each row's tiles
+        # over a cluster of up to 8 CTAs, still one wave
+        splits = min(8, tiles, sms // groups)
+        chunk_tiles = math.ceil(tiles / splits)
+        splits = math.ceil(tiles / chunk_tiles)
+    return chunk_tiles, splits, 1 < splits <= 8 and groups * splits <= sms
 
 
 def stream_forward(q, k, v, positions, scale, window=0, floor=None, idx=None, sink=None, chunk_tiles=None):
@@ -176,19 +205,21 @@ def stream_forward(q, k, v, positions, scale, window=0, floor=None, idx=None, si
         K = idx.shape[-1]
     if sink is not None and (sink.dtype != torch.float32 or not sink.is_contiguous()):
         sink = sink.float().contiguous()
-    chunk_tiles, splits = _stream_plan(B, T, H, N, K, window, gather, sm_count(q.device), chunk_tiles)
+    dev = q.device
+    chunk_tiles, splits, cluster = _stream_plan(B, T, H, N, K, window, gather, sm_count(dev), chunk_tiles)
     out = torch.empty_like(q)
-    lse = torch.empty(B, T, H, dtype=torch.float32, device=q.device)
+    lse = torch.empty((B, T, H), dtype=torch.float32, device=dev)
     part_o = part_lse = None
-    if splits > 1:
-        part_o = torch.empty(splits, B * T * H, C, dtype=torch.float32, device=q.device)
-        part_lse = torch.empty(splits, B * T * H, dtype=torch.float32, device=q.device)
+    if splits > 1 and not cluster:
+        part_o = torch.empty((splits, B * T * H, C), dtype=torch.float32, device=dev)
+        part_lse = torch.empty((splits, B * T * H), dtype=torch.float32, device=dev)
+    ks, vs = k.stride(), v.stride()
     _lib.check(_lib.lib().wpt_attn_decode(
-        _lib.ptr(q), _lib.ptr(k), _lib.ptr(v), k.stride(0), k.stride(1), v.stride(0), v.stride(1),
-        _lib.ptr(positions), _lib.ptr(floor), _lib.ptr(idx), K, _lib.ptr(sink), _lib.ptr(out), _lib.ptr(lse),
+        q.data_ptr(), k.data_ptr(), v.data_ptr(), ks[0], ks[1], vs[0], vs[1],
+        positions.data_ptr(), _lib.ptr(floor), _lib.ptr(idx), K, _lib.ptr(sink), out.data_ptr(), lse.data_ptr(),
         _lib.ptr(part_o), _lib.ptr(part_lse), splits, chunk_tiles, B, T, H, C, N, int(window), float(scale),
-        _lib.stream(q.device)))
-    LAUNCHES[0] += 1 + (splits > 1)
+        _lib.stream(dev)))
+    LAUNCHES[0] += 1 + (splits > 1 and not cluster)
     return out, lse
 
 
@@ -196,7 +227,7 @@ def partials_plan(q_shape, N, device, window=0):
     """(splits, chunk_tiles) the key-stream kernel uses for partials of a
     (B, T, H, C) query block over N keys: at least two splits."""
     B, T, H, C = q_shape
-    chunk_tiles, splits = _stream_plan(B, T, H, N, 0, window, False, sm_count(device), None)
+    chunk_tiles, splits, _ = _stream_plan(B, T, H, N, 0, window, False, sm_count(device), None)
     if splits < 2:  # at least two partials, so that the caller always has partials to merge
         chunk_tiles, splits = max(1, math.ceil(chunk_tiles / 2)), 2
     return splits, chunk_tiles
@@ -240,6 +271,21 @@ def stream_partials(q, k, v, positions, scale, window=0, into=None, splits=None)
         chunk_tiles, B, T, H, C, N, int(window), float(scale), _lib.stream(q.device)))
     LAUNCHES[0] += 1
     return part_o, part_lse
+
+
+def merge_partial(part_o, part_lse, out_o=None, out_lse=None):
+    """Merge of S split partials (part_o (S, rows, C), part_lse (S, rows)
+    fp32) into one partial of the same kind, no sink: (out_o (rows, C) fp32,
+    the splits' output normalised by their common sum; out_lse (rows,), its
+    log). out_o / out_lse: write there (contiguous fp32) instead."""
+    _need_cuda(part_o, part_lse, out_o, out_lse)
+    S, rows, C = part_o.shape
+    out_o = torch.empty(rows, C, dtype=torch.float32, device=part_o.device) if out_o is None else out_o
+    out_lse = torch.empty(rows, dtype=torch.float32, device=part_o.device) if out_lse is None else out_lse
+    _lib.check(_lib.lib().wpt_attn_merge_partial(_lib.ptr(part_o), _lib.ptr(part_lse), S, rows, rows, C,
+                                                 _lib.ptr(out_o), _lib.ptr(out_lse), _lib.stream(part_o.device)))
+    LAUNCHES[0] += 1
+    return out_o, out_lse
 
 
 def merge_groups(parts, per, rows, H, C, sink=None, out=None, lse=None):
