@@ -672,6 +672,12 @@ def profile_case(args):
         q = (torch.randn(B, 1, 32, C, generator=g, device=device) * 0.5).bfloat16()
         pos = (L - 1).to(device)[:, None].contiguous()
         fn = lambda: ops.stream_forward(q, table[..., :C], table[..., C:], pos, C ** -0.5)  # noqa: E731
+    elif args.case == "decode_window":  # config 3's window-1024 rows with the sink, the first B of them
+        L, table, q, sink, pos = config3_inputs(device, 0)
+        table, q, pos = table[:B].contiguous(), q[:B].contiguous(), pos[:B].contiguous()
+        k, v = table[..., :C], table[..., C:]
+        empty = torch.empty(B, 1, 0, dtype=torch.int64, device=device)
+        fn = lambda: wpt_b200.sparse_attention(q, k, v, sink, empty, pos, C ** -0.5, 1024)  # noqa: E731
     elif args.case == "select":  # config 3's first B rows: exact + top-1024 choice, then the sparse layer
         L = config3_lengths()[:B]
         g = torch.Generator(device=device).manual_seed(10)
@@ -735,8 +741,8 @@ def main():
     parser.add_argument("--no-secondary", action="store_true")
     parser.add_argument("--e2e-steps", type=int, default=10)
     parser.add_argument("--case", default=None,
-                        help="profile one path: prefill, window, decode, select (A4 + A5), verify, accept, "
-                             "backward; bars (the Triton form) or config5 (end-to-end decode)")
+                        help="profile one path: prefill, window, decode, decode_window, select (A4 + A5), verify, "
+                             "accept, backward; bars (the Triton form) or config5 (end-to-end decode)")
     parser.add_argument("--case-batch", type=int, default=4)
     args = parser.parse_args()
     if args.case:

@@ -1,7 +1,8 @@
 """The multi-GPU long row on real GPUs: one process per GPU over NCCL, each
 holding a contiguous shard of a long row's keys; multi.long_decode's
-production branch (partials into the shared-layout buffer, one in-place
-all-gather, the grouped merge) must equal one GPU's call over the whole row
+production branch (each rank's split partials merged into one partial in
+its own chunk of the shared buffer, one in-place all-gather, the grouped
+merge) must equal one GPU's call over the whole row
 and the CPU oracle, on every rank, twice in a row (the plan's buffer is
 reused). Skipped with fewer than two GPUs; the same logic runs on gloo
 ranks on CPU in tests/test_multi_cpu.py."""

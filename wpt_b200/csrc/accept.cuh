@@ -37,6 +37,7 @@ namespace wpt {
 constexpr int ACCEPT_THREADS = 1024;  // the top-k statistics kernel
 constexpr int STAT_THREADS = 256;     // the segment statistics kernel
 constexpr int STAT_SEG = 8192;        // entries of one statistics unit (one warp)
+constexpr int STAT_VEC = 8;           // 16-byte loads a lane has in each batch (two batches in flight)
 constexpr int DRAW_THREADS = 256;
 constexpr int DRAW_WARPS = DRAW_THREADS / 32;
 constexpr int DRAW_CHUNK = 256;       // entries of one float64 chunk sum
@@ -451,25 +452,25 @@ __global__ void __launch_bounds__(STAT_THREADS) accept_stats_kernel(const Accept
     const float* x = p.scores + ij * p.V;
     const int v0 = s * STAT_SEG, v1 = min(p.V, v0 + STAT_SEG);
     float m = -INFINITY, z = 0.f;
-    if (vec) {  // lane l: 16-byte vectors l, l + 32, ... of the unit, in batches of four,
+    if (vec) {  // lane l: 16-byte vectors l, l + 32, ... of the unit, in batches of STAT_VEC,
                 // the next batch's loads in flight while a batch is reduced
       const float4* x4 = reinterpret_cast<const float4*>(x);
       const int e1 = v1 / 4;
-      auto fetch = [&](int b, float4 (&f)[4]) {
+      auto fetch = [&](int b, float4 (&f)[STAT_VEC]) {
 #pragma unroll
-        for (int k = 0; k < 4; ++k) {
+        for (int k = 0; k < STAT_VEC; ++k) {
           const int e = b + 32 * k;
           f[k] = e < e1 ? __ldg(x4 + e) : make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
         }
       };
-      float4 cur[4], nxt[4];
+      float4 cur[STAT_VEC], nxt[STAT_VEC];
       int b = v0 / 4 + lane;
       fetch(b, cur);
-      for (; b < e1; b += 4 * 32) {
-        fetch(b + 4 * 32, nxt);
-        float y[16];
+      for (; b < e1; b += STAT_VEC * 32) {
+        fetch(b + STAT_VEC * 32, nxt);
+        float y[4 * STAT_VEC];
 #pragma unroll
-        for (int k = 0; k < 4; ++k) {
+        for (int k = 0; k < STAT_VEC; ++k) {
           y[4 * k] = cur[k].x;
           y[4 * k + 1] = cur[k].y;
           y[4 * k + 2] = cur[k].z;
@@ -477,11 +478,11 @@ __global__ void __launch_bounds__(STAT_THREADS) accept_stats_kernel(const Accept
         }
         if (!UNIT_TEMP) {
 #pragma unroll
-          for (int k = 0; k < 16; ++k) y[k] = scale(y[k]);
+          for (int k = 0; k < 4 * STAT_VEC; ++k) y[k] = scale(y[k]);
         }
         accept_stat_batch<GREEDY>(m, z, y);
 #pragma unroll
-        for (int k = 0; k < 4; ++k) cur[k] = nxt[k];
+        for (int k = 0; k < STAT_VEC; ++k) cur[k] = nxt[k];
       }
     } else {  // lane l: entries l, l + 32, ...
       for (int b = v0 + lane; b < v1; b += 4 * 32) {

@@ -36,7 +36,11 @@ struct SplitLayout {
   }
 };
 
-// One warp per row; lane j handles columns j, j + 32, ...
+// One warp per row; lane j handles columns j, j + 32, ... Splits are taken
+// MERGE_BATCH at a time with all their loads issued together (log-sums,
+// then output rows), so a row costs about two memory round trips per batch
+// instead of one per split.
+constexpr int MERGE_BATCH = 8;
 template <int C>
 __global__ void __launch_bounds__(256) merge_kernel(const float* __restrict__ part_o,
                                                     const float* __restrict__ part_lse, int splits,
@@ -49,7 +53,13 @@ __global__ void __launch_bounds__(256) merge_kernel(const float* __restrict__ pa
   if (row >= rows) return;
   const int h = static_cast<int>(row % H);
   float m = -INFINITY;
-  for (int s = 0; s < splits; ++s) m = fmaxf(m, part_lse[lay.l(s) + row]);
+  for (int s0 = 0; s0 < splits; s0 += MERGE_BATCH) {
+    float l8[MERGE_BATCH];
+#pragma unroll
+    for (int k = 0; k < MERGE_BATCH; ++k) l8[k] = s0 + k < splits ? part_lse[lay.l(s0 + k) + row] : -INFINITY;
+#pragma unroll
+    for (int k = 0; k < MERGE_BATCH; ++k) m = fmaxf(m, l8[k]);
+  }
   const float sk = sink != nullptr ? sink[h] : -INFINITY;
   m = fmaxf(m, sk);
   float acc[C / 32];
@@ -57,14 +67,29 @@ __global__ void __launch_bounds__(256) merge_kernel(const float* __restrict__ pa
   for (int i = 0; i < C / 32; ++i) acc[i] = 0.f;
   float denom = 0.f;
   if (m != -INFINITY) {
-    for (int s = 0; s < splits; ++s) {
-      const float ls = part_lse[lay.l(s) + row];
-      if (ls == -INFINITY) continue;
-      const float w = __expf(ls - m);
-      denom += w;
-      const float* o = part_o + lay.o(s, C) + row * C;
+    for (int s0 = 0; s0 < splits; s0 += MERGE_BATCH) {
+      float w8[MERGE_BATCH], o8[MERGE_BATCH][C / 32];
 #pragma unroll
-      for (int i = 0; i < C / 32; ++i) acc[i] = fmaf(w, o[lane + 32 * i], acc[i]);
+      for (int k = 0; k < MERGE_BATCH; ++k) {
+        const int s = s0 + k;
+        const float ls = s < splits ? part_lse[lay.l(s) + row] : -INFINITY;
+        w8[k] = ls == -INFINITY ? 0.f : __expf(ls - m);
+        if (s < splits) {  // predicated: the batch's loads still issue together
+          const float* o = part_o + lay.o(s, C) + row * C;
+#pragma unroll
+          for (int i = 0; i < C / 32; ++i) o8[k][i] = o[lane + 32 * i];
+        } else {
+#pragma unroll
+          for (int i = 0; i < C / 32; ++i) o8[k][i] = 0.f;
+        }
+      }
+#pragma unroll
+      for (int k = 0; k < MERGE_BATCH; ++k) {
+        if (w8[k] == 0.f) continue;  // an empty split's output row is not defined
+        denom += w8[k];
+#pragma unroll
+        for (int i = 0; i < C / 32; ++i) acc[i] = fmaf(w8[k], o8[k][i], acc[i]);
+      }
     }
     if (sink != nullptr) denom += __expf(sk - m);
   }

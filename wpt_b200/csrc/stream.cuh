@@ -22,10 +22,11 @@
 // more than one split every CTA writes a partial result for the merge
 // kernel (merge.cuh), or, in cluster mode (at most 8 splits, the grid one
 // wave), the splits of a query group form one thread-block cluster: each
-// CTA leaves its unnormalised output and its columns' maximum and sum in
-// its own shared memory, and after a cluster barrier CTA k combines columns
-// k, k + splits, ... from all of them (distributed shared memory loads) and
-// writes the final output, so neither partials in HBM nor a second launch.
+// CTA pushes (remote shared-memory stores) its unnormalised output and its
+// columns' maximum and sum to the CTA that owns each column (column c: CTA
+// c % splits), and after a cluster barrier every CTA combines its columns
+// from its own shared memory and writes the final output, so neither
+// partials in HBM nor a second launch.
 //
 // Loads: range mode takes whole tiles by TMA. Gather mode: 2 loader warps
 // copy each slot's 256-byte K and V rows with 16-byte cp.async (coalesced:
@@ -130,22 +131,28 @@ __device__ __forceinline__ void stream_pv_steps(uint32_t d, uint64_t dv, uint64_
 }
 
 // Cluster mode's combine, run by every thread of every CTA of the cluster
-// (one query group's splits). Each CTA has left, for its columns, the lazy
-// maximum (s_m, base 2), the sum of exponentials (s_l; 0 when the split saw
-// no visible key or failed) and the unnormalised output (s_o, column-major
-// with 128 floats per column). CTA k writes columns k, k + S, ...: the
-// output row sum_i w_i o_i / L and its log-sum, w_i = 2^(m_i - M) and
-// L = sum_i w_i l_i plus the sink's exp(sink - M), M the largest maximum.
+// (one query group's splits) after each CTA has left, for its columns, the
+// lazy maximum (s_m, base 2), the sum of exponentials (s_l; 0 when the
+// split saw no visible key or a wait failed) and the unnormalised output
+// (s_o, 128 floats a column) in its own shared memory. CTA k owns columns
+// k, k + S, ...: after a cluster barrier its threads read every split's
+// (m, l) of those columns once (distributed shared memory loads), turn them
+// into weights w_i / L (w_i = 2^(m_i - M) over the splits with l_i > 0, L =
+// sum_i w_i l_i plus the sink's exp(sink - M), M their largest m), then each
+// 4-float chunk of an owned column's output takes all S splits' chunks in
+// one round of loads. A second barrier keeps every CTA's memory in place
+// until the others have read it.
 __device__ __forceinline__ void stream_cluster_merge(const StreamParams& p, const float* s_m, const float* s_l,
-                                                     const float* s_o, int64_t row0, int ncols) {
+                                                     const float* s_o, float* s_w, int64_t row0, int ncols) {
   constexpr int C = 128;
   cluster_sync();
   const int S = p.cluster;
   const int rank = static_cast<int>(cluster_rank());
   const int mine = ncols > rank ? (ncols - rank + S - 1) / S : 0;  // columns rank, rank + S, ...
   const uint32_t am = smem_u32(s_m), al = smem_u32(s_l), ao = smem_u32(s_o);
-  for (int item = threadIdx.x; item < mine * (C / 4); item += blockDim.x) {
-    const int c = rank + (item / (C / 4)) * S, quad = item % (C / 4);
+  // s_w[cl * 9 + i]: split i's weight over L for owned column cl; s_w[cl * 9 + 8]: the log-sum
+  if (static_cast<int>(threadIdx.x) < mine) {
+    const int cl = threadIdx.x, c = rank + cl * S;
     float mi[8], li[8];
     float M = -INFINITY;
 #pragma unroll
@@ -155,31 +162,47 @@ __device__ __forceinline__ void stream_cluster_merge(const StreamParams& p, cons
       if (i < S) {
         mi[i] = dsmem_ld(dsmem_map(am + c * 4, i));
         li[i] = dsmem_ld(dsmem_map(al + c * 4, i));
-        if (li[i] > 0.f) M = fmaxf(M, mi[i]);
       }
     }
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+      if (li[i] > 0.f) M = fmaxf(M, mi[i]);
     const float msub = M == -INFINITY ? 0.f : M;
-    float L = 0.f;
-    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    float w[8], L = 0.f;
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
-      if (i < S && li[i] > 0.f) {
-        const float w = fast_exp2(mi[i] - msub);
-        const float4 o = dsmem_ld4(dsmem_map(ao + (c * C + quad * 4) * 4, i));
-        L = fmaf(w, li[i], L);
-        acc.x = fmaf(w, o.x, acc.x);
-        acc.y = fmaf(w, o.y, acc.y);
-        acc.z = fmaf(w, o.z, acc.z);
-        acc.w = fmaf(w, o.w, acc.w);
-      }
+      w[i] = li[i] > 0.f ? fast_exp2(mi[i] - msub) : 0.f;
+      L = fmaf(w[i], li[i], L);
     }
     if (p.sink != nullptr) L += fast_exp2(fmaf(p.sink[c % p.H], LOG2E, -msub));
     const float inv = L > 0.f ? 1.f / L : 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) s_w[cl * 9 + i] = w[i] * inv;
+    s_w[cl * 9 + 8] = L > 0.f ? (msub + log2f(L)) * LN2 : -INFINITY;
+  }
+  __syncthreads();
+  for (int item = threadIdx.x; item < mine * (C / 4); item += blockDim.x) {
+    const int cl = item / (C / 4), quad = item % (C / 4), c = rank + cl * S;
+    float4 o[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+      if (i < S && s_w[cl * 9 + i] != 0.f) o[i] = dsmem_ld4(dsmem_map(ao + (c * C + quad * 4) * 4, i));
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const float w = i < S ? s_w[cl * 9 + i] : 0.f;
+      if (w != 0.f) {
+        acc.x = fmaf(w, o[i].x, acc.x);
+        acc.y = fmaf(w, o[i].y, acc.y);
+        acc.z = fmaf(w, o[i].z, acc.z);
+        acc.w = fmaf(w, o[i].w, acc.w);
+      }
+    }
     uint2 packed;
-    packed.x = pack_bf16(acc.x * inv, acc.y * inv);
-    packed.y = pack_bf16(acc.z * inv, acc.w * inv);
+    packed.x = pack_bf16(acc.x, acc.y);
+    packed.y = pack_bf16(acc.z, acc.w);
     *reinterpret_cast<uint2*>(p.out + (row0 + c) * C + quad * 4) = packed;
-    if (quad == 0) p.lse[row0 + c] = L > 0.f ? (msub + log2f(L)) * LN2 : -INFINITY;
+    if (quad == 0) p.lse[row0 + c] = s_w[cl * 9 + 8];
   }
   cluster_sync();  // no CTA leaves while another still reads its shared memory
 }
@@ -223,29 +246,60 @@ __global__ void __launch_bounds__(STREAM_THREADS, 1)
   constexpr bool gather = GATHER;
   const int64_t rows_total = static_cast<int64_t>(p.B) * p.T * p.H;
 
-  if (threadIdx.x == 0) {
-    s_range[0] = INT_MAX;
-    s_range[1] = -1;
-  }
-  if (threadIdx.x < 64) {
-    s_m[threadIdx.x] = -INFINITY;
-    s_qlo[threadIdx.x] = 0;
-    s_qhi[threadIdx.x] = -1;
-    const int tq = static_cast<int>(threadIdx.x) / p.H;  // column -> its query in the group, -1 for padding
-    s_colq[threadIdx.x] = (static_cast<int>(threadIdx.x) < NCOL && tq < TQg) ? tq : -1;
-  }
-  __syncthreads();
-  if (static_cast<int>(threadIdx.x) < TQg) {
-    int lo, hi;
-    stream_query_rows(p, b, t0 + threadIdx.x, lo, hi);
-    s_qlo[threadIdx.x] = lo;
-    s_qhi[threadIdx.x] = hi;
-    if (!gather && hi >= lo) {
-      atomicMin(&s_range[0], lo);
-      atomicMax(&s_range[1], hi);
+  // Set-up, one barrier: warp 0 reads the group's query positions (their
+  // rows, and in range mode the union of their ranges) while warp 1 clears
+  // the column state, warp 2 the unused query slots, warp 3 initialises the
+  // mbarriers and warp 4 allocates TMEM.
+  const int lane = threadIdx.x & 31;
+  if (warp == 0) {
+    int rlo = INT_MAX, rhi = -1;
+    for (int tq = lane; tq < TQg; tq += 32) {
+      int lo, hi;
+      stream_query_rows(p, b, t0 + tq, lo, hi);
+      s_qlo[tq] = lo;
+      s_qhi[tq] = hi;
+      if (hi >= lo) {
+        rlo = min(rlo, lo);
+        rhi = max(rhi, hi);
+      }
     }
+    rlo = __reduce_min_sync(0xffffffffu, rlo);
+    rhi = __reduce_max_sync(0xffffffffu, rhi);
+    if (lane == 0) {
+      s_range[0] = rlo;
+      s_range[1] = rhi;
+    }
+  } else if (warp == 1 || warp == 2) {
+    for (int i = lane; i < 64; i += 32) {
+      if (warp == 1) {
+        s_m[i] = -INFINITY;
+        const int tq = i / p.H;  // column -> its query in the group, -1 for padding
+        s_colq[i] = (i < NCOL && tq < TQg) ? tq : -1;
+      } else if (i >= TQg) {
+        s_qlo[i] = 0;
+        s_qhi[i] = -1;
+      }
+    }
+  } else if (warp == 3 && lane == 0) {
+    mbar_init(q_full, STREAM_LOADERS);
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(full + s, GATHER ? STREAM_LOADERS : 1);
+      mbar_init(kv_empty + s, 1);
+    }
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(s_full + s, 1);
+      mbar_init(p_ready + s, 128);
+    }
+    mbar_init(o_done, 1);
+    mbar_init(o_final, 1);
+    fence_mbar_init();
+  } else if (warp == 4) {
+    tmem_alloc(s_tmem, L::TMEM_COLS);
+    tmem_relinquish();
   }
+  tc_fence_before();
   __syncthreads();
+  tc_fence_after();
   // this CTA's slots: [slot0, slot_end) of `total`
   int64_t total;
   int range_lo = 0;
@@ -288,16 +342,15 @@ __global__ void __launch_bounds__(STREAM_THREADS, 1)
   };
 
   if (ntiles == 0) {  // nothing to read: an empty partial, or the sink alone
+    const int64_t row0 = (static_cast<int64_t>(b) * p.T + t0) * p.H;
     if (p.cluster > 1) {  // an empty share of the cluster's combine (s_m holds -inf)
       if (threadIdx.x < 64) s_l[threadIdx.x] = 0.f;
-      stream_cluster_merge(p, s_m, s_l, reinterpret_cast<const float*>(sP),
-                           (static_cast<int64_t>(b) * p.T + t0) * p.H, TQg * p.H);
-      return;
-    }
-    if (static_cast<int>(threadIdx.x) < NCOL) {
+      stream_cluster_merge(p, s_m, s_l, reinterpret_cast<const float*>(sP), reinterpret_cast<float*>(sK), row0,
+                           TQg * p.H);
+    } else if (static_cast<int>(threadIdx.x) < NCOL) {
       const int col = threadIdx.x, tq = col / p.H, h = col - tq * p.H;
       if (tq < TQg) {
-        const int64_t orow = (static_cast<int64_t>(b) * p.T + t0 + tq) * p.H + h;
+        const int64_t orow = row0 + tq * p.H + h;
         if (p.splits > 1) {
           p.part_lse[split * rows_total + orow] = -INFINITY;
         } else {
@@ -306,30 +359,15 @@ __global__ void __launch_bounds__(STREAM_THREADS, 1)
         }
       }
     }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 4) {
+      tc_fence_after();
+      tmem_dealloc(*s_tmem, L::TMEM_COLS);
+    }
     return;
   }
 
-  if (threadIdx.x == 0) {
-    mbar_init(q_full, STREAM_LOADERS);
-    for (int s = 0; s < STAGES; ++s) {
-      mbar_init(full + s, GATHER ? STREAM_LOADERS : 1);
-      mbar_init(kv_empty + s, 1);
-    }
-    for (int s = 0; s < 2; ++s) {
-      mbar_init(s_full + s, 1);
-      mbar_init(p_ready + s, 128);
-    }
-    mbar_init(o_done, 1);
-    mbar_init(o_final, 1);
-    fence_mbar_init();
-  }
-  if (warp == 4) {
-    tmem_alloc(s_tmem, L::TMEM_COLS);
-    tmem_relinquish();
-  }
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
   const uint32_t tmem = *s_tmem;
   griddep_launch();  // the merge that follows may start launching (it waits for this grid's results)
 
@@ -692,8 +730,8 @@ __global__ void __launch_bounds__(STREAM_THREADS, 1)
       }
     }
     named_barrier(1, 128);
+    float o[NCOL];
     if (ok) {
-      float o[NCOL];
       if constexpr (NCOL == 16) {
         uint32_t x[16];
         tmem_ld16(tO, x);
@@ -708,14 +746,18 @@ __global__ void __launch_bounds__(STREAM_THREADS, 1)
           for (int c = 0; c < 32; ++c) o[c32 * 32 + c] = __uint_as_float(x[c]);
         }
       }
-      // thread r holds element r of the head width for every column (query, head)
-      if (p.cluster > 1) {
-        // unnormalised, into the P buffers (2 x NCOL x 128 bf16 = NCOL x 128
-        // floats; the last P V product, which read them, has completed)
+    }
+    // thread r holds element r of the head width for every column (query, head)
+    if (p.cluster > 1) {
+      // unnormalised, into the P buffers (2 x NCOL x 128 bf16 = NCOL x 128
+      // floats; the last P V product, which read them, has completed)
+      if (ok) {
         float* dst = reinterpret_cast<float*>(sP) + r;
 #pragma unroll
         for (int c = 0; c < NCOL; ++c) dst[c * C] = o[c];
-      } else if (p.splits == 1) {
+      }
+    } else if (ok) {
+      if (p.splits == 1) {
         __nv_bfloat16* dst = p.out + row0 * C + r;
 #pragma unroll
         for (int c = 0; c < NCOL; ++c)
@@ -735,8 +777,8 @@ __global__ void __launch_bounds__(STREAM_THREADS, 1)
     tmem_dealloc(tmem, L::TMEM_COLS);
   }
   if (p.cluster > 1)
-    stream_cluster_merge(p, s_m, s_l, reinterpret_cast<const float*>(sP), (static_cast<int64_t>(b) * p.T + t0) * p.H,
-                         TQg * p.H);
+    stream_cluster_merge(p, s_m, s_l, reinterpret_cast<const float*>(sP), reinterpret_cast<float*>(sK),
+                         (static_cast<int64_t>(b) * p.T + t0) * p.H, TQg * p.H);
 }
 
 }  // namespace wpt
