@@ -130,22 +130,35 @@ __global__ void __launch_bounds__(128) bwd_prep_kernel(const BwdParams p) {
   const int t = j * p.TQ + tq;
   const bool valid = tq < p.TQ && t < p.T;
   __shared__ float s_sink[128];
+  __shared__ float s_delta[128];
   __shared__ int s_lo[4], s_hi[4];
   if (r < p.H) s_sink[r] = 0.f;
+  // delta = rowsum(dO * O) of the warp's 32 rows: per step each half-warp
+  // reads one row of O and dO (16 lanes x 16 bytes, coalesced) and sums its
+  // dot product over the half
+  {
+    const int half = lane >> 4, ch = lane & 15;
+#pragma unroll 4
+    for (int k = 0; k < 16; ++k) {
+      const int rr = warp * 32 + 2 * k + half;
+      const int tq2 = rr / p.H, t2 = j * p.TQ + tq2;
+      float d = 0.f;
+      if (tq2 < p.TQ && t2 < p.T) {
+        const int64_t row2 = (static_cast<int64_t>(b) * p.T + t2) * p.H + (rr - tq2 * p.H);
+        d = bf16_dot8(reinterpret_cast<const uint4*>(p.out + row2 * 128)[ch],
+                      reinterpret_cast<const uint4*>(p.d_out + row2 * 128)[ch]);
+      }
+#pragma unroll
+      for (int o = 8; o > 0; o >>= 1) d += __shfl_xor_sync(0xffffffffu, d, o);
+      if (ch == 0) s_delta[rr] = d;
+    }
+  }
   __syncthreads();
   float lse2 = 0.f, delta = 0.f;
   int lo = INT_MAX, hi = -1;
   if (valid) {
     const int64_t row = (static_cast<int64_t>(b) * p.T + t) * p.H + h;
-    const uint4* o = reinterpret_cast<const uint4*>(p.out + row * 128);
-    const uint4* g = reinterpret_cast<const uint4*>(p.d_out + row * 128);
-    float acc0 = 0.f, acc1 = 0.f;
-#pragma unroll
-    for (int i = 0; i < 16; i += 2) {
-      acc0 += bf16_dot8(o[i], g[i]);
-      acc1 += bf16_dot8(o[i + 1], g[i + 1]);
-    }
-    delta = acc0 + acc1;
+    delta = s_delta[r];
     const float l = p.lse[row];
     lse2 = l * LOG2E;
     // a row that reads nothing has lse = sink (or -inf without one) and out = 0

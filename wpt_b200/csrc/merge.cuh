@@ -37,9 +37,9 @@ struct SplitLayout {
 };
 
 // One warp per row; lane j handles columns j, j + 32, ... Splits are taken
-// MERGE_BATCH at a time with all their loads issued together (log-sums,
-// then output rows), so a row costs about two memory round trips per batch
-// instead of one per split.
+// MERGE_BATCH at a time with all their loads (log-sums and output rows)
+// issued together, in one online pass, so a row costs about one memory round
+// trip per batch instead of one per split.
 constexpr int MERGE_BATCH = 8;
 template <int C>
 __global__ void __launch_bounds__(256) merge_kernel(const float* __restrict__ part_o,
@@ -52,47 +52,50 @@ __global__ void __launch_bounds__(256) merge_kernel(const float* __restrict__ pa
   const int lane = threadIdx.x & 31;
   if (row >= rows) return;
   const int h = static_cast<int>(row % H);
-  float m = -INFINITY;
-  for (int s0 = 0; s0 < splits; s0 += MERGE_BATCH) {
-    float l8[MERGE_BATCH];
-#pragma unroll
-    for (int k = 0; k < MERGE_BATCH; ++k) l8[k] = s0 + k < splits ? part_lse[lay.l(s0 + k) + row] : -INFINITY;
-#pragma unroll
-    for (int k = 0; k < MERGE_BATCH; ++k) m = fmaxf(m, l8[k]);
-  }
+  // one pass: each batch's log-sums and output rows are loaded together, and
+  // the running maximum m (with acc and denom scaled to it) only rises
   const float sk = sink != nullptr ? sink[h] : -INFINITY;
-  m = fmaxf(m, sk);
+  float m = sk;  // the sink joins the maximum (it is one more term of the denominator)
   float acc[C / 32];
 #pragma unroll
   for (int i = 0; i < C / 32; ++i) acc[i] = 0.f;
   float denom = 0.f;
-  if (m != -INFINITY) {
-    for (int s0 = 0; s0 < splits; s0 += MERGE_BATCH) {
-      float w8[MERGE_BATCH], o8[MERGE_BATCH][C / 32];
+  for (int s0 = 0; s0 < splits; s0 += MERGE_BATCH) {
+    float l8[MERGE_BATCH], o8[MERGE_BATCH][C / 32];
 #pragma unroll
-      for (int k = 0; k < MERGE_BATCH; ++k) {
-        const int s = s0 + k;
-        const float ls = s < splits ? part_lse[lay.l(s) + row] : -INFINITY;
-        w8[k] = ls == -INFINITY ? 0.f : __expf(ls - m);
-        if (s < splits) {  // predicated: the batch's loads still issue together
-          const float* o = part_o + lay.o(s, C) + row * C;
+    for (int k = 0; k < MERGE_BATCH; ++k) {
+      const int s = s0 + k;
+      if (s < splits) {  // predicated: the batch's loads issue together
+        l8[k] = part_lse[lay.l(s) + row];
+        const float* o = part_o + lay.o(s, C) + row * C;
 #pragma unroll
-          for (int i = 0; i < C / 32; ++i) o8[k][i] = o[lane + 32 * i];
-        } else {
+        for (int i = 0; i < C / 32; ++i) o8[k][i] = o[lane + 32 * i];
+      } else {
+        l8[k] = -INFINITY;
 #pragma unroll
-          for (int i = 0; i < C / 32; ++i) o8[k][i] = 0.f;
-        }
-      }
-#pragma unroll
-      for (int k = 0; k < MERGE_BATCH; ++k) {
-        if (w8[k] == 0.f) continue;  // an empty split's output row is not defined
-        denom += w8[k];
-#pragma unroll
-        for (int i = 0; i < C / 32; ++i) acc[i] = fmaf(w8[k], o8[k][i], acc[i]);
+        for (int i = 0; i < C / 32; ++i) o8[k][i] = 0.f;
       }
     }
-    if (sink != nullptr) denom += __expf(sk - m);
+    float mb = m;
+#pragma unroll
+    for (int k = 0; k < MERGE_BATCH; ++k) mb = fmaxf(mb, l8[k]);
+    if (mb != m) {  // the maximum rises: what is summed so far is rescaled (m = -inf: nothing summed yet)
+      const float r = m == -INFINITY ? 0.f : __expf(m - mb);
+      denom *= r;
+#pragma unroll
+      for (int i = 0; i < C / 32; ++i) acc[i] *= r;
+      m = mb;
+    }
+#pragma unroll
+    for (int k = 0; k < MERGE_BATCH; ++k) {
+      if (l8[k] == -INFINITY) continue;  // an empty split's output row is not defined
+      const float w = __expf(l8[k] - m);
+      denom += w;
+#pragma unroll
+      for (int i = 0; i < C / 32; ++i) acc[i] = fmaf(w, o8[k][i], acc[i]);
+    }
   }
+  if (sink != nullptr && m != -INFINITY) denom += __expf(sk - m);
   const float inv = denom > 0.f ? 1.f / denom : 0.f;
   if (out_f32 != nullptr) {  // a partial of its own (normalised output, fp32) for a later merge
 #pragma unroll
