@@ -91,7 +91,8 @@ def long_decode(q, k_shard, v_shard, shard_start, positions, scale, sink=None, g
     would share the buffers."""
     B, T, H, C = q.shape
     world = dist.get_world_size(group) if dist.is_initialized() else 1
-    local = positions - shard_start  # rows of this shard the query sees: 0 .. local (none when negative)
+    # rows of this shard the query sees: 0 .. local (none when negative)
+    local = positions if shard_start == 0 else positions - shard_start
     if world == 1:  # the whole row is here: one kernel call
         return ops.stream_forward(q, k_shard, v_shard, local, scale, sink=sink)
     rank = dist.get_rank(group)
