@@ -342,6 +342,29 @@ def secondary(wb, ops, device, rank, world, hbm):
                           "graph_value": round(flops_v / gms_v / 1e9, 1), "graph_ms": round(gms_v, 4),
                           "algorithmic_flops": flops_v}
     del t4
+    # the writer's sampling step at config 5's decode shape (64 rows, d_model 2048, vocabulary 65536):
+    # the output head's product on the tensor cores, then the draw; rows in equal shares. torch's own
+    # product (cuBLAS) of the same operands is timed beside it.
+    Rh, Dh, Vh = 64, 2048, 65536
+    gh = torch.Generator(device=device).manual_seed(6)
+    hh = torch.randn(Rh, Dh, generator=gh, device=device).bfloat16()
+    wh = (torch.randn(Vh, Dh, generator=gh, device=device) * Dh ** -0.5).bfloat16()
+    rh = torch.rand(Rh, generator=gh, device=device)
+    mine_h = multi.shard_rows(Rh, world, rank)
+    hh, rh = hh[mine_h].contiguous(), rh[mine_h].contiguous()
+    f_h = lambda: ops.head_scores(hh, wh)  # noqa: E731
+    f_hs = lambda: wb.head_sample(hh, wh, rh, 1.0, None)  # noqa: E731
+    f_hc = lambda: hh @ wh.T  # noqa: E731
+    ms_h, gms_h = both(f_h)
+    ms_hs, gms_hs = both(f_hs)
+    ms_hc, gms_hc = both(f_hc)
+    bytes_h = Vh * Dh * 2 * world + Rh * Dh * 2 + Rh * Vh * 4  # the weight once per GPU, h, the scores
+    out["head_scores"] = bw_line("output head scores (config 5 decode shape: 64 x 2048 @ 65536 x 2048), HBM GB/s",
+                                 bytes_h, ms_h, gms_h, hbm, world)
+    out["head_scores"]["torch_matmul_graph_ms"] = round(gms_hc, 4)
+    out["head_sample"] = {"metric": "head + sampling step (64 rows, vocabulary 65536), ms", "unit": "ms",
+                          "ms": round(ms_hs, 4), "graph_ms": round(gms_hs, 4)}
+    del wh
     # config 4: acceptance step, rows in equal shares
     R, n, V = 32, 16, 65536
     ga = torch.Generator(device=device).manual_seed(4)
@@ -695,6 +718,11 @@ def profile_case(args):
         t4, q4, cl = t4[:B].contiguous(), q4[:B].contiguous(), cl[:B].contiguous()
         par4 = torch.tensor(parents, device=device)
         fn = lambda: wpt_b200.tree_attention(q4, t4[..., :C], t4[..., C:], cl, par4, C ** -0.5)  # noqa: E731
+    elif args.case == "head":  # the output head's product at config 5's decode shape, B rows
+        gh = torch.Generator(device=device).manual_seed(6)
+        hh = torch.randn(B, 2048, generator=gh, device=device).bfloat16()
+        wh = (torch.randn(65536, 2048, generator=gh, device=device) * 2048 ** -0.5).bfloat16()
+        fn = lambda: ops.head_scores(hh, wh)  # noqa: E731
     elif args.case == "accept":  # config 4's acceptance on B rows, stochastic then greedy
         R, n, V = B, 16, 65536
         ga = torch.Generator(device=device).manual_seed(4)
@@ -742,7 +770,7 @@ def main():
     parser.add_argument("--e2e-steps", type=int, default=10)
     parser.add_argument("--case", default=None,
                         help="profile one path: prefill, window, decode, decode_window, select (A4 + A5), verify, "
-                             "accept, backward; bars (the Triton form) or config5 (end-to-end decode)")
+                             "head, accept, backward; bars (the Triton form) or config5 (end-to-end decode)")
     parser.add_argument("--case-batch", type=int, default=4)
     args = parser.parse_args()
     if args.case:

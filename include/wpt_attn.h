@@ -239,6 +239,24 @@ int wpt_attn_merge_groups(const float* parts, int groups, int per, int64_t rows,
                           const float* sink, void* out, float* lse, void* stream);
 
 /*
+ * The output head's product ahead of sampling: scores (R, V) fp32 =
+ * h (R, D) W (V, D)^T, bf16 inputs with fp32 accumulation on the tensor
+ * cores (the vocabulary rows as the MMA's M, W streamed once). Replaces the
+ * head call of a decode step (packages/wpt-model/src/wpt_model/model.py:267,
+ * 471: nn.Linear(d_model, vocab, bias=False), bf16 under autocast, widened
+ * with .float()), whose scores then feed wpt_accept's statistics and draw
+ * (wpt_inference/__init__.py:173-182).
+ *   h          bf16 (R, D), row stride h_stride elements (a multiple of 8)
+ *   w          bf16 (V, D), row stride w_stride elements (a multiple of 8)
+ *   D          a multiple of 64
+ *   round_bf16 1: each score rounded to bf16 first, as the reference's
+ *              autocast head returns it
+ *   scores     fp32 (R, V), contiguous
+ */
+int wpt_head_scores(const void* h, int64_t h_stride, const void* w, int64_t w_stride, int R, int D, int V,
+                    int round_bf16, float* scores, void* stream);
+
+/*
  * The acceptance step of speculative decoding, WPT's rule
  * (packages/wpt-inference/src/wpt_inference/__init__.py:173-179 the
  * probabilities, :210-222 the loop), for R rows at once:

@@ -25,6 +25,19 @@ two rules.
 import numpy as np
 
 
+def head_scores(h, weight, round_bf16=True):
+    """model.py:267,471: the output head, h (R, D) @ weight (V, D)^T (an
+    nn.Linear without bias), in float64 here; round_bf16 rounds each score to
+    bf16 (round to nearest even), as the reference's head under bf16 autocast
+    returns it before .float()."""
+    s = np.asarray(h, np.float64) @ np.asarray(weight, np.float64).T
+    if not round_bf16:
+        return s.astype(np.float32)
+    bits = s.astype(np.float32).view(np.uint32).astype(np.uint64)
+    bits = (bits + 0x7FFF + ((bits >> 16) & 1)) >> 16 << 16
+    return bits.astype(np.uint32).view(np.float32)
+
+
 def probabilities(scores, temperature, top_k):
     """__init__.py:173-179 in float32: (..., V) -> (..., V)."""
     x = np.asarray(scores, np.float32) / np.float32(temperature)

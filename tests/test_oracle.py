@@ -233,3 +233,11 @@ def test_cache_append_restatement_matches_the_reference_rows(gold):
         assert table.shape == d[f"table{step}"].shape
         assert np.array_equal(table, d[f"table{step}"])
         lengths = lengths + counts
+
+
+def test_head_scores_rounding_is_bf16_nearest_even():
+    # the reference's head under bf16 autocast returns bf16 scores (model.py:471)
+    from oracle import accept as oa
+    x = np.array([[1.0, 3.14159265, -2.718281828, 1e-3, 65504.5, 1.0 + 2.0 ** -8, 1.0 + 3 * 2.0 ** -8]])
+    want = torch.tensor(x).float().bfloat16().float().numpy()
+    assert np.array_equal(oa.head_scores(x, np.eye(x.shape[1])), want)

@@ -262,6 +262,18 @@ def sample(scores, resample, temperature=1.0, top_k=None):
     return tokens[:, 0]
 
 
+def head_sample(h, weight, resample, temperature=1.0, top_k=None, round_bf16=True):
+    """The writer's step from the last hidden state of each row:
+    the output head's scores on the tensor cores (model.py:267,471,
+    ops.head_scores; rounded to bf16 as the reference's autocast head gives
+    them), then sample(): softmax of the top_k-masked scores / temperature and
+    the inverse-CDF draw with resample (wpt_inference/__init__.py:173-182).
+    h (R, D) bf16 (final-normed), weight (V, D) bf16, resample (R,).
+    Returns (tokens (R,) int64, scores (R, V) fp32)."""
+    scores = ops.head_scores(h, weight, round_bf16)
+    return sample(scores, resample, temperature, top_k), scores
+
+
 # ------------------------------------------------------------ cache append
 
 def cache_append(held, new, first, counts, need=None):

@@ -26,6 +26,7 @@ SIGNATURES = {
                         _I, _I, _I, _I, _I, _I, _F, _P],
     "wpt_attn_topk": [_P, _P, _I64, _I64, _P, _P, _P, _I64, _P, _I, _I, _I, _I, _I, _I, _I, _F, _P],
     "wpt_accept": [_P, _P, _P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _F, _I, _P],
+    "wpt_head_scores": [_P, _I64, _P, _I64, _I, _I, _I, _I, _P, _P],
     "wpt_accept_scratch_bytes": [_I, _I, _I],
     "wpt_temperature_scale": [_P, _I64, _F, _P, _P],
     "wpt_attn_decode_noalloc": [_P, _P, _P, _I64, _I64, _I64, _I64, _P, _P, _P, _I, _P, _P, _P, _I, _I, _I, _I,

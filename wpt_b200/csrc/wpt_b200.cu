@@ -16,6 +16,7 @@
 #include "backward.cuh"
 #include "cache.cuh"
 #include "common.cuh"
+#include "head.cuh"
 #include "merge.cuh"
 #include "prefill.cuh"
 #include "select.cuh"
@@ -931,6 +932,65 @@ extern "C" int wpt_temperature_scale(const float* x, int64_t n, float temperatur
 extern "C" size_t wpt_accept_scratch_bytes(int R, int n, int V) {
   if (R < 0 || n < 0 || V < 1) return 0;
   return wpt::accept_scratch(R, n, V).bytes;
+}
+
+namespace {
+template <int N>
+int launch_head(const CUtensorMap& tw, const CUtensorMap& th, const wpt::HeadParams& p, cudaStream_t stream) {
+  using L = wpt::HeadLayout<N>;
+  static_assert(L::BYTES <= 232448, "head kernel shared memory exceeds 227 KB");
+  auto kernel = wpt::head_kernel<N>;
+  if (int rc = allow_smem(kernel, L::BYTES)) return rc;
+  int sms = 148;
+  current_device(&sms);
+  const int grid = p.tiles < sms ? p.tiles : sms;  // persistent: one CTA per SM walks the vocabulary tiles
+  kernel<<<grid, wpt::HEAD_THREADS, L::BYTES, stream>>>(tw, th, p);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "head_kernel launch");
+  return WPT_OK;
+}
+}  // namespace
+
+extern "C" int wpt_head_scores(const void* h, int64_t h_stride, const void* w, int64_t w_stride, int R, int D,
+                               int V, int round_bf16, float* scores, void* stream) {
+  if (R < 1 || D < 1 || V < 1) return fail(WPT_ERR_INVALID, "empty shape R=%d D=%d V=%d", R, D, V);
+  if (D % 64 != 0) return fail(WPT_ERR_UNSUPPORTED, "model width %d: the head kernel takes multiples of 64", D);
+  if (!h || !w || !scores) return fail(WPT_ERR_INVALID, "a required pointer is NULL");
+  if (!aligned16(h) || !aligned16(w)) return fail(WPT_ERR_INVALID, "h and the head weight must be 16-byte aligned");
+  if (h_stride < D || w_stride < D || h_stride % 8 || w_stride % 8)
+    return fail(WPT_ERR_INVALID, "row strides must be at least D and multiples of 8 elements");
+  if (static_cast<int64_t>(R) * V >= (int64_t(1) << 40)) return fail(WPT_ERR_UNSUPPORTED, "R*V too large");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int tiles = (V + 127) / 128;
+  CUtensorMap tw;
+  {
+    cuuint64_t dims[2] = {static_cast<cuuint64_t>(D), static_cast<cuuint64_t>(V)};
+    cuuint64_t strides[1] = {static_cast<cuuint64_t>(w_stride) * 2};
+    cuuint32_t box[2] = {64, 128};
+    if (int rc = tensor_map(&tw, w, 2, dims, strides, box)) return rc;
+  }
+  for (int r0 = 0; r0 < R; r0 += 128) {  // up to 128 rows of h per launch (the MMA's N)
+    const int rows = R - r0 < 128 ? R - r0 : 128;
+    const int n = rows <= 32 ? 32 : rows <= 64 ? 64 : 128;
+    const void* hb = static_cast<const __nv_bfloat16*>(h) + static_cast<int64_t>(r0) * h_stride;
+    CUtensorMap th;
+    cuuint64_t dims[2] = {static_cast<cuuint64_t>(D), static_cast<cuuint64_t>(rows)};
+    cuuint64_t strides[1] = {static_cast<cuuint64_t>(h_stride) * 2};
+    cuuint32_t box[2] = {64, static_cast<cuuint32_t>(n)};
+    if (int rc = tensor_map(&th, hb, 2, dims, strides, box)) return rc;
+    wpt::HeadParams p;
+    p.scores = scores + static_cast<int64_t>(r0) * V;
+    if (int rc = status_word(&p.status)) return rc;
+    p.R = rows;
+    p.V = V;
+    p.D = D;
+    p.tiles = tiles;
+    p.round_bf16 = round_bf16 ? 1 : 0;
+    const int rc = n == 32 ? launch_head<32>(tw, th, p, s) : n == 64 ? launch_head<64>(tw, th, p, s)
+                                                                     : launch_head<128>(tw, th, p, s);
+    if (rc) return rc;
+  }
+  return WPT_OK;
 }
 
 extern "C" int wpt_accept(const float* scores, const int64_t* drafted, const float* q, const float* uniforms,

@@ -465,6 +465,29 @@ def tree_bits(parents, B, base=None):
     return bits, positions
 
 
+def head_scores(h, weight, round_bf16=True):
+    """(R, V) fp32 scores = h (R, D) @ weight (V, D)^T from the tcgen05 head
+    kernel (model.py:267,471: the output head, bias-free; with round_bf16 each
+    score is rounded to bf16 first, as the reference's autocast head returns
+    it). h and weight bf16 with contiguous rows; D a multiple of 64."""
+    _need_cuda(h, weight)
+    if h.dtype != torch.bfloat16 or weight.dtype != torch.bfloat16:
+        raise NotImplementedError("the head kernel takes bf16 hidden states and weights")
+    if h.stride(-1) != 1:
+        h = h.contiguous()
+    if weight.stride(-1) != 1:
+        weight = weight.contiguous()
+    R, D = h.shape
+    V = weight.shape[0]
+    if weight.shape[1] != D:
+        raise ValueError(f"hidden width {D} against a head weight of {tuple(weight.shape)}")
+    scores = torch.empty(R, V, dtype=torch.float32, device=h.device)
+    _lib.check(_lib.lib().wpt_head_scores(h.data_ptr(), h.stride(0), weight.data_ptr(), weight.stride(0), R, D, V,
+                                          1 if round_bf16 else 0, scores.data_ptr(), _lib.stream(h.device)))
+    LAUNCHES[0] += math.ceil(R / 128)
+    return scores
+
+
 def accept(scores, drafted, q, uniforms, resample, temperature=1.0, top_k=None, lengths=None):
     """The acceptance step for R rows (wpt_inference/__init__.py:173-179,
     210-222) with explicit draws: returns (tokens (R, n + 1) int64, -1
