@@ -252,6 +252,10 @@ __global__ void __launch_bounds__(STREAM_THREADS, 1)
   // mbarriers and warp 4 allocates TMEM.
   const int lane = threadIdx.x & 31;
   if (warp == 0) {
+    // launched as a programmatic dependent of the kernel before it on the
+    // stream: everything above runs while that kernel finishes, and nothing
+    // in global memory is read or written before it has
+    griddep_wait();
     int rlo = INT_MAX, rhi = -1;
     for (int tq = lane; tq < TQg; tq += 32) {
       int lo, hi;
@@ -297,6 +301,7 @@ __global__ void __launch_bounds__(STREAM_THREADS, 1)
     tmem_alloc(s_tmem, L::TMEM_COLS);
     tmem_relinquish();
   }
+  griddep_wait();
   tc_fence_before();
   __syncthreads();
   tc_fence_after();

@@ -276,6 +276,17 @@ int launch_prefill(const wpt::PrefillParams& p, const CUtensorMap& tq, const CUt
   }
 }
 
+// 1: the key-stream kernel launches as a programmatic dependent of the
+// kernel before it on the stream (WPT_B200_PDL = 0 or 1 overrides).
+int stream_pdl() {
+  static int v = -1;
+  if (v < 0) {
+    const char* env = getenv("WPT_B200_PDL");
+    v = env ? (atoi(env) != 0) : 1;
+  }
+  return v;
+}
+
 template <int NCOL, int STAGES, bool GATHER>
 int launch_stream_n(const CUtensorMap& tk, const CUtensorMap& tv, const wpt::StreamParams& p, int groups,
                     cudaStream_t stream) {
@@ -284,13 +295,20 @@ int launch_stream_n(const CUtensorMap& tk, const CUtensorMap& tv, const wpt::Str
   auto kernel = wpt::stream_kernel<NCOL, STAGES, GATHER>;
   if (int rc = allow_smem(kernel, L::BYTES)) return rc;
   cudaLaunchConfig_t cfg = {};
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeClusterDimension;  // cluster mode: one group's splits per cluster
-  attr[0].val.clusterDim.x = 1;
-  attr[0].val.clusterDim.y = p.cluster > 1 ? p.cluster : 1;
-  attr[0].val.clusterDim.z = 1;
+  cudaLaunchAttribute attr[2];
+  int na = 0;
+  if (stream_pdl()) {  // its set-up overlaps the tail of the kernel before it (it waits on the device)
+    attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[na++].val.programmaticStreamSerializationAllowed = 1;
+  }
+  if (p.cluster > 1) {  // cluster mode: one group's splits per cluster
+    attr[na].id = cudaLaunchAttributeClusterDimension;
+    attr[na].val.clusterDim.x = 1;
+    attr[na].val.clusterDim.y = p.cluster;
+    attr[na++].val.clusterDim.z = 1;
+  }
   cfg.attrs = attr;
-  cfg.numAttrs = p.cluster > 1 ? 1 : 0;
+  cfg.numAttrs = na;
   cfg.gridDim = dim3(groups, p.splits);
   cfg.blockDim = dim3(wpt::STREAM_THREADS);
   cfg.dynamicSmemBytes = L::BYTES;
