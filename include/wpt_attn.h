@@ -239,6 +239,41 @@ int wpt_attn_merge_groups(const float* parts, int groups, int per, int64_t rows,
                           const float* sink, void* out, float* lse, void* stream);
 
 /*
+ * The long row's exchange without a collective library (no reference
+ * counterpart: the reference decodes on one GPU). Each rank of a long row
+ * whose keys are split over `world` GPUs (one process per GPU, never two
+ * ranks on one GPU: the ranks' kernels wait for one another) sets up once:
+ *   wpt_peer_bytes(world, rows, C)   bytes of its exchange buffer (0: the
+ *                                    shape is not taken: C 128, world
+ *                                    1..8, rows 1..4096)
+ *   wpt_peer_alloc(bytes, &buf, h)   cudaMalloc + zero-fill + synchronise;
+ *                                    h receives its 64-byte CUDA IPC handle
+ *   (the caller exchanges the handles, e.g. over its process group)
+ *   wpt_peer_open(h_peer, &ptr)      maps a peer's buffer into this process
+ *   (then a barrier over the ranks: no rank may write into a buffer before
+ *   its owner has zeroed it)
+ *   wpt_peer_close(ptr, opened)      unmaps (opened = 1) or frees (0)
+ * Per call, after this rank's split partials (wpt_attn_decode in
+ * partials-only mode over its shard), wpt_attn_exchange launches one kernel
+ * that merges them, stores the result into every rank's buffer through the
+ * mappings (NVLink), signals each rank, waits (bounded: 2 s, then status bit
+ * 0 and no output) for every rank's result of the same call, and writes the
+ * merged out (rows, C) bf16 and lse (rows,) with the sink. peers: host array
+ * of the world buffers as mapped in this process (its own at [rank]). Every
+ * rank must make the same sequence of calls with the same shape on its
+ * buffer; calls on one stream are ordered, calls that overlap on several
+ * streams race on the buffer. The call count lives in the buffer, so the
+ * call can be replayed from a CUDA graph.
+ */
+size_t wpt_peer_bytes(int world, int64_t rows, int C);
+int wpt_peer_alloc(size_t bytes, void** buffer, void* handle);
+int wpt_peer_open(const void* handle, void** buffer);
+int wpt_peer_close(void* buffer, int opened);
+int wpt_attn_exchange(const float* part_o, const float* part_lse, int splits, int64_t rows, int H, int C,
+                      const float* sink, void* const* peers, int world, int rank, void* out, float* lse,
+                      void* stream);
+
+/*
  * The output head's product ahead of sampling: scores (R, V) fp32 =
  * h (R, D) W (V, D)^T, bf16 inputs with fp32 accumulation on the tensor
  * cores (the vocabulary rows as the MMA's M, W streamed once). Replaces the

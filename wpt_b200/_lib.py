@@ -41,10 +41,15 @@ SIGNATURES = {
     "wpt_cache_append": [_P, _I64, _I64, _P, _I64, _I64, _P, _P, _I, _I, _I, _I64, _P],
     "wpt_attn_merge_groups": [_P, _I, _I, _I64, _I64, _I, _I, _P, _P, _P, _P],
     "wpt_attn_merge_partial": [_P, _P, _I, _I64, _I64, _I, _P, _P, _P],
+    "wpt_peer_bytes": [_I, _I64, _I],
+    "wpt_peer_alloc": [ctypes.c_size_t, ctypes.POINTER(_P), _P],
+    "wpt_peer_open": [_P, ctypes.POINTER(_P)],
+    "wpt_peer_close": [_P, _I],
+    "wpt_attn_exchange": [_P, _P, _I, _I64, _I, _I, _P, ctypes.POINTER(_P), _I, _I, _P, _P, _P],
 }
 
 RESTYPES = {"wpt_last_error": ctypes.c_char_p, "wpt_accept_scratch_bytes": ctypes.c_size_t,
-            "wpt_attn_backward_scratch_bytes": ctypes.c_size_t}
+            "wpt_attn_backward_scratch_bytes": ctypes.c_size_t, "wpt_peer_bytes": ctypes.c_size_t}
 
 _lib = None
 

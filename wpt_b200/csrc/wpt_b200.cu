@@ -16,6 +16,7 @@
 #include "backward.cuh"
 #include "cache.cuh"
 #include "common.cuh"
+#include "exchange.cuh"
 #include "head.cuh"
 #include "merge.cuh"
 #include "prefill.cuh"
@@ -739,6 +740,89 @@ extern "C" int wpt_attn_merge_groups(const float* parts, int groups, int per, in
   const int splits = groups * per;
   return C == 128 ? launch_merge<128>(parts, part_lse, splits, rows, lay, H, sink, out, lse, s)
                   : launch_merge<64>(parts, part_lse, splits, rows, lay, H, sink, out, lse, s);
+}
+
+extern "C" size_t wpt_peer_bytes(int world, int64_t rows, int C) {
+  if (C != 128 || world < 1 || world > wpt::EXCH_MAX_WORLD || rows < 1 || rows > wpt::EXCH_MAX_CTAS) return 0;
+  const int64_t chunk = (rows * (C + 1) + 3) / 4 * 4;
+  return static_cast<size_t>(wpt::EXCH_CTRL_BYTES + 2 * world * chunk * 4);
+}
+
+extern "C" int wpt_peer_alloc(size_t bytes, void** buffer, void* handle) {
+  if (bytes == 0 || !buffer || !handle) return fail(WPT_ERR_INVALID, "peer buffer: bad arguments");
+  void* p = nullptr;
+  cudaError_t e = cudaMalloc(&p, bytes);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaMalloc(peer buffer)");
+  e = cudaMemset(p, 0, bytes);
+  if (e == cudaSuccess) e = cudaDeviceSynchronize();  // zeroed before any peer can write into it
+  cudaIpcMemHandle_t h;
+  if (e == cudaSuccess) e = cudaIpcGetMemHandle(&h, p);
+  if (e != cudaSuccess) {
+    cudaFree(p);
+    return cuda_fail(e, "peer buffer set-up");
+  }
+  std::memcpy(handle, &h, sizeof(h));
+  *buffer = p;
+  return WPT_OK;
+}
+
+extern "C" int wpt_peer_open(const void* handle, void** buffer) {
+  if (!handle || !buffer) return fail(WPT_ERR_INVALID, "peer open: bad arguments");
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, handle, sizeof(h));
+  cudaError_t e = cudaIpcOpenMemHandle(buffer, h, cudaIpcMemLazyEnablePeerAccess);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaIpcOpenMemHandle");
+  return WPT_OK;
+}
+
+extern "C" int wpt_peer_close(void* buffer, int opened) {
+  cudaError_t e = opened ? cudaIpcCloseMemHandle(buffer) : cudaFree(buffer);
+  if (e != cudaSuccess) return cuda_fail(e, opened ? "cudaIpcCloseMemHandle" : "cudaFree(peer buffer)");
+  return WPT_OK;
+}
+
+extern "C" int wpt_attn_exchange(const float* part_o, const float* part_lse, int splits, int64_t rows, int H, int C,
+                                 const float* sink, void* const* peers, int world, int rank, void* out, float* lse,
+                                 void* stream) {
+  if (C != 128) return fail(WPT_ERR_UNSUPPORTED, "head width %d: the exchange takes 128", C);
+  if (world < 1 || world > wpt::EXCH_MAX_WORLD || rank < 0 || rank >= world)
+    return fail(WPT_ERR_UNSUPPORTED, "world %d rank %d: 1 to %d ranks", world, rank, wpt::EXCH_MAX_WORLD);
+  if (rows < 1 || rows > wpt::EXCH_MAX_CTAS)
+    return fail(WPT_ERR_UNSUPPORTED, "%lld rows: the exchange takes 1 to %d", static_cast<long long>(rows),
+                wpt::EXCH_MAX_CTAS);
+  if (splits < 1 || H < 1) return fail(WPT_ERR_INVALID, "bad exchange shape splits=%d H=%d", splits, H);
+  if (!part_o || !part_lse || !peers || !out || !lse) return fail(WPT_ERR_INVALID, "a required pointer is NULL");
+  wpt::ExchangeParams p = {};
+  p.part_o = part_o;
+  p.part_lse = part_lse;
+  p.sink = sink;
+  for (int g = 0; g < world; ++g) {
+    if (!peers[g] || reinterpret_cast<uintptr_t>(peers[g]) % 256 != 0)
+      return fail(WPT_ERR_INVALID, "peer buffer %d is NULL or not 256-byte aligned", g);
+    p.peers[g] = static_cast<uint8_t*>(peers[g]);
+  }
+  p.local = p.peers[rank];
+  p.out = static_cast<__nv_bfloat16*>(out);
+  p.lse = lse;
+  if (int rc = status_word(&p.status)) return rc;
+  p.chunk = (rows * (C + 1) + 3) / 4 * 4;
+  p.splits = splits;
+  p.rows = static_cast<int>(rows);
+  p.H = H;
+  p.world = world;
+  p.rank = rank;
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;  // waits for the partials on the device
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cfg.gridDim = dim3(static_cast<unsigned>(rows));  // one row per CTA
+  cfg.blockDim = dim3(wpt::EXCH_THREADS);
+  cfg.stream = static_cast<cudaStream_t>(stream);
+  cudaError_t e = cudaLaunchKernelEx(&cfg, wpt::exchange_kernel<128>, p);
+  if (e != cudaSuccess) return cuda_fail(e, "exchange_kernel launch");
+  return WPT_OK;
 }
 
 extern "C" int wpt_attn_decode(const void* q, const void* k, const void* v, int64_t k_stride_b, int64_t k_stride_n,

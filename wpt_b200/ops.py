@@ -304,6 +304,26 @@ def merge_groups(parts, per, rows, H, C, sink=None, out=None, lse=None):
     return out, lse
 
 
+def exchange(part_o, part_lse, peers, world, rank, H, sink=None):
+    """The long row's combine across GPUs in one kernel (wpt_attn_exchange):
+    this rank's split partials (part_o (S, rows, C), part_lse (S, rows)
+    fp32) are merged, stored into every rank's exchange buffer (peers: a
+    ctypes array of the world buffers as mapped here), and, once every
+    rank's result of the same call has landed, merged with the sink into
+    (out (rows, C) bf16, lse (rows,) fp32)."""
+    _need_cuda(part_o, part_lse, sink)
+    S, rows, C = part_o.shape
+    if sink is not None:
+        sink = sink.float().contiguous()
+    out = torch.empty(rows, C, dtype=torch.bfloat16, device=part_o.device)
+    lse = torch.empty(rows, dtype=torch.float32, device=part_o.device)
+    _lib.check(_lib.lib().wpt_attn_exchange(_lib.ptr(part_o), _lib.ptr(part_lse), S, rows, H, C, _lib.ptr(sink),
+                                            peers, world, rank, _lib.ptr(out), _lib.ptr(lse),
+                                            _lib.stream(part_o.device)))
+    LAUNCHES[0] += 1
+    return out, lse
+
+
 def attention_forward(q, k, v, positions, scale, window=0, floor=None, sink=None):
     """Range attention by the kernel that suits the shape: the key-stream
     kernel for few queries per row, the prefill kernel otherwise."""
