@@ -68,7 +68,12 @@ int wpt_status(unsigned* status, int reset);
  *   tree_base   int64 (B,) or NULL (required with tree_bits)
  *   sink        fp32 (H,) or NULL: one logit per head added to the denominator
  *   splits      > 1 splits each CTA's rows; part_o (splits, B*T*H, C) fp32
- *               and part_lse (splits, B*T*H) fp32 are then caller scratch
+ *               and part_lse (splits, B*T*H) fp32 are then caller scratch.
+ *               splits == 2 with part_o == part_lse == NULL: cluster mode,
+ *               for shapes of at most one work item (pair of 128-row query
+ *               tiles and split) per SM: a pair's two splits run as one
+ *               2-CTA cluster and combine in shared memory (no scratch, no
+ *               merge launch); more items than SMs return WPT_ERR_INVALID
  */
 int wpt_attn_prefill(const void* q, const void* k, const void* v, int64_t k_stride_b, int64_t k_stride_n,
                      int64_t v_stride_b, int64_t v_stride_n, const int64_t* positions, const int64_t* floor_rows,

@@ -92,6 +92,16 @@ def test_cluster_mode_takes_at_most_8_splits(library):
     assert rc == _lib.ERR_INVALID and b"at most 8" in lib.wpt_last_error()
 
 
+def test_prefill_without_scratch_takes_only_two_splits(library):
+    # part_o == part_lse == NULL with 2 splits selects the prefill kernel's cluster combine; other split
+    # counts need the scratch
+    from wpt_b200 import _lib
+    lib = _lib.lib()
+    rc = lib.wpt_attn_prefill(None, None, None, 0, 0, 0, 0, None, None, None, None, None, None, None, None, None, 3,
+                              1, 256, 16, 128, 1024, 0, 1.0, None)
+    assert rc == _lib.ERR_INVALID and b"or neither, for 2" in lib.wpt_last_error()
+
+
 def test_cpu_tensors_are_refused_not_computed():
     import wpt_b200
     q = torch.zeros(1, 4, 2, 128, dtype=torch.bfloat16)

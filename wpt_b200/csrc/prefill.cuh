@@ -56,7 +56,11 @@
 //
 // Split-KV: an item's key tiles may be split; with splits > 1 each split
 // writes its normalised partial output and LSE (no sink) for the merge
-// kernel, which adds the sink.
+// kernel, which adds the sink. Cluster mode (2 splits, one item per CTA):
+// the two splits of a pair are one 2-CTA cluster; each CTA leaves its
+// partials in its idle K/V ring and, after a cluster barrier, the CTA of
+// rank w combines query tile w's rows from both (distributed shared memory)
+// with the sink, so no partials go to HBM and no merge kernel runs.
 //
 // Barrier phases run on across items: key tile g (counted over the CTA's
 // items) is ring entries prefill_k_entry(g) (K) and prefill_v_entry(g) (V);
@@ -83,6 +87,8 @@ struct PrefillParams {
   unsigned* status;
   int B, T, H, N, window, TQ, splits, items;
   int tma_out;       // 1: full query tiles leave through shared memory and a TMA store (tm_o)
+  int cluster;       // 1: splits == 2, one item per CTA, a pair's two splits one 2-CTA cluster that
+                     // combines them in shared memory (no partials in HBM, no merge launch)
   float scale_log2;  // softmax scale * log2(e)
 };
 
@@ -111,7 +117,13 @@ struct PrefillLayout {
   static constexpr int REGS_LAUNCH = 168, REGS_CONTROL = 56, REGS_SOFTMAX = 224;
   static_assert(128 * REGS_CONTROL + 256 * REGS_SOFTMAX == THREADS * REGS_LAUNCH, "register split");
   static constexpr int ITEM_READERS = 9;  // the issuer warp and the 8 softmax warps
+  // cluster mode: each query tile's normalised partial, (C / 4) x 128 rows of
+  // float4 then 128 log-sums, in the K/V ring (idle once the item's last
+  // product is done)
+  static constexpr int STASH_BYTES = C * 128 * 4 + 128 * 4;
+  static_assert(2 * STASH_BYTES <= NS * KV_BYTES, "cluster stash exceeds the K/V ring");
 };
+
 
 __device__ __forceinline__ void prefill_query_rows(const PrefillParams& p, int b, int t, int& lo, int& hi) {
   const int64_t pos = p.positions[static_cast<int64_t>(b) * p.T + t];
@@ -320,6 +332,52 @@ __device__ __forceinline__ void prefill_issue_pv(uint32_t tmem, uint32_t kv_addr
                                            first ? 0u : 1u);
 }
 
+// Cluster mode, after the item: the rows of query tile `w` (= this CTA's
+// rank in the pair's cluster) from this CTA's stash and its partner's
+// (distributed shared memory), with the sink: out and lse of those rows.
+template <int C, int STASH_BYTES>
+__device__ __forceinline__ void prefill_cluster_combine(const PrefillParams& p, uint8_t* sKV, int w, int row) {
+  const PrefillItem it = prefill_place(p, blockIdx.x);
+  const int tq = row / p.H, h = row - tq * p.H;
+  const int t = it.t0 + w * p.TQ + tq;
+  if (tq >= p.TQ || t >= p.T) return;
+  const int64_t orow = (static_cast<int64_t>(it.b) * p.T + t) * p.H + h;
+  const uint32_t mine = smem_u32(sKV) + w * STASH_BYTES;
+  const uint32_t theirs = dsmem_map(mine, static_cast<uint32_t>(w ^ 1));
+  const float* own = reinterpret_cast<const float*>(sKV + w * STASH_BYTES);
+  const float l0 = own[C * 128 + row];
+  const float l1 = dsmem_ld(theirs + (C * 128 + row) * 4);
+  const float sk = p.sink != nullptr ? p.sink[h] : -INFINITY;
+  const float m = fmaxf(fmaxf(l0, l1), sk);
+  float w0 = 0.f, w1 = 0.f, den = 0.f;
+  if (m > -INFINITY) {
+    w0 = __expf(l0 - m);
+    w1 = __expf(l1 - m);
+    den = w0 + w1 + __expf(sk - m);
+  }
+  const float inv = den > 0.f ? 1.f / den : 0.f;
+  w0 *= inv;
+  w1 *= inv;
+  uint4* dst = reinterpret_cast<uint4*>(p.out + orow * C);
+#pragma unroll 4
+  for (int c8 = 0; c8 < C / 8; ++c8) {
+    float4 a[2], b[2];
+#pragma unroll
+    for (int u = 0; u < 2; ++u) {
+      const int v4 = 2 * c8 + u;
+      a[u] = w0 > 0.f ? *reinterpret_cast<const float4*>(own + (v4 * 128 + row) * 4) : make_float4(0.f, 0.f, 0.f, 0.f);
+      b[u] = w1 > 0.f ? dsmem_ld4(theirs + (v4 * 128 + row) * 16) : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+    uint4 o;
+    o.x = pack_bf16(w0 * a[0].x + w1 * b[0].x, w0 * a[0].y + w1 * b[0].y);
+    o.y = pack_bf16(w0 * a[0].z + w1 * b[0].z, w0 * a[0].w + w1 * b[0].w);
+    o.z = pack_bf16(w0 * a[1].x + w1 * b[1].x, w0 * a[1].y + w1 * b[1].y);
+    o.w = pack_bf16(w0 * a[1].z + w1 * b[1].z, w0 * a[1].w + w1 * b[1].w);
+    dst[c8] = o;
+  }
+  p.lse[orow] = den > 0.f ? m + __logf(den) : -INFINITY;
+}
+
 template <int C, int QB, int NS, int POLY8>
 __global__ void __launch_bounds__(PrefillLayout<C, QB, NS>::THREADS, 1)
     prefill_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
@@ -454,6 +512,10 @@ __global__ void __launch_bounds__(PrefillLayout<C, QB, NS>::THREADS, 1)
     if (lane == 0 && ok && pend_g >= 0) load(prefill_v_entry(pend_g), true, pend_n0, pend_b);
     // the consumers wait for every copy issued here before the CTA leaves
     // (or time out together with this thread), so nothing lands after exit
+    if (p.cluster) {  // the softmax warpgroups' two cluster barriers
+      cluster_sync();
+      cluster_sync();
+    }
     tc_fence_before();
     __syncthreads();
   } else if (warp == L::MMA_WARP) {
@@ -521,11 +583,19 @@ __global__ void __launch_bounds__(PrefillLayout<C, QB, NS>::THREADS, 1)
       g += nt;
       ++n;
     }
+    if (p.cluster) {
+      cluster_sync();
+      cluster_sync();
+    }
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
     tmem_dealloc(tmem, 512);
   } else {
+    if (p.cluster) {
+      cluster_sync();
+      cluster_sync();
+    }
     tc_fence_before();
     __syncthreads();
   }
@@ -556,7 +626,9 @@ __global__ void __launch_bounds__(PrefillLayout<C, QB, NS>::THREADS, 1)
       const int64_t orow = (static_cast<int64_t>(it.b) * p.T + t) * p.H + h;
       if (nt == 0) {  // an empty split: nothing to read
         if (valid) {
-          if (p.splits > 1) {
+          if (p.cluster) {  // its stash: no rows (the K/V ring is idle: nothing was loaded)
+            reinterpret_cast<float*>(sKV + w * L::STASH_BYTES)[C * 128 + row] = -INFINITY;
+          } else if (p.splits > 1) {
             p.part_lse[static_cast<int64_t>(it.split) * rows_all + orow] = -INFINITY;
           } else {
             for (int c = 0; c < C; ++c) p.out[orow * C + c] = __float2bfloat16_rn(0.f);
@@ -635,6 +707,10 @@ __global__ void __launch_bounds__(PrefillLayout<C, QB, NS>::THREADS, 1)
       // 128-byte-swizzled layout of the TMA box, then one TMA store per 64
       // columns; the buffer is handed back to the loader (q_stored) once the
       // store has read it. Other tiles store their rows directly.
+      if (p.cluster) {  // the stash goes into the K/V ring: the other tile's products must be done too
+        ok = __all_sync(0xffffffffu, mbar_wait(o_final + (w ^ 1), n & 1, p.status));
+        if (!ok) break;
+      }
       const bool stage = p.tma_out && p.splits == 1 && p.TQ * p.H == BM && it.t0 + (w + 1) * p.TQ <= p.T;
       uint8_t* tile = sQ + (n % QB) * L::Q_BYTES + w * L::QT_BYTES;
       if (stage) {
@@ -670,6 +746,14 @@ __global__ void __launch_bounds__(PrefillLayout<C, QB, NS>::THREADS, 1)
             dst[v4] = u;
           }
           p.lse[orow] = denom > 0.f ? (msub + log2f(denom)) * LN2 : -INFINITY;
+        } else if (p.cluster) {  // this split's normalised partial of the row, for the pair's combine
+          float* st = reinterpret_cast<float*>(sKV + w * L::STASH_BYTES);
+#pragma unroll
+          for (int v4 = 0; v4 < C / 4; ++v4)
+            *reinterpret_cast<float4*>(st + (v4 * 128 + row) * 4) =
+                make_float4(__uint_as_float(o[v4 * 4]) * inv, __uint_as_float(o[v4 * 4 + 1]) * inv,
+                            __uint_as_float(o[v4 * 4 + 2]) * inv, __uint_as_float(o[v4 * 4 + 3]) * inv);
+          st[C * 128 + row] = l > 0.f ? (msub + log2f(l)) * LN2 : -INFINITY;
         } else {
           const int64_t prow = static_cast<int64_t>(it.split) * rows_all + orow;
           float4* dst = reinterpret_cast<float4*>(p.part_o + prow * C);
@@ -685,6 +769,15 @@ __global__ void __launch_bounds__(PrefillLayout<C, QB, NS>::THREADS, 1)
       ++n;
     }
     if (quad == 0 && lane == 0) bulk_wait_all();  // this warpgroup's output stores have landed
+    if (p.cluster) {
+      // every role of both CTAs comes here (after a time-out too), so the
+      // cluster barriers always complete: the pair's stashes are written,
+      // tile w's rows are combined by the CTA of rank w, and the partner's
+      // stash is read before either CTA leaves
+      cluster_sync();
+      if (w == static_cast<int>(cluster_rank())) prefill_cluster_combine<C, L::STASH_BYTES>(p, sKV, w, row);
+      cluster_sync();
+    }
     tc_fence_before();
     __syncthreads();
   }

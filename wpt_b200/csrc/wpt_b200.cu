@@ -258,8 +258,21 @@ int launch_prefill_p(const wpt::PrefillParams& p, const CUtensorMap& tq, const C
   int sms = 148;
   current_device(&sms);
   const int grid = p.items < sms ? p.items : sms;  // persistent: one CTA per SM walks the items
-  kernel<<<grid, L::THREADS, L::BYTES, stream>>>(tq, tk, tv, to, p);
-  cudaError_t e = cudaGetLastError();
+  if (p.cluster && (grid != p.items || p.items % 2 != 0))
+    return fail(WPT_ERR_INVALID, "prefill cluster mode needs one item per CTA (%d items, %d SMs)", p.items, sms);
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;  // cluster mode: a pair's two splits per cluster
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = p.cluster ? 1 : 0;
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(L::THREADS);
+  cfg.dynamicSmemBytes = L::BYTES;
+  cfg.stream = stream;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, tq, tk, tv, to, p);
   if (e != cudaSuccess) return cuda_fail(e, "prefill_kernel launch");
   return WPT_OK;
 }
@@ -423,8 +436,11 @@ extern "C" int wpt_attn_prefill(const void* q, const void* k, const void* v, int
   if (B < 1 || T < 1 || N < 1) return fail(WPT_ERR_INVALID, "empty shape B=%d T=%d N=%d", B, T, N);
   if (static_cast<int64_t>(B) * T * H + 256 >= (int64_t(1) << 31)) return fail(WPT_ERR_UNSUPPORTED, "B*T*H too large");
   if (splits < 1) return fail(WPT_ERR_INVALID, "splits must be >= 1");
-  if (splits > 1 && (part_o == nullptr || part_lse == nullptr))
-    return fail(WPT_ERR_INVALID, "splits > 1 needs part_o and part_lse scratch");
+  // part_o and part_lse both NULL with 2 splits: cluster mode (a pair's two
+  // splits combine in shared memory; no scratch, no merge launch)
+  const bool cluster = splits == 2 && part_o == nullptr && part_lse == nullptr;
+  if (splits > 1 && !cluster && (part_o == nullptr || part_lse == nullptr))
+    return fail(WPT_ERR_INVALID, "splits > 1 needs part_o and part_lse scratch (or neither, for 2)");
   if (tree_bits != nullptr && tree_base == nullptr) return fail(WPT_ERR_INVALID, "tree_bits needs tree_base");
   if (!q || !k || !v || !positions || !out || !lse) return fail(WPT_ERR_INVALID, "a required pointer is NULL");
   if (!aligned16(q) || !aligned16(out)) return fail(WPT_ERR_INVALID, "q and out must be 16-byte aligned");
@@ -446,7 +462,8 @@ extern "C" int wpt_attn_prefill(const void* q, const void* k, const void* v, int
   p.floor_rows = floor_rows;
   p.tree_bits = tree_bits;
   p.tree_base = tree_base;
-  p.sink = splits > 1 ? nullptr : sink;
+  p.sink = splits > 1 && !cluster ? nullptr : sink;  // cluster mode: its combine adds the sink
+  p.cluster = cluster ? 1 : 0;
   p.out = static_cast<__nv_bfloat16*>(out);
   p.lse = lse;
   p.part_o = part_o;
@@ -469,7 +486,7 @@ extern "C" int wpt_attn_prefill(const void* q, const void* k, const void* v, int
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   int rc = C == 128 ? launch_prefill<128>(p, tq, tk, tv, to, s) : launch_prefill<64>(p, tq, tk, tv, to, s);
   if (rc) return rc;
-  if (splits > 1) {
+  if (splits > 1 && !cluster) {
     const int64_t rows = static_cast<int64_t>(B) * T * H;
     rc = C == 128 ? launch_merge<128>(part_o, part_lse, splits, rows, rows, H, sink, out, lse, s, true)
                   : launch_merge<64>(part_o, part_lse, splits, rows, rows, H, sink, out, lse, s, true);

@@ -19,6 +19,8 @@ from . import _lib
 LAUNCHES = [0]  # kernels this module has launched (read by bench.py around its timed region)
 # key tiles per key-stream CTA when set (WPT_B200_CHUNK, read once): overrides the split heuristic
 CHUNK_TILES = int(os.environ.get("WPT_B200_CHUNK", "0"))
+# the prefill kernel's 2-split cluster combine (WPT_B200_PREFILL_CLUSTER=0 turns it off)
+PREFILL_CLUSTER = os.environ.get("WPT_B200_PREFILL_CLUSTER", "1") != "0"
 
 
 def _need_cuda(*tensors):
@@ -108,7 +110,10 @@ def prefill_forward(q, k, v, positions, scale, window=0, floor=None, tree_bits=N
         tiles = window // 128 + 2 if window else (N + 127) // 128
         splits = _splits_for(B * math.ceil(T / (2 * TQ)), tiles, sm_count(q.device))  # one item per tile pair
     part_o = part_lse = None
-    if splits > 1:
+    # two splits with one work item per SM: the pair's splits combine as one
+    # 2-CTA cluster in shared memory (no partials, no merge launch)
+    cluster = (splits == 2 and PREFILL_CLUSTER and 2 * B * math.ceil(T / (2 * TQ)) <= sm_count(q.device))
+    if splits > 1 and not cluster:
         part_o = torch.empty(splits, B * T * H, C, dtype=torch.float32, device=q.device)
         part_lse = torch.empty(splits, B * T * H, dtype=torch.float32, device=q.device)
     _lib.check(_lib.lib().wpt_attn_prefill(
@@ -116,7 +121,7 @@ def prefill_forward(q, k, v, positions, scale, window=0, floor=None, tree_bits=N
         _lib.ptr(positions), _lib.ptr(floor), _lib.ptr(tree_bits), _lib.ptr(tree_base), _lib.ptr(sink),
         _lib.ptr(out), _lib.ptr(lse), _lib.ptr(part_o), _lib.ptr(part_lse), int(splits),
         B, T, H, C, N, int(window), float(scale), _lib.stream(q.device)))
-    LAUNCHES[0] += 1 + (splits > 1)
+    LAUNCHES[0] += 1 + (splits > 1 and not cluster)
     return out, lse
 
 
