@@ -88,7 +88,8 @@ struct PrefillParams {
   int B, T, H, N, window, TQ, splits, items;
   int tma_out;       // 1: full query tiles leave through shared memory and a TMA store (tm_o)
   int cluster;       // 1: splits == 2, one item per CTA, a pair's two splits one 2-CTA cluster that
-                     // combines them in shared memory (no partials in HBM, no merge launch)
+                     // combines them in shared memory (no partials in HBM, no merge launch); the
+                     // kernel's CLUSTER instance
   float scale_log2;  // softmax scale * log2(e)
 };
 
@@ -378,7 +379,7 @@ __device__ __forceinline__ void prefill_cluster_combine(const PrefillParams& p, 
   p.lse[orow] = den > 0.f ? m + __logf(den) : -INFINITY;
 }
 
-template <int C, int QB, int NS, int POLY8>
+template <int C, int QB, int NS, int POLY8, bool CLUSTER>
 __global__ void __launch_bounds__(PrefillLayout<C, QB, NS>::THREADS, 1)
     prefill_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                    const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_o,
@@ -512,7 +513,7 @@ __global__ void __launch_bounds__(PrefillLayout<C, QB, NS>::THREADS, 1)
     if (lane == 0 && ok && pend_g >= 0) load(prefill_v_entry(pend_g), true, pend_n0, pend_b);
     // the consumers wait for every copy issued here before the CTA leaves
     // (or time out together with this thread), so nothing lands after exit
-    if (p.cluster) {  // the softmax warpgroups' two cluster barriers
+    if constexpr (CLUSTER) {  // the softmax warpgroups' two cluster barriers
       cluster_sync();
       cluster_sync();
     }
@@ -583,7 +584,7 @@ __global__ void __launch_bounds__(PrefillLayout<C, QB, NS>::THREADS, 1)
       g += nt;
       ++n;
     }
-    if (p.cluster) {
+    if constexpr (CLUSTER) {
       cluster_sync();
       cluster_sync();
     }
@@ -592,7 +593,7 @@ __global__ void __launch_bounds__(PrefillLayout<C, QB, NS>::THREADS, 1)
     tc_fence_after();
     tmem_dealloc(tmem, 512);
   } else {
-    if (p.cluster) {
+    if constexpr (CLUSTER) {
       cluster_sync();
       cluster_sync();
     }
@@ -626,7 +627,7 @@ __global__ void __launch_bounds__(PrefillLayout<C, QB, NS>::THREADS, 1)
       const int64_t orow = (static_cast<int64_t>(it.b) * p.T + t) * p.H + h;
       if (nt == 0) {  // an empty split: nothing to read
         if (valid) {
-          if (p.cluster) {  // its stash: no rows (the K/V ring is idle: nothing was loaded)
+          if constexpr (CLUSTER) {  // its stash: no rows (the K/V ring is idle: nothing was loaded)
             reinterpret_cast<float*>(sKV + w * L::STASH_BYTES)[C * 128 + row] = -INFINITY;
           } else if (p.splits > 1) {
             p.part_lse[static_cast<int64_t>(it.split) * rows_all + orow] = -INFINITY;
@@ -707,7 +708,7 @@ __global__ void __launch_bounds__(PrefillLayout<C, QB, NS>::THREADS, 1)
       // 128-byte-swizzled layout of the TMA box, then one TMA store per 64
       // columns; the buffer is handed back to the loader (q_stored) once the
       // store has read it. Other tiles store their rows directly.
-      if (p.cluster) {  // the stash goes into the K/V ring: the other tile's products must be done too
+      if constexpr (CLUSTER) {  // the stash goes into the K/V ring: the other tile's products must be done too
         ok = __all_sync(0xffffffffu, mbar_wait(o_final + (w ^ 1), n & 1, p.status));
         if (!ok) break;
       }
@@ -746,7 +747,7 @@ __global__ void __launch_bounds__(PrefillLayout<C, QB, NS>::THREADS, 1)
             dst[v4] = u;
           }
           p.lse[orow] = denom > 0.f ? (msub + log2f(denom)) * LN2 : -INFINITY;
-        } else if (p.cluster) {  // this split's normalised partial of the row, for the pair's combine
+        } else if constexpr (CLUSTER) {  // this split's normalised partial of the row, for the pair's combine
           float* st = reinterpret_cast<float*>(sKV + w * L::STASH_BYTES);
 #pragma unroll
           for (int v4 = 0; v4 < C / 4; ++v4)
@@ -769,7 +770,7 @@ __global__ void __launch_bounds__(PrefillLayout<C, QB, NS>::THREADS, 1)
       ++n;
     }
     if (quad == 0 && lane == 0) bulk_wait_all();  // this warpgroup's output stores have landed
-    if (p.cluster) {
+    if constexpr (CLUSTER) {
       // every role of both CTAs comes here (after a time-out too), so the
       // cluster barriers always complete: the pair's stashes are written,
       // tile w's rows are combined by the CTA of rank w, and the partner's

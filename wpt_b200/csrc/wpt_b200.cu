@@ -234,13 +234,13 @@ int prefill_poly8() {
   return v;
 }
 
-template <int C, int POLY8>
+template <int C, int POLY8, bool CLUSTER>
 int launch_prefill_p(const wpt::PrefillParams& p, const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
                      const CUtensorMap& to, cudaStream_t stream) {
   constexpr int QB = PrefillShape<C>::QB, NS = PrefillShape<C>::NS;
   using L = wpt::PrefillLayout<C, QB, NS>;
   static_assert(L::BYTES <= 232448, "prefill kernel shared memory exceeds 227 KB");
-  auto kernel = wpt::prefill_kernel<C, QB, NS, POLY8>;
+  auto kernel = wpt::prefill_kernel<C, QB, NS, POLY8, CLUSTER>;
   if (int rc = allow_smem(kernel, L::BYTES)) return rc;
   // setmaxnreg redistributes the registers the block was launched with: a
   // kernel built with fewer than REGS_LAUNCH would leave the softmax
@@ -281,12 +281,14 @@ template <int C>
 int launch_prefill(const wpt::PrefillParams& p, const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
                    const CUtensorMap& to,
                    cudaStream_t stream) {
+  // the cluster-combine instance (the POLY8 overrides are for sweeps of the plain one)
+  if (p.cluster) return launch_prefill_p<C, 1, true>(p, tq, tk, tv, to, stream);
   switch (prefill_poly8()) {
-    case 0: return launch_prefill_p<C, 0>(p, tq, tk, tv, to, stream);
-    case 3: return launch_prefill_p<C, 3>(p, tq, tk, tv, to, stream);
-    case 4: return launch_prefill_p<C, 4>(p, tq, tk, tv, to, stream);
-    case 2: return launch_prefill_p<C, 2>(p, tq, tk, tv, to, stream);
-    default: return launch_prefill_p<C, 1>(p, tq, tk, tv, to, stream);
+    case 0: return launch_prefill_p<C, 0, false>(p, tq, tk, tv, to, stream);
+    case 3: return launch_prefill_p<C, 3, false>(p, tq, tk, tv, to, stream);
+    case 4: return launch_prefill_p<C, 4, false>(p, tq, tk, tv, to, stream);
+    case 2: return launch_prefill_p<C, 2, false>(p, tq, tk, tv, to, stream);
+    default: return launch_prefill_p<C, 1, false>(p, tq, tk, tv, to, stream);
   }
 }
 
