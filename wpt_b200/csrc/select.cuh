@@ -399,43 +399,59 @@ __device__ __forceinline__ void block_minmax(uint32_t& lo, uint32_t& hi, uint32_
   __syncthreads();
 }
 
-// One CTA per query: chosen[b, t, :K] from scores[b*T + t, 0 .. last].
-// The K-th largest key: a histogram of the keys over SELECT_BINS equal
-// ranges of [min key, max key] (a monotone map, so the bins are ordered)
-// finds the bin where the count from the top reaches K; the keys of that
-// bin, usually a few dozen, are gathered and sorted in shared memory. When
-// that bin holds more than SELECT_CAND keys, four 8-bit radix passes find
-// the key instead.
+// SLICES CTAs per query (SLICES = 2: one thread-block cluster; CTA r takes
+// the r-th contiguous slice of the row's candidates): chosen[b, t, :K] from
+// scores[b*T + t, 0 .. last]. The K-th largest key: a histogram of the keys
+// over SELECT_BINS equal ranges of [min key, max key] (a monotone map, so the
+// bins are ordered; with two slices the minimum, maximum and histogram are
+// summed over the cluster through distributed shared memory) finds the bin
+// where the count from the top reaches K; the keys of that bin, usually a
+// few dozen, are gathered (from both slices) and sorted in shared memory,
+// the same on every CTA of the cluster. When that bin holds more than
+// SELECT_CAND keys, four 8-bit radix passes over the whole row find the key
+// instead. Each CTA then writes its slice's chosen rows at the offsets its
+// partner's counts give.
+template <int SLICES>
 __global__ void __launch_bounds__(TOPK_THREADS)
     topk_kernel(const float* __restrict__ scores, int64_t ld, const int64_t* __restrict__ positions,
                 int64_t* __restrict__ chosen, int T, int N, int K, int window, int cache_cap) {
+  static_assert(SLICES == 1 || SLICES == 2, "one CTA or a pair per query");
   // dynamic shared memory: cache_cap keys, SELECT_BINS bins, SELECT_CAND
   // 8-byte candidates (8-byte aligned), 64 reduction slots
   extern __shared__ uint32_t s_keys[];
   uint32_t* s_hist = s_keys + cache_cap;
   uint64_t* s_cand = reinterpret_cast<uint64_t*>(s_hist + SELECT_BINS + (cache_cap & 1));
   int* s_warp = reinterpret_cast<int*>(s_cand + SELECT_CAND);
-  __shared__ uint32_t s_sel[2];
+  __shared__ uint32_t s_sel[3];
   __shared__ int s_ncand;
+  __shared__ uint32_t s_mm[2];  // this slice's minimum and maximum key
+  __shared__ int s_tot[2];      // this slice's keys above the threshold and equal to it
   if (K <= 0) return;
-  const int64_t row = blockIdx.x;
+  const int64_t row = blockIdx.x / SLICES;
+  const uint32_t rank = SLICES > 1 ? cluster_rank() : 0u;
   const int64_t pos = positions[row];
   int64_t last = pos - window;
   if (last > N - 1) last = N - 1;
   const int count = last < 0 ? 0 : static_cast<int>(last + 1);
   int64_t* out = chosen + row * K;
-  if (count <= K) {  // every candidate, in row order, then -1
-    for (int i = threadIdx.x; i < K; i += blockDim.x) out[i] = i < count ? i : -1;
+  if (count <= K) {  // every candidate, in row order, then -1 (the same decision on both CTAs)
+    if (rank == 0)
+      for (int i = threadIdx.x; i < K; i += blockDim.x) out[i] = i < count ? i : -1;
     return;
   }
-  const float* src = scores + row * ld;
-  const bool cached = count <= cache_cap;
-  auto key_at = [&](int i) { return cached ? s_keys[i] : order_key(src[i]); };
+  // this CTA's slice of the candidates: rows [base, base + n_local)
+  const int s_len = SLICES == 1 ? count : ((count + 1) / 2 + 3) & ~3;
+  const int base = static_cast<int>(rank) * s_len;
+  const int n_local = max(0, min(count, base + s_len) - base);
+  const float* row_src = scores + row * ld;
+  const float* src = row_src + base;
+  const bool cached = n_local <= cache_cap;
+  auto key_at = [&](int i) { return cached ? s_keys[i] : order_key(src[i]); };  // i: slice index
   uint32_t lo = UINT_MAX, hi = 0;
-  // the row's keys (16-byte loads, four in flight per thread) into shared
+  // the slice's keys (16-byte loads, four in flight per thread) into shared
   // memory with their minimum and maximum
   const bool vec = cached && (ld & 3) == 0 && (reinterpret_cast<uintptr_t>(scores) & 15) == 0;
-  const int n4 = vec ? count / 4 : 0;
+  const int n4 = vec ? n_local / 4 : 0;
   for (int i4 = threadIdx.x; i4 < n4; i4 += 4 * TOPK_THREADS) {
     float4 f[4];
 #pragma unroll
@@ -452,7 +468,7 @@ __global__ void __launch_bounds__(TOPK_THREADS)
       }
     }
   }
-  for (int i = 4 * n4 + threadIdx.x; i < count; i += blockDim.x) {
+  for (int i = 4 * n4 + threadIdx.x; i < n_local; i += blockDim.x) {
     const uint32_t key = order_key(src[i]);
     if (cached) s_keys[i] = key;
     lo = min(lo, key);
@@ -461,47 +477,65 @@ __global__ void __launch_bounds__(TOPK_THREADS)
   for (int i = threadIdx.x; i < SELECT_BINS; i += blockDim.x) s_hist[i] = 0;
   if (threadIdx.x == 0) s_ncand = 0;
   block_minmax(lo, hi, reinterpret_cast<uint32_t*>(s_warp));
+  if constexpr (SLICES > 1) {  // the row's minimum and maximum over both slices
+    if (threadIdx.x == 0) {
+      s_mm[0] = lo;
+      s_mm[1] = hi;
+    }
+    cluster_sync();
+    const uint32_t other = dsmem_map(smem_u32(s_mm), rank ^ 1u);
+    lo = min(lo, __float_as_uint(dsmem_ld(other)));
+    hi = max(hi, __float_as_uint(dsmem_ld(other + 4)));
+  }
   // bin(key) = floor((key - lo) * SELECT_BINS / (hi - lo + 1)) in float: monotone in key
   const float bscale = static_cast<float>(SELECT_BINS) / (static_cast<float>(hi - lo) + 1.f);
   auto bin_of = [&](uint32_t key) {
     return min(SELECT_BINS - 1, static_cast<int>(static_cast<float>(key - lo) * bscale));
   };
 #pragma unroll 4
-  for (int i = threadIdx.x; i < count; i += blockDim.x) atomicAdd(&s_hist[bin_of(key_at(i))], 1u);
+  for (int i = threadIdx.x; i < n_local; i += blockDim.x) atomicAdd(&s_hist[bin_of(key_at(i))], 1u);
   __syncthreads();
   // the bin where the count from the top reaches K: thread t sums bins
-  // SELECT_BINS - 1 - (t * PER + e), e < PER, highest first
+  // SELECT_BINS - 1 - (t * PER + e), e < PER, highest first (both slices')
   constexpr int PER = SELECT_BINS / TOPK_THREADS;
+  if constexpr (SLICES > 1) cluster_sync();  // the partner's histogram is complete
+  uint32_t hb[PER];
   int mine = 0;
 #pragma unroll
-  for (int e = 0; e < PER; ++e) mine += s_hist[SELECT_BINS - 1 - (threadIdx.x * PER + e)];
+  for (int e = 0; e < PER; ++e) {
+    const int bin = SELECT_BINS - 1 - (threadIdx.x * PER + e);
+    hb[e] = s_hist[bin];
+    if constexpr (SLICES > 1) hb[e] += __float_as_uint(dsmem_ld(dsmem_map(smem_u32(s_hist + bin), rank ^ 1u)));
+    mine += static_cast<int>(hb[e]);
+  }
   int total;
   const int before = block_exclusive_scan(mine, s_warp, &total);
   if (before < K && before + mine >= K) {
     int acc = before;
     for (int e = 0; e < PER; ++e) {
       const int bin = SELECT_BINS - 1 - (threadIdx.x * PER + e);
-      if (acc + static_cast<int>(s_hist[bin]) >= K) {
+      if (acc + static_cast<int>(hb[e]) >= K) {
         s_sel[0] = static_cast<uint32_t>(bin);
         s_sel[1] = static_cast<uint32_t>(acc);  // keys in higher bins
+        s_sel[2] = hb[e];                       // keys in this bin
         break;
       }
-      acc += s_hist[bin];
+      acc += hb[e];
     }
   }
   __syncthreads();
   const int tbin = static_cast<int>(s_sel[0]);
   const int above_bin = static_cast<int>(s_sel[1]);
-  const int nbin = static_cast<int>(s_hist[tbin]);
-  // Rows are read in warp spans: warp w takes rows [w * span, (w + 1) * span),
-  // 32 at a time (lane l reads row base + l, so shared memory serves a warp
-  // without bank conflicts); ballots rank keys inside a step.
+  const int nbin = static_cast<int>(s_sel[2]);
+  // Slice rows are read in warp spans: warp w takes rows [w * span, (w + 1) *
+  // span) of the slice, 32 at a time (lane l reads row base + l, so shared
+  // memory serves a warp without bank conflicts); ballots rank keys inside a step.
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   constexpr int WARPS = TOPK_THREADS / 32;
-  const int span = (count + WARPS - 1) / WARPS;
-  const int w0 = min(count, warp * span), w1 = min(count, w0 + span);
+  const int span = (n_local + WARPS - 1) / WARPS;
+  const int w0 = min(n_local, warp * span), w1 = min(n_local, w0 + span);
   uint32_t thr;
-  int remaining;    // keys equal to thr that are taken
+  int remaining;       // keys equal to thr that are taken
   int gt = 0, eq = 0;  // this warp's keys above thr and equal to it
   if (nbin <= SELECT_CAND) {
     // one pass: the threshold bin's (key, row) pairs into shared memory, and
@@ -509,14 +543,30 @@ __global__ void __launch_bounds__(TOPK_THREADS)
     if (threadIdx.x < 64) s_warp[threadIdx.x] = 0;
     int hi_w = 0;
 #pragma unroll 4
-    for (int base = w0; base < w1; base += 32) {
-      const int i = base + lane;
+    for (int b0 = w0; b0 < w1; b0 += 32) {
+      const int i = b0 + lane;
       const uint32_t key = i < w1 ? key_at(i) : 0u;
       const int bin = i < w1 ? bin_of(key) : -1;
       hi_w += __popc(__ballot_sync(0xffffffffu, bin > tbin));
-      if (bin == tbin) s_cand[atomicAdd(&s_ncand, 1)] = (static_cast<uint64_t>(key) << 32) | static_cast<uint32_t>(i);
+      if (bin == tbin)
+        s_cand[atomicAdd(&s_ncand, 1)] = (static_cast<uint64_t>(key) << 32) | static_cast<uint32_t>(base + i);
     }
     __syncthreads();
+    if constexpr (SLICES > 1) {
+      // the partner's candidates after this slice's (together the bin's nbin
+      // keys), then a barrier before either CTA sorts its copy in place
+      cluster_sync();
+      const int own = s_ncand;
+      const uint32_t other_n = dsmem_map(smem_u32(&s_ncand), rank ^ 1u);
+      const int theirs = static_cast<int>(__float_as_uint(dsmem_ld(other_n)));
+      const uint32_t other_c = dsmem_map(smem_u32(s_cand), rank ^ 1u);
+      for (int e = threadIdx.x; e < theirs; e += blockDim.x) {
+        const uint32_t a = other_c + e * 8;
+        s_cand[own + e] = static_cast<uint64_t>(__float_as_uint(dsmem_ld(a))) |
+                          (static_cast<uint64_t>(__float_as_uint(dsmem_ld(a + 4))) << 32);
+      }
+      cluster_sync();
+    }
     int size = 2;
     while (size < nbin) size <<= 1;
     for (int e = nbin + threadIdx.x; e < size; e += blockDim.x) s_cand[e] = 0ull;  // below every pair
@@ -540,10 +590,12 @@ __global__ void __launch_bounds__(TOPK_THREADS)
     int first = need - 1;  // the first position of thr in the sorted bin
     while (first > 0 && static_cast<uint32_t>(s_cand[first - 1] >> 32) == thr) --first;
     remaining = need - first;
-    // the bin's keys above thr and equal to it, counted into their rows' warps
+    // this slice's keys of the bin above thr and equal to it, counted into their rows' warps
     for (int e = threadIdx.x; e < nbin; e += blockDim.x) {
       const uint32_t key = static_cast<uint32_t>(s_cand[e] >> 32);
-      const int w = static_cast<int>(static_cast<uint32_t>(s_cand[e])) / span;
+      const int r = static_cast<int>(static_cast<uint32_t>(s_cand[e])) - base;
+      if (r < 0 || r >= n_local) continue;
+      const int w = r / span;
       if (key > thr) atomicAdd(&s_warp[w], 1);
       else if (key == thr) atomicAdd(&s_warp[32 + w], 1);
     }
@@ -551,14 +603,18 @@ __global__ void __launch_bounds__(TOPK_THREADS)
     gt = hi_w + s_warp[warp];
     eq = s_warp[32 + warp];
     __syncthreads();
-  } else {  // a bin too full to gather: radix passes over all keys
+  } else {  // a bin too full to gather: radix passes over all the row's keys
+    if constexpr (SLICES > 1) cluster_sync();  // the partner has read this CTA's histogram
+    auto row_key = [&](int i) {                // i: row index
+      return SLICES == 1 ? key_at(i) : order_key(row_src[i]);
+    };
     uint32_t prefix = 0, mask = 0;
     remaining = K;
     for (int shift = 24; shift >= 0; shift -= 8) {
       for (int i = threadIdx.x; i < 256; i += blockDim.x) s_hist[i] = 0;
       __syncthreads();
       for (int i = threadIdx.x; i < count; i += blockDim.x) {
-        const uint32_t key = key_at(i);
+        const uint32_t key = row_key(i);
         if ((key & mask) == prefix) atomicAdd(&s_hist[(key >> shift) & 255u], 1u);
       }
       __syncthreads();
@@ -598,15 +654,16 @@ __global__ void __launch_bounds__(TOPK_THREADS)
     }
     thr = prefix;
 #pragma unroll 4
-    for (int base = w0; base < w1; base += 32) {
-      const int i = base + lane;
+    for (int b0 = w0; b0 < w1; b0 += 32) {
+      const int i = b0 + lane;
       const uint32_t key = i < w1 ? key_at(i) : 0u;
       gt += __popc(__ballot_sync(0xffffffffu, i < w1 && key > thr));
       eq += __popc(__ballot_sync(0xffffffffu, i < w1 && key == thr));
     }
   }
   // every key above thr, and the `remaining` lowest-indexed keys equal to
-  // it, in row order: the warps' counts place the warps
+  // it, in row order: the warps' counts (and, for the second slice, the
+  // first slice's totals) place the warps
   const int above = K - remaining;
   if (lane == 0) {
     s_warp[warp] = gt;
@@ -618,21 +675,39 @@ __global__ void __launch_bounds__(TOPK_THREADS)
     gt_off += s_warp[v];
     eq_off += s_warp[32 + v];
   }
+  if constexpr (SLICES > 1) {
+    if (threadIdx.x == 0) {
+      int tg = 0, te = 0;
+      for (int v = 0; v < WARPS; ++v) {
+        tg += s_warp[v];
+        te += s_warp[32 + v];
+      }
+      s_tot[0] = tg;
+      s_tot[1] = te;
+    }
+    cluster_sync();
+    if (rank == 1) {
+      const uint32_t other = dsmem_map(smem_u32(s_tot), 0u);
+      gt_off += static_cast<int>(__float_as_uint(dsmem_ld(other)));
+      eq_off += static_cast<int>(__float_as_uint(dsmem_ld(other + 4)));
+    }
+  }
   const unsigned below = (1u << lane) - 1u;
 #pragma unroll 4
-  for (int base = w0; base < w1; base += 32) {
-    const int i = base + lane;
+  for (int b0 = w0; b0 < w1; b0 += 32) {
+    const int i = b0 + lane;
     const uint32_t key = i < w1 ? key_at(i) : 0u;
     const bool is_gt = i < w1 && key > thr, is_eq = i < w1 && key == thr;
     const unsigned bg = __ballot_sync(0xffffffffu, is_gt), be = __ballot_sync(0xffffffffu, is_eq);
-    if (is_gt) out[gt_off + __popc(bg & below)] = i;
+    if (is_gt) out[gt_off + __popc(bg & below)] = base + i;
     if (is_eq) {
       const int e = eq_off + __popc(be & below);
-      if (e < remaining) out[above + e] = i;
+      if (e < remaining) out[above + e] = base + i;
     }
     gt_off += __popc(bg);
     eq_off += __popc(be);
   }
+  if constexpr (SLICES > 1) cluster_sync();  // the partner has read this CTA's totals
 }
 
 }  // namespace wpt

@@ -989,10 +989,36 @@ extern "C" int wpt_attn_topk(const void* q, const void* k, int64_t k_stride_b, i
   if (rc) return rc;
   const int cap = N < 47104 ? N : 47104;  // keys cached in shared memory (the rest of it: bins, candidates)
   const int smem = (cap + 1 + wpt::SELECT_BINS + 2 * wpt::SELECT_CAND + 64) * 4;
-  if (int rc2 = allow_smem(wpt::topk_kernel, smem)) return rc2;
-  wpt::topk_kernel<<<static_cast<unsigned>(static_cast<int64_t>(B) * T), wpt::TOPK_THREADS, smem, s>>>(
-      scores, ld_scores, positions, chosen, T, N, K, window, cap);
-  cudaError_t e = cudaGetLastError();
+  int sms = 148;
+  current_device(&sms);
+  const int64_t queries = static_cast<int64_t>(B) * T;
+  // fewer queries than SMs: each query's candidates in two slices, a 2-CTA
+  // cluster per query (WPT_B200_TOPK_PAIR=0 keeps one CTA)
+  static const int pair_env = [] {
+    const char* env = getenv("WPT_B200_TOPK_PAIR");
+    return env ? atoi(env) : 1;
+  }();
+  const bool pair = pair_env != 0 && queries < sms;
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pair ? 1 : 0;
+  cfg.gridDim = dim3(static_cast<unsigned>(pair ? 2 * queries : queries));
+  cfg.blockDim = dim3(wpt::TOPK_THREADS);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaError_t e;
+  if (pair) {
+    if (int rc2 = allow_smem(wpt::topk_kernel<2>, smem)) return rc2;
+    e = cudaLaunchKernelEx(&cfg, wpt::topk_kernel<2>, scores, ld_scores, positions, chosen, T, N, K, window, cap);
+  } else {
+    if (int rc2 = allow_smem(wpt::topk_kernel<1>, smem)) return rc2;
+    e = cudaLaunchKernelEx(&cfg, wpt::topk_kernel<1>, scores, ld_scores, positions, chosen, T, N, K, window, cap);
+  }
   if (e != cudaSuccess) return cuda_fail(e, "topk_kernel launch");
   return WPT_OK;
 }
