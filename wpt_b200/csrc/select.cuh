@@ -108,6 +108,7 @@ __global__ void __launch_bounds__(192, 1)
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int groups = p.B * p.groups_per_row;
+  griddep_wait();  // lse comes from the kernel before (programmatic dependent launch)
 
   // the CTA's range of work
   int64_t range_lo = 0, range_hi = 0;
@@ -426,6 +427,7 @@ __global__ void __launch_bounds__(TOPK_THREADS)
   __shared__ int s_ncand;
   __shared__ uint32_t s_mm[2];  // this slice's minimum and maximum key
   __shared__ int s_tot[2];      // this slice's keys above the threshold and equal to it
+  griddep_wait();  // the scores come from the kernel before (programmatic dependent launch)
   if (K <= 0) return;
   const int64_t row = blockIdx.x / SLICES;
   const uint32_t rank = SLICES > 1 ? cluster_rank() : 0u;

@@ -355,8 +355,17 @@ int launch_score(const CUtensorMap& tq, const CUtensorMap& tk, const wpt::ScoreP
   int sms = 148;
   current_device(&sms);
   const dim3 grid = p.balanced ? dim3(sms) : dim3(groups, splits);  // balanced: one CTA per SM
-  kernel<<<grid, 192, L::BYTES, stream>>>(tq, tk, p);
-  cudaError_t e = cudaGetLastError();
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;  // waits for lse on the device
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cfg.gridDim = grid;
+  cfg.blockDim = dim3(192);
+  cfg.dynamicSmemBytes = L::BYTES;
+  cfg.stream = stream;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, tq, tk, p);
   if (e != cudaSuccess) return cuda_fail(e, "score_kernel launch");
   return WPT_OK;
 }
@@ -1000,13 +1009,15 @@ extern "C" int wpt_attn_topk(const void* q, const void* k, int64_t k_stride_b, i
   }();
   const bool pair = pair_env != 0 && queries < sms;
   cudaLaunchConfig_t cfg = {};
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = 2;
-  attr[0].val.clusterDim.y = 1;
-  attr[0].val.clusterDim.z = 1;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;  // waits for the scores on the device
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  attr[1].id = cudaLaunchAttributeClusterDimension;
+  attr[1].val.clusterDim.x = 2;
+  attr[1].val.clusterDim.y = 1;
+  attr[1].val.clusterDim.z = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = pair ? 1 : 0;
+  cfg.numAttrs = pair ? 2 : 1;
   cfg.gridDim = dim3(static_cast<unsigned>(pair ? 2 * queries : queries));
   cfg.blockDim = dim3(wpt::TOPK_THREADS);
   cfg.dynamicSmemBytes = smem;
