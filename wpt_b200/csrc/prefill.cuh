@@ -444,11 +444,6 @@ __global__ void __launch_bounds__(PrefillLayout<C, QB, NS>::THREADS, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *s_tmem;  // S_A at column 0, S_B at 128, O_A at 256, O_B at 256 + C
-  // launched as a programmatic dependent of the kernel before it on the
-  // stream: the set-up above ran while that kernel finished; nothing in
-  // global memory is read or written before it has (a no-op otherwise)
-  griddep_wait();
-  griddep_launch();  // the kernel after this one may start its own set-up
 
   // Each role ends with its own __syncthreads (the CTA's last barrier), so
   // no code runs under two different register limits.

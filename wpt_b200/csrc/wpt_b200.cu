@@ -234,17 +234,6 @@ int prefill_poly8() {
   return v;
 }
 
-// 1: the key-stream and prefill kernels launch as programmatic dependents
-// of the kernel before them on the stream (WPT_B200_PDL = 0 or 1 overrides).
-int pdl_enabled() {
-  static int v = -1;
-  if (v < 0) {
-    const char* env = getenv("WPT_B200_PDL");
-    v = env ? (atoi(env) != 0) : 1;
-  }
-  return v;
-}
-
 template <int C, int POLY8, bool CLUSTER>
 int launch_prefill_p(const wpt::PrefillParams& p, const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
                      const CUtensorMap& to, cudaStream_t stream) {
@@ -272,20 +261,13 @@ int launch_prefill_p(const wpt::PrefillParams& p, const CUtensorMap& tq, const C
   if (p.cluster && (grid != p.items || p.items % 2 != 0))
     return fail(WPT_ERR_INVALID, "prefill cluster mode needs one item per CTA (%d items, %d SMs)", p.items, sms);
   cudaLaunchConfig_t cfg = {};
-  cudaLaunchAttribute attr[2];
-  int na = 0;
-  if (pdl_enabled()) {  // its set-up overlaps the tail of the kernel before it (it waits on the device)
-    attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[na++].val.programmaticStreamSerializationAllowed = 1;
-  }
-  if (p.cluster) {  // cluster mode: a pair's two splits per cluster
-    attr[na].id = cudaLaunchAttributeClusterDimension;
-    attr[na].val.clusterDim.x = 2;
-    attr[na].val.clusterDim.y = 1;
-    attr[na++].val.clusterDim.z = 1;
-  }
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;  // cluster mode: a pair's two splits per cluster
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = na;
+  cfg.numAttrs = p.cluster ? 1 : 0;
   cfg.gridDim = dim3(grid);
   cfg.blockDim = dim3(L::THREADS);
   cfg.dynamicSmemBytes = L::BYTES;
@@ -310,6 +292,17 @@ int launch_prefill(const wpt::PrefillParams& p, const CUtensorMap& tq, const CUt
   }
 }
 
+// 1: the key-stream kernel launches as a programmatic dependent of the
+// kernel before it on the stream (WPT_B200_PDL = 0 or 1 overrides).
+int stream_pdl() {
+  static int v = -1;
+  if (v < 0) {
+    const char* env = getenv("WPT_B200_PDL");
+    v = env ? (atoi(env) != 0) : 1;
+  }
+  return v;
+}
+
 template <int NCOL, int STAGES, bool GATHER>
 int launch_stream_n(const CUtensorMap& tk, const CUtensorMap& tv, const wpt::StreamParams& p, int groups,
                     cudaStream_t stream) {
@@ -320,7 +313,7 @@ int launch_stream_n(const CUtensorMap& tk, const CUtensorMap& tv, const wpt::Str
   cudaLaunchConfig_t cfg = {};
   cudaLaunchAttribute attr[2];
   int na = 0;
-  if (pdl_enabled()) {  // its set-up overlaps the tail of the kernel before it (it waits on the device)
+  if (stream_pdl()) {  // its set-up overlaps the tail of the kernel before it (it waits on the device)
     attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[na++].val.programmaticStreamSerializationAllowed = 1;
   }
