@@ -17,12 +17,14 @@
 // (coalesced: consecutive threads, consecutive keys). Key tiles of a query
 // group are split over gridDim.y; scores need no merge.
 //
-// topk_kernel: one CTA per query. Scores become order-preserving 32-bit
-// keys (cached in shared memory when the row fits); a histogram over the
-// keys' range and a sort of the one bin that holds the top_k-th key find it
-// (radix passes when that bin is crowded); a block scan then writes every
-// row above it and, among rows equal to it, the lowest row indices until
-// top_k are chosen. Deterministic; ties resolve by row index.
+// topk_kernel: one CTA per query, or (fewer queries than SMs) a 2-CTA
+// cluster per query, each CTA one half of the row. Scores become
+// order-preserving 32-bit keys (cached in shared memory when the slice
+// fits); a histogram over the keys' range (summed over the cluster) and a
+// sort of the one bin that holds the top_k-th key find it (radix passes
+// when that bin is crowded); a block scan then writes every row above it
+// and, among rows equal to it, the lowest row indices until top_k are
+// chosen. Deterministic; ties resolve by row index.
 #pragma once
 
 #include <climits>
