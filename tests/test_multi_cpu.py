@@ -5,7 +5,9 @@ their merge into one partial in the rank's chunk of the shared buffer, the
 in-place all-gather, the grouped merge) with the GPU calls it makes
 (ops.partials_plan, ops.stream_partials, ops.merge_partial,
 ops.merge_groups) replaced by CPU restatements, since this suite has no
-GPU; the kernels themselves are checked by the gpu tests."""
+GPU; the kernels themselves are checked by the gpu tests. The peer
+exchange's set-up (multi.PeerExchange) runs with its library calls faked, to
+show that a failure on one rank fails every rank together."""
 
 import os
 import socket
@@ -136,3 +138,75 @@ def test_long_row_split_over_gloo_ranks_equals_whole(world, with_sink):
     ref, ref_lse = oat.range_attention(q.numpy(), k.numpy(), v.numpy(), np.array([[700, 999]]), 0.25, sink=sink)
     assert np.abs(result["out"] - ref).max() < 1e-5
     assert np.abs(result["lse"] - ref_lse).max() < 1e-5
+
+
+class _FakePeerLib:
+    """Stands in for the library's peer-buffer calls on a CPU rank: `fail`
+    names the call that fails on this rank ("alloc", "open" or None)."""
+
+    def __init__(self, rank, fail):
+        self.rank, self.fail, self.closed = rank, fail, []
+
+    def wpt_peer_bytes(self, world, rows, C):
+        return 4096
+
+    def wpt_peer_alloc(self, nbytes, buffer, handle):
+        if self.fail == "alloc":
+            return 3
+        buffer._obj.value = 256 * (self.rank + 1)
+        handle.raw = bytes([self.rank]) * 64
+        return 0
+
+    def wpt_peer_open(self, handle, buffer):
+        if self.fail == "open":
+            return 3
+        buffer._obj.value = 4096 * (handle[0] + 1)
+        return 0
+
+    def wpt_peer_close(self, buffer, opened):
+        self.closed.append((buffer, opened))
+        return 0
+
+    def wpt_last_error(self):
+        return b"no peer memory here"
+
+
+def _peer_setup_rank(rank, world, port, fail_rank, fail, result):
+    import contextlib
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        fake = _FakePeerLib(rank, fail if rank == fail_rank else None)
+        multi._lib.lib = lambda: fake
+        multi.torch.cuda.device = lambda device: contextlib.nullcontext()
+        try:
+            multi.PeerExchange(8, 128, world, rank, None, "cpu")
+            result[rank] = ("built", fake.closed)
+        except multi.PeerSetupFailed:
+            result[rank] = ("failed", fake.closed)
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("fail", ["alloc", "open", None])
+def test_peer_setup_fails_on_every_rank_together(fail):
+    """A rank that cannot allocate or map an exchange buffer makes every rank
+    raise PeerSetupFailed (so all of them take the all-gather exchange), each
+    having unmapped what it mapped and freed its own buffer; with no failure
+    every rank builds it."""
+    world = 3
+    manager = mp.get_context("spawn").Manager()
+    result = manager.dict()
+    mp.start_processes(_peer_setup_rank, args=(world, _free_port(), 1, fail, result), nprocs=world,
+                       start_method="spawn", join=True)
+    for rank in range(world):
+        state, closed = result[rank]
+        if fail is None:
+            assert state == "built" and closed == []
+            continue
+        assert state == "failed"
+        own = [c for c in closed if c[1] == 0]
+        assert own == ([] if (fail == "alloc" and rank == 1) else [(256 * (rank + 1), 0)])
+        mapped = [c for c in closed if c[1] == 1]
+        if fail == "open" and rank != 1:  # the ranks that mapped their peers unmapped them
+            assert len(mapped) == world - 1

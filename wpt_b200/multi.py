@@ -62,32 +62,54 @@ def key_shard(n_rows, world, rank):
 _PLANS = {}  # (shape, shard length, world, device, group) -> the long row's buffers on this rank
 
 
+class PeerSetupFailed(RuntimeError):
+    """Some rank could not allocate or map an exchange buffer; every rank
+    raises it together (and has released what it made), so the ranks fall
+    back to the all-gather exchange together."""
+
+
 class PeerExchange:
     """This rank's exchange buffer for one long-row shape and the other
     ranks' buffers mapped into this process (wpt_peer_alloc / wpt_peer_open
-    over CUDA IPC). Built by every rank of `group` together (it gathers the
-    handles and ends with a barrier, so no rank writes into a buffer before
-    its owner has zeroed it); kept for the life of the process."""
+    over CUDA IPC). Built by every rank of `group` together: the handles are
+    gathered, every rank reports whether it could allocate and map, and the
+    set-up ends with a barrier, so no rank writes into a buffer before its
+    owner has zeroed it. A failure on any rank raises PeerSetupFailed on
+    every rank. Kept for the life of the process."""
 
     def __init__(self, rows, C, world, rank, group, device):
         lib = _lib.lib()
         nbytes = lib.wpt_peer_bytes(world, rows, C)
-        if nbytes == 0:
-            raise NotImplementedError(f"peer exchange of {rows} rows over {world} ranks")
         own = ctypes.c_void_p()
         handle = ctypes.create_string_buffer(64)
+        self.peers = (ctypes.c_void_p * world)()
+        opened = []
         with torch.cuda.device(device):
-            _lib.check(lib.wpt_peer_alloc(nbytes, ctypes.byref(own), handle))
+            ok = nbytes > 0 and lib.wpt_peer_alloc(nbytes, ctypes.byref(own), handle) == _lib.OK
             handles = [None] * world
-            dist.all_gather_object(handles, handle.raw, group=group)
-            self.peers = (ctypes.c_void_p * world)()
-            for g in range(world):
-                if g == rank:
-                    self.peers[g] = own.value
-                else:
+            dist.all_gather_object(handles, handle.raw if ok else None, group=group)
+            ok = ok and all(h is not None for h in handles)
+            if ok:
+                for g in range(world):
+                    if g == rank:
+                        self.peers[g] = own.value
+                        continue
                     mapped = ctypes.c_void_p()
-                    _lib.check(lib.wpt_peer_open(handles[g], ctypes.byref(mapped)))
+                    if lib.wpt_peer_open(handles[g], ctypes.byref(mapped)) != _lib.OK:
+                        ok = False
+                        break
                     self.peers[g] = mapped.value
+                    opened.append(mapped.value)
+            flags = [None] * world
+            dist.all_gather_object(flags, bool(ok), group=group)
+            if not all(flags):
+                for ptr in opened:
+                    lib.wpt_peer_close(ptr, 1)
+                dist.barrier(group=group)  # every rank has unmapped before any buffer is freed
+                if own.value:
+                    lib.wpt_peer_close(own.value, 0)
+                raise PeerSetupFailed("a rank could not set up its exchange buffer: " +
+                                      lib.wpt_last_error().decode(errors="replace"))
             dist.barrier(group=group)
         self.world, self.rank = world, rank
 
@@ -120,9 +142,13 @@ def _long_plan(q, n_local, world, group):
         splits, _ = ops.partials_plan(q.shape, n_local, q.device)
         part_o = torch.empty(splits, rows, C, dtype=torch.float32, device=q.device)
         part_lse = torch.empty(splits, rows, dtype=torch.float32, device=q.device)
+        parts = None
         if _peer_capable(q, world, rows, group):
-            parts = PeerExchange(rows, C, world, dist.get_rank(group), group, q.device)
-        else:
+            try:
+                parts = PeerExchange(rows, C, world, dist.get_rank(group), group, q.device)
+            except PeerSetupFailed:
+                parts = None  # every rank takes the all-gather exchange
+        if parts is None:
             chunk = (rows * (C + 1) + 3) // 4 * 4
             parts = torch.empty(world, chunk, dtype=torch.float32, device=q.device)
         plan = _PLANS[key] = (splits, part_o, part_lse, parts)
