@@ -112,3 +112,54 @@ def test_long_row_over_nccl_ranks_equals_one_gpu_and_oracle(peer):
                 g_out, g_lse, g_status = result[(rank, "graph")]
                 assert g_status == 0
                 assert np.array_equal(g_out, out) and np.array_equal(g_lse, lse)
+
+
+def _skip_rank(rank, world, port, N, result):
+    import datetime
+
+    import torch.distributed as dist
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), WPT_B200_PEER="1", NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    device = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
+                            device_id=device)
+    try:
+        import wpt_b200
+        from wpt_b200 import multi
+        start, stop = multi.key_shard(N, world, rank)
+        q, e, sink = _inputs(N, 1)
+        qd, shard, sd = q.to(device), e[:, start:stop].to(device), sink.to(device)
+        pos = torch.tensor([[N - 8]], device=device)
+        multi.long_decode(qd, shard[..., :C], shard[..., C:], start, pos, C ** -0.5, sink=sd)
+        torch.cuda.synchronize()
+        first = wpt_b200.device_status()
+        dist.barrier()  # between steps: nothing of either rank in flight
+        if rank == 0:  # rank 1 skips this call: rank 0's wait for its partial runs out
+            t = __import__("time").perf_counter()
+            multi.long_decode(qd, shard[..., :C], shard[..., C:], start, pos, C ** -0.5, sink=sd)
+            torch.cuda.synchronize()
+            result[rank] = (first, wpt_b200.device_status(), __import__("time").perf_counter() - t)
+        else:
+            result[rank] = (first, wpt_b200.device_status(), 0.0)
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_a_rank_that_skips_a_call_makes_the_others_wait_run_out():
+    """Rank 1 skips a call between steps: rank 0's exchange kernel waits for
+    its partial for the bounded 2 s, then returns with status bit 0 set (no
+    fault, no hang); the first call, made by both ranks, reported nothing.
+    Child processes on two GPUs, NVLS off, plain peer stores only."""
+    from wpt_b200 import build
+    build.build()
+    world, N = 2, 20000
+    manager = mp.get_context("spawn").Manager()
+    result = manager.dict()
+    mp.start_processes(_skip_rank, args=(world, _free_port(), N, result), nprocs=world, start_method="spawn",
+                       join=True)
+    first0, after0, seconds = result[0]
+    first1, after1, _ = result[1]
+    assert first0 == 0 and first1 == 0 and after1 == 0
+    assert after0 & 1 and 1.5 < seconds < 30
