@@ -1,8 +1,9 @@
 """The multi-GPU partitioning logic on CPU gloo ranks (world size 2 and 3):
 row sharding, length-balanced decode rows, and the long-row key split. The
-long row runs long_decode's production branch (each rank's split partials,
+long row runs long_decode's all-gather branch, the one a gloo group (and any
+group that cannot map its peers' memory) takes: each rank's split partials,
 their merge into one partial in the rank's chunk of the shared buffer, the
-in-place all-gather, the grouped merge) with the GPU calls it makes
+in-place all-gather, the grouped merge, with the GPU calls it makes
 (ops.partials_plan, ops.stream_partials, ops.merge_partial,
 ops.merge_groups) replaced by CPU restatements, since this suite has no
 GPU; the kernels themselves are checked by the gpu tests. The peer
