@@ -1,10 +1,11 @@
 /*
  * wpt_attn.h: the C ABI of the B200 (sm_100a) attention library
  * libwpt_b200.so. Plain pointers, sizes and a CUDA stream handle; no torch
- * types. Every entry point only enqueues work on `stream` (no host
- * synchronisation, no allocation: buffers, including scratch, come from
- * the caller) and returns WPT_OK or an error code whose text
- * wpt_last_error() gives.
+ * types. Every entry point that computes only enqueues work on `stream` (no
+ * host synchronisation, no allocation: buffers, including scratch, come from
+ * the caller; the long row's one-time exchange set-up, wpt_peer_alloc and
+ * wpt_peer_open, is the exception) and returns WPT_OK or an error code whose
+ * text wpt_last_error() gives.
  *
  * These replace the kernel-form contract of the reference (paths relative
  * to the reference repository, packages/wpt-model/src/wpt_model/):
