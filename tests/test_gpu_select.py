@@ -168,3 +168,24 @@ def test_decode_choice_over_rows_longer_than_the_key_cache(wb):
     k = _np(e[..., :C])
     _, _, expected = oat.exact_attention(_np(q), k, _np(e[..., C:]), positions.numpy(), C ** -0.5, top_k, window)
     _assert_chosen_alike(_np(q), k, positions.numpy(), C ** -0.5, chosen.cpu().numpy(), expected)
+
+
+@pytest.mark.parametrize("top_k", [64, 1])
+def test_decode_choice_with_a_few_more_rows_than_top_k(wb, top_k):
+    """Decode rows with top_k + 1 .. top_k + 16 candidates and a few about
+    twice top_k: with fewer queries than SMs each query's candidates are cut
+    into two slices (the second from the row's rounded middle), so the
+    second slice is small, or empty (2 candidates, top_k 1), and the bin's
+    keys come from both."""
+    g = torch.Generator().manual_seed(13 + top_k)
+    B, T, H, C, N, window = 20, 1, 32, 128, 1024, 8
+    q = torch.randn(B, T, H, C, generator=g).bfloat16()
+    e = torch.randn(B, N, 2 * C, generator=g).bfloat16()
+    counts = torch.tensor(list(range(top_k + 1, top_k + 17)) + [2 * top_k - 1, 2 * top_k, 2 * top_k + 3, 5])
+    positions = (counts + window - 1).view(B, 1)  # count = position - window + 1 candidates
+    qd, ed = q.cuda(), e.cuda()
+    _, chosen = wb.exact_attention(qd, ed[..., :C], ed[..., C:], positions.cuda(), C ** -0.5, top_k, window)
+    assert wb.device_status() == 0
+    k = _np(e[..., :C])
+    _, _, expected = oat.exact_attention(_np(q), k, _np(e[..., C:]), positions.numpy(), C ** -0.5, top_k, window)
+    _assert_chosen_alike(_np(q), k, positions.numpy(), C ** -0.5, chosen.cpu().numpy(), expected)
