@@ -15,8 +15,9 @@ bracketed by barriers and its time is the maximum over ranks. A secondary
 line keeps the weak-scaling form (8 rows on every rank). Other secondary
 lines: decode attention GB/s (config 3, global and window-1024 rows, the
 64 rows balanced over the ranks by length; the 262,144-token row split
-along its keys over the ranks with one NCCL all-gather), tree verification
-(config 4) and the acceptance step (config 4).
+along its keys over the ranks, each rank's partial sent to the others over
+NVLink by one exchange kernel), tree verification (config 4) and the
+acceptance step (config 4).
 
 --case config5 runs BASELINE config 5 end to end (the reference's own WPT
 model, 64 rows, 2048-token prompts, 256 generated tokens) once with the
